@@ -1,0 +1,575 @@
+// Module registry: which code images are loaded, under which content hash,
+// and which entry points they export. Graph persistence stores kernel nodes as
+// (image hash, entry name) and resolves them back to functions on LOAD.
+//
+// Two kinds of image:
+//  * own images: cubins built by this repository, loaded through
+//    fb_registry_load_image with their exact bytes and size. They are hashed
+//    (CRC-64/XZ over the bytes) and stored in fatbin_image_packed.img.
+//  * foreign images: loaded by other code (e.g. cudart inside torch) through
+//    the interposed cuLibraryLoadData / cuModuleLoadData*. Their bytes are
+//    never read or copied: the image is identified by the shared object that
+//    contains it (dladdr) and the offset of the image pointer from that
+//    object's load base, and re-loaded on LOAD by handing the driver the same
+//    pointer in the new process. Images not backed by a loaded object (heap
+//    buffers) cannot be identified; graphs using them fail at SAVE.
+//
+// Parity: reference csrc/hook.cpp:558-727 (dump_fatbin_and_info), 1059-1182
+// (entry-point enumeration), 1589-1700 (pack format), 3514-3572 (queries),
+// 3687-4183 (load_cuda_modules_and_libraries). The pack files keep the
+// reference's layout ([u64 hash][u64 size][bytes] records; text blocks of
+// hash / loader,options / count / names / ---) so archives look alike.
+#include <dlfcn.h>
+#include <fcntl.h>
+#include <link.h>
+#include <limits.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <fstream>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../common/fb_crc64.h"
+#include "hook_internal.h"
+
+namespace fbh {
+namespace {
+
+struct Image {
+  uint64_t hash = 0;
+  std::string loader = "cuLibraryLoadData";  // base function name of the load
+  bool own = false;
+  bool used = false;
+  std::vector<uint8_t> bytes;   // own images only
+  std::string src_file;         // foreign: shared object path
+  uint64_t src_offset = 0;      // foreign: image pointer - object load base
+  CUlibrary lib = nullptr;
+  CUmodule mod = nullptr;
+  std::vector<std::string> names;
+  std::unordered_map<std::string, CUkernel> kernels;
+  std::unordered_map<std::string, CUfunction> functions;  // module-loaded images
+};
+
+struct FnKey {
+  uint64_t hash;
+  std::string name;
+};
+
+std::recursive_mutex g_mu;
+std::map<uint64_t, std::unique_ptr<Image>> g_images;
+std::unordered_map<CUlibrary, uint64_t> g_lib_to_hash;
+std::unordered_map<CUmodule, uint64_t> g_mod_to_hash;
+std::unordered_map<CUfunction, FnKey> g_fn_to_key;
+std::unordered_map<CUkernel, FnKey> g_kernel_to_key;
+bool g_skip_processing = false;
+std::string g_pack_on_exit;
+thread_local int t_own_load_depth = 0;
+
+void enumerate_library(Image& img) {
+  const FbDriver* d = fb_driver();
+  unsigned int count = 0;
+  if (!d->cuLibraryGetKernelCount || d->cuLibraryGetKernelCount(&count, img.lib) != CUDA_SUCCESS)
+    return;
+  std::vector<CUkernel> ks(count);
+  if (count && d->cuLibraryEnumerateKernels(ks.data(), count, img.lib) != CUDA_SUCCESS) return;
+  img.names.clear();
+  for (CUkernel k : ks) {
+    const char* name = nullptr;
+    if (d->cuKernelGetName(&name, k) != CUDA_SUCCESS || !name) continue;
+    img.names.emplace_back(name);
+    img.kernels[name] = k;
+    g_kernel_to_key[k] = FnKey{img.hash, name};
+  }
+  CUmodule mod = nullptr;
+  if (d->cuLibraryGetModule && d->cuLibraryGetModule(&mod, img.lib) == CUDA_SUCCESS && mod)
+    g_mod_to_hash[mod] = img.hash;
+}
+
+void enumerate_module(Image& img) {
+  const FbDriver* d = fb_driver();
+  unsigned int count = 0;
+  if (!d->cuModuleGetFunctionCount || d->cuModuleGetFunctionCount(&count, img.mod) != CUDA_SUCCESS)
+    return;
+  std::vector<CUfunction> fs(count);
+  if (count && d->cuModuleEnumerateFunctions(fs.data(), count, img.mod) != CUDA_SUCCESS) return;
+  img.names.clear();
+  for (CUfunction f : fs) {
+    const char* name = nullptr;
+    if (d->cuFuncGetName(&name, f) != CUDA_SUCCESS || !name) continue;
+    img.names.emplace_back(name);
+    img.functions[name] = f;
+    g_fn_to_key[f] = FnKey{img.hash, name};
+  }
+  g_mod_to_hash[img.mod] = img.hash;
+}
+
+// Identify a foreign image pointer by the loaded object that contains it.
+bool identify_foreign(const void* code, std::string* file, uint64_t* offset) {
+  Dl_info info;
+  if (!code || dladdr(code, &info) == 0 || !info.dli_fname || !info.dli_fbase) return false;
+  char resolved[PATH_MAX];
+  const char* path = realpath(info.dli_fname, resolved) ? resolved : info.dli_fname;
+  *file = path;
+  *offset = reinterpret_cast<uint64_t>(code) - reinterpret_cast<uint64_t>(info.dli_fbase);
+  return true;
+}
+
+uint64_t foreign_hash(const std::string& file, uint64_t offset) {
+  struct stat st;
+  uint64_t fsize = (stat(file.c_str(), &st) == 0) ? static_cast<uint64_t>(st.st_size) : 0;
+  std::string key = "file:" + file + "@" + std::to_string(offset) + "#" + std::to_string(fsize);
+  return fb::crc64(key.data(), key.size());
+}
+
+// Load base of a shared object in this process (loading it if needed).
+const uint8_t* object_base(const std::string& file) {
+  void* h = dlopen(file.c_str(), RTLD_NOLOAD | RTLD_LAZY);
+  if (!h) h = dlopen(file.c_str(), RTLD_LAZY | RTLD_LOCAL);
+  if (!h) return nullptr;
+  struct link_map* lm = nullptr;
+  if (dlinfo(h, RTLD_DI_LINKMAP, &lm) != 0 || !lm) return nullptr;
+  return reinterpret_cast<const uint8_t*>(lm->l_addr);
+}
+
+Image* register_foreign(const void* code, const char* tag) {
+  std::string file;
+  uint64_t off = 0;
+  if (!identify_foreign(code, &file, &off)) return nullptr;
+  uint64_t h = foreign_hash(file, off);
+  auto& slot = g_images[h];
+  if (!slot) {
+    slot.reset(new Image());
+    slot->hash = h;
+    slot->src_file = file;
+    slot->src_offset = off;
+  }
+  slot->loader = tag;
+  return slot.get();
+}
+
+std::string hex16(uint64_t v) {
+  char buf[24];
+  snprintf(buf, sizeof(buf), "%016llx", static_cast<unsigned long long>(v));
+  return buf;
+}
+
+void pack_at_exit() {
+  if (!g_pack_on_exit.empty()) fb_registry_pack(g_pack_on_exit.c_str());
+}
+
+}  // namespace
+
+bool registry_in_own_load() { return t_own_load_depth > 0; }
+
+void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g_skip_processing || t_own_load_depth > 0) return;
+  Image* img = register_foreign(code, tag);
+  if (!img) return;
+  img->lib = lib;
+  g_lib_to_hash[lib] = img->hash;
+  enumerate_library(*img);
+}
+
+void registry_on_module_loaded(CUmodule mod, const void* code, const char* tag) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g_skip_processing || t_own_load_depth > 0) return;
+  Image* img = register_foreign(code, tag);
+  if (!img) return;
+  img->mod = mod;
+  enumerate_module(*img);
+}
+
+void registry_on_library_file_loaded(CUlibrary lib, const char* path) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g_skip_processing || !path) return;
+  char resolved[PATH_MAX];
+  std::string file = realpath(path, resolved) ? resolved : path;
+  uint64_t h = foreign_hash(file, UINT64_MAX);
+  auto& slot = g_images[h];
+  if (!slot) slot.reset(new Image());
+  slot->hash = h;
+  slot->src_file = file;
+  slot->src_offset = UINT64_MAX;  // whole file
+  slot->loader = "cuLibraryLoadFromFile";
+  slot->lib = lib;
+  g_lib_to_hash[lib] = h;
+  enumerate_library(*slot);
+}
+
+void registry_on_module_file_loaded(CUmodule mod, const char* path) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g_skip_processing || !path) return;
+  char resolved[PATH_MAX];
+  std::string file = realpath(path, resolved) ? resolved : path;
+  uint64_t h = foreign_hash(file, UINT64_MAX);
+  auto& slot = g_images[h];
+  if (!slot) slot.reset(new Image());
+  slot->hash = h;
+  slot->src_file = file;
+  slot->src_offset = UINT64_MAX;
+  slot->loader = "cuModuleLoad";
+  slot->mod = mod;
+  enumerate_module(*slot);
+}
+
+}  // namespace fbh
+
+using namespace fbh;
+
+extern "C" {
+
+fb_status fb_registry_load_image(const void* data, size_t size, const char* tag,
+                                 CUlibrary* out_lib, uint64_t* out_hash) {
+  if (!data || size == 0) {
+    fb_set_error(FB_ERR_INVALID, "load_image: empty image");
+    return FB_ERR_INVALID;
+  }
+  const uint64_t h = fb::crc64(data, size);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto& slot = g_images[h];
+  if (slot && slot->lib) {
+    if (out_lib) *out_lib = slot->lib;
+    if (out_hash) *out_hash = h;
+    return FB_OK;
+  }
+  if (!slot) slot.reset(new Image());
+  Image& img = *slot;
+  img.hash = h;
+  img.own = true;
+  img.loader = "cuLibraryLoadData";
+  img.bytes.assign(static_cast<const uint8_t*>(data), static_cast<const uint8_t*>(data) + size);
+  (void)tag;
+  const FbDriver* d = fb_driver();
+  if (!d->cuLibraryLoadData) {
+    fb_set_error(FB_ERR_DRIVER, "CUDA driver not available (%s)", fb_driver_path());
+    return FB_ERR_DRIVER;
+  }
+  ++t_own_load_depth;
+  CUresult rc = d->cuLibraryLoadData(&img.lib, img.bytes.data(), nullptr, nullptr, 0, nullptr,
+                                     nullptr, 0);
+  --t_own_load_depth;
+  if (rc != CUDA_SUCCESS) return drv_error(rc, "cuLibraryLoadData(own image)");
+  g_lib_to_hash[img.lib] = h;
+  enumerate_library(img);
+  if (out_lib) *out_lib = img.lib;
+  if (out_hash) *out_hash = h;
+  return FB_OK;
+}
+
+fb_status fb_registry_library(uint64_t hash, CUlibrary* out_lib) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto it = g_images.find(hash);
+  if (it == g_images.end() || !it->second->lib) {
+    fb_set_error(FB_ERR_NOT_FOUND, "no loaded library with hash %016llx", (unsigned long long)hash);
+    return FB_ERR_NOT_FOUND;
+  }
+  *out_lib = it->second->lib;
+  return FB_OK;
+}
+
+fb_status fb_registry_function(uint64_t hash, const char* name, CUfunction* out_fn,
+                               CUkernel* out_kernel) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto it = g_images.find(hash);
+  if (it == g_images.end()) {
+    fb_set_error(FB_ERR_NOT_FOUND, "image %016llx is not loaded (missing from the archive?)",
+                 (unsigned long long)hash);
+    return FB_ERR_NOT_FOUND;
+  }
+  Image& img = *it->second;
+  const FbDriver* d = fb_driver();
+  if (img.lib) {
+    auto kit = img.kernels.find(name);
+    CUkernel k = nullptr;
+    if (kit != img.kernels.end()) {
+      k = kit->second;
+    } else {
+      CUresult rc = d->cuLibraryGetKernel(&k, img.lib, name);
+      if (rc != CUDA_SUCCESS) {
+        fb_set_error(FB_ERR_NOT_FOUND, "entry point '%s' not found in image %016llx", name,
+                     (unsigned long long)hash);
+        return FB_ERR_NOT_FOUND;
+      }
+      img.kernels[name] = k;
+      g_kernel_to_key[k] = FnKey{hash, name};
+    }
+    CUfunction f = nullptr;
+    CUresult rc = d->cuKernelGetFunction(&f, k);
+    if (rc != CUDA_SUCCESS) return drv_error(rc, "cuKernelGetFunction");
+    g_fn_to_key[f] = FnKey{hash, name};
+    if (out_fn) *out_fn = f;
+    if (out_kernel) *out_kernel = k;
+    return FB_OK;
+  }
+  if (img.mod) {
+    auto fit = img.functions.find(name);
+    CUfunction f = nullptr;
+    if (fit != img.functions.end()) {
+      f = fit->second;
+    } else if (d->cuModuleGetFunction(&f, img.mod, name) != CUDA_SUCCESS) {
+      fb_set_error(FB_ERR_NOT_FOUND, "entry point '%s' not found in module %016llx", name,
+                   (unsigned long long)hash);
+      return FB_ERR_NOT_FOUND;
+    }
+    g_fn_to_key[f] = FnKey{hash, name};
+    if (out_fn) *out_fn = f;
+    if (out_kernel) *out_kernel = nullptr;
+    return FB_OK;
+  }
+  fb_set_error(FB_ERR_NOT_FOUND, "image %016llx has no live handle", (unsigned long long)hash);
+  return FB_ERR_NOT_FOUND;
+}
+
+fb_status fb_registry_identify(CUfunction fn, uint64_t* out_hash, char* name_buf, size_t cap) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  const FnKey* key = nullptr;
+  auto it = g_fn_to_key.find(fn);
+  if (it != g_fn_to_key.end()) key = &it->second;
+  if (!key) {
+    auto kit = g_kernel_to_key.find(reinterpret_cast<CUkernel>(fn));
+    if (kit != g_kernel_to_key.end()) key = &kit->second;
+  }
+  FnKey tmp;
+  if (!key) {
+    // Fall back to the driver: owning module + name.
+    const FbDriver* d = fb_driver();
+    CUmodule mod = nullptr;
+    const char* name = nullptr;
+    if (d->cuFuncGetModule && d->cuFuncGetModule(&mod, fn) == CUDA_SUCCESS && mod &&
+        d->cuFuncGetName && d->cuFuncGetName(&name, fn) == CUDA_SUCCESS && name) {
+      auto mit = g_mod_to_hash.find(mod);
+      if (mit != g_mod_to_hash.end()) {
+        tmp = FnKey{mit->second, name};
+        key = &tmp;
+        g_fn_to_key[fn] = tmp;
+      }
+    }
+    if (!key) {
+      const char* n = nullptr;
+      if (d->cuFuncGetName) d->cuFuncGetName(&n, fn);
+      fb_set_error(FB_ERR_UNSUPPORTED,
+                   "kernel '%s' comes from a module the registry did not see load; it cannot be "
+                   "persisted (load the hook with LD_PRELOAD, or use kernels built in-tree)",
+                   n ? n : "?");
+      return FB_ERR_UNSUPPORTED;
+    }
+  }
+  if (out_hash) *out_hash = key->hash;
+  if (name_buf && cap) {
+    snprintf(name_buf, cap, "%s", key->name.c_str());
+  }
+  return FB_OK;
+}
+
+fb_status fb_registry_mark_used(uint64_t hash) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto it = g_images.find(hash);
+  if (it == g_images.end()) {
+    fb_set_error(FB_ERR_NOT_FOUND, "mark_used: unknown image %016llx", (unsigned long long)hash);
+    return FB_ERR_NOT_FOUND;
+  }
+  it->second->used = true;
+  return FB_OK;
+}
+
+fb_status fb_registry_pack(const char* folder) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  std::string dir(folder);
+  mkdir(dir.c_str(), 0755);
+  std::ofstream img(dir + "/fatbin_image_packed.img", std::ios::binary | std::ios::trunc);
+  std::ofstream txt(dir + "/fatbin_entrypoint_packed.txt", std::ios::trunc);
+  if (!img || !txt) {
+    fb_set_error(FB_ERR_IO, "cannot write pack files in %s", folder);
+    return FB_ERR_IO;
+  }
+  for (auto& kv : g_images) {
+    const Image& im = *kv.second;
+    if (!im.used) continue;
+    txt << hex16(im.hash) << "\n" << im.loader;
+    if (im.own) {
+      const uint64_t h = im.hash, n = im.bytes.size();
+      img.write(reinterpret_cast<const char*>(&h), 8);
+      img.write(reinterpret_cast<const char*>(&n), 8);
+      img.write(reinterpret_cast<const char*>(im.bytes.data()), static_cast<std::streamsize>(n));
+    } else {
+      // Foreign image: identified, not copied.
+      txt << ",source=" << im.src_file << ",source_offset=" << im.src_offset;
+    }
+    txt << ",binary_flags=" << (im.own ? 0 : 1) << "\n" << im.names.size() << "\n";
+    for (const auto& n : im.names) txt << n << "\n";
+    txt << "---\n";
+  }
+  img.flush();
+  txt.flush();
+  if (!img || !txt) {
+    fb_set_error(FB_ERR_IO, "short write of pack files in %s", folder);
+    return FB_ERR_IO;
+  }
+  return FB_OK;
+}
+
+fb_status fb_registry_load_archive(const char* folder) {
+  std::string dir(folder);
+  std::ifstream txt(dir + "/fatbin_entrypoint_packed.txt");
+  if (!txt) {
+    fb_set_error(FB_ERR_NOT_FOUND, "missing %s/fatbin_entrypoint_packed.txt", folder);
+    return FB_ERR_NOT_FOUND;
+  }
+  // Read all own images from the .img into memory (hash -> bytes).
+  std::map<uint64_t, std::vector<uint8_t>> blobs;
+  {
+    std::ifstream img(dir + "/fatbin_image_packed.img", std::ios::binary);
+    if (img) {
+      for (;;) {
+        uint64_t h = 0, n = 0;
+        if (!img.read(reinterpret_cast<char*>(&h), 8)) break;
+        if (!img.read(reinterpret_cast<char*>(&n), 8)) {
+          fb_set_error(FB_ERR_IO, "truncated image record header in %s", folder);
+          return FB_ERR_IO;
+        }
+        if (n > (1ull << 34)) {
+          fb_set_error(FB_ERR_IO, "corrupt image size %llu", (unsigned long long)n);
+          return FB_ERR_IO;
+        }
+        std::vector<uint8_t> b(n);
+        if (n && !img.read(reinterpret_cast<char*>(b.data()), static_cast<std::streamsize>(n))) {
+          fb_set_error(FB_ERR_IO, "truncated image %016llx in %s", (unsigned long long)h, folder);
+          return FB_ERR_IO;
+        }
+        if (fb::crc64(b.data(), b.size()) != h) {
+          fb_set_error(FB_ERR_IO, "image %016llx fails its CRC-64 check (corrupt archive)",
+                       (unsigned long long)h);
+          return FB_ERR_IO;
+        }
+        blobs[h] = std::move(b);
+      }
+    }
+  }
+  std::string line;
+  const FbDriver* d = fb_driver();
+  while (std::getline(txt, line)) {
+    if (line.empty()) continue;
+    uint64_t h = strtoull(line.c_str(), nullptr, 16);
+    std::string spec;
+    if (!std::getline(txt, spec)) {
+      fb_set_error(FB_ERR_IO, "truncated entry-point list");
+      return FB_ERR_IO;
+    }
+    std::string count_s;
+    std::getline(txt, count_s);
+    size_t count = strtoull(count_s.c_str(), nullptr, 10);
+    std::vector<std::string> names(count);
+    for (size_t i = 0; i < count; ++i) std::getline(txt, names[i]);
+    std::string sep;
+    std::getline(txt, sep);
+    if (sep != "---") {
+      fb_set_error(FB_ERR_IO, "malformed entry-point list for %016llx", (unsigned long long)h);
+      return FB_ERR_IO;
+    }
+    // spec: loader[,key=value]*
+    std::map<std::string, std::string> opts;
+    std::string loader;
+    {
+      std::stringstream ss(spec);
+      std::string tok;
+      bool first = true;
+      while (std::getline(ss, tok, ',')) {
+        if (first) {
+          loader = tok;
+          first = false;
+          continue;
+        }
+        auto eq = tok.find('=');
+        if (eq != std::string::npos) opts[tok.substr(0, eq)] = tok.substr(eq + 1);
+      }
+    }
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    auto& slot = g_images[h];
+    if (slot && (slot->lib || slot->mod)) continue;  // already loaded in this process
+    if (!slot) slot.reset(new Image());
+    Image& im = *slot;
+    im.hash = h;
+    im.loader = loader;
+    im.used = true;
+    CUresult rc = CUDA_SUCCESS;
+    if (opts.count("source")) {
+      im.src_file = opts["source"];
+      im.src_offset = strtoull(opts["source_offset"].c_str(), nullptr, 10);
+      if (im.src_offset == UINT64_MAX) {
+        rc = loader == "cuModuleLoad"
+                 ? d->cuModuleLoad(&im.mod, im.src_file.c_str())
+                 : d->cuLibraryLoadFromFile(&im.lib, im.src_file.c_str(), nullptr, nullptr, 0,
+                                            nullptr, nullptr, 0);
+      } else {
+        const uint8_t* base = object_base(im.src_file);
+        if (!base) {
+          fb_set_error(FB_ERR_NOT_FOUND, "cannot map %s for image %016llx", im.src_file.c_str(),
+                       (unsigned long long)h);
+          return FB_ERR_NOT_FOUND;
+        }
+        const void* code = base + im.src_offset;
+        if (loader.rfind("cuModule", 0) == 0)
+          rc = d->cuModuleLoadData(&im.mod, code);
+        else
+          rc = d->cuLibraryLoadData(&im.lib, code, nullptr, nullptr, 0, nullptr, nullptr, 0);
+      }
+    } else {
+      auto bit = blobs.find(h);
+      if (bit == blobs.end()) {
+        fb_set_error(FB_ERR_IO, "image %016llx listed but missing from the .img pack",
+                     (unsigned long long)h);
+        return FB_ERR_IO;
+      }
+      im.own = true;
+      im.bytes = std::move(bit->second);
+      ++t_own_load_depth;
+      rc = d->cuLibraryLoadData(&im.lib, im.bytes.data(), nullptr, nullptr, 0, nullptr, nullptr, 0);
+      --t_own_load_depth;
+    }
+    if (rc != CUDA_SUCCESS) return drv_error(rc, "reloading archived image");
+    if (im.lib) {
+      g_lib_to_hash[im.lib] = h;
+      enumerate_library(im);
+    } else {
+      enumerate_module(im);
+    }
+    if (im.names.size() != count) {
+      fb_set_error(FB_ERR_IO, "image %016llx exports %zu entry points, archive lists %zu",
+                   (unsigned long long)h, im.names.size(), count);
+      return FB_ERR_IO;
+    }
+  }
+  return FB_OK;
+}
+
+void fb_registry_set_skip_processing(int enabled) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  g_skip_processing = enabled != 0;
+}
+
+void fb_registry_set_pack_on_exit(const char* folder_or_null) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  static bool registered = false;
+  g_pack_on_exit = folder_or_null ? folder_or_null : "";
+  if (!registered && !g_pack_on_exit.empty()) {
+    atexit(pack_at_exit);
+    registered = true;
+  }
+}
+
+size_t fb_registry_count(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return g_images.size();
+}
+
+}  // extern "C"

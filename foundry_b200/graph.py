@@ -1,0 +1,322 @@
+"""CUDA graph capture, persistence and restore (Python API).
+
+``CUDAGraph`` captures with torch's graph machinery (so torch's private
+memory pools and RNG registration keep working) and hands the captured
+``cudaGraph_t`` to the native core, which walks it node by node and can write
+it to ``graph_N.json`` + ``graph_N.cugraph``. A later process restores graphs
+with ``CUDAGraph.load`` or the two-phase ``start_graph_builds`` /
+``finish_graph_loads`` pipeline; restored graphs replay through the native
+restore engine (templates + on-demand parameter patches, see csrc/core/restore.h).
+
+Parity: reference python/foundry/graph.py:17-242 (CUDAGraph, graph,
+save_graph_manifest) and csrc/binding.cpp:115-338.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import sys
+from typing import Any, Sequence
+
+import torch
+
+from ._native import core
+
+OutputTensors = torch.Tensor | list[torch.Tensor] | tuple[torch.Tensor, ...]
+
+__all__ = ["CUDAGraph", "graph", "save_graph_manifest", "graph_pool_handle"]
+
+
+def graph_pool_handle():
+    return torch.cuda.graph_pool_handle()
+
+
+def _stream_handle() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+# ---- output tensor metadata --------------------------------------------------------------
+
+def _encode_outputs(outputs: OutputTensors | None) -> str:
+    if outputs is None:
+        return ""
+    if isinstance(outputs, torch.Tensor):
+        kind, items = "tensor", [outputs]
+    elif isinstance(outputs, (list, tuple)):
+        kind, items = ("list" if isinstance(outputs, list) else "tuple"), list(outputs)
+    else:
+        raise TypeError(f"output_tensors must be a tensor, list or tuple, got {type(outputs)}")
+    metas = []
+    for t in items:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise TypeError("output tensors must be CUDA tensors")
+        metas.append({
+            "data_ptr": t.data_ptr(),
+            "sizes": list(t.shape),
+            "strides": list(t.stride()),
+            "dtype": str(t.dtype).replace("torch.", ""),
+            "element_size": t.element_size(),
+            "numel": t.numel(),
+            "device_type": "cuda",
+            "device_index": t.device.index if t.device.index is not None else 0,
+            "requires_grad": bool(t.requires_grad),
+        })
+    return json.dumps({"type": kind, "tensors": metas})
+
+
+class _DevicePtr:
+    """Minimal ``__cuda_array_interface__`` exporter for a raw device byte span."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {
+            "data": (ptr, False), "shape": (nbytes,), "typestr": "|u1", "version": 3, "strides": None,
+        }
+
+
+def tensor_from_ptr(ptr: int, sizes: Sequence[int], strides: Sequence[int], dtype: torch.dtype) -> torch.Tensor:
+    """Wraps existing device memory as a tensor (no copy, no ownership)."""
+    esize = torch.empty((), dtype=dtype).element_size()
+    span = 1
+    for s, st in zip(sizes, strides):
+        if s == 0:
+            span = 0
+            break
+        span += (s - 1) * st
+    nbytes = max(span, 1) * esize
+    raw = torch.as_tensor(_DevicePtr(ptr, nbytes), device="cuda")
+    return raw.view(dtype).as_strided(tuple(sizes), tuple(strides))
+
+
+def _decode_outputs(text: str) -> OutputTensors | None:
+    if not text:
+        return None
+    meta = json.loads(text)
+    tensors = [
+        tensor_from_ptr(m["data_ptr"], m["sizes"], m["strides"], getattr(torch, m["dtype"]))
+        for m in meta["tensors"]
+    ]
+    if meta["type"] == "tensor":
+        return tensors[0]
+    return tensors if meta["type"] == "list" else tuple(tensors)
+
+
+# ---- CUDAGraph ---------------------------------------------------------------------------
+
+class CUDAGraph:
+    """A CUDA graph that can be saved to disk and restored in another process.
+
+    Captured graphs replay through torch; restored graphs through the native
+    restore engine. ``save`` requires every kernel of the graph to come from
+    an image the module registry saw load (this repository's kernels always
+    are; other libraries' kernels are when libfoundry_hook.so is preloaded).
+    """
+
+    def __init__(self, keep_graph: bool = False):
+        self._keep_graph = keep_graph
+        self._torch: torch.cuda.CUDAGraph | None = None
+        self._desc = None
+        self._analysis_error: str | None = None
+        self._restored = None
+        self._events_json = ""
+
+    # -- capture ----------------------------------------------------------------------------
+    def capture_begin(self, pool=None, capture_error_mode: str = "global") -> None:
+        self._torch = torch.cuda.CUDAGraph(keep_graph=True)
+        core().start_hook_record()
+        self._torch.capture_begin(pool=pool, capture_error_mode=capture_error_mode)
+
+    def capture_end(self) -> None:
+        assert self._torch is not None, "capture_begin was not called"
+        self._torch.capture_end()
+        c = core()
+        c.end_hook_record()
+        self._events_json = c.hook_events_json() if c.region_active() else ""
+        try:
+            self._desc = c.analyze_graph(self._torch.raw_cuda_graph())
+            if self._events_json:
+                ev = json.loads(self._events_json)
+                if ev.get("events"):
+                    self._desc.allocator_events_json = self._events_json
+        except RuntimeError as e:  # persisted later only if save() is called
+            self._desc = None
+            self._analysis_error = str(e)
+        self._torch.instantiate()
+
+    def register_generator_state(self, generator) -> None:
+        if self._torch is None:
+            self._torch = torch.cuda.CUDAGraph(keep_graph=True)
+        self._torch.register_generator_state(generator)
+
+    def instantiate(self) -> None:
+        if self._torch is not None:
+            self._torch.instantiate()
+
+    def replay(self) -> None:
+        if self._restored is not None:
+            self._restored.launch(_stream_handle())
+        elif self._torch is not None:
+            self._torch.replay()
+        else:
+            raise RuntimeError("graph was neither captured nor loaded")
+
+    def reset(self) -> None:
+        if self._torch is not None:
+            self._torch.reset()
+        self._torch = None
+        self._desc = None
+        self._restored = None
+
+    def pool(self):
+        if self._torch is None:
+            raise RuntimeError("pool() is only available for captured graphs")
+        return self._torch.pool()
+
+    def enable_debug_mode(self) -> None:
+        if self._torch is not None:
+            self._torch.enable_debug_mode()
+
+    def debug_dump(self, debug_path: str) -> None:
+        if self._torch is not None:
+            self._torch.debug_dump(debug_path)
+        elif self._restored is not None:
+            with open(debug_path, "w") as f:
+                f.write(self._restored.desc.to_json())
+
+    def raw_cuda_graph(self) -> int:
+        return self._torch.raw_cuda_graph() if self._torch is not None else 0
+
+    def raw_cuda_graph_exec(self) -> int:
+        if self._restored is not None:
+            return self._restored.exec_handle
+        return self._torch.raw_cuda_graph_exec() if self._torch is not None else 0
+
+    # -- persistence ------------------------------------------------------------------------
+    @property
+    def desc(self):
+        return self._desc if self._restored is None else self._restored.desc
+
+    def save(self, json_path: str, output_tensors: OutputTensors | None = None) -> None:
+        """Writes ``json_path`` (JSON) and the ``.cugraph`` binary next to it."""
+        if self._desc is None:
+            raise RuntimeError(
+                f"graph cannot be persisted: {self._analysis_error or 'not captured'}"
+            )
+        self._desc.output_tensors_json = _encode_outputs(output_tensors)
+        os.makedirs(os.path.dirname(os.path.abspath(json_path)), exist_ok=True)
+        self._desc.save(json_path)
+
+    @classmethod
+    def _from_restored(cls, restored) -> tuple["CUDAGraph", OutputTensors | None]:
+        g = cls()
+        g._restored = restored
+        return g, _decode_outputs(restored.output_tensors_json)
+
+    @staticmethod
+    def load(json_path: str, pool=None) -> "CUDAGraph | tuple[CUDAGraph, OutputTensors]":
+        torch.cuda.synchronize()
+        restored = core().load_graph(json_path)
+        g, outputs = CUDAGraph._from_restored(restored)
+        return g if outputs is None else (g, outputs)
+
+    @staticmethod
+    def start_graph_builds(json_paths: list[str], pool=None, num_threads: int = 4):
+        """Reads every graph (in parallel) and starts building templates on a
+        background thread; returns immediately with a pending handle."""
+        torch.cuda.synchronize()
+        return core().start_graph_builds(list(json_paths), num_threads)
+
+    @staticmethod
+    def finish_one_graph_load(pending, index: int) -> tuple["CUDAGraph", OutputTensors | None]:
+        """Finishes graph ``index``: waits for the builds, replays its allocator
+        events (call in SAVE capture order), rebuilds its output tensors."""
+        return CUDAGraph._from_restored(pending.finish_one(index))
+
+    @staticmethod
+    def finish_graph_loads(pending) -> list[tuple["CUDAGraph", OutputTensors | None]]:
+        return [CUDAGraph.finish_one_graph_load(pending, i) for i in range(pending.num_graphs)]
+
+    def materialize(self) -> None:
+        """Gives a restored graph its own executable (no parameter patching on
+        later replays). Safe to call from a background thread."""
+        if self._restored is not None:
+            self._restored.materialize()
+
+
+class graph:
+    """Context manager capturing into a ``CUDAGraph`` on a side stream."""
+
+    default_capture_stream: torch.cuda.Stream | None = None
+
+    def __init__(self, cuda_graph: CUDAGraph, pool=None, stream: torch.cuda.Stream | None = None,
+                 capture_error_mode: str = "global"):
+        if self.__class__.default_capture_stream is None:
+            self.__class__.default_capture_stream = torch.cuda.Stream()
+        self.pool = () if pool is None else (pool,)
+        self.capture_stream = stream if stream is not None else self.__class__.default_capture_stream
+        self.stream_ctx = torch.cuda.stream(self.capture_stream)
+        self.cuda_graph = cuda_graph
+        self.capture_error_mode = capture_error_mode
+
+    def __enter__(self) -> None:
+        # No empty_cache here: the region cursor only moves forward, so freeing
+        # between captures would inflate the final offset without reusing memory.
+        torch.cuda.synchronize()
+        self.stream_ctx.__enter__()
+        self.cuda_graph.capture_begin(*self.pool, capture_error_mode=self.capture_error_mode)
+
+    def __exit__(self, *args) -> None:
+        self.cuda_graph.capture_end()
+        self.stream_ctx.__exit__(*args)
+
+
+def _graph_index(name: str) -> int:
+    try:
+        return int(name.split("_")[1].split(".")[0])
+    except (IndexError, ValueError):
+        return 1 << 30
+
+
+def save_graph_manifest(archive_dir: str) -> dict[str, Any] | None:
+    """Groups ``graph_*.json`` in ``archive_dir`` by topology key, marks the
+    first of each group as its template, strips the dependency table from the
+    other members' JSON (the binary keeps it) and writes graph_manifest.json.
+
+    Parity: reference python/foundry/graph.py:170-242.
+    """
+    files = sorted(
+        (f for f in os.listdir(archive_dir) if f.startswith("graph_") and f.endswith(".json")
+         and f != "graph_manifest.json"),
+        key=_graph_index,
+    )
+    if not files:
+        return None
+    groups: dict[str, list[str]] = {}
+    for fname in files:
+        with open(os.path.join(archive_dir, fname)) as f:
+            key = json.load(f).get("topology_key", "")
+        if not key:
+            return None
+        groups.setdefault(key, []).append(fname)
+    manifest = {"topology_groups": [
+        {"topology_key": k, "template": v[0], "members": v} for k, v in groups.items()
+    ]}
+    with open(os.path.join(archive_dir, "graph_manifest.json"), "w") as f:
+        json.dump(manifest, f, indent=2)
+    templates = {v[0] for v in groups.values()}
+    stripped = 0
+    for fname in files:
+        if fname in templates:
+            continue
+        path = os.path.join(archive_dir, fname)
+        with open(path) as f:
+            data = json.load(f)
+        if "dependencies" in data:
+            del data["dependencies"]
+            with open(path, "w") as f:
+                json.dump(data, f)
+            stripped += 1
+    n_on_demand = sum(len(v) - 1 for v in groups.values())
+    print(f"[foundry] Saved graph_manifest.json: {len(groups)} topology groups "
+          f"({len(groups)} templates, {n_on_demand} on-demand, {stripped} stripped)", file=sys.stderr)
+    return manifest

@@ -1,0 +1,239 @@
+"""Dense decoder (Llama-3 family) on foundry_b200's own kernels.
+
+Weights use the nn.Linear layout ([out, in]); q/k/v projections are fused into
+one [ (Hq + 2 Hkv) * 128, H ] matrix and gate/up into one [2 I, H] matrix, so a
+layer is 4 GEMMs. Per decode step and layer the kernels are:
+
+    rmsnorm -> GEMM(qkv) -> rope+kv-write -> decode-attention(+combine)
+    -> GEMM(o, += residual) -> rmsnorm -> GEMM(gate_up) -> silu*mul
+    -> GEMM(down, += residual)
+
+Everything a step touches lives in the runner's static arena, so a decode
+step is capturable as a CUDA graph and restorable in a fresh process.
+``reference_forward`` is a plain fp32 PyTorch implementation used as the
+numerics oracle in tests.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field
+
+import torch
+
+from .. import ops
+
+
+@dataclass
+class LlamaConfig:
+    name: str = "llama-3-8b"
+    hidden: int = 4096
+    layers: int = 32
+    n_q: int = 32
+    n_kv: int = 8
+    head_dim: int = 128
+    inter: int = 14336
+    vocab: int = 128256
+    eps: float = 1e-5
+    rope_theta: float = 500000.0
+    rope_scaling: dict | None = None
+    qk_norm: bool = False  # Qwen3-style per-head RMSNorm on q and k
+    tie_embeddings: bool = False
+    init_std: float = 0.02
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def qkv_dim(self) -> int:
+        return (self.n_q + 2 * self.n_kv) * self.head_dim
+
+    def num_params(self) -> int:
+        h, i = self.hidden, self.inter
+        per_layer = h * self.qkv_dim + self.n_q * self.head_dim * h + 2 * h * i + i * h + 2 * h
+        emb = self.vocab * h * (1 if self.tie_embeddings else 2)
+        return self.layers * per_layer + emb + h
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+def llama3_8b() -> LlamaConfig:
+    return LlamaConfig()
+
+
+def llama3_70b() -> LlamaConfig:
+    return LlamaConfig(name="llama-3-70b", hidden=8192, layers=80, n_q=64, n_kv=8, inter=28672)
+
+
+def tiny(layers: int = 2, vocab: int = 4096) -> LlamaConfig:
+    """Small config with the Llama-3-8B per-layer shapes (tests, smoke)."""
+    return LlamaConfig(name=f"llama-3-8b-{layers}l", layers=layers, vocab=vocab)
+
+
+def toy() -> LlamaConfig:
+    return LlamaConfig(name="toy", hidden=512, layers=2, n_q=8, n_kv=2, inter=1024, vocab=1024)
+
+
+CONFIGS = {"llama-3-8b": llama3_8b, "llama-3-70b": llama3_70b}
+
+
+class LlamaWeights:
+    """All parameters, allocated from an arena and initialised deterministically."""
+
+    def __init__(self, cfg: LlamaConfig, arena, seed: int = 0, init: bool = True):
+        self.cfg = cfg
+        h, d = cfg.hidden, cfg.head_dim
+        self.embed = arena.empty((cfg.vocab, h))
+        self.layers = []
+        for _ in range(cfg.layers):
+            lw = {
+                "attn_norm": arena.empty((h,)),
+                "qkv": arena.empty((cfg.qkv_dim, h)),
+                "o": arena.empty((h, cfg.n_q * d)),
+                "mlp_norm": arena.empty((h,)),
+                "gate_up": arena.empty((2 * cfg.inter, h)),
+                "down": arena.empty((h, cfg.inter)),
+            }
+            if cfg.qk_norm:
+                lw["q_norm"] = arena.empty((d,))
+                lw["k_norm"] = arena.empty((d,))
+            self.layers.append(lw)
+        self.final_norm = arena.empty((h,))
+        self.lm_head = self.embed if cfg.tie_embeddings else arena.empty((cfg.vocab, h))
+        if init:
+            self.init(seed)
+
+    def tensors(self):
+        yield "embed", self.embed
+        for i, lw in enumerate(self.layers):
+            for k, v in lw.items():
+                yield f"layers.{i}.{k}", v
+        yield "final_norm", self.final_norm
+        if not self.cfg.tie_embeddings:
+            yield "lm_head", self.lm_head
+
+    def init(self, seed: int) -> None:
+        """Random init N(0, init_std) for matrices, ones for norm weights."""
+        for idx, (name, t) in enumerate(self.tensors()):
+            if t.dim() == 1:
+                ops.fill_(t, 1.0)
+            else:
+                ops.init_normal_(t, seed=(seed * 1_000_003 + idx) & ((1 << 63) - 1), std=self.cfg.init_std)
+
+
+class LlamaModel:
+    """Forward passes over preallocated buffers (no allocation inside a step)."""
+
+    def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, cos_sin: torch.Tensor):
+        self.cfg = cfg
+        self.w = weights
+        self.cos_sin = cos_sin
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    # ---- one decode step for B sequences (graph-capturable) -------------------------------
+    def decode(self, st, b: int) -> None:
+        """``st`` is a DecodeState (runner/engine.py) with static buffers; uses rows [:b]."""
+        cfg, w = self.cfg, self.w
+        ops.decode_advance(st.seq_lens[:b], st.positions[:b], st.slots[:b], st.block_tables[:b], st.page,
+                           st.active[:b])
+        h = st.hidden[:b]
+        x = st.normed[:b]
+        ops.embedding(st.input_ids[:b], w.embed, h)
+        splits = st.attn_splits[b]
+        for li, lw in enumerate(w.layers):
+            ops.rmsnorm(h, lw["attn_norm"], x, cfg.eps)
+            qkv = ops.linear(x, lw["qkv"], out=st.qkv[:b], ws=st.gemm_ws)
+            ops.rope_kv_write(qkv, st.positions[:b], self.cos_sin, st.q[:b], st.k_cache[li], st.v_cache[li],
+                              st.slots[:b], cfg.n_q, cfg.n_kv, lw.get("q_norm"), lw.get("k_norm"), cfg.eps)
+            ops.decode_attention(st.q[:b], st.k_cache[li], st.v_cache[li], st.block_tables[:b], st.seq_lens[:b],
+                                 st.attn_out[:b].view(b, cfg.n_q, cfg.head_dim), st.max_pages, st.attn_ws,
+                                 scale=self.scale, splits=splits)
+            ops.linear(st.attn_out[:b], lw["o"], out=h, residual=h, ws=st.gemm_ws)
+            ops.rmsnorm(h, lw["mlp_norm"], x, cfg.eps)
+            gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:b], ws=st.gemm_ws)
+            ops.silu_mul(gu, st.act[:b])
+            ops.linear(st.act[:b], lw["down"], out=h, residual=h, ws=st.gemm_ws)
+        ops.rmsnorm(h, w.final_norm, x, cfg.eps)
+        ops.linear(x, w.lm_head, out=st.logits[:b], ws=st.gemm_ws)
+        ops.argmax(st.logits[:b], st.next_ids[:b])
+
+    # ---- prefill of a packed batch of prompts (eager) --------------------------------------
+    def prefill(self, pb) -> None:
+        """``pb`` is a PrefillBatch (runner/engine.py): packed ids, positions,
+        slots, cu_seqlens, tile tables and scratch buffers; writes KV into the
+        cache and the greedy next token of every prompt into pb.next_ids."""
+        cfg, w = self.cfg, self.w
+        t = pb.num_tokens
+        h, x = pb.hidden[:t], pb.normed[:t]
+        ops.embedding(pb.input_ids[:t], w.embed, h)
+        nqd = cfg.n_q * cfg.head_dim
+        nkvd = cfg.n_kv * cfg.head_dim
+        for li, lw in enumerate(w.layers):
+            ops.rmsnorm(h, lw["attn_norm"], x, cfg.eps)
+            qkv = ops.linear(x, lw["qkv"], out=pb.qkv[:t], ws=pb.gemm_ws)
+            # Rotated q -> pb.q, rotated k -> paged cache and packed pb.k_rot, v -> cache.
+            ops.rope_kv_write(qkv, pb.positions[:t], self.cos_sin, pb.q[:t], pb.k_cache[li], pb.v_cache[li],
+                              pb.slots[:t], cfg.n_q, cfg.n_kv, lw.get("q_norm"), lw.get("k_norm"), cfg.eps,
+                              k_out=pb.k_rot[:t])
+            v_src = qkv[:, nqd + nkvd:]  # v heads read in place (row stride = qkv row)
+            ops.prefill_attention(pb.q[:t].view(t, nqd), pb.k_rot[:t].view(t, nkvd), v_src, pb.attn_out[:t],
+                                  pb.cu_seqlens, pb.tile_seq, pb.tile_start, cfg.n_q, cfg.n_kv, scale=self.scale)
+            ops.linear(pb.attn_out[:t], lw["o"], out=h, residual=h, ws=pb.gemm_ws)
+            ops.rmsnorm(h, lw["mlp_norm"], x, cfg.eps)
+            gu = ops.linear(x, lw["gate_up"], out=pb.gate_up[:t], ws=pb.gemm_ws)
+            ops.silu_mul(gu, pb.act[:t])
+            ops.linear(pb.act[:t], lw["down"], out=h, residual=h, ws=pb.gemm_ws)
+        # last token of every prompt -> logits -> greedy token
+        n = pb.num_seqs
+        last = pb.last_rows[:n]
+        torch.index_select(h, 0, last, out=pb.last_hidden[:n])
+        ops.rmsnorm(pb.last_hidden[:n], w.final_norm, pb.last_normed[:n], cfg.eps)
+        ops.linear(pb.last_normed[:n], w.lm_head, out=pb.logits[:n], ws=pb.gemm_ws)
+        ops.argmax(pb.logits[:n], pb.next_ids[:n])
+
+
+# ---- fp32 reference (tests) --------------------------------------------------------------
+
+def _rms(x, w, eps):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def _rope(x, pos, cos_sin):
+    # x: [T, H, 128]; half rotation
+    cs = cos_sin[pos]  # [T, 64, 2]
+    c, s = cs[..., 0][:, None, :], cs[..., 1][:, None, :]
+    x1, x2 = x[..., :64], x[..., 64:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def reference_forward(cfg: LlamaConfig, weights: LlamaWeights, ids: torch.Tensor, cos_sin: torch.Tensor,
+                      layers: int | None = None) -> torch.Tensor:
+    """fp32 causal forward of one sequence; returns logits [T, vocab]."""
+    f = lambda t: t.float()  # noqa: E731
+    t_len = ids.numel()
+    pos = torch.arange(t_len, device=ids.device)
+    h = f(weights.embed)[ids.long()]
+    d = cfg.head_dim
+    g = cfg.n_q // cfg.n_kv
+    for lw in weights.layers[: layers or cfg.layers]:
+        x = _rms(h, f(lw["attn_norm"]), cfg.eps)
+        qkv = x @ f(lw["qkv"]).T
+        q = qkv[:, : cfg.n_q * d].view(t_len, cfg.n_q, d)
+        k = qkv[:, cfg.n_q * d: (cfg.n_q + cfg.n_kv) * d].view(t_len, cfg.n_kv, d)
+        v = qkv[:, (cfg.n_q + cfg.n_kv) * d:].view(t_len, cfg.n_kv, d)
+        if cfg.qk_norm:
+            q = _rms(q, f(lw["q_norm"]), cfg.eps)
+            k = _rms(k, f(lw["k_norm"]), cfg.eps)
+        q, k = _rope(q, pos, cos_sin), _rope(k, pos, cos_sin)
+        k = k.repeat_interleave(g, dim=1)
+        v = v.repeat_interleave(g, dim=1)
+        att = torch.einsum("thd,shd->hts", q, k) / math.sqrt(d)
+        mask = torch.triu(torch.ones(t_len, t_len, dtype=torch.bool, device=ids.device), 1)
+        att = att.masked_fill(mask, float("-inf")).softmax(-1)
+        o = torch.einsum("hts,shd->thd", att, v).reshape(t_len, cfg.n_q * d)
+        h = h + o @ f(lw["o"]).T
+        x = _rms(h, f(lw["mlp_norm"]), cfg.eps)
+        gu = x @ f(lw["gate_up"]).T
+        gate, up = gu[:, : cfg.inter], gu[:, cfg.inter:]
+        h = h + (torch.nn.functional.silu(gate) * up) @ f(lw["down"]).T
+    x = _rms(h, f(weights.final_norm), cfg.eps)
+    return x @ f(weights.lm_head).T

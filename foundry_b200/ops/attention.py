@@ -1,0 +1,90 @@
+"""Attention ops (csrc/kernels/attention.cu): paged split-KV decode attention
+and causal prefill attention. head_dim is 128 and the KV page is 64 tokens."""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _rt
+
+_IMG = "attention"
+PAGE = 64
+LOG2E = 1.4426950408889634
+
+
+def decode_smem(group: int) -> int:
+    return 2 * 2 * PAGE * 128 * 2 + (group * PAGE * 2 + group + group * 128) * 4
+
+
+def decode_splits(batch: int, n_kv: int, max_pages: int, sms: int | None = None) -> tuple[int, int]:
+    """(num_splits, pages_per_split) so that batch * n_kv * splits fills the GPU."""
+    sms = sms or _rt.sm_count()
+    want = max(1, math.ceil(2 * sms * 3 / max(1, batch * n_kv)))
+    splits = max(1, min(want, max_pages))
+    pps = math.ceil(max_pages / splits)
+    splits = math.ceil(max_pages / pps)
+    return splits, pps
+
+
+class DecodeWorkspace:
+    def __init__(self, max_batch: int, n_q: int, max_splits: int, device=None,
+                 o_part: torch.Tensor | None = None, ml_part: torch.Tensor | None = None):
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        n = max_batch * n_q * max_splits
+        self.o_part = o_part if o_part is not None else torch.empty(n * 128, dtype=torch.float32, device=device)
+        self.ml_part = ml_part if ml_part is not None else torch.empty(n * 2, dtype=torch.float32, device=device)
+        self.capacity = n
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                     seq_lens: torch.Tensor, out: torch.Tensor, max_pages: int, ws: DecodeWorkspace,
+                     scale: float | None = None, splits: tuple[int, int] | None = None) -> torch.Tensor:
+    """q: [B, Hq, 128]; caches [blocks, Hkv, 64, 128]; block_tables [B, max_blocks] int32;
+    seq_lens [B] int32 (tokens in cache incl. the current one). Grid covers
+    ``max_pages`` pages per sequence so the launch shape is static."""
+    b, n_q, d = q.shape
+    assert d == 128 and k_cache.shape[2] == PAGE
+    n_kv = k_cache.shape[1]
+    g = n_q // n_kv
+    if g not in (4, 8):
+        raise ValueError(f"GQA group {g} not supported (4 or 8)")
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    s, pps = splits or decode_splits(b, n_kv, max_pages)
+    if s > 1 and b * n_q * s > ws.capacity:
+        raise RuntimeError("decode attention workspace too small")
+    _rt.launch(_IMG, f"fb_decode_attn_g{g}", (s, n_kv, b), (128,), [
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr(), block_tables.shape[1],
+        seq_lens.data_ptr(), out.data_ptr(), ws.o_part.data_ptr(), ws.ml_part.data_ptr(), n_kv, pps,
+        float(scale * LOG2E),
+    ], smem=decode_smem(g))
+    if s > 1:
+        _rt.launch(_IMG, "fb_decode_attn_combine", (b, n_q), (128,), [
+            ws.o_part.data_ptr(), ws.ml_part.data_ptr(), out.data_ptr(), n_q, s,
+        ])
+    return out
+
+
+def prefill_tiles(seqlens: list[int]) -> tuple[list[int], list[int]]:
+    tile_seq, tile_start = [], []
+    for i, n in enumerate(seqlens):
+        for s0 in range(0, n, 64):
+            tile_seq.append(i)
+            tile_start.append(s0)
+    return tile_seq, tile_start
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                      cu_seqlens: torch.Tensor, tile_seq: torch.Tensor, tile_start: torch.Tensor,
+                      n_q: int, n_kv: int, scale: float | None = None) -> torch.Tensor:
+    """Causal attention over packed prompts. q: [T, *] with head h at columns
+    h*128 (row stride q.stride(0)); k, v likewise with n_kv heads; out [T, n_q*128]."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(128)
+    n_tiles = tile_seq.numel()
+    _rt.launch(_IMG, "fb_prefill_attn", (n_tiles, n_q), (128,), [
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), k.stride(0), v.stride(0), out.data_ptr(),
+        out.stride(0),
+        cu_seqlens.data_ptr(), tile_seq.data_ptr(), tile_start.data_ptr(), n_q, n_kv, float(scale * LOG2E),
+    ])
+    return out

@@ -1,0 +1,212 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device="cuda") * scale).to(torch.bfloat16)
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    from foundry_b200 import ops
+
+    yield
+    for img in ("gemm_bf16", "elementwise", "attention"):
+        if img in ops._rt.loaded_images():
+            assert ops.status(img) == 0, f"{img} reported a device-side error"
+
+
+@pytest.mark.parametrize("t,n,k", [
+    (1, 512, 256), (7, 384, 512), (16, 6144, 4096), (100, 1024, 1024), (256, 4096, 4096),
+    (300, 1024, 512), (512, 2048, 1024), (1000, 768, 2048),
+])
+def test_linear(t, n, k):
+    from foundry_b200 import ops
+
+    x = _bf(t, k, seed=1)
+    w = _bf(n, k, scale=0.05, seed=2)
+    out = ops.linear(x, w)
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(out.float(), ref, atol=2e-2 * math.sqrt(k / 256), rtol=2e-2)
+
+
+@pytest.mark.parametrize("t,n,k", [(8, 4096, 4096), (64, 1024, 14336), (600, 512, 1024)])
+def test_linear_residual(t, n, k):
+    from foundry_b200 import ops
+
+    x = _bf(t, k, seed=3)
+    w = _bf(n, k, scale=0.02, seed=4)
+    h = _bf(t, n, seed=5)
+    ref = h.float() + x.float() @ w.float().T
+    out = ops.linear(x, w, out=h, residual=h)
+    assert out.data_ptr() == h.data_ptr()
+    torch.testing.assert_close(out.float(), ref, atol=5e-2, rtol=2e-2)
+
+
+def test_linear_split_determinism():
+    from foundry_b200 import ops
+    from foundry_b200.ops.gemm import plan
+
+    x = _bf(32, 4096, seed=6)
+    w = _bf(1024, 4096, scale=0.02, seed=7)
+    p = plan(32, 1024, 4096)
+    assert p.splits > 1
+    a = ops.linear(x, w).clone()
+    b = ops.linear(x, w).clone()
+    assert torch.equal(a, b)
+
+
+def test_rmsnorm_silu_embedding_argmax():
+    from foundry_b200 import ops
+
+    x = _bf(33, 4096, seed=8)
+    w = _bf(4096, seed=9)
+    out = torch.empty_like(x)
+    ops.rmsnorm(x, w, out, 1e-5)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=1e-2)
+
+    gu = _bf(17, 2 * 1024, seed=10)
+    act = torch.empty(17, 1024, dtype=torch.bfloat16, device="cuda")
+    ops.silu_mul(gu, act)
+    g, u = gu.float()[:, :1024], gu.float()[:, 1024:]
+    torch.testing.assert_close(act.float(), torch.nn.functional.silu(g) * u, atol=2e-2, rtol=1e-2)
+
+    table = _bf(1000, 256, seed=11)
+    ids = torch.randint(0, 1000, (9,), device="cuda", dtype=torch.int32)
+    emb = torch.empty(9, 256, dtype=torch.bfloat16, device="cuda")
+    ops.embedding(ids, table, emb)
+    assert torch.equal(emb, table[ids.long()])
+
+    logits = _bf(5, 128256, seed=12)
+    am = torch.empty(5, dtype=torch.int32, device="cuda")
+    ops.argmax(logits, am)
+    assert torch.equal(am.long(), logits.float().argmax(-1))
+
+
+def test_init_normal_deterministic():
+    from foundry_b200 import ops
+
+    a = torch.empty(1 << 20, dtype=torch.bfloat16, device="cuda")
+    b = torch.empty_like(a)
+    ops.init_normal_(a, seed=123, std=0.02)
+    ops.init_normal_(b, seed=123, std=0.02)
+    assert torch.equal(a, b)
+    assert abs(a.float().std().item() - 0.02) < 1e-3
+    assert abs(a.float().mean().item()) < 1e-3
+
+
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_rope_kv_write(qk_norm):
+    from foundry_b200 import ops
+
+    t, nq, nkv, d, page = 10, 8, 2, 128, 64
+    qkv = _bf(t, (nq + 2 * nkv) * d, seed=13)
+    pos = torch.tensor([0, 1, 2, 63, 64, 65, 100, 5, 7, 200], dtype=torch.int32, device="cuda")
+    cs = ops.rope_cos_sin(256, 500000.0, device="cuda")
+    q_out = torch.empty(t, nq, d, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(8, nkv, page, d, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    slots = torch.arange(t, dtype=torch.int32, device="cuda") * 37 % (8 * page)
+    qn = _bf(d, seed=14) if qk_norm else None
+    kn = _bf(d, seed=15) if qk_norm else None
+    k_out = torch.empty(t, nkv, d, dtype=torch.bfloat16, device="cuda")
+    ops.rope_kv_write(qkv, pos, cs, q_out, kc, vc, slots, nq, nkv, qn, kn, 1e-6, k_out=k_out)
+
+    f = qkv.float()
+    q = f[:, : nq * d].view(t, nq, d)
+    k = f[:, nq * d:(nq + nkv) * d].view(t, nkv, d)
+    v = f[:, (nq + nkv) * d:].view(t, nkv, d)
+    if qk_norm:
+        q = q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + 1e-6) * qn.float()
+        k = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + 1e-6) * kn.float()
+    c = cs[pos.long(), :, 0][:, None, :]
+    s = cs[pos.long(), :, 1][:, None, :]
+
+    def rot(x):
+        return torch.cat([x[..., :64] * c - x[..., 64:] * s, x[..., 64:] * c + x[..., :64] * s], -1)
+
+    torch.testing.assert_close(q_out.float(), rot(q), atol=3e-2, rtol=2e-2)
+    torch.testing.assert_close(k_out.float(), rot(k), atol=3e-2, rtol=2e-2)
+    for i in range(t):
+        sl = int(slots[i])
+        torch.testing.assert_close(kc[sl // page, :, sl % page].float(), rot(k)[i], atol=3e-2, rtol=2e-2)
+        assert torch.equal(vc[sl // page, :, sl % page], qkv[i, (nq + nkv) * d:].view(nkv, d))
+
+
+def _ref_decode(q, kc, vc, tables, lens, page=64):
+    b, nq, d = q.shape
+    nkv = kc.shape[1]
+    g = nq // nkv
+    out = torch.empty(b, nq, d, device=q.device)
+    for i in range(b):
+        n = int(lens[i])
+        pages = tables[i, : math.ceil(n / page)].long()
+        k = kc[pages].permute(0, 2, 1, 3).reshape(-1, nkv, d)[:n].float()
+        v = vc[pages].permute(0, 2, 1, 3).reshape(-1, nkv, d)[:n].float()
+        k = k.repeat_interleave(g, 1)
+        v = v.repeat_interleave(g, 1)
+        att = torch.einsum("hd,shd->hs", q[i].float(), k) / math.sqrt(d)
+        out[i] = torch.einsum("hs,shd->hd", att.softmax(-1), v)
+    return out
+
+
+@pytest.mark.parametrize("b,nq,nkv,lens", [
+    (3, 32, 8, [1, 64, 130]), (5, 64, 8, [640, 17, 333, 64, 65]), (2, 32, 4, [700, 2]),
+    (64, 32, 8, None),
+])
+def test_decode_attention(b, nq, nkv, lens):
+    from foundry_b200 import ops
+
+    page, d = 64, 128
+    max_pages = 12
+    nb = b * max_pages
+    kc = _bf(nb, nkv, page, d, seed=16)
+    vc = _bf(nb, nkv, page, d, seed=17)
+    q = _bf(b, nq, d, seed=18)
+    if lens is None:
+        lens = [1 + (37 * i) % (max_pages * page) for i in range(b)]
+    lens_t = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(0)).to(torch.int32).cuda()
+    tables = perm.view(b, max_pages).contiguous()
+    ws = ops.DecodeWorkspace(b, nq, 16)
+    out = torch.empty(b, nq, d, dtype=torch.bfloat16, device="cuda")
+    ref = _ref_decode(q, kc, vc, tables, lens_t)
+    for splits in (None, (1, max_pages), (4, 3)):
+        ops.decode_attention(q, kc, vc, tables, lens_t, out, max_pages, ws, splits=splits)
+        torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_prefill_attention():
+    from foundry_b200 import ops
+
+    nq, nkv, d = 8, 2, 128
+    seqlens = [1, 70, 129, 64]
+    t = sum(seqlens)
+    q = _bf(t, nq * d, seed=19)
+    k = _bf(t, nkv * d, seed=20)
+    v = _bf(t, nkv * d, seed=21)
+    cu = torch.tensor([0] + list(torch.tensor(seqlens).cumsum(0)), dtype=torch.int32, device="cuda")
+    ts, tst = ops.prefill_tiles(seqlens)
+    out = torch.empty(t, nq * d, dtype=torch.bfloat16, device="cuda")
+    ops.prefill_attention(q, k, v, out, cu, torch.tensor(ts, dtype=torch.int32, device="cuda"),
+                          torch.tensor(tst, dtype=torch.int32, device="cuda"), nq, nkv)
+    g = nq // nkv
+    off = 0
+    for n in seqlens:
+        qq = q[off:off + n].float().view(n, nq, d)
+        kk = k[off:off + n].float().view(n, nkv, d).repeat_interleave(g, 1)
+        vv = v[off:off + n].float().view(n, nkv, d).repeat_interleave(g, 1)
+        att = torch.einsum("thd,shd->hts", qq, kk) / math.sqrt(d)
+        mask = torch.triu(torch.ones(n, n, dtype=torch.bool, device="cuda"), 1)
+        ref = torch.einsum("hts,shd->thd", att.masked_fill(mask, float("-inf")).softmax(-1), vv)
+        torch.testing.assert_close(out[off:off + n].float().view(n, nq, d), ref, atol=2e-2, rtol=2e-2)
+        off += n
