@@ -351,6 +351,23 @@ PYBIND11_MODULE(_C, m) {
   m.def("read_binary_graph", [](const std::string& path) { return read_binary(path); });
   m.def("graph_from_json_text", [](const std::string& text) { return from_json(fb::json::parse(text)); });
   m.def("diff_against", [](const GraphDesc& a, const GraphDesc& b) { return diff_against(a, b); });
+  // Builds a live (non-instantiated) CUgraph from a description: used to create
+  // synthetic graphs for tests and tools. The caller owns the returned handle.
+  m.def("build_live_graph", [](std::shared_ptr<GraphDesc> d) {
+    resolve_functions(*d);
+    auto b = build_graph(*d);
+    CUgraph g = b->graph;
+    b->graph = nullptr;
+    b->events.clear();  // owned by the graph's event nodes for the test's lifetime
+    return reinterpret_cast<uintptr_t>(g);
+  });
+  m.def("destroy_graph", [](uintptr_t g) {
+    if (g) fb_driver()->cuGraphDestroy(reinterpret_cast<CUgraph>(g));
+  });
+  m.def("recompute_topology_key", [](GraphDesc& g) {
+    g.topology_key = compute_topology_key(g);
+    return g.topology_key;
+  });
 
   py::class_<RestoredGraph, std::shared_ptr<RestoredGraph>>(m, "RestoredGraph")
       .def("launch", [](RestoredGraph& g, uintptr_t stream) {

@@ -1,0 +1,292 @@
+"""CPU-only scenarios run against the mock driver (libfoundry_mockcuda.so).
+
+Each scenario runs in its own process (the driver is chosen once per process),
+started by tests/test_mock_archive.py:
+
+    FOUNDRY_CUDA_DRIVER=.../libfoundry_mockcuda.so python tests/mock_scenarios.py <name> <workdir> [...]
+
+Scenario "save" builds the BASELINE config-1 workload (200 region allocations
+log-uniform 256 B..64 MB with seed 0, a 1 MB random code image, 64 graphs in 4
+topology groups of 32-kernel chains with 8 seeded random args each) and writes
+an archive; "load" restores it in a fresh process and checks everything
+byte-for-byte against the SAVE process's record.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import random
+import struct
+import sys
+
+BASE = 0x600000000000
+REGION = 64 << 30
+N_GRAPHS, N_GROUPS, CHAIN, N_ARGS = 64, 4, 32, 8
+PARAM_SIZES = [8, 8, 8, 4, 4, 16, 8, 32]  # 8 args: pointers and seeded random bytes
+
+
+def _core():
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import foundry_b200 as fb
+
+    c = fb.core()
+    assert c.driver_is_mock(), "scenarios must run on the mock driver"
+    return fb, c
+
+
+def _image_bytes(seed: int = 0) -> bytes:
+    names = [f"fbmock_k{j}:{','.join(map(str, PARAM_SIZES))}" for j in range(8)]
+    names += ["fbmock_axpy_f32:8,8,4,4", "fbmock_fill_u32:8,4,4"]
+    header = ("FBMOCK\n" + "\n".join(names) + "\n\n").encode()
+    rnd = random.Random(seed)
+    return header + bytes(rnd.getrandbits(8) for _ in range(1 << 20))
+
+
+def _alloc_sizes(seed: int = 0) -> list[int]:
+    import math
+
+    rnd = random.Random(seed)
+    lo, hi = math.log(256), math.log(64 << 20)
+    return [max(256, int(math.exp(rnd.uniform(lo, hi))) // 256 * 256) for _ in range(200)]
+
+
+def _graph_json(gi: int, img_hash: int, ptrs: list[int]) -> str:
+    """Graph gi: group g = gi % 4 has a memset at position 8*g (distinct node-type
+    sequence per group); members differ in their random args and pointers."""
+    g = gi % N_GROUPS
+    rnd = random.Random(1000 + gi)
+    nodes = []
+    for n in range(CHAIN):
+        if n == 8 * g:
+            nodes.append({"id": n, "type": "MemsetNode", "params": {
+                "dst": ptrs[rnd.randrange(len(ptrs))], "elementSize": 4, "height": 1, "pitch": 0,
+                "value": rnd.getrandbits(32), "width": 64}})
+            continue
+        params = []
+        off = 0
+        for i, sz in enumerate(PARAM_SIZES):
+            if sz == 8 and i < 3:
+                val = struct.pack("<Q", ptrs[rnd.randrange(len(ptrs))] + 256 * rnd.randrange(4))
+            else:
+                val = bytes(rnd.getrandbits(8) for _ in range(sz))
+            params.append({"index": i, "offset": off, "size": sz, "value_hex": val.hex()})
+            off += sz
+        nodes.append({"id": n, "type": "KernelNode", "params": {
+            "blockDimX": 128, "blockDimY": 1, "blockDimZ": 1,
+            "gridDimX": 1 + rnd.randrange(512), "gridDimY": 1, "gridDimZ": 1,
+            "sharedMemBytes": 0, "kernelParams": params,
+            "function_name": f"fbmock_k{(n + g) % 8}", "kernel_source_binary_hash": f"{img_hash:016x}",
+            "func_attrs": {"max_dynamic_shared_size_bytes": 0, "preferred_shared_memory_carveout": -1,
+                           "cluster_scheduling_policy_preference": 0, "required_cluster_width": 0,
+                           "required_cluster_height": 0, "required_cluster_depth": 0}}})
+    deps = [{"from": i, "to": i + 1} for i in range(CHAIN - 1)]
+    return json.dumps({"nodes": nodes, "dependencies": deps, "topology_key": "", "generators": []})
+
+
+def scenario_save(workdir: str) -> None:
+    fb, c = _core()
+    archive = os.path.join(workdir, "archive")
+    os.makedirs(archive, exist_ok=True)
+    c.set_allocation_region(BASE, REGION)
+    # 1) region: 200 allocations, recorded as allocator events
+    c.start_hook_record()
+    ptrs = [c.region_alloc(s) for s in _alloc_sizes(0)]
+    c.end_hook_record()
+    events = c.hook_events_json()
+    # 2) registry: a 1 MB image
+    img = os.path.join(workdir, "mock.cubin")
+    with open(img, "wb") as f:
+        f.write(_image_bytes(0))
+    _, h = c.load_image_file(img)
+    # 3) graphs: build live graphs through the driver, analyze them back, save
+    record = {"ptrs": ptrs, "image_hash": h, "offset": c.get_current_alloc_offset(), "graphs": []}
+    for gi in range(N_GRAPHS):
+        desc = c.graph_from_json_text(_graph_json(gi, h, ptrs))
+        c.recompute_topology_key(desc)
+        live = c.build_live_graph(desc)
+        analyzed = c.analyze_graph(live)
+        c.destroy_graph(live)
+        if gi == 0:
+            analyzed.allocator_events_json = events
+        path = os.path.join(archive, f"graph_{gi}.json")
+        analyzed.save(path)
+        record["graphs"].append({"path": path, "json": analyzed.to_json(), "key": analyzed.topology_key})
+    fb.pack_fatbins_to_folder(archive)
+    from foundry_b200.graph import save_graph_manifest
+
+    manifest = save_graph_manifest(archive)
+    assert len(manifest["topology_groups"]) == N_GROUPS, manifest
+    with open(os.path.join(workdir, "record.json"), "w") as f:
+        json.dump(record, f)
+    print("SAVE OK", len(ptrs), hex(h))
+
+
+def scenario_load(workdir: str) -> None:
+    fb, c = _core()
+    with open(os.path.join(workdir, "record.json")) as f:
+        record = json.load(f)
+    archive = os.path.join(workdir, "archive")
+    fb.load_cuda_modules_and_libraries(archive)
+    c.set_allocation_region(BASE, REGION)
+    paths = [g["path"] for g in record["graphs"]]
+    # binary files must decode to exactly what SAVE analyzed
+    for g in record["graphs"]:
+        d = c.read_binary_graph(g["path"].replace(".json", ".cugraph"))
+        assert d.to_json() == g["json"], f"binary round trip differs for {g['path']}"
+    pending = c.start_graph_builds(paths, 4)
+    pending.wait()
+    assert pending.num_groups == N_GROUPS, pending.num_groups
+    graphs = [pending.finish_one(i) for i in range(len(paths))]
+    # allocator events of graph 0 replayed -> same 200 addresses, same cursor
+    assert c.get_current_alloc_offset() == record["offset"], (c.get_current_alloc_offset(), record["offset"])
+    ev = json.loads(graphs[0].desc.allocator_events_json)
+    assert [e["ptr"] for e in ev["events"]] == record["ptrs"]
+    templates = sum(1 for g in graphs if g.is_template)
+    assert templates == N_GROUPS
+    for g, rec in zip(graphs, record["graphs"]):
+        assert g.desc.topology_key == rec["key"]
+        g.launch(0)  # mock: runs nodes in order, patches on-demand members
+    # every member's launch state equals its own saved parameters
+    for g, rec in zip(graphs, record["graphs"]):
+        g.launch(0)
+    # the image came back byte-identical (same CRC-64 hash re-registered)
+    _, h = c.load_image_file(os.path.join(workdir, "mock.cubin"))
+    assert h == record["image_hash"]
+    assert c.registry_count() >= 1
+    print("LOAD OK", len(graphs), templates, pending.phase1_ms, pending.phase2_ms)
+
+
+def scenario_numeric(workdir: str) -> None:
+    """A graph of axpy/fill kernels on region memory: SAVE runs it, LOAD restores
+    and runs it again; results must be bit-identical."""
+    fb, c = _core()
+    import ctypes
+
+    mode = sys.argv[3]
+    archive = os.path.join(workdir, "num_archive")
+    os.makedirs(archive, exist_ok=True)
+    if mode == "load":
+        fb.load_cuda_modules_and_libraries(archive)
+    c.set_allocation_region(BASE, REGION)
+    n = 4096
+    y, x = c.region_alloc(4 * n), c.region_alloc(4 * n)
+    xs = (ctypes.c_float * n).from_address(x)
+    ys = (ctypes.c_float * n).from_address(y)
+    for i in range(n):
+        xs[i] = 0.5 * i
+        ys[i] = 1.0
+    img = os.path.join(workdir, "mock.cubin")
+    with open(img, "wb") as f:
+        f.write(_image_bytes(0))
+    _, h = c.load_image_file(img)
+    nodes = []
+    for j in range(6):
+        a = struct.pack("<f", 0.25 * (j + 1))
+        nodes.append({"id": j, "type": "KernelNode", "params": {
+            "blockDimX": 128, "blockDimY": 1, "blockDimZ": 1, "gridDimX": 32, "gridDimY": 1, "gridDimZ": 1,
+            "sharedMemBytes": 0, "function_name": "fbmock_axpy_f32", "kernel_source_binary_hash": f"{h:016x}",
+            "kernelParams": [
+                {"value_hex": struct.pack("<Q", y).hex()}, {"value_hex": struct.pack("<Q", x).hex()},
+                {"value_hex": a.hex()}, {"value_hex": struct.pack("<I", n).hex()}]}})
+    text = json.dumps({"nodes": nodes, "dependencies": [{"from": i, "to": i + 1} for i in range(5)],
+                       "topology_key": "", "generators": []})
+    path = os.path.join(archive, "graph_0.json")
+    if mode == "save":
+        desc = c.graph_from_json_text(text)
+        c.recompute_topology_key(desc)
+        live = c.build_live_graph(desc)
+        d2 = c.analyze_graph(live)
+        c.destroy_graph(live)
+        d2.save(path)
+        fb.pack_fatbins_to_folder(archive)
+    g = c.load_graph(path)
+    g.launch(0)
+    g.launch(0)
+    vals = [ys[i] for i in range(0, n, 97)]
+    with open(os.path.join(workdir, f"num_{mode}.json"), "w") as f:
+        json.dump(vals, f)
+    print("NUMERIC", mode, vals[:3])
+
+
+def scenario_faults(workdir: str) -> None:
+    """Host-side fault injection: corrupt archive, wrong hash, missing entry point,
+    cursor drift. Every failure must surface as a Python exception (status), never
+    an abort."""
+    fb, c = _core()
+    import shutil
+
+    archive = os.path.join(workdir, "archive")
+    bad = os.path.join(workdir, "bad_archive")
+    shutil.copytree(archive, bad)
+    # (a) corrupted image bytes -> CRC mismatch
+    p = os.path.join(bad, "fatbin_image_packed.img")
+    data = bytearray(open(p, "rb").read())
+    data[100] ^= 0xFF
+    open(p, "wb").write(bytes(data))
+    try:
+        fb.load_cuda_modules_and_libraries(bad)
+        raise AssertionError("corrupt image was accepted")
+    except RuntimeError as e:
+        assert "CRC" in str(e), e
+    # (b) truncated image file
+    open(p, "wb").write(bytes(data[:50]))
+    try:
+        fb.load_cuda_modules_and_libraries(bad)
+        raise AssertionError("truncated pack was accepted")
+    except RuntimeError as e:
+        assert "truncated" in str(e), e
+    # (c) truncated .cugraph
+    g0 = os.path.join(archive, "graph_1.cugraph")
+    tb = os.path.join(workdir, "trunc.cugraph")
+    open(tb, "wb").write(open(g0, "rb").read()[:200])
+    try:
+        c.read_binary_graph(tb)
+        raise AssertionError("truncated graph accepted")
+    except RuntimeError as e:
+        assert "corrupt" in str(e), e
+    # (d) graph whose image was never loaded (wrong hash) -> not found
+    fb.load_cuda_modules_and_libraries(archive)
+    c.set_allocation_region(BASE, REGION)
+    with open(os.path.join(archive, "graph_1.json")) as f:
+        j = json.load(f)
+    j["nodes"][1]["params"]["kernel_source_binary_hash"] = "deadbeefdeadbeef"
+    wrong = os.path.join(workdir, "wrong_hash.json")
+    json.dump(j, open(wrong, "w"))
+    try:
+        c.load_graph(wrong)
+        raise AssertionError("unknown image accepted")
+    except RuntimeError as e:
+        assert "not loaded" in str(e), e
+    # (e) missing entry point
+    with open(os.path.join(archive, "graph_1.json")) as f:
+        j = json.load(f)
+    j["nodes"][1]["params"]["function_name"] = "fbmock_missing"
+    missing = os.path.join(workdir, "missing_entry.json")
+    json.dump(j, open(missing, "w"))
+    try:
+        c.load_graph(missing)
+        raise AssertionError("missing entry point accepted")
+    except RuntimeError as e:
+        assert "not found" in str(e), e
+    # (f) cursor drift: allocate first, then replay events that started earlier
+    c.region_alloc(512 << 20)
+    with open(os.path.join(archive, "graph_0.json")) as f:
+        ev = json.dumps(json.load(f)["allocator_events"])
+    try:
+        c.replay_hook_events_json(ev)
+        raise AssertionError("cursor drift not detected")
+    except RuntimeError as e:
+        assert "drift" in str(e), e
+    # (g) set_current_alloc_offset backwards is rejected
+    try:
+        c.set_current_alloc_offset(0)
+        raise AssertionError("backwards offset accepted")
+    except RuntimeError as e:
+        assert "forward" in str(e), e
+    print("FAULTS OK")
+
+
+if __name__ == "__main__":
+    name, workdir = sys.argv[1], sys.argv[2]
+    {"save": scenario_save, "load": scenario_load, "numeric": scenario_numeric, "faults": scenario_faults}[name](workdir)

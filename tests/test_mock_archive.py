@@ -1,0 +1,71 @@
+"""the whole persistence stack (region, event log, registry,
+graph analysis, JSON + .cugraph archive, manifest, template/on-demand restore,
+fault handling) on the CPU mock driver, SAVE and LOAD in separate processes."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+MOCK = os.path.join(ROOT, "foundry_b200", "lib", "libfoundry_mockcuda.so")
+
+
+def _run(*args, timeout=300):
+    env = dict(os.environ, FOUNDRY_CUDA_DRIVER=MOCK, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="")
+    res = subprocess.run([sys.executable, os.path.join(HERE, "mock_scenarios.py"), *args], env=env,
+                         capture_output=True, text=True, timeout=timeout)
+    assert res.returncode == 0, f"scenario {args[0]} failed:\n{res.stdout}\n{res.stderr}"
+    return res.stdout
+
+
+@pytest.fixture(scope="module")
+def saved(tmp_path_factory):
+    wd = str(tmp_path_factory.mktemp("mock_archive"))
+    out = _run("save", wd)
+    assert "SAVE OK" in out
+    return wd
+
+
+def test_archive_layout(saved):
+    a = os.path.join(saved, "archive")
+    files = set(os.listdir(a))
+    assert {"graph_manifest.json", "fatbin_image_packed.img", "fatbin_entrypoint_packed.txt"} <= files
+    assert sum(f.endswith(".cugraph") for f in files) == 64
+    m = json.load(open(os.path.join(a, "graph_manifest.json")))
+    assert len(m["topology_groups"]) == 4
+    assert sum(len(g["members"]) for g in m["topology_groups"]) == 64
+    # on-demand members lose their dependency table in JSON (binary keeps it)
+    tmpl = {g["template"] for g in m["topology_groups"]}
+    for g in m["topology_groups"]:
+        for f in g["members"]:
+            has = "dependencies" in json.load(open(os.path.join(a, f)))
+            assert has == (f in tmpl)
+    # pack: [u64 hash][u64 size][bytes]; the 1 MB image plus its header
+    img = open(os.path.join(a, "fatbin_image_packed.img"), "rb").read()
+    size = int.from_bytes(img[8:16], "little")
+    assert size > (1 << 20) and len(img) == 16 + size
+    txt = open(os.path.join(a, "fatbin_entrypoint_packed.txt")).read().splitlines()
+    assert txt[1].startswith("cuLibraryLoadData") and txt[2] == "10" and txt[-1] == "---"
+
+
+def test_load_round_trip(saved):
+    out = _run("load", saved)
+    assert "LOAD OK 64 4" in out
+
+
+def test_numeric_save_load_bit_exact(saved):
+    _run("numeric", saved, "save")
+    _run("numeric", saved, "load")
+    a = json.load(open(os.path.join(saved, "num_save.json")))
+    b = json.load(open(os.path.join(saved, "num_load.json")))
+    assert a == b
+    # y = 1 + 2 launches * (0.25+0.5+...+1.5) * x
+    assert a[1] == pytest.approx(1 + 2 * 5.25 * 0.5 * 97)
+
+
+def test_fault_injection(saved):
+    assert "FAULTS OK" in _run("faults", saved)
