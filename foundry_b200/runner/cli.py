@@ -1,0 +1,120 @@
+"""Command line for the serving runner: SAVE an archive, LOAD it (with
+cold-start timing), or serve a synthetic load.
+
+    python -m foundry_b200.runner.cli save  --archive DIR [--model llama-3-8b] ...
+    python -m foundry_b200.runner.cli load  --archive DIR   # prints timings as JSON
+    python -m foundry_b200.runner.cli serve --archive DIR --prompts 256 --prompt-len 512 --gen 128
+
+``load`` measures cold start from FOUNDRY_SPAWN_T0_NS (set by the launching
+process just before the spawn, as in the reference's vllm/hooks.py:100-112)
+to the first generated token of a fresh request.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+T_IMPORT0 = time.time_ns()
+
+
+def _t0_ns() -> int:
+    v = os.environ.get("FOUNDRY_SPAWN_T0_NS")
+    return int(v) if v else T_IMPORT0
+
+
+def build_engine_config(args):
+    from ..models import llama
+    from .engine import EngineConfig, default_graph_sizes
+
+    cfg = llama.CONFIGS[args.model]() if args.model in llama.CONFIGS else None
+    if cfg is None and args.model.startswith("llama-3-8b-"):
+        cfg = llama.tiny(layers=int(args.model.split("-")[-1].rstrip("l")))
+    if cfg is None:
+        raise SystemExit(f"unknown model {args.model}")
+    max_seq = args.prompt_len + args.gen
+    pages = -(-max_seq // 64)
+    sizes = default_graph_sizes(args.max_graph_batch)
+    return EngineConfig(
+        model=cfg, max_batch=max(args.max_graph_batch, args.prompts), max_seq_len=max_seq,
+        num_blocks=args.prompts * pages + 64, max_prefill_tokens=args.max_prefill_tokens,
+        max_prefill_seqs=max(1, args.max_prefill_tokens // args.prompt_len), graph_sizes=sizes,
+        region_base=int(args.region_base, 16), region_size=args.region_size, seed=args.seed)
+
+
+def add_common(p):
+    p.add_argument("--archive", required=True)
+    p.add_argument("--model", default="llama-3-8b")
+    p.add_argument("--prompts", type=int, default=256)
+    p.add_argument("--prompt-len", type=int, default=512)
+    p.add_argument("--gen", type=int, default=128)
+    p.add_argument("--max-graph-batch", type=int, default=1024)
+    p.add_argument("--max-prefill-tokens", type=int, default=8192)
+    p.add_argument("--region-base", default="0x600000000000")
+    p.add_argument("--region-size", default="96GB")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--device", type=int, default=None)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="foundry_b200.runner.cli")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    for name in ("save", "load", "serve"):
+        add_common(sub.add_parser(name))
+    args = ap.parse_args(argv)
+
+    import torch
+
+    if args.device is not None:
+        torch.cuda.set_device(args.device)
+    from . import persist
+
+    if args.cmd == "save":
+        from .engine import LLMEngine
+
+        t0 = time.perf_counter()
+        eng = LLMEngine(build_engine_config(args))
+        st = persist.save(eng, args.archive)
+        st["engine_setup_s"] = eng.setup_s
+        st["wall_s"] = time.perf_counter() - t0
+        print(json.dumps({"save": {k: v for k, v in st.items() if k != "engine"}}))
+        return 0
+
+    if args.cmd == "load":
+        eng, timings = persist.load(args.archive)
+        # First token of a fresh request through the restored engine.
+        g = torch.Generator().manual_seed(args.seed + 7)
+        prompt = torch.randint(0, eng.ecfg.model.vocab, (args.prompt_len,), generator=g).tolist()
+        reqs = eng.add_requests([prompt], max_new_tokens=2)
+        eng.prefill(reqs)
+        first = time.time_ns()
+        b = eng.start_decode(reqs)
+        eng.decode_step(b)
+        second = time.time_ns()
+        eng.release(reqs)
+        timings.update({
+            "cold_start_first_token_s": (first - _t0_ns()) / 1e9,
+            "cold_start_first_decode_token_s": (second - _t0_ns()) / 1e9,
+            "python_import_s": (T_IMPORT0 - _t0_ns()) / 1e9 if os.environ.get("FOUNDRY_SPAWN_T0_NS") else None,
+        })
+        print(json.dumps({"load": timings}))
+        return 0
+
+    if args.cmd == "serve":
+        eng, timings = persist.load(args.archive)
+        g = torch.Generator().manual_seed(args.seed + 11)
+        prompts = torch.randint(0, eng.ecfg.model.vocab, (args.prompts, args.prompt_len), generator=g).tolist()
+        t0 = time.perf_counter()
+        outs = eng.generate(prompts, args.gen)
+        dt = time.perf_counter() - t0
+        print(json.dumps({"serve": {"requests": len(outs), "gen_tokens": sum(map(len, outs)), "wall_s": dt,
+                                    "restore": timings}}))
+        return 0
+    return 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
