@@ -111,6 +111,68 @@ extern "C" __global__ void __launch_bounds__(256) fb_rmsnorm(const bf16* __restr
   rmsnorm_row<8>(x + static_cast<size_t>(t) * H, w, out + static_cast<size_t>(t) * H, H, eps);
 }
 
+// Residual add of split-K GEMM slices fused with the next RMSNorm:
+//   h[t] = bf16(sum_s part[s][t] + h[t]);  x[t] = rmsnorm(h[t]) * w
+// (sum in split order, then the residual: the same arithmetic as the GEMM's
+// own residual epilogue, so split and unsplit GEMMs round the same way).
+extern "C" __global__ void __launch_bounds__(256) fb_add_rmsnorm_partials(
+    const float* __restrict__ part, int S, long long stride, bf16* __restrict__ h, const bf16* __restrict__ w,
+    bf16* __restrict__ x, int T, int H, float eps) {
+  constexpr int VPT = 4;  // H <= 256 threads * 4 vectors * 8
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  if (H > 256 * VPT * 8) {
+    set_status(FB_KERR_BAD_ARG);
+    return;
+  }
+  const int nv = H / 8;
+  bf16* hrow = h + static_cast<size_t>(t) * H;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nv) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < S; ++s) {
+      const float4* p = reinterpret_cast<const float4*>(part + s * stride + static_cast<size_t>(t) * H + i * 8);
+      const float4 a = __ldcs(p), b = __ldcs(p + 1);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+      acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+    float r[8];
+    unpack8(reinterpret_cast<const uint4*>(hrow)[i], r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] += r[e];
+    const uint4 packed = pack8(acc);
+    reinterpret_cast<uint4*>(hrow)[i] = packed;
+    unpack8(packed, v[k]);  // normalise the rounded value, as the unsplit path does
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    s = warp_sum(s);
+    if (threadIdx.x == 0) red[0] = s;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / static_cast<float>(H) + eps);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nv) continue;
+    float wf[8], o[8];
+    unpack8(reinterpret_cast<const uint4*>(w)[i], wf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = v[k][e] * inv * wf[e];
+    reinterpret_cast<uint4*>(x + static_cast<size_t>(t) * H)[i] = pack8(o);
+  }
+}
+
 // ---- SiLU * mul ---------------------------------------------------------------------
 // gu[t] = [gate (I) | up (I)]; out[t, i] = silu(gate) * up.
 extern "C" __global__ void fb_silu_mul(const bf16* __restrict__ gu, bf16* __restrict__ out, int T, int I) {
@@ -134,22 +196,39 @@ extern "C" __global__ void fb_silu_mul(const bf16* __restrict__ gu, bf16* __rest
 // One warp per head; lane l holds dims [4l, 4l+4). RoPE is the half-rotation
 // form (dim i pairs with i+64) with a precomputed fp32 (cos, sin) table
 // [max_pos, 64]. K/V go to the paged cache [blocks, Hkv, page, 128] at
-// slot_mapping[t] (negative slot = padding token, not written). If k_out is
-// non-null the rotated K heads are also written packed to k_out [T, Hkv, 128]
-// (prefill attention reads them from there).
+// slot_mapping[t] (negative slot = padding token, not written). If k_out /
+// v_out are non-null the rotated K and the V heads are also written packed to
+// [T, Hkv, 128] (prefill attention reads them from there). With S > 0 the
+// input is the S fp32 split-K slices of the QKV GEMM ([S][T][ld_qkv], summed
+// here in split order) instead of the bf16 qkv matrix.
 extern "C" __global__ void __launch_bounds__(256) fb_rope_kv_write(
     const bf16* __restrict__ qkv, int ld_qkv, const int* __restrict__ positions, const float2* __restrict__ cos_sin,
     const bf16* __restrict__ q_norm_w, const bf16* __restrict__ k_norm_w, float eps, int use_qk_norm,
     bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, const int* __restrict__ slots,
-    int T, int Hq, int Hkv, int page, bf16* __restrict__ k_out) {
+    int T, int Hq, int Hkv, int page, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
+    const float* __restrict__ part, int S, long long part_stride) {
   const int t = blockIdx.x;
   const int h = blockIdx.y * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T || h >= Hq + 2 * Hkv) return;
-  const bf16* src = qkv + static_cast<size_t>(t) * ld_qkv + h * 128 + lane * 4;
-  const uint2 raw = *reinterpret_cast<const uint2*>(src);
+  const size_t col = static_cast<size_t>(t) * ld_qkv + h * 128 + lane * 4;
   float x[4];
-  {
+  if (S > 0) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < S; ++s) {
+      const float4 p = __ldcs(reinterpret_cast<const float4*>(part + s * part_stride + col));
+      acc.x += p.x;
+      acc.y += p.y;
+      acc.z += p.z;
+      acc.w += p.w;
+    }
+    // Round through bf16 like the unsplit GEMM epilogue does.
+    x[0] = bf2f(f2bf(acc.x));
+    x[1] = bf2f(f2bf(acc.y));
+    x[2] = bf2f(f2bf(acc.z));
+    x[3] = bf2f(f2bf(acc.w));
+  } else {
+    const uint2 raw = *reinterpret_cast<const uint2*>(qkv + col);
     const float2 a = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.x));
     const float2 b = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.y));
     x[0] = a.x;
@@ -186,7 +265,8 @@ extern "C" __global__ void __launch_bounds__(256) fb_rope_kv_write(
     return;
   }
   const int kvh = is_v ? h - Hq - Hkv : h - Hq;
-  if (k_out && !is_v) *reinterpret_cast<uint2*>(k_out + (static_cast<size_t>(t) * Hkv + kvh) * 128 + lane * 4) = o;
+  bf16* packed = is_v ? v_out : k_out;
+  if (packed) *reinterpret_cast<uint2*>(packed + (static_cast<size_t>(t) * Hkv + kvh) * 128 + lane * 4) = o;
   const int slot = slots[t];
   if (slot < 0) return;
   const size_t blk = static_cast<size_t>(slot / page), off = static_cast<size_t>(slot % page);

@@ -18,9 +18,11 @@
 //               bf16 global stores; double-buffered TMEM accumulators let the
 //               epilogue of tile i overlap the MMAs of tile i+1
 // Split-K (splits > 1) spreads the K loop of one output tile over several
-// CTAs; each writes an fp32 partial tile to a workspace and the last one to
-// finish (per-tile arrival counter) sums the partials in split order
-// (deterministic) and writes the output, then re-arms the counter.
+// CTAs, so narrow decode GEMMs still put every SM on the weight stream. Each
+// split writes its fp32 slice of the output ([split][rows][ldo], coalesced)
+// and the kernel that consumes the output (fused add+RMSNorm, RoPE, ...) sums
+// the slices while reading them: no in-kernel reduction tail, no atomics, a
+// fixed summation order (deterministic).
 //
 // No TMA multicast anywhere (this kernel is also used on multi-GPU runs).
 // All waits are bounded (fb_common.cuh).
@@ -50,12 +52,10 @@ struct Cfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-__device__ __forceinline__ void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
 template <int BN>
 __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
                                           const bf16* residual, int M, int N, int K, int ldo, int mode, int splits,
-                                          float* __restrict__ ws, int* __restrict__ counters) {
+                                          float* __restrict__ ws, long long split_stride) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -67,8 +67,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  int* abort_flag = last_flag + 1;
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -269,59 +268,36 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
       } else {
-        // Split-K: publish this split's fp32 partial tile.
-        float* my = ws + (static_cast<size_t>(mn) * splits + sp) * (BM * BN);
+        // Split-K: write this split's fp32 slice of the output, in the output's
+        // own layout ([split][rows][ldo]); the consuming kernel sums the slices.
+        float* part = ws + static_cast<size_t>(sp) * split_stride;
+        if (gm < M) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(t_row + c0, r);
-          tmem_ld_wait();
-          float4* dst = reinterpret_cast<float4*>(my + row * BN + c0);
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(t_row + c0, r);
+            tmem_ld_wait();
+            const int gn0 = n_blk * BN + c0;
+            if (mode & EPI_TRANSPOSE) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+              for (int i = 0; i < 16; ++i)
+                if (gn0 + i < N) part[static_cast<size_t>(gn0 + i) * ldo + gm] = __uint_as_float(r[i]);
+            } else if (gn0 + 16 <= N) {
+              float4* dst = reinterpret_cast<float4*>(part + static_cast<size_t>(gm) * ldo + gn0);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                     __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (gn0 + i < N) part[static_cast<size_t>(gm) * ldo + gn0 + i] = __uint_as_float(r[i]);
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);  // TMEM free for the next tile
-        __threadfence();
-        named_bar_epi();
-        if (threadIdx.x == 64) {
-          const int prev = atomicAdd(&counters[mn], 1);
-          *(volatile int*)last_flag = (prev == splits - 1) ? 1 : 0;
-        }
-        named_bar_epi();
-        if (*(volatile int*)last_flag) {
-          __threadfence();
-          const float* part0 = ws + static_cast<size_t>(mn) * splits * (BM * BN);
-          if (gm < M) {
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 4) {
-              float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-              for (int q = 0; q < splits; ++q) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(part0 + q * (BM * BN) + row * BN + c0));
-                s.x += v.x;
-                s.y += v.y;
-                s.z += v.z;
-                s.w += v.w;
-              }
-              const float vals[4] = {s.x, s.y, s.z, s.w};
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int gn = n_blk * BN + c0 + i;
-                if (gn >= N) continue;
-                const size_t idx = (mode & EPI_TRANSPOSE) ? static_cast<size_t>(gn) * ldo + gm
-                                                          : static_cast<size_t>(gm) * ldo + gn;
-                float v = vals[i];
-                if (mode & EPI_RESIDUAL) v += bf2f(residual[idx]);
-                out[idx] = f2bf(v);
-              }
-            }
-          }
-          named_bar_epi();
-          if (threadIdx.x == 64) counters[mn] = 0;  // re-arm for the next launch / graph replay
-        }
+        if (lane == 0) mbar_arrive(&tempty[acc]);
       }
     }
   }
@@ -337,8 +313,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
 #define FB_GEMM_INSTANCE(BN)                                                                                        \
   extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_bf16_bn##BN(                                 \
       const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
-      const bf16* residual, int M, int N, int K, int ldo, int mode, int splits, float* ws, int* counters) {         \
-    gemm_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, counters);                            \
+      const bf16* residual, int M, int N, int K, int ldo, int mode, int splits, float* ws,                          \
+      long long split_stride) {                                                                                      \
+    gemm_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);                        \
   }
 
 FB_GEMM_INSTANCE(16)

@@ -139,22 +139,31 @@ class LlamaModel:
         x = st.normed[:b]
         ops.embedding(st.input_ids[:b], w.embed, h)
         splits = st.attn_splits[b]
+        pending = None  # split-K slices of the previous down-projection, not yet added to h
         for li, lw in enumerate(w.layers):
-            ops.rmsnorm(h, lw["attn_norm"], x, cfg.eps)
-            qkv = ops.linear(x, lw["qkv"], out=st.qkv[:b], ws=st.gemm_ws)
+            self._norm(pending, h, lw["attn_norm"], x)
+            qkv = ops.linear(x, lw["qkv"], out=st.qkv[:b], partials=st.part)
             ops.rope_kv_write(qkv, st.positions[:b], self.cos_sin, st.q[:b], st.k_cache[li], st.v_cache[li],
                               st.slots[:b], cfg.n_q, cfg.n_kv, lw.get("q_norm"), lw.get("k_norm"), cfg.eps)
             ops.decode_attention(st.q[:b], st.k_cache[li], st.v_cache[li], st.block_tables[:b], st.seq_lens[:b],
                                  st.attn_out[:b].view(b, cfg.n_q, cfg.head_dim), st.max_pages, st.attn_ws,
                                  scale=self.scale, splits=splits)
-            ops.linear(st.attn_out[:b], lw["o"], out=h, residual=h, ws=st.gemm_ws)
-            ops.rmsnorm(h, lw["mlp_norm"], x, cfg.eps)
-            gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:b], ws=st.gemm_ws)
+            o = ops.linear(st.attn_out[:b], lw["o"], out=h, residual=h, partials=st.part)
+            self._norm(o if isinstance(o, ops.Partial) else None, h, lw["mlp_norm"], x)
+            gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:b])
             ops.silu_mul(gu, st.act[:b])
-            ops.linear(st.act[:b], lw["down"], out=h, residual=h, ws=st.gemm_ws)
-        ops.rmsnorm(h, w.final_norm, x, cfg.eps)
-        ops.linear(x, w.lm_head, out=st.logits[:b], ws=st.gemm_ws)
+            d = ops.linear(st.act[:b], lw["down"], out=h, residual=h, partials=st.part)
+            pending = d if isinstance(d, ops.Partial) else None
+        self._norm(pending, h, w.final_norm, x)
+        ops.linear(x, w.lm_head, out=st.logits[:b])
         ops.argmax(st.logits[:b], st.next_ids[:b])
+
+    def _norm(self, pending, h, weight, x) -> None:
+        """x = rmsnorm(h), first adding pending split-K slices into h."""
+        if pending is None:
+            ops.rmsnorm(h, weight, x, self.cfg.eps)
+        else:
+            ops.add_rmsnorm_partials(pending, h, weight, x, self.cfg.eps)
 
     # ---- prefill of a packed batch of prompts (eager) --------------------------------------
     def prefill(self, pb) -> None:
@@ -169,25 +178,25 @@ class LlamaModel:
         nkvd = cfg.n_kv * cfg.head_dim
         for li, lw in enumerate(w.layers):
             ops.rmsnorm(h, lw["attn_norm"], x, cfg.eps)
-            qkv = ops.linear(x, lw["qkv"], out=pb.qkv[:t], ws=pb.gemm_ws)
-            # Rotated q -> pb.q, rotated k -> paged cache and packed pb.k_rot, v -> cache.
+            qkv = ops.linear(x, lw["qkv"], out=pb.qkv[:t])
+            # Rotated q -> pb.q; rotated k and v -> paged cache and packed pb.k_rot / pb.v_rot.
             ops.rope_kv_write(qkv, pb.positions[:t], self.cos_sin, pb.q[:t], pb.k_cache[li], pb.v_cache[li],
                               pb.slots[:t], cfg.n_q, cfg.n_kv, lw.get("q_norm"), lw.get("k_norm"), cfg.eps,
-                              k_out=pb.k_rot[:t])
-            v_src = qkv[:, nqd + nkvd:]  # v heads read in place (row stride = qkv row)
-            ops.prefill_attention(pb.q[:t].view(t, nqd), pb.k_rot[:t].view(t, nkvd), v_src, pb.attn_out[:t],
-                                  pb.cu_seqlens, pb.tile_seq, pb.tile_start, cfg.n_q, cfg.n_kv, scale=self.scale)
-            ops.linear(pb.attn_out[:t], lw["o"], out=h, residual=h, ws=pb.gemm_ws)
+                              k_out=pb.k_rot[:t], v_out=pb.v_rot[:t])
+            ops.prefill_attention(pb.q[:t].view(t, nqd), pb.k_rot[:t].view(t, nkvd), pb.v_rot[:t].view(t, nkvd),
+                                  pb.attn_out[:t], pb.cu_seqlens, pb.tile_seq, pb.tile_start, cfg.n_q, cfg.n_kv,
+                                  scale=self.scale)
+            ops.linear(pb.attn_out[:t], lw["o"], out=h, residual=h)
             ops.rmsnorm(h, lw["mlp_norm"], x, cfg.eps)
-            gu = ops.linear(x, lw["gate_up"], out=pb.gate_up[:t], ws=pb.gemm_ws)
+            gu = ops.linear(x, lw["gate_up"], out=pb.gate_up[:t])
             ops.silu_mul(gu, pb.act[:t])
-            ops.linear(pb.act[:t], lw["down"], out=h, residual=h, ws=pb.gemm_ws)
+            ops.linear(pb.act[:t], lw["down"], out=h, residual=h)
         # last token of every prompt -> logits -> greedy token
         n = pb.num_seqs
         last = pb.last_rows[:n]
         torch.index_select(h, 0, last, out=pb.last_hidden[:n])
         ops.rmsnorm(pb.last_hidden[:n], w.final_norm, pb.last_normed[:n], cfg.eps)
-        ops.linear(pb.last_normed[:n], w.lm_head, out=pb.logits[:n], ws=pb.gemm_ws)
+        ops.linear(pb.last_normed[:n], w.lm_head, out=pb.logits[:n])
         ops.argmax(pb.logits[:n], pb.next_ids[:n])
 
 

@@ -9,6 +9,7 @@ from .attention import (
     prefill_tiles,
 )
 from .basic import (
+    add_rmsnorm_partials,
     argmax,
     copy_i32,
     decode_advance,
@@ -20,14 +21,14 @@ from .basic import (
     rope_kv_write,
     silu_mul,
 )
-from .gemm import GemmWorkspace, default_workspace, linear, plan
+from .gemm import Partial, PartialBuffer, linear, plan
 
 status = _rt.status
 clear_status = _rt.clear_status
 
 __all__ = [
-    "DecodeWorkspace", "GemmWorkspace", "argmax", "clear_status", "copy_i32", "decode_advance",
-    "decode_attention", "decode_splits", "default_workspace", "embedding", "fill_", "init_normal_",
+    "DecodeWorkspace", "Partial", "PartialBuffer", "add_rmsnorm_partials", "argmax", "clear_status", "copy_i32", "decode_advance",
+    "decode_attention", "decode_splits", "embedding", "fill_", "init_normal_",
     "linear", "plan", "prefill_attention", "prefill_tiles", "rmsnorm", "rope_cos_sin", "rope_kv_write",
     "silu_mul", "status",
 ]

@@ -8,6 +8,7 @@ import math
 import torch
 
 from . import _rt
+from .gemm import Partial
 
 _IMG = "elementwise"
 
@@ -79,23 +80,39 @@ def rope_cos_sin(max_pos: int, theta: float, head_dim: int = 128, device=None,
     return torch.stack([ang.cos(), ang.sin()], dim=-1).to(torch.float32).contiguous().to(device)
 
 
-def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, q_out: torch.Tensor,
+def rope_kv_write(qkv, positions: torch.Tensor, cos_sin: torch.Tensor, q_out: torch.Tensor,
                   k_cache: torch.Tensor, v_cache: torch.Tensor, slots: torch.Tensor, n_q: int, n_kv: int,
                   q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None,
-                  eps: float = 1e-6, k_out: torch.Tensor | None = None) -> None:
+                  eps: float = 1e-6, k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None) -> None:
     """Rotates q (into q_out [T, n_q, 128]) and k, writes k/v into the paged
     caches [blocks, n_kv, page, 128]; optional per-head RMSNorm on q/k first.
-    With ``k_out`` the rotated k is also written packed [T, n_kv, 128]."""
-    t_tok = qkv.shape[0]
+    ``qkv`` is the bf16 [T, (n_q+2n_kv)*128] GEMM output or a ``Partial``
+    (split-K slices, summed here). With ``k_out``/``v_out`` the rotated k and
+    the v heads are also written packed [T, n_kv, 128]."""
+    if isinstance(qkv, Partial):
+        t_tok, ld = qkv.rows, qkv.cols
+        src, part, s, stride = 0, qkv.buf.data_ptr(), qkv.splits, qkv.stride
+    else:
+        t_tok, ld = qkv.shape[0], qkv.stride(0)
+        src, part, s, stride = qkv.data_ptr(), 0, 0, 0
     page = k_cache.shape[2]
     use_norm = 1 if q_norm is not None else 0
     heads = n_q + 2 * n_kv
     _rt.launch(_IMG, "fb_rope_kv_write", (t_tok, math.ceil(heads / 8)), (256,), [
-        qkv.data_ptr(), qkv.stride(0), positions.data_ptr(), cos_sin.data_ptr(),
+        src, ld, positions.data_ptr(), cos_sin.data_ptr(),
         q_norm.data_ptr() if use_norm else 0, k_norm.data_ptr() if use_norm else 0, float(eps), use_norm,
         q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), slots.data_ptr(), t_tok, n_q, n_kv, page,
-        k_out.data_ptr() if k_out is not None else 0,
+        k_out.data_ptr() if k_out is not None else 0, v_out.data_ptr() if v_out is not None else 0,
+        part, s, stride,
     ])
+
+
+def add_rmsnorm_partials(p: Partial, h: torch.Tensor, w: torch.Tensor, x: torch.Tensor, eps: float) -> None:
+    """h = bf16(sum of split slices + h); x = rmsnorm(h) * w (one pass)."""
+    t_tok, hid = h.shape
+    assert p.rows == t_tok and p.cols == hid and h.is_contiguous() and x.is_contiguous()
+    _rt.launch(_IMG, "fb_add_rmsnorm_partials", (t_tok,), (256,), [
+        p.buf.data_ptr(), p.splits, p.stride, h.data_ptr(), w.data_ptr(), x.data_ptr(), t_tok, hid, float(eps)])
 
 
 def argmax(logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:

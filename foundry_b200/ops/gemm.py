@@ -3,9 +3,14 @@
 ``linear(x, w)`` computes ``x @ w.T`` (nn.Linear layout: ``w`` is
 [out_features, in_features]). Small token counts (decode) run "swap-AB": the
 weight rows fill the 128-row MMA M dimension and the tokens become the MMA N
-dimension (16..256), the output is written transposed back to [tokens, out].
-Narrow problems are split along K so every SM streams weights; split partials
-are reduced deterministically inside the kernel.
+dimension (16..256); the output is written transposed back to [tokens, out].
+
+When a problem has too few output tiles to occupy every SM, the planner
+splits K. Split GEMMs do not reduce in-kernel: each split writes its fp32
+slice of the output and ``linear`` returns a ``Partial`` that the consuming
+op (``add_rmsnorm_partials``, ``rope_kv_write``, ``reduce_partials``) sums
+while it reads its input. Callers that cannot consume slices pass no
+``partials`` buffer and get an unsplit GEMM.
 """
 
 from __future__ import annotations
@@ -23,6 +28,12 @@ EPI_TRANSPOSE, EPI_RESIDUAL, EPI_A_STREAM, EPI_B_STREAM = 1, 2, 4, 8
 _BF16 = 9  # CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
 _SWIZZLE_128B = 3
 _BNS = (16, 32, 64, 128, 256)
+# Cost model constants (measured on B200): per-CTA shared-memory fill rate of
+# the TMA pipeline, per-SM bf16 tensor rate, and achievable HBM bandwidth.
+_CTA_FILL_BPS = 90e9
+_SM_MMA_FLOPS = 14e12
+_HBM_BPS = 6.0e12
+MAX_SPLITS = 8
 
 
 def smem_bytes(bn: int) -> int:
@@ -31,34 +42,31 @@ def smem_bytes(bn: int) -> int:
     return stages * stage + 1024 + 256
 
 
-class GemmWorkspace:
-    """Split-K partial tiles (fp32) and per-tile arrival counters.
+@dataclass
+class Partial:
+    """fp32 split-K slices of a GEMM output: ``buf[s * stride + row * cols + col]``."""
 
-    Counters must start at zero; the kernel re-arms them, so a workspace can be
-    reused by any number of launches and graph replays, but not by two GEMMs
-    running concurrently.
-    """
-
-    def __init__(self, nbytes: int = 64 << 20, n_counters: int = 1 << 16, device=None,
-                 ws: torch.Tensor | None = None, counters: torch.Tensor | None = None):
-        device = device or torch.device("cuda", torch.cuda.current_device())
-        self.ws = ws if ws is not None else torch.empty(nbytes // 4, dtype=torch.float32, device=device)
-        self.counters = counters if counters is not None else torch.zeros(n_counters, dtype=torch.int32, device=device)
+    buf: torch.Tensor
+    splits: int
+    rows: int
+    cols: int
 
     @property
-    def nbytes(self) -> int:
-        return self.ws.numel() * 4
+    def stride(self) -> int:
+        return self.rows * self.cols
 
 
-_default_ws: dict[int, GemmWorkspace] = {}
+class PartialBuffer:
+    """Scratch for split slices (fp32). Must not be shared by GEMMs whose
+    slices are still unconsumed."""
 
+    def __init__(self, numel: int | None = None, device=None, buf: torch.Tensor | None = None):
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        self.buf = buf if buf is not None else torch.empty(numel, dtype=torch.float32, device=device)
 
-def default_workspace() -> GemmWorkspace:
-    dev = torch.cuda.current_device()
-    ws = _default_ws.get(dev)
-    if ws is None:
-        ws = _default_ws[dev] = GemmWorkspace()
-    return ws
+    @property
+    def numel(self) -> int:
+        return self.buf.numel()
 
 
 _tmaps: dict[tuple, bytes] = {}
@@ -74,7 +82,7 @@ def tmap(t: torch.Tensor, box_rows: int) -> bytes:
         if t.stride(1) != 1 or (ld * 2) % 16 or t.data_ptr() % 16:
             raise ValueError("GEMM operands must be K-contiguous with 16-byte aligned rows")
         m = core().make_tmap_2d(t.data_ptr(), _BF16, k, rows, ld * 2, BK, box_rows, _SWIZZLE_128B)
-        if len(_tmaps) > 4096:
+        if len(_tmaps) > 8192:
             _tmaps.clear()
         _tmaps[key] = m
     return m
@@ -86,61 +94,79 @@ class Plan:
     splits: int
     grid: int
     swap: bool
+    est_us: float = 0.0
 
 
-def plan(m_tok: int, n_out: int, k: int, sms: int | None = None) -> Plan:
+def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bool = True) -> Plan:
+    """Chooses the tile width and split count with a small cost model:
+    waves of CTAs x k-blocks per CTA x time per k-block, bounded below by the
+    HBM time of the operands, plus the traffic of split slices."""
     sms = sms or _rt.sm_count()
     swap = m_tok <= 256
-    if swap:
-        mg, ng = n_out, m_tok
-        bn = next(b for b in _BNS if b >= ng)
-    else:
-        mg, ng = m_tok, n_out
-        bn = 256 if ng >= 256 else next(b for b in _BNS if b >= ng)
-    tiles = math.ceil(mg / BM) * math.ceil(ng / bn)
+    mg, ng = (n_out, m_tok) if swap else (m_tok, n_out)
     kb = math.ceil(k / BK)
-    splits = 1
-    if tiles < sms:
-        splits = max(1, min(math.ceil(sms / tiles), kb // 4, 16))
-    grid = min(tiles * splits, sms)
-    return Plan(bn=bn, splits=splits, grid=grid, swap=swap)
+    tm = math.ceil(mg / BM)
+    dram = (mg * k + ng * k) * 2 / _HBM_BPS
+    best = None
+    if swap:
+        cands = [b for b in _BNS if b >= min(ng, 256) / 4 or b == 256]
+    else:
+        cands = [128, 256]
+    for bn in cands:
+        tn = math.ceil(ng / bn)
+        for s in range(1, (MAX_SPLITS if allow_split else 1) + 1):
+            if s > 1 and kb // s < 4:
+                break
+            units = tm * tn * s
+            waves = math.ceil(units / sms)
+            kbp = math.ceil(kb / s)
+            t_kb = max((BM * BK * 2 + bn * BK * 2) / _CTA_FILL_BPS, 2 * BM * bn * BK / _SM_MMA_FLOPS)
+            t = max(waves * (kbp * t_kb + 1.5e-6), dram)
+            if s > 1:
+                t += 2 * s * mg * ng * 4 / _HBM_BPS
+            if best is None or t < best.est_us * 1e-6 * 0.97:
+                best = Plan(bn=bn, splits=s, grid=min(units, sms), swap=swap, est_us=t * 1e6)
+    return best
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
-           residual: torch.Tensor | None = None, ws: GemmWorkspace | None = None,
-           plan_override: Plan | None = None) -> torch.Tensor:
+           residual: torch.Tensor | None = None, partials: PartialBuffer | None = None,
+           plan_override: Plan | None = None):
     """out = x @ w.T (+ residual). x: [T, K] bf16, w: [N, K] bf16, out: [T, N] bf16.
 
-    ``residual`` may alias ``out`` (in-place residual add).
+    Returns ``out`` - or, when ``partials`` is given and the plan splits K, a
+    ``Partial`` whose slices the caller's next op must consume (``residual``
+    is then NOT applied; the consumer adds it). ``residual`` may alias ``out``.
     """
     assert x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
     t_tok, k = x.shape
     n_out, k2 = w.shape
     assert k == k2, f"K mismatch {k} vs {k2}"
-    if out is None:
-        out = torch.empty(t_tok, n_out, dtype=torch.bfloat16, device=x.device)
-    assert out.stride(1) == 1 and out.shape == (t_tok, n_out)
-    p = plan_override or plan(t_tok, n_out, k)
-    ws = ws or default_workspace()
+    p = plan_override or plan(t_tok, n_out, k, allow_split=partials is not None)
     mode = 0
     if p.swap:
         a, b, mg, ng = w, x, n_out, t_tok
-        mode |= EPI_TRANSPOSE | EPI_A_STREAM
+        mode |= EPI_TRANSPOSE
+        if math.ceil(ng / p.bn) == 1:
+            mode |= EPI_A_STREAM  # each weight byte is read once: evict-first
     else:
         a, b, mg, ng = x, w, t_tok, n_out
+    if p.splits > 1:
+        assert partials is not None
+        need = p.splits * t_tok * n_out
+        if need > partials.numel:
+            raise RuntimeError(f"split-K slice buffer too small: need {need} floats, have {partials.numel}")
+        args = [tmap(a, BM), tmap(b, p.bn), 0, 0, mg, ng, k, n_out, mode, p.splits,
+                partials.buf.data_ptr(), t_tok * n_out]
+        _rt.launch("gemm_bf16", f"fb_gemm_bf16_bn{p.bn}", (p.grid,), (192,), args, smem=smem_bytes(p.bn))
+        return Partial(partials.buf, p.splits, t_tok, n_out)
+    if out is None:
+        out = torch.empty(t_tok, n_out, dtype=torch.bfloat16, device=x.device)
+    assert out.stride(1) == 1 and out.shape == (t_tok, n_out)
     if residual is not None:
         assert residual.shape == out.shape and residual.stride() == out.stride()
         mode |= EPI_RESIDUAL
-    if p.splits > 1:
-        need = math.ceil(mg / BM) * math.ceil(ng / p.bn) * p.splits * BM * p.bn * 4
-        if need > ws.nbytes:
-            raise RuntimeError(f"GEMM workspace too small: need {need} bytes, have {ws.nbytes}")
-        if math.ceil(mg / BM) * math.ceil(ng / p.bn) > ws.counters.numel():
-            raise RuntimeError("GEMM workspace has too few tile counters")
-    args = [
-        tmap(a, BM), tmap(b, p.bn), out.data_ptr(),
-        residual.data_ptr() if residual is not None else 0,
-        mg, ng, k, out.stride(0), mode, p.splits, ws.ws.data_ptr(), ws.counters.data_ptr(),
-    ]
+    args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
+            mg, ng, k, out.stride(0), mode, 1, 0, 0]
     _rt.launch("gemm_bf16", f"fb_gemm_bf16_bn{p.bn}", (p.grid,), (192,), args, smem=smem_bytes(p.bn))
     return out

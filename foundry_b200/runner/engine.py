@@ -28,7 +28,7 @@ import torch
 from .. import ops
 from ..models.llama import LlamaConfig, LlamaModel, LlamaWeights
 from ..ops.attention import DecodeWorkspace, decode_splits, prefill_tiles
-from ..ops.gemm import GemmWorkspace
+from ..ops.gemm import MAX_SPLITS, PartialBuffer
 from .arena import Arena
 
 PAGE = 64
@@ -53,7 +53,6 @@ class EngineConfig:
     region_base: int | None = 0x600000000000
     region_size: int | str = "96GB"
     seed: int = 0
-    gemm_ws_bytes: int = 64 << 20
     extra: dict = field(default_factory=dict)
 
     @property
@@ -64,7 +63,7 @@ class EngineConfig:
 class DecodeState:
     """Static device buffers of a decode step for up to max_batch rows."""
 
-    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, gemm_ws: GemmWorkspace):
+    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache):
         cfg = ecfg.model
         b = ecfg.max_batch
         self.page = PAGE
@@ -86,7 +85,8 @@ class DecodeState:
         self.act = arena.empty((b, cfg.inter))
         self.logits = arena.empty((b, cfg.vocab))
         self.k_cache, self.v_cache = k_cache, v_cache
-        self.gemm_ws = gemm_ws
+        # fp32 split-K slices of the decode GEMMs (consumed by the next op)
+        self.part = PartialBuffer(buf=arena.empty((MAX_SPLITS * b * max(cfg.qkv_dim, cfg.hidden),), torch.float32))
         sizes = ecfg.graph_sizes or default_graph_sizes(b)
         self.attn_splits = {s: decode_splits(s, cfg.n_kv, self.max_pages) for s in sizes}
         for s in range(1, b + 1):
@@ -101,7 +101,7 @@ class DecodeState:
 class PrefillBatch:
     """Static device buffers of one packed prefill chunk."""
 
-    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, gemm_ws: GemmWorkspace):
+    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache):
         cfg = ecfg.model
         t, n = ecfg.max_prefill_tokens, ecfg.max_prefill_seqs
         i32 = torch.int32
@@ -119,6 +119,7 @@ class PrefillBatch:
         self.qkv = arena.empty((t, cfg.qkv_dim))
         self.q = arena.empty((t, cfg.n_q, cfg.head_dim))
         self.k_rot = arena.empty((t, cfg.n_kv, cfg.head_dim))
+        self.v_rot = arena.empty((t, cfg.n_kv, cfg.head_dim))
         self.attn_out = arena.empty((t, cfg.n_q * cfg.head_dim))
         self.gate_up = arena.empty((t, 2 * cfg.inter))
         self.act = arena.empty((t, cfg.inter))
@@ -127,7 +128,6 @@ class PrefillBatch:
         self.logits = arena.empty((n, cfg.vocab))
         self.next_ids = arena.zeros((n,), i32)
         self.k_cache, self.v_cache = k_cache, v_cache
-        self.gemm_ws = gemm_ws
         self.num_tokens = 0
         self.num_seqs = 0
         # host staging (pinned)
@@ -169,13 +169,11 @@ class LLMEngine:
         self.num_blocks = nb
         self.k_cache = [self.arena.empty((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
         self.v_cache = [self.arena.empty((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
-        self.gemm_ws = GemmWorkspace(ws=self.arena.empty((ecfg.gemm_ws_bytes // 4,), torch.float32),
-                                     counters=self.arena.zeros((1 << 16,), torch.int32))
         self.cos_sin = self.arena.empty((ecfg.max_seq_len, cfg.head_dim // 2, 2), torch.float32)
         self.cos_sin.copy_(ops.rope_cos_sin(ecfg.max_seq_len, cfg.rope_theta, cfg.head_dim,
                                             scaling=cfg.rope_scaling))
-        self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache, self.gemm_ws)
-        self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache, self.gemm_ws)
+        self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache)
+        self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache)
         self.model = LlamaModel(cfg, self.weights, self.cos_sin)
         self.graph_sizes = sorted(ecfg.graph_sizes or default_graph_sizes(ecfg.max_batch))
         self.graphs: dict[int, object] = {}

@@ -34,7 +34,7 @@ def engine_config_to_dict(e: EngineConfig) -> dict:
         "model": e.model.to_dict(), "max_batch": e.max_batch, "max_seq_len": e.max_seq_len,
         "num_blocks": e.num_blocks, "max_prefill_tokens": e.max_prefill_tokens,
         "max_prefill_seqs": e.max_prefill_seqs, "graph_sizes": e.graph_sizes, "region_base": e.region_base,
-        "region_size": e.region_size, "seed": e.seed, "gemm_ws_bytes": e.gemm_ws_bytes,
+        "region_size": e.region_size, "seed": e.seed,
     }
 
 

@@ -50,17 +50,35 @@ def test_linear_residual(t, n, k):
     torch.testing.assert_close(out.float(), ref, atol=5e-2, rtol=2e-2)
 
 
-def test_linear_split_determinism():
+@pytest.mark.parametrize("t,n,k", [(32, 1024, 4096), (256, 4096, 4096), (256, 4096, 14336), (7, 6144, 4096)])
+def test_linear_split_partials(t, n, k):
+    """Split-K GEMMs return fp32 slices; consumers sum them (deterministically)."""
     from foundry_b200 import ops
-    from foundry_b200.ops.gemm import plan
 
-    x = _bf(32, 4096, seed=6)
-    w = _bf(1024, 4096, scale=0.02, seed=7)
-    p = plan(32, 1024, 4096)
-    assert p.splits > 1
-    a = ops.linear(x, w).clone()
-    b = ops.linear(x, w).clone()
-    assert torch.equal(a, b)
+    x = _bf(t, k, seed=6)
+    w = _bf(n, k, scale=0.02, seed=7)
+    pb = ops.PartialBuffer(8 * t * n)
+    p = ops.plan(t, n, k, allow_split=True)
+    assert p.splits > 1, p
+    r = ops.linear(x, w, partials=pb)
+    assert isinstance(r, ops.Partial) and r.splits == p.splits
+    total = r.buf[: r.splits * r.stride].view(r.splits, t, n).sum(0)
+    torch.testing.assert_close(total, x.float() @ w.float().T, atol=2e-2 * math.sqrt(k / 256), rtol=2e-2)
+    # consumer: fused residual add + RMSNorm
+    h = _bf(t, n, seed=8)
+    h0 = h.clone()
+    wn = _bf(n, seed=9)
+    xo = torch.empty_like(h)
+    ops.add_rmsnorm_partials(r, h, wn, xo, 1e-5)
+    href = (total + h0.float()).to(torch.bfloat16)
+    assert torch.equal(h, href)
+    hf = href.float()
+    ref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * wn.float()
+    torch.testing.assert_close(xo.float(), ref, atol=2e-2, rtol=1e-2)
+    # determinism: the same launch twice gives identical slices
+    s1 = r.buf[: r.splits * r.stride].clone()
+    ops.linear(x, w, partials=pb)
+    assert torch.equal(s1, pb.buf[: r.splits * r.stride])
 
 
 def test_rmsnorm_silu_embedding_argmax():
