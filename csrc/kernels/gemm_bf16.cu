@@ -9,14 +9,18 @@
 // tokens still use full 128xN tensor-core tiles. The epilogue writes D either
 // as out[m][n] or transposed as out[n][m], optionally adding a residual.
 //
-// Structure (one CTA per SM, persistent over output tiles):
+// Structure (one CTA per SM, persistent over work units):
 //   warp 0      TMA producer: A/B tiles (128B-swizzled) into a STAGES-deep ring
 //   warp 1      allocates TMEM; one elected lane issues tcgen05.mma (M=128,
 //               N=BN, K=16) and tcgen05.commit to release smem stages and to
 //               publish finished accumulators
 //   warps 2-5   epilogue: tcgen05.ld (32 lanes x 16 columns) -> registers ->
-//               bf16 global stores; double-buffered TMEM accumulators let the
-//               epilogue of tile i overlap the MMAs of tile i+1
+//               global stores; when TMEM has room the accumulators are double
+//               buffered so the epilogue of one unit overlaps the next unit's MMAs
+// A work unit is MT (1 or 2) 128-row A tiles x one BN-column B tile: with
+// MT = 2 the B tile in shared memory feeds two MMAs per K step, halving the
+// B bytes each SM has to pull per A byte (decode GEMMs are bound by how fast
+// an SM can ingest tiles, and B is re-read for every A tile).
 // Split-K (splits > 1) spreads the K loop of one output tile over several
 // CTAs, so narrow decode GEMMs still put every SM on the weight stream. Each
 // split writes its fp32 slice of the output ([split][rows][ldo], coalesced)
@@ -42,26 +46,32 @@ constexpr int EPI_A_STREAM = 4;  // L2 evict-first hint on A loads
 constexpr int EPI_B_STREAM = 8;  // L2 evict-first hint on B loads
 constexpr int NUM_THREADS = 192;
 
-template <int BN>
+constexpr uint32_t tmem_cols_for(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
+template <int BN, int MT>
 struct Cfg {
-  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int A_BYTES = BM * BK * 2;         // one 128-row A tile per K step
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = MT * A_BYTES + B_BYTES;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int ACC_COLS = MT * BN;             // TMEM columns of one accumulator set
+  static constexpr int ACC_BUFS = (2 * ACC_COLS <= 512) ? 2 : 1;
+  static constexpr uint32_t TMEM_COLS = tmem_cols_for(ACC_BUFS * ACC_COLS);
 };
 
-template <int BN>
+template <int BN, int MT>
 __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
                                           const bf16* residual, int M, int N, int K, int ldo, int mode, int splits,
                                           float* __restrict__ ws, long long split_stride) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MT>;
   constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::ACC_BUFS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint8_t* sA = smem;                               // [STAGES][MT][128 x 64]
+  uint8_t* sB = smem + STAGES * MT * C::A_BYTES;     // [STAGES][BN x 64]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -71,11 +81,11 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (M + BM - 1) / BM;
+  const int num_m = (M + BM * MT - 1) / (BM * MT);   // units along M
   const int num_n = (N + BN - 1) / BN;
   const int KB = (K + BK - 1) / BK;
   const int kb_per = (KB + splits - 1) / splits;
-  const int num_tiles = num_m * num_n * splits;
+  const int num_units = num_m * num_n * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -108,9 +118,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      const uint64_t pol_a = policy_evict_first();
-      for (int t = blockIdx.x; t < num_tiles && !*(volatile int*)abort_flag; t += gridDim.x) {
-        const int mn = t / splits, sp = t % splits;
+      const uint64_t pol = policy_evict_first();
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
+        const int mn = u / splits, sp = u % splits;
         const int m_blk = mn % num_m, n_blk = mn / num_m;
         const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -121,12 +131,17 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           // Operands read exactly once per launch (decode weights) are hinted
           // evict-first so they do not push reused activations out of L2.
-          if (mode & EPI_A_STREAM)
-            tma_load_2d_hint(sA + stage * C::A_BYTES, tmA, &full[stage], kb * BK, m_blk * BM, pol_a);
-          else
-            tma_load_2d(sA + stage * C::A_BYTES, tmA, &full[stage], kb * BK, m_blk * BM);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            uint8_t* dst = sA + (stage * MT + mt) * C::A_BYTES;
+            const int row = (m_blk * MT + mt) * BM;
+            if (mode & EPI_A_STREAM)
+              tma_load_2d_hint(dst, tmA, &full[stage], kb * BK, row, pol);
+            else
+              tma_load_2d(dst, tmA, &full[stage], kb * BK, row);
+          }
           if (mode & EPI_B_STREAM)
-            tma_load_2d_hint(sB + stage * C::B_BYTES, tmB, &full[stage], kb * BK, n_blk * BN, pol_a);
+            tma_load_2d_hint(sB + stage * C::B_BYTES, tmB, &full[stage], kb * BK, n_blk * BN, pol);
           else
             tma_load_2d(sB + stage * C::B_BYTES, tmB, &full[stage], kb * BK, n_blk * BN);
           if (++stage == STAGES) {
@@ -137,8 +152,6 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       }
       // Drain: every armed stage must complete before the CTA may exit.
       for (int s = 0; s < STAGES; ++s) {
-        // The last phase armed on stage s completes when its consumer released it;
-        // waiting on `empty` with the producer's parity covers both cases.
         mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
         if (++stage == STAGES) {
           stage = 0;
@@ -153,17 +166,17 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*(volatile int*)abort_flag; t += gridDim.x, ++it) {
-        const int sp = t % splits;
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
+        const int sp = u % splits;
         const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
-        const int acc = it & 1;
-        const uint32_t aphase = (it >> 1) & 1;
+        const int acc = NBUF == 2 ? (it & 1) : 0;
+        const uint32_t aphase = NBUF == 2 ? ((it >> 1) & 1) : (it & 1);
         if (!mbar_wait(&tempty[acc], aphase ^ 1, FB_KERR_TIMEOUT_TMEM)) {
           *(volatile int*)abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
@@ -171,13 +184,16 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = sdesc_sw128(smem_u32(sA + stage * C::A_BYTES));
           const uint64_t bdesc = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // +32 bytes per 16-element K step inside the 128-byte swizzle row.
-            mma_bf16(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
-                     (kb > kb0 || k > 0) ? 1u : 0u);
+          for (int mt = 0; mt < MT; ++mt) {
+            const uint64_t adesc = sdesc_sw128(smem_u32(sA + (stage * MT + mt) * C::A_BYTES));
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              // +32 bytes per 16-element K step inside the 128-byte swizzle row.
+              mma_bf16(d_tmem + mt * BN, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                       (kb > kb0 || k > 0) ? 1u : 0u);
+            }
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -195,89 +211,32 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles && !*(volatile int*)abort_flag; t += gridDim.x, ++it) {
-      const int mn = t / splits, sp = t % splits;
+    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
+      const int mn = u / splits, sp = u % splits;
       const int m_blk = mn % num_m, n_blk = mn / num_m;
-      const int acc = it & 1;
-      const uint32_t aphase = (it >> 1) & 1;
+      const int acc = NBUF == 2 ? (it & 1) : 0;
+      const uint32_t aphase = NBUF == 2 ? ((it >> 1) & 1) : (it & 1);
       if (!mbar_wait(&tfull[acc], aphase, FB_KERR_TIMEOUT_TMEM)) {
         *(volatile int*)abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      const int gm = m_blk * BM + row;  // D row
-      if (splits == 1) {
+      float* part = splits > 1 ? ws + static_cast<size_t>(sp) * split_stride : nullptr;
+#pragma unroll 1
+      for (int mt = 0; mt < MT; ++mt) {
+        const int gm = (m_blk * MT + mt) * BM + quarter * 32 + lane;  // D row of this thread
+        const uint32_t t_row =
+            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::ACC_COLS + mt * BN;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 16) {
           uint32_t r[16];
           tmem_ld16(t_row + c0, r);
           tmem_ld_wait();
           const int gn0 = n_blk * BN + c0;
-          if (gm < M) {
-            if (mode & EPI_TRANSPOSE) {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int gn = gn0 + i;
-                if (gn < N) {
-                  const size_t idx = static_cast<size_t>(gn) * ldo + gm;
-                  float v = __uint_as_float(r[i]);
-                  if (mode & EPI_RESIDUAL) v += bf2f(residual[idx]);
-                  out[idx] = f2bf(v);
-                }
-              }
-            } else {
-              const size_t base = static_cast<size_t>(gm) * ldo + gn0;
-              if (gn0 + 16 <= N) {
-                float f[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(r[i]);
-                if (mode & EPI_RESIDUAL) {
-                  float a[8], b[8];
-                  unpack8(*reinterpret_cast<const uint4*>(residual + base), a);
-                  unpack8(*reinterpret_cast<const uint4*>(residual + base + 8), b);
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) {
-                    f[i] += a[i];
-                    f[8 + i] += b[i];
-                  }
-                }
-                float lo[8], hi[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  lo[i] = f[i];
-                  hi[i] = f[8 + i];
-                }
-                *reinterpret_cast<uint4*>(out + base) = pack8(lo);
-                *reinterpret_cast<uint4*>(out + base + 8) = pack8(hi);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                  if (gn0 + i < N) {
-                    float v = __uint_as_float(r[i]);
-                    if (mode & EPI_RESIDUAL) v += bf2f(residual[base + i]);
-                    out[base + i] = f2bf(v);
-                  }
-              }
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
-      } else {
-        // Split-K: write this split's fp32 slice of the output, in the output's
-        // own layout ([split][rows][ldo]); the consuming kernel sums the slices.
-        float* part = ws + static_cast<size_t>(sp) * split_stride;
-        if (gm < M) {
-#pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            uint32_t r[16];
-            tmem_ld16(t_row + c0, r);
-            tmem_ld_wait();
-            const int gn0 = n_blk * BN + c0;
+          if (gm >= M) continue;
+          if (part) {
+            // Split-K: fp32 slice in the output's layout.
             if (mode & EPI_TRANSPOSE) {
 #pragma unroll
               for (int i = 0; i < 16; ++i)
@@ -293,12 +252,53 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
               for (int i = 0; i < 16; ++i)
                 if (gn0 + i < N) part[static_cast<size_t>(gm) * ldo + gn0 + i] = __uint_as_float(r[i]);
             }
+          } else if (mode & EPI_TRANSPOSE) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int gn = gn0 + i;
+              if (gn < N) {
+                const size_t idx = static_cast<size_t>(gn) * ldo + gm;
+                float v = __uint_as_float(r[i]);
+                if (mode & EPI_RESIDUAL) v += bf2f(residual[idx]);
+                out[idx] = f2bf(v);
+              }
+            }
+          } else {
+            const size_t base = static_cast<size_t>(gm) * ldo + gn0;
+            if (gn0 + 16 <= N) {
+              float lo[8], hi[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                lo[i] = __uint_as_float(r[i]);
+                hi[i] = __uint_as_float(r[8 + i]);
+              }
+              if (mode & EPI_RESIDUAL) {
+                float a[8], b[8];
+                unpack8(*reinterpret_cast<const uint4*>(residual + base), a);
+                unpack8(*reinterpret_cast<const uint4*>(residual + base + 8), b);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  lo[i] += a[i];
+                  hi[i] += b[i];
+                }
+              }
+              *reinterpret_cast<uint4*>(out + base) = pack8(lo);
+              *reinterpret_cast<uint4*>(out + base + 8) = pack8(hi);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (gn0 + i < N) {
+                  float v = __uint_as_float(r[i]);
+                  if (mode & EPI_RESIDUAL) v += bf2f(residual[base + i]);
+                  out[base + i] = f2bf(v);
+                }
+            }
           }
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
 
@@ -310,16 +310,21 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
 
 }  // namespace
 
-#define FB_GEMM_INSTANCE(BN)                                                                                        \
-  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_bf16_bn##BN(                                 \
+#define FB_GEMM_INSTANCE(BN, MT)                                                                                    \
+  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_bf16_bn##BN##_m##MT(                         \
       const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
       const bf16* residual, int M, int N, int K, int ldo, int mode, int splits, float* ws,                          \
       long long split_stride) {                                                                                      \
-    gemm_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);                        \
+    gemm_body<BN, MT>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);                    \
   }
 
-FB_GEMM_INSTANCE(16)
-FB_GEMM_INSTANCE(32)
-FB_GEMM_INSTANCE(64)
-FB_GEMM_INSTANCE(128)
-FB_GEMM_INSTANCE(256)
+FB_GEMM_INSTANCE(16, 1)
+FB_GEMM_INSTANCE(32, 1)
+FB_GEMM_INSTANCE(64, 1)
+FB_GEMM_INSTANCE(128, 1)
+FB_GEMM_INSTANCE(256, 1)
+FB_GEMM_INSTANCE(16, 2)
+FB_GEMM_INSTANCE(32, 2)
+FB_GEMM_INSTANCE(64, 2)
+FB_GEMM_INSTANCE(128, 2)
+FB_GEMM_INSTANCE(256, 2)

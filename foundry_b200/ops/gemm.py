@@ -36,8 +36,8 @@ _HBM_BPS = 6.0e12
 MAX_SPLITS = 8
 
 
-def smem_bytes(bn: int) -> int:
-    stage = BM * BK * 2 + bn * BK * 2
+def smem_bytes(bn: int, mt: int = 1) -> int:
+    stage = mt * BM * BK * 2 + bn * BK * 2
     stages = min(8, (200 * 1024) // stage)
     return stages * stage + 1024 + 256
 
@@ -95,6 +95,11 @@ class Plan:
     grid: int
     swap: bool
     est_us: float = 0.0
+    mt: int = 1  # 128-row A tiles per work unit (2 = two MMAs share each B tile)
+
+    @property
+    def kernel(self) -> str:
+        return f"fb_gemm_bf16_bn{self.bn}_m{self.mt}"
 
 
 def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bool = True) -> Plan:
@@ -112,20 +117,22 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
         cands = [b for b in _BNS if b >= min(ng, 256) / 4 or b == 256]
     else:
         cands = [128, 256]
-    for bn in cands:
-        tn = math.ceil(ng / bn)
-        for s in range(1, (MAX_SPLITS if allow_split else 1) + 1):
-            if s > 1 and kb // s < 4:
-                break
-            units = tm * tn * s
-            waves = math.ceil(units / sms)
-            kbp = math.ceil(kb / s)
-            t_kb = max((BM * BK * 2 + bn * BK * 2) / _CTA_FILL_BPS, 2 * BM * bn * BK / _SM_MMA_FLOPS)
-            t = max(waves * (kbp * t_kb + 1.5e-6), dram)
-            if s > 1:
-                t += 2 * s * mg * ng * 4 / _HBM_BPS
-            if best is None or t < best.est_us * 1e-6 * 0.97:
-                best = Plan(bn=bn, splits=s, grid=min(units, sms), swap=swap, est_us=t * 1e6)
+    for mt in (1, 2):
+        tmm = math.ceil(mg / (BM * mt))
+        for bn in cands:
+            tn = math.ceil(ng / bn)
+            for s in range(1, (MAX_SPLITS if allow_split else 1) + 1):
+                if s > 1 and kb // s < 4:
+                    break
+                units = tmm * tn * s
+                waves = math.ceil(units / sms)
+                kbp = math.ceil(kb / s)
+                t_kb = max((mt * BM * BK * 2 + bn * BK * 2) / _CTA_FILL_BPS, mt * 2 * BM * bn * BK / _SM_MMA_FLOPS)
+                t = max(waves * (kbp * t_kb + 1.5e-6 * mt), dram)
+                if s > 1:
+                    t += 2 * s * mg * ng * 4 / _HBM_BPS
+                if best is None or t < best.est_us * 1e-6 * 0.97:
+                    best = Plan(bn=bn, splits=s, grid=min(units, sms), swap=swap, est_us=t * 1e6, mt=mt)
     return best
 
 
@@ -158,7 +165,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
             raise RuntimeError(f"split-K slice buffer too small: need {need} floats, have {partials.numel}")
         args = [tmap(a, BM), tmap(b, p.bn), 0, 0, mg, ng, k, n_out, mode, p.splits,
                 partials.buf.data_ptr(), t_tok * n_out]
-        _rt.launch("gemm_bf16", f"fb_gemm_bf16_bn{p.bn}", (p.grid,), (192,), args, smem=smem_bytes(p.bn))
+        _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))
         return Partial(partials.buf, p.splits, t_tok, n_out)
     if out is None:
         out = torch.empty(t_tok, n_out, dtype=torch.bfloat16, device=x.device)
@@ -168,5 +175,5 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         mode |= EPI_RESIDUAL
     args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
             mg, ng, k, out.stride(0), mode, 1, 0, 0]
-    _rt.launch("gemm_bf16", f"fb_gemm_bf16_bn{p.bn}", (p.grid,), (192,), args, smem=smem_bytes(p.bn))
+    _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))
     return out
