@@ -118,6 +118,16 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, const void* tmap, ui
       : "memory");
 }
 
+// L2 prefetch of one 2-D tile (no shared-memory destination, no completion
+// tracking): warms L2 far ahead of the shared-memory ring so the ring's own
+// loads see L2 latency instead of DRAM latency.
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -44,6 +44,7 @@ constexpr int EPI_TRANSPOSE = 1;
 constexpr int EPI_RESIDUAL = 2;
 constexpr int EPI_A_STREAM = 4;  // L2 evict-first hint on A loads
 constexpr int EPI_B_STREAM = 8;  // L2 evict-first hint on B loads
+// mode bits 8..15: how many k-blocks ahead of the ring A tiles are prefetched into L2
 constexpr int NUM_THREADS = 192;
 
 constexpr uint32_t tmem_cols_for(int cols) {
@@ -119,11 +120,20 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       int stage = 0;
       uint32_t phase = 0;
       const uint64_t pol = policy_evict_first();
+      const int pf_dist = (mode >> 8) & 0xFF;  // k-blocks of L2 prefetch lead (0 = off)
       for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
         const int mn = u / splits, sp = u % splits;
         const int m_blk = mn % num_m, n_blk = mn / num_m;
         const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
+        // Streamed A tiles: keep the L2 pf_dist k-blocks ahead of the ring.
+        for (int kb = kb0; kb < min(kb1, kb0 + pf_dist); ++kb)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) tma_prefetch_2d(tmA, kb * BK, (m_blk * MT + mt) * BM);
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (pf_dist && kb + pf_dist < kb1) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, (m_blk * MT + mt) * BM);
+          }
           if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
             *(volatile int*)abort_flag = 1;
             break;

@@ -96,6 +96,7 @@ class Plan:
     swap: bool
     est_us: float = 0.0
     mt: int = 1  # 128-row A tiles per work unit (2 = two MMAs share each B tile)
+    pf: int = 0  # k-blocks of L2 prefetch lead for streamed A tiles (0 = off)
 
     @property
     def kernel(self) -> str:
@@ -158,6 +159,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
             mode |= EPI_A_STREAM  # each weight byte is read once: evict-first
     else:
         a, b, mg, ng = x, w, t_tok, n_out
+    mode |= (min(p.pf, 255) & 0xFF) << 8
     if p.splits > 1:
         assert partials is not None
         need = p.splits * t_tok * n_out
