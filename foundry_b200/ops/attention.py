@@ -19,13 +19,37 @@ def decode_smem(group: int) -> int:
 
 
 def decode_splits(batch: int, n_kv: int, max_pages: int, sms: int | None = None) -> tuple[int, int]:
-    """(num_splits, pages_per_split) so that batch * n_kv * splits fills the GPU."""
+    """(num_splits, pages_per_split) so that batch * n_kv * splits work items
+    fill the GPU. pages_per_split is even: the tensor-core kernel works in
+    128-token (two-page) chunks."""
     sms = sms or _rt.sm_count()
-    want = max(1, math.ceil(2 * sms * 3 / max(1, batch * n_kv)))
-    splits = max(1, min(want, max_pages))
-    pps = math.ceil(max_pages / splits)
-    splits = math.ceil(max_pages / pps)
-    return splits, pps
+    max_chunks = math.ceil(max_pages / 2)
+    want = max(1, math.ceil(2 * sms / max(1, batch * n_kv)))
+    splits = max(1, min(want, max_chunks))
+    cps = math.ceil(max_chunks / splits)
+    splits = math.ceil(max_chunks / cps)
+    return splits, 2 * cps
+
+
+_tmaps: dict[tuple, bytes] = {}
+
+
+def _cache_tmap(cache: torch.Tensor) -> bytes:
+    """TMA map of a paged cache [blocks, Hkv, 64, 128] viewed as [rows, 128]: 64x64 boxes, 128B swizzle."""
+    key = (cache.data_ptr(), cache.shape)
+    m = _tmaps.get(key)
+    if m is None:
+        from .._native import core
+
+        rows = cache.shape[0] * cache.shape[1] * cache.shape[2]
+        m = core().make_tmap_2d(cache.data_ptr(), 9, 128, rows, 256, 64, 64, 3)
+        if len(_tmaps) > 4096:
+            _tmaps.clear()
+        _tmaps[key] = m
+    return m
+
+
+TC_SMEM = 208 * 1024
 
 
 class DecodeWorkspace:
@@ -40,10 +64,14 @@ class DecodeWorkspace:
 
 def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                      seq_lens: torch.Tensor, out: torch.Tensor, max_pages: int, ws: DecodeWorkspace,
-                     scale: float | None = None, splits: tuple[int, int] | None = None) -> torch.Tensor:
+                     scale: float | None = None, splits: tuple[int, int] | None = None,
+                     impl: str = "tc") -> torch.Tensor:
     """q: [B, Hq, 128]; caches [blocks, Hkv, 64, 128]; block_tables [B, max_blocks] int32;
-    seq_lens [B] int32 (tokens in cache incl. the current one). Grid covers
-    ``max_pages`` pages per sequence so the launch shape is static."""
+    seq_lens [B] int32 (tokens in cache incl. the current one). The launch
+    covers ``max_pages`` pages per sequence so its shape is static.
+
+    ``impl="tc"``: tcgen05 kernel (csrc/kernels/attention_tc.cu, persistent
+    grid); ``impl="simt"``: CUDA-core flash-decoding kernel (attention.cu)."""
     b, n_q, d = q.shape
     assert d == 128 and k_cache.shape[2] == PAGE
     n_kv = k_cache.shape[1]
@@ -54,11 +82,21 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     s, pps = splits or decode_splits(b, n_kv, max_pages)
     if s > 1 and b * n_q * s > ws.capacity:
         raise RuntimeError("decode attention workspace too small")
-    _rt.launch(_IMG, f"fb_decode_attn_g{g}", (s, n_kv, b), (128,), [
-        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr(), block_tables.shape[1],
-        seq_lens.data_ptr(), out.data_ptr(), ws.o_part.data_ptr(), ws.ml_part.data_ptr(), n_kv, pps,
-        float(scale * LOG2E),
-    ], smem=decode_smem(g))
+    if impl == "tc":
+        if pps % 2:
+            raise ValueError("pages_per_split must be even for the tensor-core kernel")
+        items = b * n_kv * s
+        _rt.launch("attention_tc", f"fb_decode_attn_tc_g{g}", (min(items, _rt.sm_count()),), (192,), [
+            _cache_tmap(k_cache), _cache_tmap(v_cache), q.data_ptr(), block_tables.data_ptr(),
+            block_tables.shape[1], seq_lens.data_ptr(), out.data_ptr(), ws.o_part.data_ptr(), ws.ml_part.data_ptr(),
+            b, n_kv, s, pps // 2, float(scale * LOG2E),
+        ], smem=TC_SMEM)
+    else:
+        _rt.launch(_IMG, f"fb_decode_attn_g{g}", (s, n_kv, b), (128,), [
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr(), block_tables.shape[1],
+            seq_lens.data_ptr(), out.data_ptr(), ws.o_part.data_ptr(), ws.ml_part.data_ptr(), n_kv, pps,
+            float(scale * LOG2E),
+        ], smem=decode_smem(g))
     if s > 1:
         _rt.launch(_IMG, "fb_decode_attn_combine", (b, n_q), (128,), [
             ws.o_part.data_ptr(), ws.ml_part.data_ptr(), out.data_ptr(), n_q, s,

@@ -201,11 +201,12 @@ def _ref_decode(q, kc, vc, tables, lens, page=64):
     return out
 
 
+@pytest.mark.parametrize("impl", ["tc", "simt"])
 @pytest.mark.parametrize("b,nq,nkv,lens", [
     (3, 32, 8, [1, 64, 130]), (5, 64, 8, [640, 17, 333, 64, 65]), (2, 32, 4, [700, 2]),
-    (64, 32, 8, None),
+    (64, 32, 8, None), (300, 32, 8, None),
 ])
-def test_decode_attention(b, nq, nkv, lens):
+def test_decode_attention(b, nq, nkv, lens, impl):
     from foundry_b200 import ops
 
     page, d = 64, 128
@@ -222,8 +223,9 @@ def test_decode_attention(b, nq, nkv, lens):
     ws = ops.DecodeWorkspace(b, nq, 16)
     out = torch.empty(b, nq, d, dtype=torch.bfloat16, device="cuda")
     ref = _ref_decode(q, kc, vc, tables, lens_t)
-    for splits in (None, (1, max_pages), (4, 3)):
-        ops.decode_attention(q, kc, vc, tables, lens_t, out, max_pages, ws, splits=splits)
+    for splits in (None, (1, max_pages), (3, 4) if impl == "tc" else (4, 3)):
+        out.zero_()
+        ops.decode_attention(q, kc, vc, tables, lens_t, out, max_pages, ws, splits=splits, impl=impl)
         torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 
