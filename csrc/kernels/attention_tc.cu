@@ -32,13 +32,13 @@ constexpr int D = 128;
 constexpr int PAGE = 64;
 constexpr int CHUNK = 128;       // tokens per MMA chunk (two pages)
 constexpr int NH = 16;           // padded head count (MMA N)
-constexpr int STAGES = 3;
 constexpr int BOX_BYTES = 64 * 128;              // 64 tokens x 64 dims x 2 B
 constexpr int KV_BYTES = 2 * 2 * BOX_BYTES;      // one chunk of K (or V): 2 pages x 2 dim-halves
 constexpr int STAGE_BYTES = 2 * KV_BYTES;        // K + V
 constexpr int HALF_STRIDE = 2 * BOX_BYTES;       // dim-half block: 128 tokens x 128 B
 constexpr int QP_BYTES = 2 * NH * 128;           // [2 halves][16 rows][128 B]
 
+template <int STAGES>
 struct Smem {
   uint8_t kv[STAGES][STAGE_BYTES];  // per stage: K [half][128 tok][128B], V same
   uint8_t q[QP_BYTES];
@@ -50,7 +50,8 @@ struct Smem {
   uint32_t tmem;
   int abort;
 };
-static_assert(sizeof(Smem) + 1024 <= 212992, "host requests 208 KB of dynamic shared memory");
+static_assert(sizeof(Smem<3>) + 1024 <= 212992, "host requests 208 KB of dynamic shared memory (3 stages)");
+static_assert(sizeof(Smem<1>) + 1024 <= 75776, "host requests 74 KB of dynamic shared memory (1 stage, 3 CTAs/SM)");
 
 // K-major, 128B-swizzled descriptor with a given stride-byte-offset.
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) { return sdesc_sw128(saddr); }
@@ -100,14 +101,14 @@ __device__ __forceinline__ Item decode_item(int idx, int Hkv, int S, int chunks_
   return it;
 }
 
-template <int G>
+template <int G, int STAGES>
 __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensorMap* tmV, const bf16* __restrict__ q,
                                           const int* __restrict__ block_tables, int max_blocks,
                                           const int* __restrict__ seq_lens, bf16* __restrict__ out,
                                           float* __restrict__ o_part, float* __restrict__ ml_part, int B, int Hkv,
                                           int S, int chunks_per_split, float scale_log2) {
   extern __shared__ uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Smem<STAGES>& sm = *reinterpret_cast<Smem<STAGES>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_items = B * Hkv * S;
   const int Hq = Hkv * G;
@@ -293,6 +294,17 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
         if (lane == 0) mbar_arrive(&sm.s_empty);
         const int tok = c * CHUNK + r;
         const bool valid = tok >= it.tok0 && tok < it.tok1;
+        if (!valid) {
+          // The PV MMA reads all 128 token rows of V: rows past the sequence
+          // hold stale or never-written cache memory, and 0 * NaN = NaN, so
+          // masked rows are zeroed here (the TMA data landed before QK ran).
+          uint8_t* vrow = sm.kv[cc % STAGES] + KV_BYTES + r * 128;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              reinterpret_cast<uint4*>(vrow + h * HALF_STRIDE)[i] = make_uint4(0, 0, 0, 0);
+        }
         float s[G], cmax[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -373,14 +385,17 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
 
 }  // namespace
 
-#define FB_ATTN_TC_INSTANCE(G)                                                                                   \
-  extern "C" __global__ void __launch_bounds__(192, 1) fb_decode_attn_tc_g##G(                                   \
+#define FB_ATTN_TC_INSTANCE(G, ST, CTAS)                                                                         \
+  extern "C" __global__ void __launch_bounds__(192, CTAS) fb_decode_attn_tc_g##G##_s##ST(                        \
       const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const bf16* q,           \
       const int* block_tables, int max_blocks, const int* seq_lens, bf16* out, float* o_part, float* ml_part,    \
       int B, int Hkv, int S, int chunks_per_split, float scale_log2) {                                            \
-    attn_body<G>(&tmK, &tmV, q, block_tables, max_blocks, seq_lens, out, o_part, ml_part, B, Hkv, S,             \
-                 chunks_per_split, scale_log2);                                                                   \
+    attn_body<G, ST>(&tmK, &tmV, q, block_tables, max_blocks, seq_lens, out, o_part, ml_part, B, Hkv, S,         \
+                     chunks_per_split, scale_log2);                                                               \
   }
 
-FB_ATTN_TC_INSTANCE(4)
-FB_ATTN_TC_INSTANCE(8)
+// 3-stage ring, one CTA per SM; or a single stage and three CTAs per SM.
+FB_ATTN_TC_INSTANCE(4, 3, 1)
+FB_ATTN_TC_INSTANCE(8, 3, 1)
+FB_ATTN_TC_INSTANCE(4, 1, 3)
+FB_ATTN_TC_INSTANCE(8, 1, 3)

@@ -49,7 +49,8 @@ def _cache_tmap(cache: torch.Tensor) -> bytes:
     return m
 
 
-TC_SMEM = 208 * 1024
+# Dynamic shared memory of the tensor-core kernel by ring depth (1 stage: three CTAs per SM).
+TC_SMEM = {3: 208 * 1024, 1: 74 * 1024}
 
 
 class DecodeWorkspace:
@@ -82,15 +83,18 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     s, pps = splits or decode_splits(b, n_kv, max_pages)
     if s > 1 and b * n_q * s > ws.capacity:
         raise RuntimeError("decode attention workspace too small")
-    if impl == "tc":
+    if impl in ("tc", "tc1", "tc3"):
         if pps % 2:
             raise ValueError("pages_per_split must be even for the tensor-core kernel")
+        stages = 3 if impl == "tc3" else 1
+        ctas_per_sm = 3 if stages == 1 else 1
         items = b * n_kv * s
-        _rt.launch("attention_tc", f"fb_decode_attn_tc_g{g}", (min(items, _rt.sm_count()),), (192,), [
+        grid = min(items, _rt.sm_count() * ctas_per_sm)
+        _rt.launch("attention_tc", f"fb_decode_attn_tc_g{g}_s{stages}", (grid,), (192,), [
             _cache_tmap(k_cache), _cache_tmap(v_cache), q.data_ptr(), block_tables.data_ptr(),
             block_tables.shape[1], seq_lens.data_ptr(), out.data_ptr(), ws.o_part.data_ptr(), ws.ml_part.data_ptr(),
             b, n_kv, s, pps // 2, float(scale * LOG2E),
-        ], smem=TC_SMEM)
+        ], smem=TC_SMEM[stages])
     else:
         _rt.launch(_IMG, f"fb_decode_attn_g{g}", (s, n_kv, b), (128,), [
             q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr(), block_tables.shape[1],

@@ -167,8 +167,10 @@ class LLMEngine:
         self.weights = LlamaWeights(cfg, self.arena, seed=ecfg.seed, init=init_weights)
         nb =ecfg.num_blocks or ecfg.max_batch * ecfg.pages_per_seq
         self.num_blocks = nb
-        self.k_cache = [self.arena.empty((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
-        self.v_cache = [self.arena.empty((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
+        # Zeroed once: cache slots past a sequence's end are read (and masked) by
+        # the attention kernels, so they must never hold NaN bit patterns.
+        self.k_cache = [self.arena.zeros((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
+        self.v_cache = [self.arena.zeros((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
         self.cos_sin = self.arena.empty((ecfg.max_seq_len, cfg.head_dim // 2, 2), torch.float32)
         self.cos_sin.copy_(ops.rope_cos_sin(ecfg.max_seq_len, cfg.rope_theta, cfg.head_dim,
                                             scaling=cfg.rope_scaling))

@@ -201,7 +201,7 @@ def _ref_decode(q, kc, vc, tables, lens, page=64):
     return out
 
 
-@pytest.mark.parametrize("impl", ["tc", "simt"])
+@pytest.mark.parametrize("impl", ["tc1", "tc3", "simt"])
 @pytest.mark.parametrize("b,nq,nkv,lens", [
     (3, 32, 8, [1, 64, 130]), (5, 64, 8, [640, 17, 333, 64, 65]), (2, 32, 4, [700, 2]),
     (64, 32, 8, None), (300, 32, 8, None),
@@ -227,6 +227,32 @@ def test_decode_attention(b, nq, nkv, lens, impl):
         out.zero_()
         ops.decode_attention(q, kc, vc, tables, lens_t, out, max_pages, ws, splits=splits, impl=impl)
         torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("impl", ["tc1", "tc3", "simt"])
+def test_decode_attention_ignores_nan_past_end(impl):
+    """Cache slots past a sequence's length may hold anything (here NaN)."""
+    from foundry_b200 import ops
+
+    b, nq, nkv, page, d, max_pages = 4, 32, 8, 64, 128, 6
+    nb = b * max_pages
+    kc = _bf(nb, nkv, page, d, seed=30)
+    vc = _bf(nb, nkv, page, d, seed=31)
+    lens = [1, 70, 129, 300]
+    tables = torch.arange(nb, dtype=torch.int32, device="cuda").view(b, max_pages)
+    for i, n in enumerate(lens):
+        for p in range(max_pages):
+            lo = max(0, n - p * page)
+            if lo < page:
+                kc[tables[i, p], :, lo:] = float("nan")
+                vc[tables[i, p], :, lo:] = float("nan")
+    q = _bf(b, nq, d, seed=32)
+    lens_t = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = torch.empty(b, nq, d, dtype=torch.bfloat16, device="cuda")
+    ops.decode_attention(q, kc, vc, tables, lens_t, out, max_pages, ops.DecodeWorkspace(b, nq, 8), impl=impl)
+    assert torch.isfinite(out.float()).all()
+    ref = _ref_decode(q, kc, vc, tables, lens_t)
+    torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 
 def test_prefill_attention():
