@@ -28,7 +28,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1)
     ap.add_argument("--ops", action="store_true", help="time each op with CUDA events (eager)")
+    ap.add_argument("--attn", default=None, help="decode attention implementation (tc1, tc3, simt)")
     args = ap.parse_args()
+    if args.attn:
+        import foundry_b200.models.llama as lm
+        from foundry_b200 import ops as _ops
+
+        _orig = _ops.decode_attention
+        lm.ops.decode_attention = lambda *a, **k: _orig(*a, impl=args.attn, **k)
 
     from ..models import llama
     from .engine import PAGE, EngineConfig, LLMEngine

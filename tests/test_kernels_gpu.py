@@ -223,7 +223,7 @@ def test_decode_attention(b, nq, nkv, lens, impl):
     ws = ops.DecodeWorkspace(b, nq, 16)
     out = torch.empty(b, nq, d, dtype=torch.bfloat16, device="cuda")
     ref = _ref_decode(q, kc, vc, tables, lens_t)
-    for splits in (None, (1, max_pages), (3, 4) if impl == "tc" else (4, 3)):
+    for splits in (None, (1, max_pages), (3, 4) if impl.startswith("tc") else (4, 3)):
         out.zero_()
         ops.decode_attention(q, kc, vc, tables, lens_t, out, max_pages, ws, splits=splits, impl=impl)
         torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
