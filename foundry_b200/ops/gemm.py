@@ -31,6 +31,8 @@ _BNS = (16, 32, 64, 128, 256)
 # Cost model constants (measured on B200): per-CTA shared-memory fill rate of
 # the TMA pipeline, per-SM bf16 tensor rate, and achievable HBM bandwidth.
 _CTA_FILL_BPS = 90e9
+_CTA_FILL_BPS_MAX = 150e9
+_TMA_LATENCY = 2.0e-6
 _SM_MMA_FLOPS = 14e12
 _HBM_BPS = 6.0e12
 MAX_SPLITS = 8
@@ -118,17 +120,23 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
         cands = [b for b in _BNS if b >= min(ng, 256) / 4 or b == 256]
     else:
         cands = [128, 256]
-    for mt in (1, 2):
+    # Measured: a CTA's TMA ring is latency bound - each stage takes about
+    # (round-trip latency + MMA time) / ring depth - and two A tiles per unit
+    # (mt=2) were never faster on decode shapes, so automatic plans use mt=1.
+    for mt in (1,):
         tmm = math.ceil(mg / (BM * mt))
         for bn in cands:
             tn = math.ceil(ng / bn)
+            stage = mt * BM * BK * 2 + bn * BK * 2
+            stages = min(8, (200 * 1024) // stage)
+            mma = mt * 2 * BM * bn * BK / _SM_MMA_FLOPS
+            t_kb = max((_TMA_LATENCY + mma) / stages, stage / _CTA_FILL_BPS_MAX, mma)
             for s in range(1, (MAX_SPLITS if allow_split else 1) + 1):
                 if s > 1 and kb // s < 4:
                     break
                 units = tmm * tn * s
                 waves = math.ceil(units / sms)
                 kbp = math.ceil(kb / s)
-                t_kb = max((mt * BM * BK * 2 + bn * BK * 2) / _CTA_FILL_BPS, mt * 2 * BM * bn * BK / _SM_MMA_FLOPS)
                 t = max(waves * (kbp * t_kb + 1.5e-6 * mt), dram)
                 if s > 1:
                     t += 2 * s * mg * ng * 4 / _HBM_BPS
