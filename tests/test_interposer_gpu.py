@@ -1,0 +1,39 @@
+"""The LD_PRELOAD interposer on the real driver: region placement of torch
+allocations, stop/resume, preallocation, and a torch graph (cuBLAS GEMMs +
+elementwise kernels from libtorch) saved in one process and restored in
+another, bit-exact."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+HOOK = os.path.join(ROOT, "foundry_b200", "lib", "libfoundry_hook.so")
+
+
+def _run(name, workdir, timeout=300):
+    env = dict(os.environ, LD_PRELOAD=HOOK, PYTHONPATH=ROOT, TORCH_CUBLASLT_UNIFIED_WORKSPACE="1")
+    res = subprocess.run([sys.executable, os.path.join(HERE, "interposer_scenarios.py"), name, workdir], env=env,
+                         capture_output=True, text=True, timeout=timeout)
+    assert res.returncode == 0, f"{name} failed:\n{res.stdout[-3000:]}\n{res.stderr[-5000:]}"
+    return json.loads(res.stdout.strip().splitlines()[-1])
+
+
+def test_region_allocations(tmp_path):
+    assert _run("region", str(tmp_path))["ok"]
+
+
+def test_preallocation(tmp_path):
+    assert _run("prealloc", str(tmp_path))["ok"]
+
+
+def test_torch_graph_save_load(tmp_path):
+    info = _run("graph_save", str(tmp_path))
+    assert info["nodes"] > 2
+    assert _run("graph_load", str(tmp_path))["ok"]
