@@ -147,8 +147,14 @@ void record(Event::Kind k, uint64_t ptr, uint64_t size, uint64_t alignment) {
 CUresult region_alloc_locked(Region& r, uint64_t size, uint64_t* out) {
   if (size == 0) size = 1;
   const uint64_t g = r.granularity;
-  const uint64_t off = align_up(r.cursor, g);
+  uint64_t off = align_up(r.cursor, g);
   const uint64_t asize = align_up(size, g);
+  // An allocation that would straddle the end of the preallocated window
+  // starts after it instead (the window's tail stays unused): it must not
+  // overlap memory that is already mapped.
+  if (r.prealloc_size && off < r.prealloc_off + r.prealloc_size &&
+      off + asize > r.prealloc_off + r.prealloc_size)
+    off = r.prealloc_off + r.prealloc_size;
   if (off + asize > r.size) return CUDA_ERROR_OUT_OF_MEMORY;
   const uint64_t ptr = r.base + off;
   const bool in_prealloc = r.prealloc_size != 0 && off >= r.prealloc_off &&
