@@ -86,12 +86,9 @@ def preallocate_cublas_workspaces() -> None:
     (a @ a).sum().item()
 
 
-def __getattr__(name):  # lazy imports keep `import foundry_b200` light
-    if name in ("CUDAGraph", "graph", "save_graph_manifest", "graph_pool_handle"):
-        from . import graph as _g
-
-        return getattr(_g, name)
-    raise AttributeError(name)
+# Same names as the reference package: `graph` is the capture context manager
+# (the implementation module is foundry_b200.graphs).
+from .graphs import CUDAGraph, graph, graph_pool_handle, save_graph_manifest  # noqa: E402
 
 
 __all__ = [

@@ -64,14 +64,14 @@ def launch(image: str, name: str, grid, block, args, smem: int = 0, stream: int 
 def status(image: str) -> int:
     """The image's device status word (0 = healthy; bits = bounded-wait timeouts)."""
     ptr, _ = core().get_global(image_hash(image), "fb_status")
-    from ..graph import tensor_from_ptr
+    from ..graphs import tensor_from_ptr
 
     return int(tensor_from_ptr(ptr, (1,), (1,), torch.int32).item())
 
 
 def clear_status(image: str) -> None:
     ptr, _ = core().get_global(image_hash(image), "fb_status")
-    from ..graph import tensor_from_ptr
+    from ..graphs import tensor_from_ptr
 
     tensor_from_ptr(ptr, (1,), (1,), torch.int32).zero_()
 

@@ -19,7 +19,7 @@ import torch
 
 from .._native import core
 from ..allocation_region import parse_size
-from ..graph import tensor_from_ptr
+from ..graphs import tensor_from_ptr
 
 _ALIGN = 256
 

@@ -339,7 +339,7 @@ class LLMEngine:
         torch.cuda.synchronize()
 
     def capture_graphs(self, sizes: list[int] | None = None) -> float:
-        from ..graph import CUDAGraph, graph
+        from ..graphs import CUDAGraph, graph
 
         sizes = sizes or self.graph_sizes
         self.warmup()

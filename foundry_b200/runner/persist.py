@@ -22,7 +22,7 @@ import time
 import torch
 
 from .. import core, load_cuda_modules_and_libraries, pack_fatbins_to_folder
-from ..graph import CUDAGraph, save_graph_manifest
+from ..graphs import CUDAGraph, save_graph_manifest
 from ..models.llama import LlamaConfig
 from .engine import EngineConfig, LLMEngine
 

@@ -113,7 +113,7 @@ def scenario_save(workdir: str) -> None:
         analyzed.save(path)
         record["graphs"].append({"path": path, "json": analyzed.to_json(), "key": analyzed.topology_key})
     fb.pack_fatbins_to_folder(archive)
-    from foundry_b200.graph import save_graph_manifest
+    from foundry_b200.graphs import save_graph_manifest
 
     manifest = save_graph_manifest(archive)
     assert len(manifest["topology_groups"]) == N_GROUPS, manifest
