@@ -49,6 +49,7 @@ struct Image {
   std::string loader = "cuLibraryLoadData";  // base function name of the load
   bool own = false;
   bool used = false;
+  bool byname = false;          // foreign kernel found by entry name among loaded images
   std::vector<uint8_t> bytes;   // own images only
   std::string src_file;         // foreign: shared object path
   uint64_t src_offset = 0;      // foreign: image pointer - object load base
@@ -73,6 +74,51 @@ std::unordered_map<CUkernel, FnKey> g_kernel_to_key;
 bool g_skip_processing = false;
 std::string g_pack_on_exit;
 thread_local int t_own_load_depth = 0;
+
+// Every foreign library/module handle loaded in this process, identified or
+// not: "byname" kernels are looked up among these. Images handed to the driver
+// from heap memory (e.g. fatbins a library decompressed at run time) cannot be
+// tied to a file without reading their bytes, which this project never does;
+// their kernels are persisted by name and found again in the LOAD process,
+// where the same library loads the same images during its own initialisation.
+struct ForeignHandle {
+  CUlibrary lib;
+  CUmodule mod;
+};
+std::vector<ForeignHandle> g_foreign;
+
+uint64_t byname_hash(const std::string& name) {
+  std::string key = "byname:" + name;
+  return fb::crc64(key.data(), key.size());
+}
+
+bool module_is_foreign(CUmodule mod) {
+  const FbDriver* d = fb_driver();
+  for (const auto& f : g_foreign) {
+    if (f.mod == mod) return true;
+    CUmodule m = nullptr;
+    if (f.lib && d->cuLibraryGetModule && d->cuLibraryGetModule(&m, f.lib) == CUDA_SUCCESS && m == mod)
+      return true;
+  }
+  return false;
+}
+
+CUfunction find_foreign_by_name(const char* name) {
+  const FbDriver* d = fb_driver();
+  for (const auto& f : g_foreign) {
+    if (f.lib) {
+      CUkernel k = nullptr;
+      CUfunction fn = nullptr;
+      if (d->cuLibraryGetKernel(&k, f.lib, name) == CUDA_SUCCESS && k &&
+          d->cuKernelGetFunction(&fn, k) == CUDA_SUCCESS)
+        return fn;
+    } else if (f.mod) {
+      CUfunction fn = nullptr;
+      if (d->cuModuleGetFunction(&fn, f.mod, name) == CUDA_SUCCESS && fn) return fn;
+    }
+  }
+  return nullptr;
+}
 
 void enumerate_library(Image& img) {
   const FbDriver* d = fb_driver();
@@ -172,7 +218,9 @@ bool registry_in_own_load() { return t_own_load_depth > 0; }
 
 void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
-  if (g_skip_processing || t_own_load_depth > 0) return;
+  if (t_own_load_depth > 0) return;
+  g_foreign.push_back(ForeignHandle{lib, nullptr});
+  if (g_skip_processing) return;
   Image* img = register_foreign(code, tag);
   if (!img) return;
   img->lib = lib;
@@ -182,7 +230,9 @@ void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag
 
 void registry_on_module_loaded(CUmodule mod, const void* code, const char* tag) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
-  if (g_skip_processing || t_own_load_depth > 0) return;
+  if (t_own_load_depth > 0) return;
+  g_foreign.push_back(ForeignHandle{nullptr, mod});
+  if (g_skip_processing) return;
   Image* img = register_foreign(code, tag);
   if (!img) return;
   img->mod = mod;
@@ -288,6 +338,22 @@ fb_status fb_registry_function(uint64_t hash, const char* name, CUfunction* out_
   }
   Image& img = *it->second;
   const FbDriver* d = fb_driver();
+  if (img.byname) {
+    auto fit = img.functions.find(name);
+    CUfunction f = fit != img.functions.end() ? fit->second : find_foreign_by_name(name);
+    if (!f) {
+      fb_set_error(FB_ERR_NOT_FOUND,
+                   "kernel '%s' (persisted by name) is not exported by any library loaded in this process; "
+                   "initialise the library that owns it (e.g. run one warm-up call) before loading graphs",
+                   name);
+      return FB_ERR_NOT_FOUND;
+    }
+    img.functions[name] = f;
+    g_fn_to_key[f] = FnKey{hash, name};
+    if (out_fn) *out_fn = f;
+    if (out_kernel) *out_kernel = nullptr;
+    return FB_OK;
+  }
   if (img.lib) {
     auto kit = img.kernels.find(name);
     CUkernel k = nullptr;
@@ -352,6 +418,22 @@ fb_status fb_registry_identify(CUfunction fn, uint64_t* out_hash, char* name_buf
         tmp = FnKey{mit->second, name};
         key = &tmp;
         g_fn_to_key[fn] = tmp;
+      } else if (module_is_foreign(mod)) {
+        // Loaded by another library from memory we cannot tie to a file:
+        // persist by entry name (see ForeignHandle).
+        const uint64_t h = byname_hash(name);
+        auto& slot = g_images[h];
+        if (!slot) {
+          slot.reset(new Image());
+          slot->hash = h;
+          slot->byname = true;
+          slot->loader = "byname";
+          slot->names = {name};
+        }
+        slot->functions[name] = fn;
+        tmp = FnKey{h, name};
+        key = &tmp;
+        g_fn_to_key[fn] = tmp;
       }
     }
     if (!key) {
@@ -396,6 +478,12 @@ fb_status fb_registry_pack(const char* folder) {
     const Image& im = *kv.second;
     if (!im.used) continue;
     txt << hex16(im.hash) << "\n" << im.loader;
+    if (im.byname) {
+      txt << ",binary_flags=2\n" << im.names.size() << "\n";
+      for (const auto& n : im.names) txt << n << "\n";
+      txt << "---\n";
+      continue;
+    }
     if (im.own) {
       const uint64_t h = im.hash, n = im.bytes.size();
       img.write(reinterpret_cast<const char*>(&h), 8);
@@ -495,12 +583,18 @@ fb_status fb_registry_load_archive(const char* folder) {
     }
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     auto& slot = g_images[h];
-    if (slot && (slot->lib || slot->mod)) continue;  // already loaded in this process
+    if (slot && (slot->lib || slot->mod || slot->byname)) continue;  // already known in this process
     if (!slot) slot.reset(new Image());
     Image& im = *slot;
     im.hash = h;
     im.loader = loader;
     im.used = true;
+    if (loader == "byname") {
+      // Resolved lazily (fb_registry_function) among the images this process loads.
+      im.byname = true;
+      im.names = names;
+      continue;
+    }
     CUresult rc = CUDA_SUCCESS;
     if (opts.count("source")) {
       im.src_file = opts["source"];
