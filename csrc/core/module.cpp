@@ -205,6 +205,97 @@ int rt_func_attr(uintptr_t fn, int attr) {
   return v;
 }
 
+// ---- raw VMM / multicast (symmetric memory substrate) --------------------------------
+
+CUmemAllocationProp vmm_prop(int device, int handle_types) {
+  CUmemAllocationProp prop;
+  memset(&prop, 0, sizeof(prop));
+  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  prop.location.id = device;
+  prop.requestedHandleTypes = static_cast<CUmemAllocationHandleType>(handle_types);
+  return prop;
+}
+
+uint64_t vmm_granularity(int device) {
+  CUmemAllocationProp prop = vmm_prop(device, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+  size_t g = 0;
+  check_drv(fb_driver()->cuMemGetAllocationGranularity(&g, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED),
+            "cuMemGetAllocationGranularity");
+  return g;
+}
+
+uint64_t vmm_create(uint64_t size, int device, int handle_types) {
+  CUmemAllocationProp prop = vmm_prop(device, handle_types);
+  CUmemGenericAllocationHandle h = 0;
+  check_drv(fb_driver()->cuMemCreate(&h, size, &prop, 0), "cuMemCreate");
+  return h;
+}
+
+int vmm_export_fd(uint64_t handle) {
+  int fd = -1;
+  check_drv(fb_driver()->cuMemExportToShareableHandle(&fd, handle, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0),
+            "cuMemExportToShareableHandle");
+  return fd;
+}
+
+uint64_t vmm_import_fd(int fd) {
+  CUmemGenericAllocationHandle h = 0;
+  check_drv(fb_driver()->cuMemImportFromShareableHandle(&h, reinterpret_cast<void*>(static_cast<intptr_t>(fd)),
+                                                        CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR),
+            "cuMemImportFromShareableHandle");
+  return h;
+}
+
+uint64_t vmm_reserve(uint64_t base, uint64_t size, uint64_t align) {
+  CUdeviceptr p = 0;
+  check_drv(fb_driver()->cuMemAddressReserve(&p, size, align, static_cast<CUdeviceptr>(base), 0),
+            "cuMemAddressReserve");
+  if (base && p != base) {
+    fb_driver()->cuMemAddressFree(p, size);
+    throw std::runtime_error("could not reserve the symmetric span at the requested address (in use?)");
+  }
+  return p;
+}
+
+void vmm_map(uint64_t va, uint64_t size, uint64_t handle, uint64_t offset) {
+  check_drv(fb_driver()->cuMemMap(static_cast<CUdeviceptr>(va), size, offset, handle, 0), "cuMemMap");
+}
+
+void vmm_set_access(uint64_t va, uint64_t size, std::vector<int> devices) {
+  std::vector<CUmemAccessDesc> d(devices.size());
+  for (size_t i = 0; i < devices.size(); ++i) {
+    memset(&d[i], 0, sizeof(d[i]));
+    d[i].location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    d[i].location.id = devices[i];
+    d[i].flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+  }
+  check_drv(fb_driver()->cuMemSetAccess(static_cast<CUdeviceptr>(va), size, d.data(), d.size()), "cuMemSetAccess");
+}
+
+uint64_t mc_granularity(int num_devices, uint64_t size) {
+  CUmulticastObjectProp p;
+  memset(&p, 0, sizeof(p));
+  p.numDevices = num_devices;
+  p.size = size;
+  p.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  size_t g = 0;
+  check_drv(fb_driver()->cuMulticastGetGranularity(&g, &p, CU_MULTICAST_GRANULARITY_RECOMMENDED),
+            "cuMulticastGetGranularity");
+  return g;
+}
+
+uint64_t mc_create(int num_devices, uint64_t size) {
+  CUmulticastObjectProp p;
+  memset(&p, 0, sizeof(p));
+  p.numDevices = num_devices;
+  p.size = size;
+  p.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  CUmemGenericAllocationHandle h = 0;
+  check_drv(fb_driver()->cuMulticastCreate(&h, &p), "cuMulticastCreate");
+  return h;
+}
+
 std::string events_json() {
   size_t n = fb_events_to_json(nullptr, 0);
   std::string s(n + 1, '\0');
@@ -301,6 +392,41 @@ PYBIND11_MODULE(_C, m) {
   m.def("get_global", &rt_get_global);
   m.def("func_attr", &rt_func_attr);
   m.def("func_num_params", [](uintptr_t fn) { return func_info(reinterpret_cast<CUfunction>(fn)).params.size(); });
+
+  // raw VMM + multicast (symmetric memory)
+  m.def("vmm_granularity", &vmm_granularity);
+  m.def("vmm_create", &vmm_create, py::arg("size"), py::arg("device"),
+        py::arg("handle_types") = static_cast<int>(CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR));
+  m.def("vmm_export_fd", &vmm_export_fd);
+  m.def("vmm_import_fd", &vmm_import_fd);
+  m.def("vmm_reserve", &vmm_reserve, py::arg("base"), py::arg("size"), py::arg("align") = 0);
+  m.def("vmm_map", &vmm_map);
+  m.def("vmm_set_access", &vmm_set_access);
+  m.def("vmm_unmap", [](uint64_t va, uint64_t size) {
+    check_drv(fb_driver()->cuMemUnmap(static_cast<CUdeviceptr>(va), size), "cuMemUnmap");
+  });
+  m.def("vmm_release", [](uint64_t h) { check_drv(fb_driver()->cuMemRelease(h), "cuMemRelease"); });
+  m.def("vmm_free_va", [](uint64_t va, uint64_t size) {
+    check_drv(fb_driver()->cuMemAddressFree(static_cast<CUdeviceptr>(va), size), "cuMemAddressFree");
+  });
+  m.def("mc_supported", []() { return fb_driver()->cuMulticastCreate != nullptr && !fb_driver()->is_mock; });
+  m.def("mc_granularity", &mc_granularity);
+  m.def("mc_create", &mc_create);
+  m.def("mc_add_device", [](uint64_t mc, int device) {
+    check_drv(fb_driver()->cuMulticastAddDevice(mc, device), "cuMulticastAddDevice");
+  });
+  m.def("mc_bind_mem", [](uint64_t mc, uint64_t mc_offset, uint64_t mem, uint64_t mem_offset, uint64_t size) {
+    check_drv(fb_driver()->cuMulticastBindMem(mc, mc_offset, mem, mem_offset, size, 0), "cuMulticastBindMem");
+  });
+  m.def("mc_unbind", [](uint64_t mc, int device, uint64_t mc_offset, uint64_t size) {
+    check_drv(fb_driver()->cuMulticastUnbind(mc, device, mc_offset, size), "cuMulticastUnbind");
+  });
+  m.def("device_attribute", [](int attr, int device) {
+    int v = 0;
+    check_drv(fb_driver()->cuDeviceGetAttribute(&v, static_cast<CUdevice_attribute>(attr), device),
+              "cuDeviceGetAttribute");
+    return v;
+  });
 
   // graphs
   py::class_<GraphDesc, std::shared_ptr<GraphDesc>>(m, "GraphDesc")

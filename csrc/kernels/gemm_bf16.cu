@@ -45,6 +45,7 @@ constexpr int EPI_RESIDUAL = 2;
 constexpr int EPI_A_STREAM = 4;  // L2 evict-first hint on A loads
 constexpr int EPI_B_STREAM = 8;  // L2 evict-first hint on B loads
 // mode bits 8..15: how many k-blocks ahead of the ring A tiles are prefetched into L2
+constexpr int EPI_MCAST = 1 << 16;  // `out` is an NVLS multicast address: stores reach every rank
 constexpr int NUM_THREADS = 192;
 
 constexpr uint32_t tmem_cols_for(int cols) {
@@ -244,7 +245,47 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
           tmem_ld16(t_row + c0, r);
           tmem_ld_wait();
           const int gn0 = n_blk * BN + c0;
+          if ((mode & EPI_MCAST) && (mode & EPI_TRANSPOSE)) {
+            // Multicast store of bf16 pairs: lanes hold consecutive output
+            // features; even lanes store (own, neighbour) as one bf16x2.
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float mine = __uint_as_float(r[i]);
+              const float nb = __shfl_xor_sync(0xffffffffu, mine, 1);
+              const int gn = gn0 + i;
+              if (!(lane & 1) && gm < M && gn < N) {
+                const bf162 pr = __floats2bfloat162_rn(mine, nb);
+                const uint64_t dst = reinterpret_cast<uint64_t>(out) + (static_cast<uint64_t>(gn) * ldo + gm) * 2;
+                asm volatile("multimem.st.relaxed.sys.global.bf16x2 [%0], %1;" ::"l"(dst),
+                             "r"(*reinterpret_cast<const uint32_t*>(&pr))
+                             : "memory");
+              }
+            }
+            continue;
+          }
           if (gm >= M) continue;
+          if (mode & EPI_MCAST) {
+            // Row-major multicast store: 16 consecutive columns = 2 x 16 B.
+            if (gn0 + 16 <= N) {
+              float f[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(r[i]);
+              uint32_t u[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const bf162 pr = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+                u[i] = *reinterpret_cast<const uint32_t*>(&pr);
+              }
+              const uint64_t dst = reinterpret_cast<uint64_t>(out) + (static_cast<uint64_t>(gm) * ldo + gn0) * 2;
+              asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(dst), "r"(u[0]),
+                           "r"(u[1]), "r"(u[2]), "r"(u[3])
+                           : "memory");
+              asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(dst + 16),
+                           "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
+                           : "memory");
+            }
+            continue;
+          }
           if (part) {
             // Split-K: fp32 slice in the output's layout.
             if (mode & EPI_TRANSPOSE) {

@@ -25,6 +25,7 @@ from . import _rt
 
 BM, BK = 128, 64
 EPI_TRANSPOSE, EPI_RESIDUAL, EPI_A_STREAM, EPI_B_STREAM = 1, 2, 4, 8
+EPI_MCAST = 1 << 16
 _BF16 = 9  # CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
 _SWIZZLE_128B = 3
 _BNS = (16, 32, 64, 128, 256)
@@ -143,6 +144,22 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
                 if best is None or t < best.est_us * 1e-6 * 0.97:
                     best = Plan(bn=bn, splits=s, grid=min(units, sms), swap=swap, est_us=t * 1e6, mt=mt)
     return best
+
+
+def linear_multicast(x: torch.Tensor, w: torch.Tensor, target: int, plan_override: Plan | None = None) -> None:
+    """x @ w.T written by the GEMM epilogue straight to ``target``, an NVLS
+    multicast address: every tile lands in the same slot of every rank's
+    buffer as soon as it is computed (the GEMM half of a fused all-reduce)."""
+    t_tok, k = x.shape
+    n_out = w.shape[0]
+    p = plan_override or plan(t_tok, n_out, k, allow_split=False)
+    assert p.splits == 1
+    if p.swap:
+        a, b, mg, ng, mode = w, x, n_out, t_tok, EPI_TRANSPOSE | EPI_MCAST
+    else:
+        a, b, mg, ng, mode = x, w, t_tok, n_out, EPI_MCAST
+    args = [tmap(a, BM), tmap(b, p.bn), target, 0, mg, ng, k, n_out, mode, 1, 0, 0]
+    _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,

@@ -1,0 +1,116 @@
+"""Collective ops on symmetric memory (csrc/kernels/comm.cu) and the slot
+exchange used by the fused GEMM -> all-reduce of tensor-parallel layers.
+
+Fused all-reduce of a row-parallel GEMM (TP):
+    1. the GEMM epilogue multicasts each output tile into this rank's slot of
+       every rank's slot buffer (``SlotExchange.gemm_target``: an NVLS
+       multicast address, so the tile crosses NVLink once, as it is produced);
+    2. ``barrier``: every rank's slot is complete everywhere;
+    3. the consumer sums the world slots in rank order (deterministic) with the
+       residual and applies RMSNorm (``add_rmsnorm_slots``).
+Two slot buffers alternate so a fast rank never overwrites slots a slower
+rank is still reading (the barrier between uses orders them).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..ops import _rt
+from .symm import CTRL_BYTES, SymmetricMemory
+
+_IMG = "comm"
+
+
+def barrier(symm: SymmetricMemory) -> None:
+    _rt.launch(_IMG, "fb_sym_barrier", (1,), (64,), [symm.base, symm.stride, symm.rank, symm.world])
+
+
+def all_reduce(symm: SymmetricMemory, offset: int, n: int, out: torch.Tensor, algo: str = "oneshot") -> torch.Tensor:
+    """Sum over ranks of the n bf16 values at ``offset`` of every rank's buffer
+    into ``out`` (local). Includes the barrier that makes the inputs visible;
+    the caller must not rewrite its input before the next barrier."""
+    assert out.dtype == torch.bfloat16 and out.numel() >= n and n % 8 == 0
+    barrier(symm)
+    if algo == "nvls" and symm.multicast:
+        # reduce a shard each, multicast it to every rank's out slot, barrier
+        out_off = offset + n * 2
+        _rt.launch(_IMG, "fb_allreduce_nvls_bf16", (min(132, math.ceil(n / 8 / 256)),), (256,),
+                   [symm.mc_ptr + offset, symm.mc_ptr + out_off, n, symm.rank, symm.world])
+        barrier(symm)
+        out.view(-1)[:n].copy_(symm.tensor(symm.rank, (n,), torch.bfloat16, out_off))
+        return out
+    _rt.launch(_IMG, "fb_allreduce_oneshot_bf16", (min(4 * 148, max(1, math.ceil(n / 8 / 256))),), (256,),
+               [symm.base, symm.stride, offset, out.data_ptr(), n, symm.world])
+    return out
+
+
+class SlotExchange:
+    """Two alternating [world][rows][cols] bf16 slot buffers in symmetric memory."""
+
+    def __init__(self, symm: SymmetricMemory, offset: int, rows: int, cols: int):
+        self.symm = symm
+        self.rows, self.cols = rows, cols
+        self.slot_bytes = rows * cols * 2
+        self.buf_bytes = symm.world * self.slot_bytes
+        self.offset = offset
+        if offset + 2 * self.buf_bytes > symm.size:
+            raise ValueError("symmetric buffer too small for the slot exchange")
+        self.which = 0
+
+    @property
+    def nbytes(self) -> int:
+        return 2 * self.buf_bytes
+
+    def _buf_off(self, which: int) -> int:
+        return self.offset + which * self.buf_bytes
+
+    def gemm_target(self, which: int) -> int:
+        """Multicast address of this rank's slot (GEMM output with EPI_MCAST), or
+        0 when the node has no multicast (then use ``local_slot`` + broadcast)."""
+        s = self.symm
+        if not s.multicast:
+            return 0
+        return s.mc_ptr + self._buf_off(which) + s.rank * self.slot_bytes
+
+    def local_slots(self, which: int) -> torch.Tensor:
+        s = self.symm
+        return s.tensor(s.rank, (s.world, self.rows, self.cols), torch.bfloat16, self._buf_off(which))
+
+    def local_slot(self, which: int) -> torch.Tensor:
+        return self.local_slots(which)[self.symm.rank]
+
+    def broadcast_local_slot(self, which: int, rows: int) -> None:
+        """No-multicast fallback: copy this rank's slot to every rank over P2P."""
+        s = self.symm
+        nbytes = rows * self.cols * 2
+        _rt.launch(_IMG, "fb_sym_broadcast", (min(4 * 148, max(1, math.ceil(nbytes / 16 / 256))),), (256,), [
+            self.local_slot(which).data_ptr(), s.base, s.stride, self._buf_off(which) + s.rank * self.slot_bytes,
+            nbytes, s.world])
+
+
+def add_rmsnorm_slots(slots: torch.Tensor, rows: int, h: torch.Tensor, w: torch.Tensor, x: torch.Tensor,
+                      eps: float) -> None:
+    """h[:rows] += sum over ranks of slots[:, :rows]; x = rmsnorm(h) * w."""
+    world, _, cols = slots.shape
+    _rt.launch(_IMG, "fb_add_rmsnorm_slots", (rows,), (256,), [
+        slots.data_ptr(), world, slots.stride(0), h.data_ptr(), w.data_ptr(), x.data_ptr(), rows, cols, float(eps)])
+
+
+def argmax_sharded(symm: SymmetricMemory, logits: torch.Tensor, vocab_offset: int, pairs_offset: int,
+                   out: torch.Tensor) -> None:
+    """Greedy token over a vocab-sharded lm_head: local shard argmax -> (value,
+    index) pairs exchanged -> barrier -> the same global argmax on every rank."""
+    t, v = logits.shape
+    s = symm
+    _rt.launch(_IMG, "fb_argmax_shard", (t,), (512,), [
+        logits.data_ptr(), logits.stride(0), t, v, vocab_offset, s.mc_ptr if s.multicast else 0, s.base, s.stride,
+        pairs_offset, s.rank, s.world])
+    barrier(s)
+    pairs = s.tensor(s.rank, (s.world, t, 2), torch.int32, pairs_offset)
+    _rt.launch(_IMG, "fb_argmax_combine", (math.ceil(t / 128),), (128,), [pairs.data_ptr(), t, s.world, out.data_ptr()])
+
+
+__all__ = ["CTRL_BYTES", "SlotExchange", "add_rmsnorm_slots", "all_reduce", "argmax_sharded", "barrier"]
