@@ -29,14 +29,14 @@ from foundry_b200.graphs import tensor_from_ptr
 
 s = SymmetricMemory(256 << 20)
 W, R = s.world, s.rank
-# 1) peer visibility through the flag barrier
+# 1) peer visibility through the flag barrier (peer memory is read by our
+#    kernels over P2P; torch cannot wrap another device's memory)
 n = 4096
 mine = s.tensor(R, (n,), torch.bfloat16, CTRL_BYTES)
 mine.fill_(float(R + 1))
-comm.barrier(s)
-for r in range(W):
-    v = s.tensor(r, (n,), torch.bfloat16, CTRL_BYTES)
-    assert torch.all(v == float(r + 1)), (r, v[:4])
+tot = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+comm.all_reduce(s, CTRL_BYTES, n, tot)
+assert torch.all(tot == float(W * (W + 1) // 2)), tot[:4]
 comm.barrier(s)
 # 2) all-reduce, one-shot (deterministic) and NVLS
 g = torch.Generator(device="cuda").manual_seed(100 + R)
