@@ -21,7 +21,7 @@ from .basic import (
     rope_kv_write,
     silu_mul,
 )
-from .gemm import Partial, PartialBuffer, linear, plan
+from .gemm import Partial, PartialBuffer, linear, linear_multicast, plan
 
 status = _rt.status
 clear_status = _rt.clear_status
