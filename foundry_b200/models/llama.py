@@ -77,30 +77,82 @@ CONFIGS = {"llama-3-8b": llama3_8b, "llama-3-70b": llama3_70b}
 
 
 class LlamaWeights:
-    """All parameters, allocated from an arena and initialised deterministically."""
+    """All parameters (this rank's tensor-parallel shard), allocated from an
+    arena and initialised deterministically.
 
-    def __init__(self, cfg: LlamaConfig, arena, seed: int = 0, init: bool = True):
+    Tensor parallel layout (tp_size > 1): q/k/v and gate/up are split by output
+    rows (heads / intermediate features, column parallel), o and down by input
+    columns (row parallel: their outputs are partial sums), lm_head by vocab
+    rows; the embedding table and the norms are replicated.
+    """
+
+    def __init__(self, cfg: LlamaConfig, arena, seed: int = 0, init: bool = True, tp_rank: int = 0,
+                 tp_size: int = 1):
         self.cfg = cfg
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        for name, v in (("n_q", cfg.n_q), ("n_kv", cfg.n_kv), ("inter", cfg.inter), ("vocab", cfg.vocab)):
+            if v % tp_size:
+                raise ValueError(f"{name}={v} is not divisible by tp={tp_size}")
+        self.nq_l, self.nkv_l = cfg.n_q // tp_size, cfg.n_kv // tp_size
+        self.inter_l, self.vocab_l = cfg.inter // tp_size, cfg.vocab // tp_size
         h, d = cfg.hidden, cfg.head_dim
+        self.qkv_dim_l = (self.nq_l + 2 * self.nkv_l) * d
         self.embed = arena.empty((cfg.vocab, h))
         self.layers = []
         for _ in range(cfg.layers):
             lw = {
                 "attn_norm": arena.empty((h,)),
-                "qkv": arena.empty((cfg.qkv_dim, h)),
-                "o": arena.empty((h, cfg.n_q * d)),
+                "qkv": arena.empty((self.qkv_dim_l, h)),
+                "o": arena.empty((h, self.nq_l * d)),
                 "mlp_norm": arena.empty((h,)),
-                "gate_up": arena.empty((2 * cfg.inter, h)),
-                "down": arena.empty((h, cfg.inter)),
+                "gate_up": arena.empty((2 * self.inter_l, h)),
+                "down": arena.empty((h, self.inter_l)),
             }
             if cfg.qk_norm:
                 lw["q_norm"] = arena.empty((d,))
                 lw["k_norm"] = arena.empty((d,))
             self.layers.append(lw)
         self.final_norm = arena.empty((h,))
-        self.lm_head = self.embed if cfg.tie_embeddings else arena.empty((cfg.vocab, h))
+        if cfg.tie_embeddings and tp_size == 1:
+            self.lm_head = self.embed
+        else:
+            self.lm_head = arena.empty((self.vocab_l, h))
         if init:
             self.init(seed)
+
+    @property
+    def vocab_offset(self) -> int:
+        return self.tp_rank * self.vocab_l
+
+    def shard_of(self, name: str, full: torch.Tensor) -> torch.Tensor:
+        """The rows/columns of a full (unsharded) parameter that this rank holds."""
+        cfg, r, d = self.cfg, self.tp_rank, self.cfg.head_dim
+        key = name.split(".")[-1]
+        if self.tp_size == 1 or key in ("attn_norm", "mlp_norm", "q_norm", "k_norm") or name in ("embed", "final_norm"):
+            return full
+        if key == "qkv":
+            q = full[r * self.nq_l * d:(r + 1) * self.nq_l * d]
+            k0 = cfg.n_q * d
+            k = full[k0 + r * self.nkv_l * d:k0 + (r + 1) * self.nkv_l * d]
+            v0 = (cfg.n_q + cfg.n_kv) * d
+            v = full[v0 + r * self.nkv_l * d:v0 + (r + 1) * self.nkv_l * d]
+            return torch.cat([q, k, v])
+        if key == "gate_up":
+            g = full[r * self.inter_l:(r + 1) * self.inter_l]
+            u = full[cfg.inter + r * self.inter_l:cfg.inter + (r + 1) * self.inter_l]
+            return torch.cat([g, u])
+        if key == "o":
+            return full[:, r * self.nq_l * d:(r + 1) * self.nq_l * d]
+        if key == "down":
+            return full[:, r * self.inter_l:(r + 1) * self.inter_l]
+        if name == "lm_head":
+            return full[r * self.vocab_l:(r + 1) * self.vocab_l]
+        raise KeyError(name)
+
+    def load_full(self, full: dict[str, torch.Tensor]) -> None:
+        """Copies this rank's shard of each full parameter (e.g. a checkpoint)."""
+        for name, t in self.tensors():
+            t.copy_(self.shard_of(name, full[name]).to(device=t.device, dtype=t.dtype))
 
     def tensors(self):
         yield "embed", self.embed
@@ -108,16 +160,19 @@ class LlamaWeights:
             for k, v in lw.items():
                 yield f"layers.{i}.{k}", v
         yield "final_norm", self.final_norm
-        if not self.cfg.tie_embeddings:
+        if self.lm_head is not self.embed:
             yield "lm_head", self.lm_head
 
     def init(self, seed: int) -> None:
-        """Random init N(0, init_std) for matrices, ones for norm weights."""
+        """Random init N(0, init_std) for matrices, ones for norm weights.
+        Replicated tensors get the same values on every rank, shards differ."""
         for idx, (name, t) in enumerate(self.tensors()):
             if t.dim() == 1:
                 ops.fill_(t, 1.0)
             else:
-                ops.init_normal_(t, seed=(seed * 1_000_003 + idx) & ((1 << 63) - 1), std=self.cfg.init_std)
+                rank_salt = 0 if name == "embed" else self.tp_rank * 7_919
+                s = (seed * 1_000_003 + idx + rank_salt * 104_729) & ((1 << 63) - 1)
+                ops.init_normal_(t, seed=s, std=self.cfg.init_std)
 
 
 class LlamaModel:
@@ -131,7 +186,11 @@ class LlamaModel:
 
     # ---- one decode step for B sequences (graph-capturable) -------------------------------
     def decode(self, st, b: int) -> None:
-        """``st`` is a DecodeState (runner/engine.py) with static buffers; uses rows [:b]."""
+        """``st`` is a DecodeState (runner/engine.py) with static buffers; uses rows [:b].
+
+        With tensor parallelism (``st.tp`` set) the row-parallel o/down GEMMs
+        multicast their tiles into the slot exchange and the next norm sums the
+        ranks' slots (fused all-reduce); the lm_head is vocab-sharded."""
         cfg, w = self.cfg, self.w
         ops.decode_advance(st.seq_lens[:b], st.positions[:b], st.slots[:b], st.block_tables[:b], st.page,
                            st.active[:b])
@@ -139,29 +198,56 @@ class LlamaModel:
         x = st.normed[:b]
         ops.embedding(st.input_ids[:b], w.embed, h)
         splits = st.attn_splits[b]
-        pending = None  # split-K slices of the previous down-projection, not yet added to h
+        pending = None  # output of the previous down-projection not yet added to h
         for li, lw in enumerate(w.layers):
-            self._norm(pending, h, lw["attn_norm"], x)
+            self._norm(st, pending, h, lw["attn_norm"], x, b)
             qkv = ops.linear(x, lw["qkv"], out=st.qkv[:b], partials=st.part)
             ops.rope_kv_write(qkv, st.positions[:b], self.cos_sin, st.q[:b], st.k_cache[li], st.v_cache[li],
-                              st.slots[:b], cfg.n_q, cfg.n_kv, lw.get("q_norm"), lw.get("k_norm"), cfg.eps)
+                              st.slots[:b], w.nq_l, w.nkv_l, lw.get("q_norm"), lw.get("k_norm"), cfg.eps)
             ops.decode_attention(st.q[:b], st.k_cache[li], st.v_cache[li], st.block_tables[:b], st.seq_lens[:b],
-                                 st.attn_out[:b].view(b, cfg.n_q, cfg.head_dim), st.max_pages, st.attn_ws,
+                                 st.attn_out[:b].view(b, w.nq_l, cfg.head_dim), st.max_pages, st.attn_ws,
                                  scale=self.scale, splits=splits)
-            o = ops.linear(st.attn_out[:b], lw["o"], out=h, residual=h, partials=st.part)
-            self._norm(o if isinstance(o, ops.Partial) else None, h, lw["mlp_norm"], x)
+            o = self._row_parallel(st, st.attn_out[:b], lw["o"], h, b, which=0)
+            self._norm(st, o, h, lw["mlp_norm"], x, b)
             gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:b])
             ops.silu_mul(gu, st.act[:b])
-            d = ops.linear(st.act[:b], lw["down"], out=h, residual=h, partials=st.part)
-            pending = d if isinstance(d, ops.Partial) else None
-        self._norm(pending, h, w.final_norm, x)
+            pending = self._row_parallel(st, st.act[:b], lw["down"], h, b, which=1)
+        self._norm(st, pending, h, w.final_norm, x, b)
         ops.linear(x, w.lm_head, out=st.logits[:b])
-        ops.argmax(st.logits[:b], st.next_ids[:b])
+        if st.tp:
+            from ..parallel import comm
 
-    def _norm(self, pending, h, weight, x) -> None:
-        """x = rmsnorm(h), first adding pending split-K slices into h."""
+            comm.argmax_sharded(st.tp.symm, st.logits[:b], w.vocab_offset, st.tp.pairs_offset, st.next_ids[:b])
+        else:
+            ops.argmax(st.logits[:b], st.next_ids[:b])
+
+    def _row_parallel(self, st, inp, weight, h, rows, which):
+        """o / down projection. TP: multicast into the slot exchange + barrier and
+        return ("slots", which); single GPU: residual epilogue (returns None) or
+        split-K slices (returns the Partial)."""
+        if st.tp:
+            from ..parallel import comm
+
+            ex = st.tp.slots
+            target = ex.gemm_target(which)
+            if target:
+                ops.linear_multicast(inp, weight, target)
+            else:
+                ops.linear(inp, weight, out=ex.local_slot(which)[:rows])
+                ex.broadcast_local_slot(which, rows)
+            comm.barrier(st.tp.symm)
+            return ("slots", which)
+        r = ops.linear(inp, weight, out=h, residual=h, partials=getattr(st, "part", None))
+        return r if isinstance(r, ops.Partial) else None
+
+    def _norm(self, st, pending, h, weight, x, rows) -> None:
+        """x = rmsnorm(h), first adding the pending projection output into h."""
         if pending is None:
             ops.rmsnorm(h, weight, x, self.cfg.eps)
+        elif isinstance(pending, tuple):
+            from ..parallel import comm
+
+            comm.add_rmsnorm_slots(st.tp.slots.local_slots(pending[1]), rows, h, weight, x, self.cfg.eps)
         else:
             ops.add_rmsnorm_partials(pending, h, weight, x, self.cfg.eps)
 
@@ -174,30 +260,44 @@ class LlamaModel:
         t = pb.num_tokens
         h, x = pb.hidden[:t], pb.normed[:t]
         ops.embedding(pb.input_ids[:t], w.embed, h)
-        nqd = cfg.n_q * cfg.head_dim
-        nkvd = cfg.n_kv * cfg.head_dim
+        nqd = w.nq_l * cfg.head_dim
+        nkvd = w.nkv_l * cfg.head_dim
+        pending = None
         for li, lw in enumerate(w.layers):
-            ops.rmsnorm(h, lw["attn_norm"], x, cfg.eps)
+            self._norm(pb, pending, h, lw["attn_norm"], x, t)
             qkv = ops.linear(x, lw["qkv"], out=pb.qkv[:t])
             # Rotated q -> pb.q; rotated k and v -> paged cache and packed pb.k_rot / pb.v_rot.
             ops.rope_kv_write(qkv, pb.positions[:t], self.cos_sin, pb.q[:t], pb.k_cache[li], pb.v_cache[li],
-                              pb.slots[:t], cfg.n_q, cfg.n_kv, lw.get("q_norm"), lw.get("k_norm"), cfg.eps,
+                              pb.slots[:t], w.nq_l, w.nkv_l, lw.get("q_norm"), lw.get("k_norm"), cfg.eps,
                               k_out=pb.k_rot[:t], v_out=pb.v_rot[:t])
             ops.prefill_attention(pb.q[:t].view(t, nqd), pb.k_rot[:t].view(t, nkvd), pb.v_rot[:t].view(t, nkvd),
-                                  pb.attn_out[:t], pb.cu_seqlens, pb.tile_seq, pb.tile_start, cfg.n_q, cfg.n_kv,
+                                  pb.attn_out[:t], pb.cu_seqlens, pb.tile_seq, pb.tile_start, w.nq_l, w.nkv_l,
                                   scale=self.scale)
-            ops.linear(pb.attn_out[:t], lw["o"], out=h, residual=h)
-            ops.rmsnorm(h, lw["mlp_norm"], x, cfg.eps)
+            o = self._row_parallel(pb, pb.attn_out[:t], lw["o"], h, t, which=0)
+            self._norm(pb, o, h, lw["mlp_norm"], x, t)
             gu = ops.linear(x, lw["gate_up"], out=pb.gate_up[:t])
             ops.silu_mul(gu, pb.act[:t])
-            ops.linear(pb.act[:t], lw["down"], out=h, residual=h)
+            pending = self._row_parallel(pb, pb.act[:t], lw["down"], h, t, which=1)
+        if pending is not None:
+            # fold the last down-projection into h (the final norm runs on gathered rows)
+            if isinstance(pending, tuple):
+                from ..parallel import comm
+
+                comm.add_rmsnorm_slots(pb.tp.slots.local_slots(pending[1]), t, h, w.final_norm, x, cfg.eps)
+            else:
+                ops.add_rmsnorm_partials(pending, h, w.final_norm, x, cfg.eps)
         # last token of every prompt -> logits -> greedy token
         n = pb.num_seqs
         last = pb.last_rows[:n]
         torch.index_select(h, 0, last, out=pb.last_hidden[:n])
         ops.rmsnorm(pb.last_hidden[:n], w.final_norm, pb.last_normed[:n], cfg.eps)
         ops.linear(pb.last_normed[:n], w.lm_head, out=pb.logits[:n])
-        ops.argmax(pb.logits[:n], pb.next_ids[:n])
+        if pb.tp:
+            from ..parallel import comm
+
+            comm.argmax_sharded(pb.tp.symm, pb.logits[:n], w.vocab_offset, pb.tp.pairs_offset, pb.next_ids[:n])
+        else:
+            ops.argmax(pb.logits[:n], pb.next_ids[:n])
 
 
 # ---- fp32 reference (tests) --------------------------------------------------------------

@@ -53,6 +53,7 @@ class EngineConfig:
     region_base: int | None = 0x600000000000
     region_size: int | str = "96GB"
     seed: int = 0
+    tp: int = 1                     # tensor-parallel ranks (= torch.distributed world)
     extra: dict = field(default_factory=dict)
 
     @property
@@ -60,12 +61,37 @@ class EngineConfig:
         return math.ceil(self.max_seq_len / PAGE)
 
 
-class DecodeState:
-    """Static device buffers of a decode step for up to max_batch rows."""
+class TPContext:
+    """Exchange buffers of a tensor-parallel engine in symmetric memory:
+    barrier control words, the (value, index) pairs of the sharded argmax and
+    the two alternating slot buffers of the row-parallel GEMMs (o, down)."""
 
-    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache):
+    def __init__(self, rows: int, hidden: int, pair_rows: int, group=None):
+        from ..parallel.comm import SlotExchange
+        from ..parallel.symm import CTRL_BYTES, SymmetricMemory
+        import torch.distributed as dist
+
+        world = dist.get_world_size(group)
+        pairs_bytes = -(-(world * pair_rows * 8) // 4096) * 4096
+        slot_off = CTRL_BYTES + pairs_bytes
+        self.symm = SymmetricMemory(slot_off + 2 * world * rows * hidden * 2, group)
+        self.pairs_offset = CTRL_BYTES
+        self.slots = SlotExchange(self.symm, slot_off, rows, hidden)
+        self.rank, self.world = self.symm.rank, world
+
+    def close(self) -> None:
+        self.symm.close()
+
+
+class DecodeState:
+    """Static device buffers of a decode step for up to max_batch rows
+    (per-rank shapes under tensor parallelism)."""
+
+    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, w: LlamaWeights, tp=None):
         cfg = ecfg.model
         b = ecfg.max_batch
+        self.tp = tp
+        nq, nkv = w.nq_l, w.nkv_l
         self.page = PAGE
         self.max_pages = ecfg.pages_per_seq
         i32 = torch.int32
@@ -78,22 +104,22 @@ class DecodeState:
         self.block_tables = arena.zeros((b, self.max_pages), i32)
         self.hidden = arena.empty((b, cfg.hidden))
         self.normed = arena.empty((b, cfg.hidden))
-        self.qkv = arena.empty((b, cfg.qkv_dim))
-        self.q = arena.empty((b, cfg.n_q, cfg.head_dim))
-        self.attn_out = arena.empty((b, cfg.n_q * cfg.head_dim))
-        self.gate_up = arena.empty((b, 2 * cfg.inter))
-        self.act = arena.empty((b, cfg.inter))
-        self.logits = arena.empty((b, cfg.vocab))
+        self.qkv = arena.empty((b, w.qkv_dim_l))
+        self.q = arena.empty((b, nq, cfg.head_dim))
+        self.attn_out = arena.empty((b, nq * cfg.head_dim))
+        self.gate_up = arena.empty((b, 2 * w.inter_l))
+        self.act = arena.empty((b, w.inter_l))
+        self.logits = arena.empty((b, w.vocab_l))
         self.k_cache, self.v_cache = k_cache, v_cache
         # fp32 split-K slices of the decode GEMMs (consumed by the next op)
-        self.part = PartialBuffer(buf=arena.empty((MAX_SPLITS * b * max(cfg.qkv_dim, cfg.hidden),), torch.float32))
+        self.part = PartialBuffer(buf=arena.empty((MAX_SPLITS * b * max(w.qkv_dim_l, cfg.hidden),), torch.float32))
         sizes = ecfg.graph_sizes or default_graph_sizes(b)
-        self.attn_splits = {s: decode_splits(s, cfg.n_kv, self.max_pages) for s in sizes}
+        self.attn_splits = {s: decode_splits(s, nkv, self.max_pages) for s in sizes}
         for s in range(1, b + 1):
-            self.attn_splits.setdefault(s, decode_splits(s, cfg.n_kv, self.max_pages))
-        cap = max(s * cfg.n_q * sp for s, (sp, _) in self.attn_splits.items())
+            self.attn_splits.setdefault(s, decode_splits(s, nkv, self.max_pages))
+        cap = max(s * nq * sp for s, (sp, _) in self.attn_splits.items())
         self.attn_ws = DecodeWorkspace(
-            b, cfg.n_q, 1, o_part=arena.empty((cap * 128,), torch.float32),
+            b, nq, 1, o_part=arena.empty((cap * 128,), torch.float32),
             ml_part=arena.empty((cap * 2,), torch.float32))
         self.attn_ws.capacity = cap
 
@@ -101,9 +127,11 @@ class DecodeState:
 class PrefillBatch:
     """Static device buffers of one packed prefill chunk."""
 
-    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache):
+    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, w: LlamaWeights, tp=None):
         cfg = ecfg.model
         t, n = ecfg.max_prefill_tokens, ecfg.max_prefill_seqs
+        self.tp = tp
+        nq, nkv = w.nq_l, w.nkv_l
         i32 = torch.int32
         self.max_tokens, self.max_seqs = t, n
         self.input_ids = arena.zeros((t,), i32)
@@ -116,16 +144,16 @@ class PrefillBatch:
         self.last_rows = arena.zeros((n,), torch.int64)
         self.hidden = arena.empty((t, cfg.hidden))
         self.normed = arena.empty((t, cfg.hidden))
-        self.qkv = arena.empty((t, cfg.qkv_dim))
-        self.q = arena.empty((t, cfg.n_q, cfg.head_dim))
-        self.k_rot = arena.empty((t, cfg.n_kv, cfg.head_dim))
-        self.v_rot = arena.empty((t, cfg.n_kv, cfg.head_dim))
-        self.attn_out = arena.empty((t, cfg.n_q * cfg.head_dim))
-        self.gate_up = arena.empty((t, 2 * cfg.inter))
-        self.act = arena.empty((t, cfg.inter))
+        self.qkv = arena.empty((t, w.qkv_dim_l))
+        self.q = arena.empty((t, nq, cfg.head_dim))
+        self.k_rot = arena.empty((t, nkv, cfg.head_dim))
+        self.v_rot = arena.empty((t, nkv, cfg.head_dim))
+        self.attn_out = arena.empty((t, nq * cfg.head_dim))
+        self.gate_up = arena.empty((t, 2 * w.inter_l))
+        self.act = arena.empty((t, w.inter_l))
         self.last_hidden = arena.empty((n, cfg.hidden))
         self.last_normed = arena.empty((n, cfg.hidden))
-        self.logits = arena.empty((n, cfg.vocab))
+        self.logits = arena.empty((n, w.vocab_l))
         self.next_ids = arena.zeros((n,), i32)
         self.k_cache, self.v_cache = k_cache, v_cache
         self.num_tokens = 0
@@ -163,19 +191,32 @@ class LLMEngine:
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.arena = Arena(ecfg.region_base, ecfg.region_size, self.device)
         t0 = time.perf_counter()
+        self.tp = None
+        tp_rank = 0
+        if ecfg.tp > 1:
+            import torch.distributed as dist
+
+            if not dist.is_initialized() or dist.get_world_size() != ecfg.tp:
+                raise RuntimeError(f"tp={ecfg.tp} needs an initialised process group of that size")
+            tp_rank = dist.get_rank()
+            # Symmetric buffers live at fixed addresses outside the arena.
+            self.tp = TPContext(max(ecfg.max_batch, ecfg.max_prefill_tokens), cfg.hidden,
+                                max(ecfg.max_batch, ecfg.max_prefill_seqs))
         # Order matters: it fixes every device address (SAVE == LOAD).
-        self.weights = LlamaWeights(cfg, self.arena, seed=ecfg.seed, init=init_weights)
-        nb =ecfg.num_blocks or ecfg.max_batch * ecfg.pages_per_seq
+        self.weights = LlamaWeights(cfg, self.arena, seed=ecfg.seed, init=init_weights, tp_rank=tp_rank,
+                                    tp_size=ecfg.tp)
+        nb = ecfg.num_blocks or ecfg.max_batch * ecfg.pages_per_seq
         self.num_blocks = nb
+        nkv = self.weights.nkv_l
         # Zeroed once: cache slots past a sequence's end are read (and masked) by
         # the attention kernels, so they must never hold NaN bit patterns.
-        self.k_cache = [self.arena.zeros((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
-        self.v_cache = [self.arena.zeros((nb, cfg.n_kv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
+        self.k_cache = [self.arena.zeros((nb, nkv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
+        self.v_cache = [self.arena.zeros((nb, nkv, PAGE, cfg.head_dim)) for _ in range(cfg.layers)]
         self.cos_sin = self.arena.empty((ecfg.max_seq_len, cfg.head_dim // 2, 2), torch.float32)
         self.cos_sin.copy_(ops.rope_cos_sin(ecfg.max_seq_len, cfg.rope_theta, cfg.head_dim,
                                             scaling=cfg.rope_scaling))
-        self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache)
-        self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache)
+        self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp)
+        self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp)
         self.model = LlamaModel(cfg, self.weights, self.cos_sin)
         self.graph_sizes = sorted(ecfg.graph_sizes or default_graph_sizes(ecfg.max_batch))
         self.graphs: dict[int, object] = {}
@@ -352,3 +393,12 @@ class LLMEngine:
             self.graphs[s] = g
         torch.cuda.synchronize()
         return time.perf_counter() - t0
+
+    def close(self) -> None:
+        """Drops the decode graphs and unmaps the tensor-parallel buffers (graphs
+        that reference the symmetric memory go first)."""
+        torch.cuda.synchronize()
+        self.graphs.clear()
+        if self.tp is not None:
+            self.tp.close()
+            self.tp = None

@@ -34,7 +34,7 @@ def engine_config_to_dict(e: EngineConfig) -> dict:
         "model": e.model.to_dict(), "max_batch": e.max_batch, "max_seq_len": e.max_seq_len,
         "num_blocks": e.num_blocks, "max_prefill_tokens": e.max_prefill_tokens,
         "max_prefill_seqs": e.max_prefill_seqs, "graph_sizes": e.graph_sizes, "region_base": e.region_base,
-        "region_size": e.region_size, "seed": e.seed,
+        "region_size": e.region_size, "seed": e.seed, "tp": e.tp,
     }
 
 
@@ -51,11 +51,27 @@ def _layout_fingerprint(eng: LLMEngine) -> dict:
         "k_cache0_ptr": eng.k_cache[0].data_ptr(),
         "arena_used": eng.arena.used,
         "final_alloc_offset": core().get_current_alloc_offset(),
+        "symm": eng.tp.symm.layout() if eng.tp is not None else None,
     }
 
 
+def rank_dir(archive: str) -> str:
+    """Per-rank subfolder of a tensor-parallel archive (``rank_<r>``); the
+    archive itself for a single-rank engine."""
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        sub = os.path.join(archive, f"rank_{dist.get_rank()}")
+        if os.path.isdir(sub) or not os.path.exists(os.path.join(archive, STATE_FILE)):
+            return sub
+    return archive
+
+
 def save(eng: LLMEngine, archive: str) -> dict:
-    """Captures (if needed) and writes every decode graph of ``eng``."""
+    """Captures (if needed) and writes every decode graph of ``eng``; a
+    tensor-parallel engine writes its rank's graphs under ``rank_<r>``."""
+    if eng.ecfg.tp > 1:
+        archive = os.path.join(archive, f"rank_{eng.tp.rank}")
     os.makedirs(archive, exist_ok=True)
     t0 = time.perf_counter()
     capture_s = 0.0
@@ -85,6 +101,7 @@ def save(eng: LLMEngine, archive: str) -> dict:
 def load(archive: str, init_weights: bool = True, num_threads: int = 8) -> tuple[LLMEngine, dict]:
     """Rebuilds the engine at the SAVE addresses and restores its decode graphs."""
     t0 = time.perf_counter()
+    archive = rank_dir(archive)
     with open(os.path.join(archive, STATE_FILE)) as f:
         state = json.load(f)
     ecfg = engine_config_from_dict(state["engine"])
@@ -96,6 +113,8 @@ def load(archive: str, init_weights: bool = True, num_threads: int = 8) -> tuple
     for k in ("embed_ptr", "state_ptr", "k_cache0_ptr", "arena_used"):
         if lay[k] != state["layout"][k]:
             raise RuntimeError(f"LOAD layout differs from SAVE at {k}: {lay[k]:#x} vs {state['layout'][k]:#x}")
+    if lay["symm"] != state["layout"].get("symm"):
+        raise RuntimeError(f"symmetric-memory layout differs from SAVE: {lay['symm']} vs {state['layout'].get('symm')}")
     t_arena = time.perf_counter()
     paths = [os.path.join(archive, f"graph_{i}.json") for i in range(len(state["graph_sizes"]))]
     pending = CUDAGraph.start_graph_builds(paths, num_threads=num_threads)
