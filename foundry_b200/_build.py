@@ -157,6 +157,24 @@ def build_kernels(force=False, jobs=None) -> list[Path]:
     return [r[0] for r in res]
 
 
+def build_noalloc(force=False) -> Path:
+    """``lib/libfoundry_noalloc.so``: the decode-attention entry point with a
+    static scratch buffer (runtime API, static cudart, one exported symbol)."""
+    out = LIB / "libfoundry_noalloc.so"
+    src = CSRC / "noalloc" / "decode_attn_noalloc.cu"
+    headers = [CSRC / "kernels" / "attention.cu", *sorted((CSRC / "kernels").glob("*.cuh"))]
+    flags = [f for f in NVCCFLAGS if f != "-Xptxas=-v"] + ["-rdc=true", "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden"]
+    d = _digest([src, *headers], " ".join(flags))
+    if not force and _up_to_date(out, d):
+        return out
+    LIB.mkdir(parents=True, exist_ok=True)
+    tmp = out.with_suffix(".so.tmp")
+    _run([NVCC, *flags, str(src), "-o", str(tmp)])
+    os.replace(tmp, out)
+    _stamp(out, d)
+    return out
+
+
 def build_all(force=False, kernels=True) -> None:
     build_hook(force)
     build_mock(force)
@@ -165,6 +183,7 @@ def build_all(force=False, kernels=True) -> None:
         if shutil.which(NVCC) is None and not Path(NVCC).exists():
             raise RuntimeError(f"nvcc not found at {NVCC}")
         build_kernels(force)
+        build_noalloc(force)
 
 
 if __name__ == "__main__":
