@@ -221,6 +221,24 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return u;
 }
 
+// Counter-based normal samples: element pair `pair` of a stream keyed by
+// `seed` (splitmix64 finalizer, Steele/Lea/Flood 2014, then Box-Muller).
+__device__ __forceinline__ uint64_t rng_mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float2 rng_normal2(uint64_t seed, uint64_t pair) {
+  const uint64_t r = rng_mix64(seed ^ rng_mix64(pair));
+  const float u1 = (static_cast<float>((r >> 40) & 0xFFFFFF) + 1.0f) * (1.0f / 16777216.0f);
+  const float u2 = static_cast<float>((r >> 16) & 0xFFFFFF) * (1.0f / 16777216.0f);
+  const float rad = sqrtf(-2.0f * logf(u1));
+  float sn, cs;
+  sincosf(6.283185307179586f * u2, &sn, &cs);
+  return make_float2(rad * cs, rad * sn);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

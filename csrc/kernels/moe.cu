@@ -1,0 +1,616 @@
+// Mixture-of-experts and block-scaled fp8 kernels (Qwen3-MoE family).
+//
+// Number format (the reference serves DeepSeek/Qwen "fp8 block" checkpoints):
+//   weights      e4m3, one fp32 scale per 128 x 128 block     W = Wq * sw[o/128, k/128]
+//   activations  e4m3, one fp32 scale per token per 128 dims  x = xq * sx[t, k/128]
+//
+// fb_moe_gemm_fp8_bn{32,64}: grouped GEMM over experts on tcgen05
+//   (kind::f8f6f4, M = 128 weight rows, N = BN tokens, K = 32 per MMA).
+//   A 128-wide K block is exactly one scale block, so every k-block's MMAs
+//   write a fresh fp32 partial into TMEM (double-buffered) and the epilogue
+//   warps promote it: acc[t] += partial[t] * sw * sx[t] (two-level
+//   accumulation, fp32 throughout). Work units are (token chunk, 128-row
+//   weight block) with the chunk table built on the device, so the launch
+//   shape is static (CUDA-graph friendly) while expert loads vary per step.
+//   Output is written transposed: out[row_start + t][o] (+ residual).
+//   The same kernel with one "expert" is the dense fp8 linear layer.
+//
+// Routing: fb_moe_topk (softmax over experts, top-k, renormalise; warp per
+//   token) -> fb_moe_plan (one CTA: per-expert counts, deterministic
+//   expert-sorted positions, chunk table) -> fb_moe_dispatch_local (quantise
+//   each token once, scatter its fp8 row to its k expert slots).
+// After the experts: fb_moe_silu_mul_quant (gate/up -> fp8 activations for
+//   the down projection) and fb_moe_combine_add_rmsnorm (top-k weighted sum
+//   + residual + the next RMSNorm, one CTA per token).
+//
+// No TMA multicast; every wait bounded (fb_common.cuh).
+#include <cuda_fp8.h>
+
+#include "fb_common.cuh"
+
+FB_DEFINE_STATUS
+
+using namespace fbk;
+
+namespace {
+
+constexpr int NUM_THREADS = 192;
+constexpr int QBLK = 128;       // scale block (tokens: 1 x 128, weights: 128 x 128)
+constexpr float FP8_MAX = 448.f;
+constexpr int EPI_RESIDUAL = 2;
+constexpr int MAX_KB = 32;      // K <= 4096
+
+constexpr uint32_t tmem_cols_for(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
+// kind::f8f6f4, A/B e4m3 (format 0), D f32, both K-major.
+template <int M, int N>
+__device__ __forceinline__ constexpr uint32_t idesc_e4m3() {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_fp8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::
+          "r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// 4 floats -> 4 e4m3 bytes (saturating, round to nearest even).
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = 128 * QBLK;  // 128 weight rows x 128 K bytes
+  static constexpr int B_BYTES = BN * QBLK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
+  static constexpr int SXS_FLOATS = BN * MAX_KB;  // per epilogue warp
+};
+
+template <int BN>
+__device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmX,
+                                              const float* __restrict__ w_scale, const float* __restrict__ x_scale,
+                                              const int4* __restrict__ chunks, const int* __restrict__ meta,
+                                              bf16* out, const bf16* residual, int O, int K, int ldo, int mode) {
+  using C = GemmCfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  // [4 epilogue warps][BN][KB] token scales of the current unit (one copy per
+  // warp, so the epilogue warps never wait on each other)
+  float* sxs_all = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sxs_all + 4 * C::SXS_FLOATS);
+  uint64_t* empty = full + STAGES;
+  uint64_t* pfull = empty + STAGES;
+  uint64_t* pempty = pfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int KB = K / QBLK;
+  const int num_ob = O / 128;
+  const int num_chunks = meta[0];
+  const int num_units = num_chunks * num_ob;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&pfull[a], 1);
+      mbar_init(&pempty[a], 4);
+    }
+    *abort_flag = (KB > MAX_KB || (K % QBLK) || (O % 128)) ? 1 : 0;
+    if (*abort_flag) set_status(FB_KERR_BAD_ARG);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(tmW);
+    tma_prefetch_desc(tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint64_t pol = policy_evict_first();
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
+        const int c = u % num_chunks, ob = u / num_chunks;
+        const int4 ch = chunks[c];
+        const int wrow = ch.x * O + ob * 128;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+            *(volatile int*)abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d_hint(sA + stage * C::A_BYTES, tmW, &full[stage], kb * QBLK, wrow, pol);
+          tma_load_2d(sB + stage * C::B_BYTES, tmX, &full[stage], kb * QBLK, ch.y);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: one fresh partial per k-block ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3<128, BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t g = 0;  // partials issued by this CTA
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb, ++g) {
+          const uint32_t buf = g & 1;
+          if (!mbar_wait(&pempty[buf], ((g >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_TMEM) ||
+              !mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128(smem_u32(sA + stage * C::A_BYTES));
+          const uint64_t bdesc = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < QBLK / 32; ++k)  // +32 bytes per 32-element K step
+            mma_fp8(tmem_base + buf * BN, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                    k > 0 ? 1u : 0u);
+          mma_commit(&empty[stage]);
+          mma_commit(&pfull[buf]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5): promote + store ----------------
+    const int quarter = warp & 3;
+    float* sxs = sxs_all + quarter * C::SXS_FLOATS;
+    uint32_t g = 0;
+    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
+      const int c = u % num_chunks, ob = u / num_chunks;
+      const int4 ch = chunks[c];
+      for (int i = lane; i < BN * KB; i += 32) {
+        const int t = i / KB, kb = i % KB;
+        sxs[i] = (t < ch.z) ? x_scale[static_cast<size_t>(ch.y + t) * KB + kb] : 0.f;
+      }
+      __syncwarp();
+      const float* wsc = w_scale + (static_cast<size_t>(ch.x) * num_ob + ob) * KB;
+      float acc[BN];
+#pragma unroll
+      for (int t = 0; t < BN; ++t) acc[t] = 0.f;
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb, ++g) {
+        const uint32_t buf = g & 1;
+        if (!mbar_wait(&pfull[buf], (g >> 1) & 1, FB_KERR_TIMEOUT_TMEM)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t r[BN];
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 16) tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&r[c0]));
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pempty[buf]);
+        const float sw = wsc[kb];
+#pragma unroll
+        for (int t = 0; t < BN; ++t) acc[t] = fmaf(__uint_as_float(r[t]), sw * sxs[t * KB + kb], acc[t]);
+      }
+      if (!ok) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      const int o = ob * 128 + quarter * 32 + lane;
+#pragma unroll
+      for (int t = 0; t < BN; ++t) {
+        if (t < ch.z) {
+          const size_t idx = static_cast<size_t>(ch.y + t) * ldo + o;
+          float v = acc[t];
+          if (mode & EPI_RESIDUAL) v += bf2f(residual[idx]);
+          out[idx] = f2bf(v);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace
+
+#define FB_MOE_GEMM_INSTANCE(BN)                                                                                    \
+  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_moe_gemm_fp8_bn##BN(                             \
+      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const float* w_scale,       \
+      const float* x_scale, const int4* chunks, const int* meta, bf16* out, const bf16* residual, int O, int K,     \
+      int ldo, int mode) {                                                                                           \
+    moe_gemm_body<BN>(&tmW, &tmX, w_scale, x_scale, chunks, meta, out, residual, O, K, ldo, mode);                  \
+  }
+
+FB_MOE_GEMM_INSTANCE(32)
+FB_MOE_GEMM_INSTANCE(64)
+
+// ---- routing -----------------------------------------------------------------------------
+// logits [T, E] bf16 (row stride ld); E % 32 == 0, E <= 256; topk <= 8.
+// Softmax over E, top-k (ties -> lower expert index), optional renormalisation
+// of the k probabilities. One warp per token.
+extern "C" __global__ void __launch_bounds__(256) fb_moe_topk(const bf16* __restrict__ logits, int ld, int T, int E,
+                                                             int topk, int renorm, int* __restrict__ ids,
+                                                             float* __restrict__ weights) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int per = E / 32;
+  float v[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = i < per ? bf2f(logits[static_cast<size_t>(t) * ld + i * 32 + lane]) : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
+  mx = warp_max(mx);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = i < per ? expf(v[i] - mx) : -1.f;  // -1: never selected
+    s += i < per ? v[i] : 0.f;
+  }
+  s = warp_sum(s);
+  const float inv = 1.f / s;
+  float sel_sum = 0.f;
+  float my_w = 0.f;
+  int my_id = 0;
+  for (int k = 0; k < topk; ++k) {
+    float best = -1.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = i * 32 + lane;
+      if (v[i] > best || (v[i] == best && e < bi)) {
+        best = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((bi & 31) == lane && (bi >> 5) == i) v[i] = -2.f;  // taken
+    const float p = best * inv;
+    sel_sum += p;
+    if (lane == k) {
+      my_w = p;
+      my_id = bi;
+    }
+  }
+  if (lane < topk) {
+    ids[t * topk + lane] = my_id;
+    weights[t * topk + lane] = renorm ? my_w / sel_sum : my_w;
+  }
+}
+
+// One CTA of 1024 threads. ids [P] (P = T * topk pairs) -> per-expert counts,
+// expert-sorted position of every pair (stable: pair order within an expert),
+// the chunk table {expert, first row, rows, 0} with chunks of <= bn rows, and
+// meta = {num_chunks, P}.
+extern "C" __global__ void __launch_bounds__(1024) fb_moe_plan(const int* __restrict__ ids, int P, int E, int bn,
+                                                              int* __restrict__ pos, int* __restrict__ counts,
+                                                              int4* __restrict__ chunks, int* __restrict__ meta) {
+  __shared__ int cnt[256], off[256], coff[256], run[256];
+  __shared__ int wcnt[32][256];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (E > 256) {
+    if (tid == 0) set_status(FB_KERR_BAD_ARG);
+    return;
+  }
+  for (int e = tid; e < E; e += 1024) {
+    cnt[e] = 0;
+    run[e] = 0;
+  }
+  __syncthreads();
+  for (int p = tid; p < P; p += 1024) atomicAdd(&cnt[ids[p]], 1);
+  __syncthreads();
+  if (tid == 0) {
+    int a = 0, b = 0;
+    for (int e = 0; e < E; ++e) {
+      off[e] = a;
+      coff[e] = b;
+      a += cnt[e];
+      b += (cnt[e] + bn - 1) / bn;
+    }
+    meta[0] = b;
+    meta[1] = P;
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += 1024) {
+    counts[e] = cnt[e];
+    const int n = cnt[e];
+    for (int j = 0, r = 0; r < n; ++j, r += bn) chunks[coff[e] + j] = make_int4(e, off[e] + r, min(bn, n - r), 0);
+  }
+  // Stable positions, 1024 pairs per round.
+  for (int base = 0; base < P; base += 1024) {
+    for (int i = tid; i < 32 * E; i += 1024) wcnt[i / E][i % E] = 0;
+    __syncthreads();
+    const int p = base + tid;
+    const int e = p < P ? ids[p] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(same & ((1u << lane) - 1));
+    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(same);
+    __syncthreads();
+    for (int x = tid; x < E; x += 1024) {
+      int r0 = run[x];
+      for (int w = 0; w < 32; ++w) {
+        const int c = wcnt[w][x];
+        wcnt[w][x] = r0;
+        r0 += c;
+      }
+      run[x] = r0;
+    }
+    __syncthreads();
+    if (e >= 0) pos[p] = off[e] + wcnt[warp][e] + rank;
+    __syncthreads();
+  }
+}
+
+// Quantise token rows to e4m3 with one scale per 128 dims and scatter each
+// row to its k destinations: xq[pos[t * k + j]] (pos == nullptr: row t).
+// One warp per token; H % 128 == 0, H <= 4096.
+extern "C" __global__ void __launch_bounds__(256) fb_moe_dispatch_local(const bf16* __restrict__ x, int ldx, int T,
+                                                                       int H, const int* __restrict__ pos, int topk,
+                                                                       uint8_t* __restrict__ xq,
+                                                                       float* __restrict__ xs) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int nb = H / QBLK;
+  uint32_t q[32];
+  float sc[32];
+#pragma unroll
+  for (int b = 0; b < 32; ++b) {
+    if (b >= nb) break;
+    const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * ldx + b * QBLK + lane * 4);
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.y));
+    const float am = warp_max(fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y))));
+    const float s = fmaxf(am, 1e-12f) / FP8_MAX;
+    const float inv = 1.f / s;
+    q[b] = pack_e4m3x4(f0.x * inv, f0.y * inv, f1.x * inv, f1.y * inv);
+    sc[b] = s;
+  }
+  for (int j = 0; j < (pos ? topk : 1); ++j) {
+    const int row = pos ? pos[t * topk + j] : t;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(xq + static_cast<size_t>(row) * H);
+#pragma unroll
+    for (int b = 0; b < 32; ++b) {
+      if (b >= nb) break;
+      dst[b * 32 + lane] = q[b];
+      if (lane == b) xs[static_cast<size_t>(row) * nb + b] = sc[b];
+    }
+  }
+}
+
+// gu [rows, 2I] bf16 (gate | up) -> act = silu(gate) * up as e4m3 [rows, I]
+// with one scale per 128 features. One warp per row; I % 128 == 0.
+extern "C" __global__ void __launch_bounds__(256) fb_moe_silu_mul_quant(const bf16* __restrict__ gu, int rows, int I,
+                                                                       const int* __restrict__ meta,
+                                                                       uint8_t* __restrict__ aq,
+                                                                       float* __restrict__ as) {
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int n = meta ? min(rows, meta[1]) : rows;
+  if (r >= n) return;
+  const int nb = I / QBLK;
+  const bf16* g = gu + static_cast<size_t>(r) * 2 * I;
+  for (int b = 0; b < nb; ++b) {
+    const uint2 rg = *reinterpret_cast<const uint2*>(g + b * QBLK + lane * 4);
+    const uint2 ru = *reinterpret_cast<const uint2*>(g + I + b * QBLK + lane * 4);
+    const float2 g0 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&rg.x));
+    const float2 g1 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&rg.y));
+    const float2 u0 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&ru.x));
+    const float2 u1 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&ru.y));
+    float a[4] = {g0.x, g0.y, g1.x, g1.y};
+    const float u[4] = {u0.x, u0.y, u1.x, u1.y};
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      a[i] = a[i] / (1.f + __expf(-a[i])) * u[i];
+      am = fmaxf(am, fabsf(a[i]));
+    }
+    am = warp_max(am);
+    const float s = fmaxf(am, 1e-12f) / FP8_MAX;
+    const float inv = 1.f / s;
+    reinterpret_cast<uint32_t*>(aq + static_cast<size_t>(r) * I)[b * 32 + lane] =
+        pack_e4m3x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
+    if (lane == 0) as[static_cast<size_t>(r) * nb + b] = s;
+  }
+}
+
+// h[t] += sum_j w[t, j] * y[pos[t * k + j]]; x[t] = rmsnorm(h[t]) * norm_w.
+// One CTA of 256 threads per token, 8 features per thread; H = 2048 exactly
+// 256 x 8 (any H % 8 == 0, H <= 4096 works with the loop).
+extern "C" __global__ void __launch_bounds__(256) fb_moe_combine_add_rmsnorm(
+    const bf16* __restrict__ y, int ldy, const int* __restrict__ pos, const float* __restrict__ w, int topk,
+    bf16* __restrict__ h, const bf16* __restrict__ norm_w, bf16* __restrict__ x, int T, int H, float eps) {
+  const int t = blockIdx.x;
+  __shared__ float red[8];
+  float acc[2][8] = {};
+  float ss = 0.f;
+#pragma unroll
+  for (int nv = 0; nv < 2; ++nv) {
+    const int c = threadIdx.x * 8 + nv * 2048;
+    if (c >= H) break;
+    float a[8];
+    unpack8(*reinterpret_cast<const uint4*>(h + static_cast<size_t>(t) * H + c), a);
+    for (int j = 0; j < topk; ++j) {
+      const int row = pos[t * topk + j];
+      const float wj = w[t * topk + j];
+      float b[8];
+      unpack8(*reinterpret_cast<const uint4*>(y + static_cast<size_t>(row) * ldy + c), b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = fmaf(wj, b[i], a[i]);
+    }
+    // round through bf16 like every other residual update
+    const uint4 hv = pack8(a);
+    *reinterpret_cast<uint4*>(h + static_cast<size_t>(t) * H + c) = hv;
+    unpack8(hv, acc[nv]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += acc[nv][i] * acc[nv][i];
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float rs = rsqrtf(tot / H + eps);
+#pragma unroll
+  for (int nv = 0; nv < 2; ++nv) {
+    const int c = threadIdx.x * 8 + nv * 2048;
+    if (c >= H) break;
+    float g[8], o[8];
+    unpack8(*reinterpret_cast<const uint4*>(norm_w + c), g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = acc[nv][i] * rs * g[i];
+    *reinterpret_cast<uint4*>(x + static_cast<size_t>(t) * H + c) = pack8(o);
+  }
+}
+
+// Block quantisation of a bf16 matrix [R, C] (R, C multiples of 128) to e4m3
+// with one fp32 scale per 128 x 128 block: scales [R/128, C/128]. One CTA per block.
+extern "C" __global__ void __launch_bounds__(256) fb_quant_block_fp8(const bf16* __restrict__ w, int R, int Cc,
+                                                                    uint8_t* __restrict__ q,
+                                                                    float* __restrict__ scales) {
+  const int bc = blockIdx.x, br = blockIdx.y;
+  __shared__ float red[8];
+  float am = 0.f;
+  // 128 rows x 128 cols: thread -> rows (tid / 16) + 16 i, cols (tid % 16) * 8 .. +8
+  const int r0 = threadIdx.x / 16, c0 = (threadIdx.x % 16) * 8;
+  float v[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const size_t row = static_cast<size_t>(br) * 128 + r0 + 16 * i;
+    unpack8(*reinterpret_cast<const uint4*>(w + row * Cc + bc * 128 + c0), v[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(v[i][j]));
+  }
+  am = warp_max(am);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, red[i]);
+  const float s = fmaxf(m, 1e-12f) / FP8_MAX;
+  const float inv = 1.f / s;
+  if (threadIdx.x == 0) scales[static_cast<size_t>(br) * (Cc / 128) + bc] = s;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const size_t row = static_cast<size_t>(br) * 128 + r0 + 16 * i;
+    uint2 o;
+    o.x = pack_e4m3x4(v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv);
+    o.y = pack_e4m3x4(v[i][4] * inv, v[i][5] * inv, v[i][6] * inv, v[i][7] * inv);
+    *reinterpret_cast<uint2*>(q + row * Cc + bc * 128 + c0) = o;
+  }
+}
+
+// Random block-scaled e4m3 weights without a bf16 staging copy: element
+// (r, c) of the [R, C] matrix is N(0, std) from the counter-based stream
+// (seed, pair ((r + row_offset) * C + c) / 2), then the 128 x 128 block is
+// quantised as in fb_quant_block_fp8. row_offset lets a shard (e.g. this
+// rank's experts) draw the same values as the full matrix. One CTA per block.
+extern "C" __global__ void __launch_bounds__(256) fb_init_fp8_block(uint8_t* __restrict__ q, float* __restrict__ scales,
+                                                                   int R, int Cc, unsigned long long seed, float std,
+                                                                   long long row_offset) {
+  const int bc = blockIdx.x, br = blockIdx.y;
+  __shared__ float red[8];
+  const int r0 = threadIdx.x / 16, c0 = (threadIdx.x % 16) * 8;
+  float v[8][8];
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint64_t row = static_cast<uint64_t>(br) * 128 + r0 + 16 * i + row_offset;
+    const uint64_t e0 = row * static_cast<uint64_t>(Cc) + bc * 128 + c0;  // even
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 z = rng_normal2(seed, e0 / 2 + j);
+      v[i][2 * j] = std * z.x;
+      v[i][2 * j + 1] = std * z.y;
+      am = fmaxf(am, fmaxf(fabsf(v[i][2 * j]), fabsf(v[i][2 * j + 1])));
+    }
+  }
+  am = warp_max(am);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+  __syncthreads();
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, red[i]);
+  const float s = fmaxf(m, 1e-12f) / FP8_MAX;
+  const float inv = 1.f / s;
+  if (threadIdx.x == 0) scales[static_cast<size_t>(br) * (Cc / 128) + bc] = s;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const size_t row = static_cast<size_t>(br) * 128 + r0 + 16 * i;
+    uint2 o;
+    o.x = pack_e4m3x4(v[i][0] * inv, v[i][1] * inv, v[i][2] * inv, v[i][3] * inv);
+    o.y = pack_e4m3x4(v[i][4] * inv, v[i][5] * inv, v[i][6] * inv, v[i][7] * inv);
+    *reinterpret_cast<uint2*>(q + row * Cc + bc * 128 + c0) = o;
+  }
+}
+
+// Dense layers as a one-"expert" grouped GEMM: chunk table of ceil(T / bn)
+// chunks over rows [0, T) with meta = {chunks, T}. One thread per chunk.
+extern "C" __global__ void fb_moe_dense_chunks(int T, int bn, int4* __restrict__ chunks, int* __restrict__ meta) {
+  const int n = (T + bn - 1) / bn;
+  for (int c = threadIdx.x; c < n; c += blockDim.x) chunks[c] = make_int4(0, c * bn, min(bn, T - c * bn), 0);
+  if (threadIdx.x == 0) {
+    meta[0] = n;
+    meta[1] = T;
+  }
+}

@@ -41,6 +41,7 @@ class LlamaConfig:
     tie_embeddings: bool = False
     init_std: float = 0.02
     extra: dict = field(default_factory=dict)
+    arch: str = "llama"
 
     @property
     def qkv_dim(self) -> int:
@@ -197,21 +198,20 @@ class LlamaModel:
         h = st.hidden[:b]
         x = st.normed[:b]
         ops.embedding(st.input_ids[:b], w.embed, h)
+        self._begin(st, b)
         splits = st.attn_splits[b]
         pending = None  # output of the previous down-projection not yet added to h
         for li, lw in enumerate(w.layers):
             self._norm(st, pending, h, lw["attn_norm"], x, b)
-            qkv = ops.linear(x, lw["qkv"], out=st.qkv[:b], partials=st.part)
+            qkv = self._qkv(st, x, lw, b)
             ops.rope_kv_write(qkv, st.positions[:b], self.cos_sin, st.q[:b], st.k_cache[li], st.v_cache[li],
                               st.slots[:b], w.nq_l, w.nkv_l, lw.get("q_norm"), lw.get("k_norm"), cfg.eps)
             ops.decode_attention(st.q[:b], st.k_cache[li], st.v_cache[li], st.block_tables[:b], st.seq_lens[:b],
                                  st.attn_out[:b].view(b, w.nq_l, cfg.head_dim), st.max_pages, st.attn_ws,
                                  scale=self.scale, splits=splits)
-            o = self._row_parallel(st, st.attn_out[:b], lw["o"], h, b, which=0)
+            o = self._o_proj(st, st.attn_out[:b], lw, h, b)
             self._norm(st, o, h, lw["mlp_norm"], x, b)
-            gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:b])
-            ops.silu_mul(gu, st.act[:b])
-            pending = self._row_parallel(st, st.act[:b], lw["down"], h, b, which=1)
+            pending = self._mlp(st, x, h, lw, b)
         self._norm(st, pending, h, w.final_norm, x, b)
         ops.linear(x, w.lm_head, out=st.logits[:b])
         if st.tp:
@@ -220,6 +220,22 @@ class LlamaModel:
             comm.argmax_sharded(st.tp.symm, st.logits[:b], w.vocab_offset, st.tp.pairs_offset, st.next_ids[:b])
         else:
             ops.argmax(st.logits[:b], st.next_ids[:b])
+
+    # ---- per-layer pieces (overridden by other model families) ---------------------------
+    def _begin(self, st, rows) -> None:
+        """Per-forward setup shared by every layer (nothing for the dense bf16 model)."""
+
+    def _qkv(self, st, x, lw, rows):
+        return ops.linear(x, lw["qkv"], out=st.qkv[:rows], partials=getattr(st, "part", None))
+
+    def _o_proj(self, st, inp, lw, h, rows):
+        return self._row_parallel(st, inp, lw["o"], h, rows, which=0)
+
+    def _mlp(self, st, x, h, lw, rows):
+        """SwiGLU FFN of x; returns the pending output that the next norm adds into h."""
+        gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:rows])
+        ops.silu_mul(gu, st.act[:rows])
+        return self._row_parallel(st, st.act[:rows], lw["down"], h, rows, which=1)
 
     def _row_parallel(self, st, inp, weight, h, rows, which):
         """o / down projection. TP: multicast into the slot exchange + barrier and
@@ -244,6 +260,8 @@ class LlamaModel:
         """x = rmsnorm(h), first adding the pending projection output into h."""
         if pending is None:
             ops.rmsnorm(h, weight, x, self.cfg.eps)
+        elif callable(pending):
+            pending(weight, x)
         elif isinstance(pending, tuple):
             from ..parallel import comm
 
@@ -262,10 +280,11 @@ class LlamaModel:
         ops.embedding(pb.input_ids[:t], w.embed, h)
         nqd = w.nq_l * cfg.head_dim
         nkvd = w.nkv_l * cfg.head_dim
+        self._begin(pb, t)
         pending = None
         for li, lw in enumerate(w.layers):
             self._norm(pb, pending, h, lw["attn_norm"], x, t)
-            qkv = ops.linear(x, lw["qkv"], out=pb.qkv[:t])
+            qkv = self._qkv(pb, x, lw, t)
             # Rotated q -> pb.q; rotated k and v -> paged cache and packed pb.k_rot / pb.v_rot.
             ops.rope_kv_write(qkv, pb.positions[:t], self.cos_sin, pb.q[:t], pb.k_cache[li], pb.v_cache[li],
                               pb.slots[:t], w.nq_l, w.nkv_l, lw.get("q_norm"), lw.get("k_norm"), cfg.eps,
@@ -273,19 +292,12 @@ class LlamaModel:
             ops.prefill_attention(pb.q[:t].view(t, nqd), pb.k_rot[:t].view(t, nkvd), pb.v_rot[:t].view(t, nkvd),
                                   pb.attn_out[:t], pb.cu_seqlens, pb.tile_seq, pb.tile_start, w.nq_l, w.nkv_l,
                                   scale=self.scale)
-            o = self._row_parallel(pb, pb.attn_out[:t], lw["o"], h, t, which=0)
+            o = self._o_proj(pb, pb.attn_out[:t], lw, h, t)
             self._norm(pb, o, h, lw["mlp_norm"], x, t)
-            gu = ops.linear(x, lw["gate_up"], out=pb.gate_up[:t])
-            ops.silu_mul(gu, pb.act[:t])
-            pending = self._row_parallel(pb, pb.act[:t], lw["down"], h, t, which=1)
+            pending = self._mlp(pb, x, h, lw, t)
         if pending is not None:
-            # fold the last down-projection into h (the final norm runs on gathered rows)
-            if isinstance(pending, tuple):
-                from ..parallel import comm
-
-                comm.add_rmsnorm_slots(pb.tp.slots.local_slots(pending[1]), t, h, w.final_norm, x, cfg.eps)
-            else:
-                ops.add_rmsnorm_partials(pending, h, w.final_norm, x, cfg.eps)
+            # fold the last FFN output into h (the final norm runs on gathered rows)
+            self._norm(pb, pending, h, w.final_norm, x, t)
         # last token of every prompt -> logits -> greedy token
         n = pb.num_seqs
         last = pb.last_rows[:n]

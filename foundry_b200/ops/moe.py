@@ -1,0 +1,184 @@
+"""Block-scaled fp8 linear layers and mixture-of-experts ops
+(csrc/kernels/moe.cu).
+
+Format: weights are e4m3 with one fp32 scale per 128 x 128 block, activations
+e4m3 with one fp32 scale per token per 128 features (the "fp8 block" format
+of the Qwen3/DeepSeek fp8 checkpoints the reference serves through vLLM /
+SGLang with DeepGEMM, reference recipe/sglang/serve_qwen3-30ba3bfp8_ep.sh:51-70).
+
+The grouped GEMM works from a device-side chunk table ({expert, first row,
+rows}), so one static launch serves any expert load - the property that
+makes MoE decode capturable in a CUDA graph. A dense fp8 linear layer is the
+same kernel with one expert and a chunk table over the token rows.
+
+Decode flow of one MoE block (single GPU):
+    router logits (bf16 GEMM) -> topk -> plan (counts, sorted positions,
+    chunks) -> dispatch_local (quantise + scatter) -> grouped GEMM gate_up
+    -> silu_mul_quant -> grouped GEMM down -> combine_add_rmsnorm
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .._native import core
+from . import _rt
+
+_IMG = "moe"
+QBLK = 128
+_U8 = 0  # CU_TENSOR_MAP_DATA_TYPE_UINT8
+_SWIZZLE_128B = 3
+MAX_KB = 32
+EPI_RESIDUAL = 2
+
+
+def gemm_smem(bn: int) -> int:
+    stage = 128 * QBLK + bn * QBLK
+    stages = min(8, (192 * 1024) // stage)
+    return stages * stage + 4 * bn * MAX_KB * 4 + 256 + 1024
+
+
+@dataclass
+class Fp8Weight:
+    """e4m3 weight ``q`` viewed as [experts * rows, cols] (uint8) with fp32
+    block scales ``scale`` [experts, rows / 128, cols / 128]."""
+
+    q: torch.Tensor
+    scale: torch.Tensor
+    experts: int
+    rows: int  # output features per expert
+    cols: int  # input features
+
+    @staticmethod
+    def empty(arena, experts: int, rows: int, cols: int) -> "Fp8Weight":
+        if rows % 128 or cols % 128:
+            raise ValueError(f"fp8 block weights need multiples of 128, got {rows} x {cols}")
+        q = arena.empty((experts * rows, cols), torch.uint8)
+        s = arena.empty((experts, rows // 128, cols // 128), torch.float32)
+        return Fp8Weight(q, s, experts, rows, cols)
+
+    def dequant(self) -> torch.Tensor:
+        """fp32 [experts * rows, cols] (tests, reference forward)."""
+        w = self.q.view(torch.float8_e4m3fn).float().view(self.experts, self.rows // 128, 128, self.cols // 128, 128)
+        return (w * self.scale[:, :, None, :, None]).reshape(self.experts * self.rows, self.cols)
+
+
+_tmaps: dict[tuple, bytes] = {}
+
+
+def fp8_tmap(t: torch.Tensor, box_rows: int) -> bytes:
+    """TMA map of a row-major [rows, K] e4m3 (uint8) matrix, 128-byte x box_rows boxes, 128B swizzle."""
+    rows, k = t.shape
+    key = (t.data_ptr(), rows, k, box_rows)
+    m = _tmaps.get(key)
+    if m is None:
+        if t.stride(1) != 1 or t.stride(0) != k or k % 16 or t.data_ptr() % 16:
+            raise ValueError("fp8 GEMM operands must be contiguous with 16-byte aligned rows")
+        m = core().make_tmap_2d(t.data_ptr(), _U8, k, rows, k, QBLK, box_rows, _SWIZZLE_128B)
+        if len(_tmaps) > 8192:
+            _tmaps.clear()
+        _tmaps[key] = m
+    return m
+
+
+def init_fp8_block_(w: Fp8Weight, seed: int, std: float, row_offset: int = 0) -> None:
+    """Random N(0, std) weights quantised per 128 x 128 block, generated in
+    place. Row r draws the values of row r + row_offset of the full matrix,
+    so a shard of experts matches the unsharded weights."""
+    r, c = w.experts * w.rows, w.cols
+    _rt.launch(_IMG, "fb_init_fp8_block", (c // 128, r // 128), (256,),
+               [w.q.data_ptr(), w.scale.data_ptr(), r, c, seed & ((1 << 64) - 1), float(std), int(row_offset)])
+
+
+def quantize_block_fp8_(w_bf16: torch.Tensor, w: Fp8Weight) -> None:
+    """Quantises a bf16 [experts * rows, cols] matrix into ``w``."""
+    r, c = w_bf16.shape
+    assert (r, c) == tuple(w.q.shape) and w_bf16.is_contiguous()
+    _rt.launch(_IMG, "fb_quant_block_fp8", (c // 128, r // 128), (256,),
+               [w_bf16.data_ptr(), r, c, w.q.data_ptr(), w.scale.data_ptr()])
+
+
+def quantize_rows(x: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, pos: torch.Tensor | None = None,
+                  topk: int = 1) -> None:
+    """x [T, H] bf16 -> e4m3 rows with per-128 scales. With ``pos`` ([T, topk]
+    int32) row t is written to rows pos[t, :] (MoE dispatch); else to row t."""
+    t, h = x.shape
+    if h % QBLK or h > 4096:
+        raise ValueError(f"hidden {h} must be a multiple of 128 and <= 4096")
+    _rt.launch(_IMG, "fb_moe_dispatch_local", (math.ceil(t / 8),), (256,), [
+        x.data_ptr(), x.stride(0), t, h, pos.data_ptr() if pos is not None else 0, topk, xq.data_ptr(),
+        xs.data_ptr()])
+
+
+def dense_chunks(t: int, bn: int, chunks: torch.Tensor, meta: torch.Tensor) -> None:
+    _rt.launch(_IMG, "fb_moe_dense_chunks", (1,), (256,), [t, bn, chunks.data_ptr(), meta.data_ptr()])
+
+
+def gemm_fp8(w: Fp8Weight, xq: torch.Tensor, xs: torch.Tensor, chunks: torch.Tensor, meta: torch.Tensor,
+             out: torch.Tensor, max_units: int, bn: int = 64, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Grouped (or, with one expert, dense) block-scaled fp8 GEMM:
+    out[r, :rows] = dequant(W[expert(r)]) @ dequant(xq[r]) for every row r of
+    every chunk in the table (+ residual). ``max_units`` bounds the chunks x
+    row-blocks of any step and sizes the persistent grid."""
+    if bn not in (32, 64):
+        raise ValueError("bn must be 32 or 64")
+    if w.cols // QBLK > MAX_KB:
+        raise ValueError(f"K = {w.cols} exceeds {MAX_KB * QBLK}")
+    mode = 0
+    if residual is not None:
+        assert residual.stride() == out.stride()
+        mode |= EPI_RESIDUAL
+    grid = max(1, min(max_units, _rt.sm_count()))
+    _rt.launch(_IMG, f"fb_moe_gemm_fp8_bn{bn}", (grid,), (192,), [
+        fp8_tmap(w.q, 128), fp8_tmap(xq, bn), w.scale.data_ptr(), xs.data_ptr(), chunks.data_ptr(),
+        meta.data_ptr(), out.data_ptr(), residual.data_ptr() if residual is not None else 0, w.rows, w.cols,
+        out.stride(0), mode], smem=gemm_smem(bn))
+    return out
+
+
+def topk(logits: torch.Tensor, k: int, ids: torch.Tensor, weights: torch.Tensor, renorm: bool = True) -> None:
+    t, e = logits.shape
+    if e % 32 or e > 256 or k > 8:
+        raise ValueError("experts must be a multiple of 32 and <= 256, top-k <= 8")
+    _rt.launch(_IMG, "fb_moe_topk", (math.ceil(t / 8),), (256,), [
+        logits.data_ptr(), logits.stride(0), t, e, k, 1 if renorm else 0, ids.data_ptr(), weights.data_ptr()])
+
+
+def plan(ids: torch.Tensor, pairs: int, experts: int, bn: int, pos: torch.Tensor, counts: torch.Tensor,
+         chunks: torch.Tensor, meta: torch.Tensor) -> None:
+    """Per-expert counts, stable expert-sorted positions of the ``pairs``
+    (token, slot) pairs in ``ids`` and the chunk table (<= bn rows each)."""
+    _rt.launch(_IMG, "fb_moe_plan", (1,), (1024,), [
+        ids.data_ptr(), pairs, experts, bn, pos.data_ptr(), counts.data_ptr(), chunks.data_ptr(), meta.data_ptr()])
+
+
+def max_chunks(pairs: int, experts: int, bn: int) -> int:
+    return pairs // bn + experts
+
+
+def silu_mul_quant(gu: torch.Tensor, rows: int, aq: torch.Tensor, as_: torch.Tensor,
+                   meta: torch.Tensor | None = None) -> None:
+    """gu [rows, 2I] (gate | up) -> e4m3 silu(gate) * up [rows, I] + per-128 scales."""
+    i = gu.shape[1] // 2
+    _rt.launch(_IMG, "fb_moe_silu_mul_quant", (math.ceil(rows / 8),), (256,), [
+        gu.data_ptr(), rows, i, meta.data_ptr() if meta is not None else 0, aq.data_ptr(), as_.data_ptr()])
+
+
+def combine_add_rmsnorm(y: torch.Tensor, pos: torch.Tensor, weights: torch.Tensor, k: int, h: torch.Tensor,
+                        norm_w: torch.Tensor, x: torch.Tensor, eps: float) -> None:
+    """h[t] += sum_j weights[t, j] * y[pos[t, j]]; x = rmsnorm(h) * norm_w."""
+    t, hd = h.shape
+    if hd % 8 or hd > 4096:
+        raise ValueError("hidden must be a multiple of 8 and <= 4096")
+    _rt.launch(_IMG, "fb_moe_combine_add_rmsnorm", (t,), (256,), [
+        y.data_ptr(), y.stride(0), pos.data_ptr(), weights.data_ptr(), k, h.data_ptr(), norm_w.data_ptr(),
+        x.data_ptr(), t, hd, float(eps)])
+
+
+__all__ = [
+    "Fp8Weight", "combine_add_rmsnorm", "dense_chunks", "fp8_tmap", "gemm_fp8", "gemm_smem", "init_fp8_block_",
+    "max_chunks", "plan", "quantize_block_fp8_", "quantize_rows", "silu_mul_quant", "topk",
+]

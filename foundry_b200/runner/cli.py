@@ -27,14 +27,13 @@ def _t0_ns() -> int:
 
 
 def build_engine_config(args):
-    from ..models import llama
+    from ..models import config_by_name
     from .engine import EngineConfig, default_graph_sizes
 
-    cfg = llama.CONFIGS[args.model]() if args.model in llama.CONFIGS else None
-    if cfg is None and args.model.startswith("llama-3-8b-"):
-        cfg = llama.tiny(layers=int(args.model.split("-")[-1].rstrip("l")))
-    if cfg is None:
-        raise SystemExit(f"unknown model {args.model}")
+    try:
+        cfg = config_by_name(args.model)
+    except KeyError as e:
+        raise SystemExit(str(e))
     max_seq = args.prompt_len + args.gen
     pages = -(-max_seq // 64)
     sizes = default_graph_sizes(args.max_graph_batch)

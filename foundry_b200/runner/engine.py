@@ -26,7 +26,8 @@ from dataclasses import dataclass, field
 import torch
 
 from .. import ops
-from ..models.llama import LlamaConfig, LlamaModel, LlamaWeights
+from ..models import family
+from ..models.llama import LlamaConfig, LlamaWeights
 from ..ops.attention import DecodeWorkspace, decode_splits, prefill_tiles
 from ..ops.gemm import MAX_SPLITS, PartialBuffer
 from .arena import Arena
@@ -54,11 +55,22 @@ class EngineConfig:
     region_size: int | str = "96GB"
     seed: int = 0
     tp: int = 1                     # tensor-parallel ranks (= torch.distributed world)
+    ep: int = 1                     # expert-parallel ranks (MoE; attention is data-parallel)
     extra: dict = field(default_factory=dict)
 
     @property
     def pages_per_seq(self) -> int:
         return math.ceil(self.max_seq_len / PAGE)
+
+
+def _model_buffers(obj, cfg, w, arena, rows) -> None:
+    """Allocates the model family's extra scratch (zeroed: padding rows of a
+    GEMM tile are read, never NaN bit patterns)."""
+    spec = getattr(family(cfg)[2], "buffers", None)
+    if spec is None:
+        return
+    for name, (shape, dtype) in spec(cfg, w, rows).items():
+        setattr(obj, name, arena.zeros(shape, dtype))
 
 
 class TPContext:
@@ -107,10 +119,12 @@ class DecodeState:
         self.qkv = arena.empty((b, w.qkv_dim_l))
         self.q = arena.empty((b, nq, cfg.head_dim))
         self.attn_out = arena.empty((b, nq * cfg.head_dim))
-        self.gate_up = arena.empty((b, 2 * w.inter_l))
-        self.act = arena.empty((b, w.inter_l))
+        if w.inter_l:
+            self.gate_up = arena.empty((b, 2 * w.inter_l))
+            self.act = arena.empty((b, w.inter_l))
         self.logits = arena.empty((b, w.vocab_l))
         self.k_cache, self.v_cache = k_cache, v_cache
+        _model_buffers(self, ecfg.model, w, arena, b)
         # fp32 split-K slices of the decode GEMMs (consumed by the next op)
         self.part = PartialBuffer(buf=arena.empty((MAX_SPLITS * b * max(w.qkv_dim_l, cfg.hidden),), torch.float32))
         sizes = ecfg.graph_sizes or default_graph_sizes(b)
@@ -149,8 +163,10 @@ class PrefillBatch:
         self.k_rot = arena.empty((t, nkv, cfg.head_dim))
         self.v_rot = arena.empty((t, nkv, cfg.head_dim))
         self.attn_out = arena.empty((t, nq * cfg.head_dim))
-        self.gate_up = arena.empty((t, 2 * w.inter_l))
-        self.act = arena.empty((t, w.inter_l))
+        if w.inter_l:
+            self.gate_up = arena.empty((t, 2 * w.inter_l))
+            self.act = arena.empty((t, w.inter_l))
+        _model_buffers(self, cfg, w, arena, t)
         self.last_hidden = arena.empty((n, cfg.hidden))
         self.last_normed = arena.empty((n, cfg.hidden))
         self.logits = arena.empty((n, w.vocab_l))
@@ -203,8 +219,16 @@ class LLMEngine:
             self.tp = TPContext(max(ecfg.max_batch, ecfg.max_prefill_tokens), cfg.hidden,
                                 max(ecfg.max_batch, ecfg.max_prefill_seqs))
         # Order matters: it fixes every device address (SAVE == LOAD).
-        self.weights = LlamaWeights(cfg, self.arena, seed=ecfg.seed, init=init_weights, tp_rank=tp_rank,
-                                    tp_size=ecfg.tp)
+        _, weights_cls, model_cls = family(cfg)
+        kw = {}
+        if ecfg.ep > 1:
+            import torch.distributed as dist
+
+            if ecfg.tp > 1 or not dist.is_initialized() or dist.get_world_size() != ecfg.ep:
+                raise RuntimeError(f"ep={ecfg.ep} needs tp=1 and an initialised process group of that size")
+            kw = {"ep_rank": dist.get_rank(), "ep_size": ecfg.ep}
+        self.weights = weights_cls(cfg, self.arena, seed=ecfg.seed, init=init_weights, tp_rank=tp_rank,
+                                   tp_size=ecfg.tp, **kw)
         nb = ecfg.num_blocks or ecfg.max_batch * ecfg.pages_per_seq
         self.num_blocks = nb
         nkv = self.weights.nkv_l
@@ -217,7 +241,7 @@ class LLMEngine:
                                             scaling=cfg.rope_scaling))
         self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp)
         self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp)
-        self.model = LlamaModel(cfg, self.weights, self.cos_sin)
+        self.model = model_cls(cfg, self.weights, self.cos_sin)
         self.graph_sizes = sorted(ecfg.graph_sizes or default_graph_sizes(ecfg.max_batch))
         self.graphs: dict[int, object] = {}
         self.free_pages = list(range(nb - 1, -1, -1))

@@ -23,7 +23,7 @@ import torch
 
 from .. import core, load_cuda_modules_and_libraries, pack_fatbins_to_folder
 from ..graphs import CUDAGraph, save_graph_manifest
-from ..models.llama import LlamaConfig
+from ..models import config_from_dict
 from .engine import EngineConfig, LLMEngine
 
 STATE_FILE = "runner_state.json"
@@ -34,13 +34,13 @@ def engine_config_to_dict(e: EngineConfig) -> dict:
         "model": e.model.to_dict(), "max_batch": e.max_batch, "max_seq_len": e.max_seq_len,
         "num_blocks": e.num_blocks, "max_prefill_tokens": e.max_prefill_tokens,
         "max_prefill_seqs": e.max_prefill_seqs, "graph_sizes": e.graph_sizes, "region_base": e.region_base,
-        "region_size": e.region_size, "seed": e.seed, "tp": e.tp,
+        "region_size": e.region_size, "seed": e.seed, "tp": e.tp, "ep": e.ep,
     }
 
 
 def engine_config_from_dict(d: dict) -> EngineConfig:
     d = dict(d)
-    d["model"] = LlamaConfig(**d["model"])
+    d["model"] = config_from_dict(d["model"])
     return EngineConfig(**d)
 
 

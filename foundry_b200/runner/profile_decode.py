@@ -31,16 +31,15 @@ def main():
     ap.add_argument("--attn", default=None, help="decode attention implementation (tc1, tc3, simt)")
     args = ap.parse_args()
     if args.attn:
-        import foundry_b200.models.llama as lm
         from foundry_b200 import ops as _ops
 
         _orig = _ops.decode_attention
-        lm.ops.decode_attention = lambda *a, **k: _orig(*a, impl=args.attn, **k)
+        _ops.decode_attention = lambda *a, **k: _orig(*a, impl=args.attn, **k)
 
-    from ..models import llama
+    from ..models import config_by_name
     from .engine import PAGE, EngineConfig, LLMEngine
 
-    cfg = llama.CONFIGS[args.model]()
+    cfg = config_by_name(args.model)
     if args.layers:
         cfg.layers = args.layers
     max_seq = args.ctx + args.warmup + args.steps + 8

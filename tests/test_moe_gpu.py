@@ -1,0 +1,233 @@
+"""Block-scaled fp8 and MoE kernels (csrc/kernels/moe.cu) against plain PyTorch
+fp32 references, and the Qwen3-MoE engine against its fp32 reference forward."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _arena():
+    from foundry_b200.runner.arena import Arena
+
+    return Arena(None, "4GB")
+
+
+def _q_rows_ref(x):
+    """Per-token-per-128 e4m3 quantisation in torch: (dequantised fp32, scales)."""
+    t, h = x.shape
+    xf = x.float().view(t, h // 128, 128)
+    s = xf.abs().amax(-1).clamp_min(1e-12) / 448.0
+    q = (xf / s[..., None]).to(torch.float8_e4m3fn).float()
+    return (q * s[..., None]).view(t, h), s
+
+
+def test_init_fp8_block_statistics_and_shards():
+    from foundry_b200.ops import moe as M
+
+    a = _arena()
+    w = M.Fp8Weight.empty(a, 4, 256, 512)
+    M.init_fp8_block_(w, seed=11, std=0.02)
+    d = w.dequant()
+    assert abs(d.mean().item()) < 1e-3 and abs(d.std().item() - 0.02) < 1e-3
+    # scales are amax / 448 of each block
+    blocks = d.view(4, 2, 128, 4, 128).abs().amax(dim=(2, 4))
+    torch.testing.assert_close(w.scale, blocks / 448.0, rtol=1e-6, atol=0)
+    # a shard with row_offset reproduces the corresponding rows of the full matrix
+    part = M.Fp8Weight.empty(a, 2, 256, 512)
+    M.init_fp8_block_(part, seed=11, std=0.02, row_offset=2 * 256)
+    assert torch.equal(part.q, w.q[2 * 256:]) and torch.equal(part.scale, w.scale[2:])
+
+
+def test_quantize_block_and_rows_match_torch():
+    from foundry_b200.ops import moe as M
+
+    a = _arena()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    wb = (torch.randn(384, 640, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+    w = M.Fp8Weight.empty(a, 1, 384, 640)
+    M.quantize_block_fp8_(wb, w)
+    s_ref = wb.float().view(3, 128, 5, 128).abs().amax(dim=(1, 3)) / 448.0
+    torch.testing.assert_close(w.scale[0], s_ref, rtol=1e-6, atol=0)
+    torch.testing.assert_close(w.dequant(), wb.float(), rtol=0.07, atol=s_ref.max().item())
+    x = torch.randn(37, 1024, device="cuda", generator=g).to(torch.bfloat16)
+    xq = torch.zeros(37, 1024, dtype=torch.uint8, device="cuda")
+    xs = torch.zeros(37, 8, dtype=torch.float32, device="cuda")
+    M.quantize_rows(x, xq, xs)
+    deq_ref, s_ref = _q_rows_ref(x)
+    torch.testing.assert_close(xs, s_ref, rtol=1e-6, atol=0)
+    deq = (xq.view(torch.float8_e4m3fn).float().view(37, 8, 128) * xs[..., None]).view(37, 1024)
+    # x * (1/s) in the kernel vs x / s in torch may round a tie differently: at most one e4m3 step, rarely
+    assert (deq != deq_ref).float().mean() < 2e-3
+    torch.testing.assert_close(deq, deq_ref, rtol=0.13, atol=1e-6)
+
+
+@pytest.mark.parametrize("t,o,k,bn", [(1, 128, 768, 32), (5, 1536, 2048, 32), (64, 5120, 2048, 64),
+                                      (130, 2048, 4096, 64), (33, 384, 1024, 64)])
+def test_dense_fp8_gemm_matches_fp32(t, o, k, bn):
+    from foundry_b200 import ops
+    from foundry_b200.ops import moe as M
+
+    a = _arena()
+    g = torch.Generator(device="cuda").manual_seed(t + o)
+    w = M.Fp8Weight.empty(a, 1, o, k)
+    M.init_fp8_block_(w, seed=t * 7 + 1, std=0.02)
+    x = torch.randn(t, k, device="cuda", generator=g).to(torch.bfloat16)
+    xq = torch.zeros(t, k, dtype=torch.uint8, device="cuda")
+    xs = torch.zeros(t, k // 128, dtype=torch.float32, device="cuda")
+    chunks = torch.zeros(t // 32 + 1, 4, dtype=torch.int32, device="cuda")
+    meta = torch.zeros(4, dtype=torch.int32, device="cuda")
+    M.quantize_rows(x, xq, xs)
+    M.dense_chunks(t, bn, chunks, meta)
+    out = torch.full((t, o), float("nan"), dtype=torch.bfloat16, device="cuda")
+    M.gemm_fp8(w, xq, xs, chunks, meta, out, max_units=math.ceil(t / bn) * o // 128, bn=bn)
+    xd = (xq.view(torch.float8_e4m3fn).float().view(t, k // 128, 128) * xs[..., None]).view(t, k)
+    ref = xd @ w.dequant().T
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * ref.abs().max().item())
+    # residual epilogue
+    res = torch.randn(t, o, device="cuda", generator=g).to(torch.bfloat16)
+    out2 = res.clone()
+    M.gemm_fp8(w, xq, xs, chunks, meta, out2, max_units=math.ceil(t / bn) * o // 128, bn=bn, residual=out2)
+    torch.testing.assert_close(out2.float(), ref + res.float(), rtol=1e-2, atol=2e-2 * max(1.0, ref.abs().max().item()))
+    assert ops.status("moe") == 0
+
+
+def test_topk_and_plan():
+    from foundry_b200.ops import moe as M
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    t, e, k = 300, 128, 8
+    logits = torch.randn(t, e, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.zeros(t, k, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(t, k, dtype=torch.float32, device="cuda")
+    M.topk(logits, k, ids, wts, renorm=True)
+    p = logits.float().softmax(-1)
+    tv, ti = p.topk(k, -1)
+    # bf16 logits tie often; the kernel breaks ties by lower expert index, so
+    # compare the selected probabilities (descending) rather than the indices
+    assert (ids.long() == ti).float().mean() > 0.95
+    got = p.gather(1, ids.long())
+    torch.testing.assert_close(got, tv, rtol=1e-5, atol=1e-7)
+    assert all(len(set(r)) == k for r in ids.tolist())  # k distinct experts per token
+    torch.testing.assert_close(wts, tv / tv.sum(-1, keepdim=True), rtol=1e-5, atol=1e-6)
+    pairs = t * k
+    for bn in (32, 64):
+        pos = torch.full((pairs,), -1, dtype=torch.int32, device="cuda")
+        counts = torch.zeros(e, dtype=torch.int32, device="cuda")
+        chunks = torch.zeros(M.max_chunks(pairs, e, 32), 4, dtype=torch.int32, device="cuda")
+        meta = torch.zeros(4, dtype=torch.int32, device="cuda")
+        M.plan(ids, pairs, e, bn, pos, counts, chunks, meta)
+        flat = ids.view(-1).long()
+        ref_counts = torch.bincount(flat, minlength=e)
+        assert torch.equal(counts.long(), ref_counts)
+        # positions: a permutation, expert-sorted, stable in pair order
+        order = torch.sort(flat * pairs + torch.arange(pairs, device="cuda")).indices
+        want = torch.empty_like(order)
+        want[order] = torch.arange(pairs, device="cuda")
+        assert torch.equal(pos.long(), want)
+        nch = int(meta[0])
+        assert nch == int(((ref_counts + bn - 1) // bn).sum()) and int(meta[1]) == pairs
+        ch = chunks[:nch].cpu()
+        assert int(ch[:, 2].sum()) == pairs and int(ch[:, 2].max()) <= bn
+        offs = torch.cumsum(ref_counts, 0) - ref_counts
+        for c in ch.tolist()[:50]:
+            ex, start, n = c[0], c[1], c[2]
+            assert offs[ex] <= start and start + n <= offs[ex] + ref_counts[ex]
+
+
+def test_moe_ffn_pipeline_matches_fp32():
+    """router top-k -> plan -> dispatch -> grouped gate_up -> silu*up -> grouped
+    down -> combine + residual + RMSNorm, against fp32 math on the same weights."""
+    from foundry_b200 import ops
+    from foundry_b200.ops import moe as M
+
+    a = _arena()
+    g = torch.Generator(device="cuda").manual_seed(5)
+    t, h, e, k, i = 48, 2048, 32, 8, 768
+    p = t * k
+    x = torch.randn(t, h, device="cuda", generator=g).to(torch.bfloat16)
+    router = (torch.randn(e, h, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w13 = M.Fp8Weight.empty(a, e, 2 * i, h)
+    w2 = M.Fp8Weight.empty(a, e, h, i)
+    M.init_fp8_block_(w13, 1, 0.02)
+    M.init_fp8_block_(w2, 2, 0.02)
+    z = lambda *s, dt=torch.int32: torch.zeros(*s, dtype=dt, device="cuda")  # noqa: E731
+    logits = torch.empty(t, e, dtype=torch.bfloat16, device="cuda")
+    ops.linear(x, router, out=logits)
+    ids, wts = z(t, k), z(t, k, dt=torch.float32)
+    M.topk(logits, k, ids, wts)
+    bn = 32
+    pos, counts, chunks, meta = z(p), z(e), z(M.max_chunks(p, e, 32), 4), z(4)
+    M.plan(ids, p, e, bn, pos, counts, chunks, meta)
+    mxq, mxs = z(p, h, dt=torch.uint8), z(p, h // 128, dt=torch.float32)
+    M.quantize_rows(x, mxq, mxs, pos=pos, topk=k)
+    y13 = z(p, 2 * i, dt=torch.bfloat16)
+    units = M.max_chunks(p, e, bn)
+    M.gemm_fp8(w13, mxq, mxs, chunks, meta, y13, max_units=units * (2 * i // 128), bn=bn)
+    maq, mas = z(p, i, dt=torch.uint8), z(p, i // 128, dt=torch.float32)
+    M.silu_mul_quant(y13, p, maq, mas)
+    y2 = z(p, h, dt=torch.bfloat16)
+    M.gemm_fp8(w2, maq, mas, chunks, meta, y2, max_units=units * (h // 128), bn=bn)
+    hres = torch.randn(t, h, device="cuda", generator=g).to(torch.bfloat16)
+    hh = hres.clone()
+    nw = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(torch.bfloat16)
+    xo = torch.empty_like(hh)
+    M.combine_add_rmsnorm(y2, pos, wts, k, hh, nw, xo, 1e-6)
+    assert ops.status("moe") == 0
+    # fp32 reference with the same routing (ids from the kernel) and dequantised weights
+    w13d = w13.dequant().view(e, 2 * i, h)
+    w2d = w2.dequant().view(e, h, i)
+    out = torch.zeros(t, h, device="cuda")
+    xf = x.float()
+    for ex in range(e):
+        rows, slot = (ids == ex).nonzero(as_tuple=True)
+        if rows.numel() == 0:
+            continue
+        gu = xf[rows] @ w13d[ex].T
+        act = torch.nn.functional.silu(gu[:, :i]) * gu[:, i:]
+        out.index_add_(0, rows, (act @ w2d[ex].T) * wts[rows, slot, None])
+    ref_h = hres.float() + out
+    err = (hh.float() - ref_h).norm() / out.norm()
+    assert err < 0.05, err  # fp8 activations: ~2^-4 relative per element, averaged by the dot products
+    hf = hh.float()
+    torch.testing.assert_close(xo.float(), hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6) * nw.float(),
+                               rtol=2e-2, atol=2e-2)
+
+
+def _moe_engine(layers=2, experts=32, max_batch=32, region=False):
+    from foundry_b200.models.qwen3_moe import tiny_moe
+    from foundry_b200.runner.engine import EngineConfig, LLMEngine
+
+    cfg = tiny_moe(layers=layers, experts=experts)
+    ecfg = EngineConfig(model=cfg, max_batch=max_batch, max_seq_len=256, max_prefill_tokens=1024,
+                        max_prefill_seqs=8, graph_sizes=[1, 2, 4, 8, 16, 32],
+                        region_base=0x630000000000 if region else None, region_size="16GB")
+    return LLMEngine(ecfg)
+
+
+def test_qwen3_moe_engine_matches_reference_and_graphs():
+    from foundry_b200 import ops
+    from foundry_b200.models.qwen3_moe import reference_forward
+
+    eng = _moe_engine()
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (5, 70, 130)]
+    outs = eng.generate(prompts, max_new_tokens=4)
+    checked = 0
+    for p, o in zip(prompts, outs):
+        seq = p + o[:-1]
+        logits = reference_forward(eng.ecfg.model, eng.weights, torch.tensor(seq, device="cuda"), eng.cos_sin)
+        for j in range(4):
+            top2 = logits[len(p) - 1 + j].topk(2)
+            # fp8 activations (not modelled by the fp32 reference) move logits by ~1e-2
+            if top2.values[0] - top2.values[1] > 0.1:
+                assert o[j] == int(top2.indices[0]), (j, o, top2)
+                checked += 1
+    assert checked >= 2, checked
+    eng.capture_graphs()
+    outs_g = eng.generate(prompts, max_new_tokens=4)
+    assert outs_g == outs
+    for img in ("moe", "gemm_bf16", "elementwise", "attention_tc"):
+        assert ops.status(img) == 0, img
