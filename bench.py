@@ -31,8 +31,20 @@ sys.path.insert(0, ROOT)
 
 REF_UNAVAILABLE = (
     "reference build needs Boost>=1.83 (CMakeLists.txt:9 find_package(Boost)); Boost is not on this image and "
-    "there is no network - pip install of /root/reference fails at CMake configure (see DESIGN.md)"
+    "there is no network; pip install of the reference fails at its CMake configure step"
 )
+
+
+# Serving loads of the benchmark configurations: prompts (per GPU for dp/ep,
+# per job for tp), prompt and output lengths, persisted decode graph sizes,
+# region size and parallel mode.
+PRESETS = {
+    "llama-3-8b": dict(batch=256, prompt_len=512, gen=128, graph_sizes="default", region="96GB", parallel="dp"),
+    "qwen3-30b-a3b": dict(batch=512, prompt_len=1024, gen=256, graph_sizes="2:512:2", region="170GB",
+                          parallel="ep"),
+    "llama-3-70b": dict(batch=1024, prompt_len=2048, gen=256, graph_sizes="default", region="170GB",
+                        parallel="tp"),
+}
 
 
 def parse():
@@ -42,12 +54,22 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="foundry", choices=["foundry", "reference"])
     ap.add_argument("--model", default="llama-3-8b")
-    ap.add_argument("--batch", type=int, default=256, help="prompts per GPU")
-    ap.add_argument("--prompt-len", type=int, default=512)
-    ap.add_argument("--gen", type=int, default=128)
+    ap.add_argument("--batch", type=int, default=None, help="prompts per GPU (dp/ep) or per job (tp)")
+    ap.add_argument("--prompt-len", type=int, default=None)
+    ap.add_argument("--gen", type=int, default=None)
+    ap.add_argument("--graph-sizes", default=None)
+    ap.add_argument("--region-size", default=None)
+    ap.add_argument("--parallel", default=None, choices=["dp", "tp", "ep"])
     ap.add_argument("--workdir", default=None)
     ap.add_argument("--skip-cold-start", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    base = args.model.split("@")[0]
+    preset = PRESETS.get(base, PRESETS["llama-3-8b"])
+    for k, v in (("batch", "batch"), ("prompt_len", "prompt_len"), ("gen", "gen"), ("graph_sizes", "graph_sizes"),
+                 ("region_size", "region"), ("parallel", "parallel")):
+        if getattr(args, k) is None:
+            setattr(args, k, preset[v])
+    return args
 
 
 class ClockSampler:
@@ -139,7 +161,8 @@ def main():
     workdir = args.workdir or f"/tmp/foundry_bench_{os.environ.get('MASTER_PORT', os.getpid())}"
     archive = os.path.join(workdir, f"rank_{rank}")
     common = ["--archive", archive, "--model", args.model, "--prompts", str(args.batch), "--prompt-len",
-              str(args.prompt_len), "--gen", str(gen), "--device", str(local)]
+              str(args.prompt_len), "--gen", str(gen), "--device", str(local), "--graph-sizes", args.graph_sizes,
+              "--region-size", args.region_size]
 
     # 1) SAVE in a fresh process: capture the 67 decode graphs and write the archive.
     t0 = time.perf_counter()
@@ -214,7 +237,7 @@ def main():
     e2e = tokens / (e2e_ms / 1e3)
     if rank == 0:
         out = {
-            "metric": "restored decode tok/s (Llama-3-8B shape, 67 persisted decode graphs)",
+            "metric": f"restored decode tok/s ({args.model} shape, {restore['num_graphs']} persisted decode graphs)",
             "value": round(value, 1),
             "unit": "tokens/s",
             "n_gpus": world,
@@ -224,14 +247,14 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "fp8-block (e4m3, 128x128 fp32 scales) + bf16" if "qwen3" in args.model else "bf16",
             "data": "synthetic (uniform random prompt token ids, random-init N(0,0.02) weights)",
             "config": {
                 "model": args.model, "global_batch": n_active * world, "seq_len": args.prompt_len + gen,
                 "prompt_len": args.prompt_len, "gen_len": args.gen, "parallelism": f"dp{world}",
                 "decode_batch_per_gpu": b, "graphs_per_rank": restore["num_graphs"],
                 "topology_groups": restore["num_groups"],
-                "l2": "inputs larger than L2 (16 GB of weights + KV cache read every step)",
+                "l2": "inputs larger than L2 (all weights + the KV cache are read every step)",
             },
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * b,
@@ -246,7 +269,7 @@ def main():
                 "restore_s_per_256_graphs": round(restore["restore_s"] * 256 / restore["num_graphs"], 4),
                 "cold_start_first_token_s": cold.get("cold_start_first_token_s"),
                 "cold_start_restore_s": cold.get("restore_s"),
-                "prefill_s_256x512": round(prefill_s, 3),
+                "prefill_s": round(prefill_s, 3),
             },
         }
         print(json.dumps(out))

@@ -38,7 +38,18 @@ constexpr int NUM_THREADS = 192;
 constexpr int QBLK = 128;       // scale block (tokens: 1 x 128, weights: 128 x 128)
 constexpr float FP8_MAX = 448.f;
 constexpr int EPI_RESIDUAL = 2;
-constexpr int MAX_KB = 32;      // K <= 4096
+constexpr int EPI_W_STREAM = 4;  // weights read once per launch: L2 evict-first
+constexpr int MAX_KB = 32;       // K <= 4096
+#ifndef FB_MOE_NBUF
+#define FB_MOE_NBUF 8
+#endif
+constexpr int NBUF = FB_MOE_NBUF;  // TMEM partial buffers (the epilogue may lag the MMAs by NBUF - 1 k-blocks)
+constexpr int EPI_PROBE_NO_PROMOTE = 1 << 8;  // timing probe: skip the TMEM reads and promotion (wrong results)
+constexpr int EPI_PROBE_NO_PEMPTY = 1 << 9;   // timing probe: MMAs do not wait for the epilogue (wrong results)
+constexpr int EPI_TMA16 = 1 << 10;  // tensor maps describe the e4m3 rows as 16-bit elements (K / 2 per row)
+constexpr int EPI_TRACE = 1 << 11;  // timing probe: CTA 0 writes clock64 stamps to `residual` (as uint64[128])
+// mode bits 12..15: L2 prefetch distance for weight tiles, in k-blocks (0 = off)
+__device__ __forceinline__ int pf_dist(int mode) { return (mode >> 12) & 15; }
 
 constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
@@ -65,16 +76,35 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
+// Scale rows are padded to a multiple of 4 floats (16 bytes) so that the
+// producer can fetch a unit's scales with one bulk copy.
+__host__ __device__ constexpr int kb_pad(int kb) { return (kb + 3) & ~3; }
+
+// Bulk (non-tensor) global -> shared copy, completion on `bar`. Both
+// addresses 16-byte aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = 128 * QBLK;  // 128 weight rows x 128 K bytes
   static constexpr int B_BYTES = BN * QBLK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
-  static constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
-  static constexpr int SXS_FLOATS = BN * MAX_KB;  // per epilogue warp
+  static constexpr uint32_t TMEM_COLS = tmem_cols_for(NBUF * BN);
+  static constexpr int XS_FLOATS = BN * MAX_KB;  // token scales of one unit [BN][KBp]
 };
 
+// Work unit u = (chunk c, weight row block ob) with c = u % num_chunks.
+// Warp 0 lane 0: per unit, one bulk copy of the unit's token scales
+//   [BN][KBp] and weight scales [KBp] into scale slot (unit & 1), then the
+//   TMA loads of the K loop; warp 1 lane 0: per k-block 4 MMAs into a fresh
+//   TMEM partial (NBUF buffers); warps 2-5: per k-block promote the partial
+//   with sw[kb] * sx[t][kb], per unit store the 128 x BN tile transposed.
 template <int BN>
 __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmX,
                                               const float* __restrict__ w_scale, const float* __restrict__ x_scale,
@@ -86,19 +116,21 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  // [4 epilogue warps][BN][KB] token scales of the current unit (one copy per
-  // warp, so the epilogue warps never wait on each other)
-  float* sxs_all = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sxs_all + 4 * C::SXS_FLOATS);
+  float* sxs = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);  // [2][BN * KBp]
+  float* sws = sxs + 2 * C::XS_FLOATS;                                       // [2][MAX_KB]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sws + 2 * MAX_KB);
   uint64_t* empty = full + STAGES;
   uint64_t* pfull = empty + STAGES;
-  uint64_t* pempty = pfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pempty + 2);
+  uint64_t* pempty = pfull + NBUF;
+  uint64_t* sfull = pempty + NBUF;
+  uint64_t* sempty = sfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int KB = K / QBLK;
+  const int KBp = kb_pad(KB);
   const int num_ob = O / 128;
   const int num_chunks = meta[0];
   const int num_units = num_chunks * num_ob;
@@ -108,9 +140,13 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NBUF; ++a) {
       mbar_init(&pfull[a], 1);
       mbar_init(&pempty[a], 4);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sfull[a], 1);
+      mbar_init(&sempty[a], 4);
     }
     *abort_flag = (KB > MAX_KB || (K % QBLK) || (O % 128)) ? 1 : 0;
     if (*abort_flag) set_status(FB_KERR_BAD_ARG);
@@ -131,29 +167,48 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- producer: scales (bulk copy) + operand tiles (TMA) ----------------
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       const uint64_t pol = policy_evict_first();
-      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
+      uint32_t j = 0;  // units of this CTA
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++j) {
         const int c = u % num_chunks, ob = u / num_chunks;
         const int4 ch = chunks[c];
         const int wrow = ch.x * O + ob * 128;
+        const uint32_t slot = j & 1;
+        if (!mbar_wait(&sempty[slot], ((j >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        const uint32_t xs_bytes = BN * KBp * 4, ws_bytes = KBp * 4;
+        const int pf = pf_dist(mode);
+        for (int kb = 0; kb < min(pf, KB); ++kb) tma_prefetch_2d(tmW, kb * QBLK, wrow);
+        mbar_arrive_expect_tx(&sfull[slot], xs_bytes + ws_bytes);
+        bulk_load(sxs + slot * C::XS_FLOATS, x_scale + static_cast<size_t>(ch.y) * KBp, xs_bytes, &sfull[slot]);
+        bulk_load(sws + slot * MAX_KB, w_scale + (static_cast<size_t>(ch.x) * num_ob + ob) * KBp, ws_bytes,
+                  &sfull[slot]);
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
             *(volatile int*)abort_flag = 1;
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d_hint(sA + stage * C::A_BYTES, tmW, &full[stage], kb * QBLK, wrow, pol);
-          tma_load_2d(sB + stage * C::B_BYTES, tmX, &full[stage], kb * QBLK, ch.y);
+          const int kx = (mode & EPI_TMA16) ? kb * (QBLK / 2) : kb * QBLK;  // 128 bytes either way
+          if (pf && kb + pf < KB) tma_prefetch_2d(tmW, (mode & EPI_TMA16) ? (kb + pf) * (QBLK / 2) : (kb + pf) * QBLK, wrow);
+          if (mode & EPI_W_STREAM)
+            tma_load_2d_hint(sA + stage * C::A_BYTES, tmW, &full[stage], kx, wrow, pol);
+          else
+            tma_load_2d(sA + stage * C::A_BYTES, tmW, &full[stage], kx, wrow);
+          tma_load_2d(sB + stage * C::B_BYTES, tmX, &full[stage], kx, ch.y);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      // Drain: every armed operand stage and scale slot completes before exit.
       for (int s = 0; s < STAGES; ++s) {
         mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
         if (++stage == STAGES) {
@@ -161,6 +216,7 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
           phase ^= 1;
         }
       }
+      for (int s = 0; s < 2; ++s, ++j) mbar_wait(&sempty[j & 1], ((j >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_EMPTY);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer: one fresh partial per k-block ----------------
@@ -172,8 +228,8 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
       for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++g) {
-          const uint32_t buf = g & 1;
-          if (!mbar_wait(&pempty[buf], ((g >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_TMEM) ||
+          const uint32_t buf = g % NBUF;
+          if ((!(mode & EPI_PROBE_NO_PEMPTY) && !mbar_wait(&pempty[buf], ((g / NBUF) & 1) ^ 1, FB_KERR_TIMEOUT_TMEM)) ||
               !mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
             ok = false;
             break;
@@ -201,28 +257,33 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
   } else {
     // ---------------- epilogue (warps 2..5): promote + store ----------------
     const int quarter = warp & 3;
-    float* sxs = sxs_all + quarter * C::SXS_FLOATS;
-    uint32_t g = 0;
-    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
+    uint32_t g = 0, j = 0;
+    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++j) {
       const int c = u % num_chunks, ob = u / num_chunks;
       const int4 ch = chunks[c];
-      for (int i = lane; i < BN * KB; i += 32) {
-        const int t = i / KB, kb = i % KB;
-        sxs[i] = (t < ch.z) ? x_scale[static_cast<size_t>(ch.y + t) * KB + kb] : 0.f;
+      const uint32_t slot = j & 1;
+      if (!mbar_wait(&sfull[slot], (j >> 1) & 1, FB_KERR_TIMEOUT_FULL)) {
+        *(volatile int*)abort_flag = 1;
+        break;
       }
-      __syncwarp();
-      const float* wsc = w_scale + (static_cast<size_t>(ch.x) * num_ob + ob) * KB;
+      const float* xsu = sxs + slot * C::XS_FLOATS;
+      const float* wsu = sws + slot * MAX_KB;
       float acc[BN];
 #pragma unroll
       for (int t = 0; t < BN; ++t) acc[t] = 0.f;
       bool ok = true;
       for (int kb = 0; kb < KB; ++kb, ++g) {
-        const uint32_t buf = g & 1;
-        if (!mbar_wait(&pfull[buf], (g >> 1) & 1, FB_KERR_TIMEOUT_TMEM)) {
+        const uint32_t buf = g % NBUF;
+        if (!mbar_wait(&pfull[buf], (g / NBUF) & 1, FB_KERR_TIMEOUT_TMEM)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (mode & EPI_PROBE_NO_PROMOTE) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&pempty[buf]);
+          continue;
+        }
         uint32_t r[BN];
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
 #pragma unroll
@@ -231,10 +292,12 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[buf]);
-        const float sw = wsc[kb];
+        const float sw = wsu[kb];
 #pragma unroll
-        for (int t = 0; t < BN; ++t) acc[t] = fmaf(__uint_as_float(r[t]), sw * sxs[t * KB + kb], acc[t]);
+        for (int t = 0; t < BN; ++t) acc[t] = fmaf(__uint_as_float(r[t]), sw * xsu[t * KBp + kb], acc[t]);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[slot]);
       if (!ok) {
         *(volatile int*)abort_flag = 1;
         break;
@@ -402,19 +465,23 @@ extern "C" __global__ void __launch_bounds__(1024) fb_moe_plan(const int* __rest
 
 // Quantise token rows to e4m3 with one scale per 128 dims and scatter each
 // row to its k destinations: xq[pos[t * k + j]] (pos == nullptr: row t).
-// One warp per token; H % 128 == 0, H <= 4096.
+// One warp per (token, group of 4 scale blocks); H % 128 == 0.
 extern "C" __global__ void __launch_bounds__(256) fb_moe_dispatch_local(const bf16* __restrict__ x, int ldx, int T,
                                                                        int H, const int* __restrict__ pos, int topk,
                                                                        uint8_t* __restrict__ xq,
                                                                        float* __restrict__ xs) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
+  constexpr int BPW = 4;
   const int nb = H / QBLK;
-  uint32_t q[32];
-  float sc[32];
+  const int groups = (nb + BPW - 1) / BPW;
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= T * groups) return;
+  const int t = w / groups, b0 = (w % groups) * BPW;
+  uint32_t q[BPW];
+  float sc[BPW];
 #pragma unroll
-  for (int b = 0; b < 32; ++b) {
+  for (int i = 0; i < BPW; ++i) {
+    const int b = b0 + i;
     if (b >= nb) break;
     const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * ldx + b * QBLK + lane * 4);
     const float2 f0 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.x));
@@ -422,17 +489,18 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_dispatch_local(const bf
     const float am = warp_max(fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y))));
     const float s = fmaxf(am, 1e-12f) / FP8_MAX;
     const float inv = 1.f / s;
-    q[b] = pack_e4m3x4(f0.x * inv, f0.y * inv, f1.x * inv, f1.y * inv);
-    sc[b] = s;
+    q[i] = pack_e4m3x4(f0.x * inv, f0.y * inv, f1.x * inv, f1.y * inv);
+    sc[i] = s;
   }
   for (int j = 0; j < (pos ? topk : 1); ++j) {
     const int row = pos ? pos[t * topk + j] : t;
     uint32_t* dst = reinterpret_cast<uint32_t*>(xq + static_cast<size_t>(row) * H);
 #pragma unroll
-    for (int b = 0; b < 32; ++b) {
+    for (int i = 0; i < BPW; ++i) {
+      const int b = b0 + i;
       if (b >= nb) break;
-      dst[b * 32 + lane] = q[b];
-      if (lane == b) xs[static_cast<size_t>(row) * nb + b] = sc[b];
+      dst[b * 32 + lane] = q[i];
+      if (lane == i) xs[static_cast<size_t>(row) * kb_pad(nb) + b] = sc[i];
     }
   }
 }
@@ -469,7 +537,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_silu_mul_quant(const bf
     const float inv = 1.f / s;
     reinterpret_cast<uint32_t*>(aq + static_cast<size_t>(r) * I)[b * 32 + lane] =
         pack_e4m3x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
-    if (lane == 0) as[static_cast<size_t>(r) * nb + b] = s;
+    if (lane == 0) as[static_cast<size_t>(r) * kb_pad(nb) + b] = s;
   }
 }
 
@@ -549,7 +617,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_quant_block_fp8(const bf16*
   for (int i = 0; i < 8; ++i) m = fmaxf(m, red[i]);
   const float s = fmaxf(m, 1e-12f) / FP8_MAX;
   const float inv = 1.f / s;
-  if (threadIdx.x == 0) scales[static_cast<size_t>(br) * (Cc / 128) + bc] = s;
+  if (threadIdx.x == 0) scales[static_cast<size_t>(br) * kb_pad(Cc / 128) + bc] = s;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const size_t row = static_cast<size_t>(br) * 128 + r0 + 16 * i;
@@ -593,7 +661,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_init_fp8_block(uint8_t* __r
   for (int i = 0; i < 8; ++i) m = fmaxf(m, red[i]);
   const float s = fmaxf(m, 1e-12f) / FP8_MAX;
   const float inv = 1.f / s;
-  if (threadIdx.x == 0) scales[static_cast<size_t>(br) * (Cc / 128) + bc] = s;
+  if (threadIdx.x == 0) scales[static_cast<size_t>(br) * kb_pad(Cc / 128) + bc] = s;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const size_t row = static_cast<size_t>(br) * 128 + r0 + 16 * i;
@@ -612,5 +680,358 @@ extern "C" __global__ void fb_moe_dense_chunks(int T, int bn, int4* __restrict__
   if (threadIdx.x == 0) {
     meta[0] = n;
     meta[1] = T;
+  }
+}
+
+// ==== weight-only fp8: e4m3 block-scaled weights x bf16 activations ===================
+//
+// fb_moe_gemm_w8_bn{32,64,128}: the grouped / dense GEMM of the fp8 checkpoints
+// with the weights dequantised on chip. Per k-block (128 K):
+//   warp 0      TMA: e4m3 weight tile [128 x 128 B] + bf16 activation tile
+//               [BN x 128] (two 64-wide boxes) into a ring stage; per unit a
+//               bulk copy of the unit's weight scales
+//   warps 2-5   converters: thread r turns weight row r into bf16,
+//               w = e4m3 * sw[kb] (exact e4m3 -> bf16 bit move, one bf16x2
+//               multiply per pair), written in the 128B-swizzled K-major
+//               layout the MMA reads; fence.proxy.async; release
+//   warp 1      MMA: 8 x tcgen05.mma kind::f16 (M = 128, N = BN, K = 16)
+//               accumulating the whole K loop in TMEM (no promotion)
+//   warps 6-9   epilogue once per unit: TMEM -> bf16, transposed store (+ residual)
+// HBM traffic is the fp8 weights (half of bf16); the tensor core runs bf16.
+namespace {
+
+constexpr int W8_THREADS = 320;
+constexpr int W8_CBUF = 2;  // converted (bf16) weight tiles in flight
+
+template <int BN>
+struct W8Cfg {
+  static constexpr int A8_BYTES = 128 * 128;         // e4m3 weight tile
+  static constexpr int B_BYTES = BN * 128 * 2;        // bf16 activations, two 64-wide halves
+  static constexpr int STAGE_BYTES = A8_BYTES + B_BYTES;
+  static constexpr int C_BYTES = 128 * 128 * 2;      // converted weight tile (two halves)
+  static constexpr int BUDGET = 216 * 1024 - W8_CBUF * C_BYTES;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 6 ? 6 : BUDGET / STAGE_BYTES;
+  static constexpr uint32_t TMEM_COLS = tmem_cols_for(2 * BN);
+};
+
+// Two e4m3 (bytes sel_lo, sel_hi of w, selected by the byte_perm selector)
+// -> bf16x2 holding value * 2^-120 exactly: sign to bit 15, exponent and
+// mantissa bits shifted into the bf16 exponent/mantissa (e4m3 bias 7 vs
+// bf16 bias 127; e4m3 subnormals land on bf16 subnormals).
+__device__ __forceinline__ uint32_t e4m3x2_bits_to_bf16x2(uint32_t w, uint32_t sel) {
+  const uint32_t t = __byte_perm(w, 0u, sel);
+  return (t & 0x80008000u) | ((t >> 4) & 0x07F007F0u);
+}
+
+template <int BN>
+__device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmX,
+                                             const float* __restrict__ w_scale, const int4* __restrict__ chunks,
+                                             const int* __restrict__ meta, bf16* out, const bf16* residual, int O,
+                                             int K, int ldo, int mode) {
+  using C = W8Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sC = smem;                                  // [W8_CBUF][2 halves][128 rows x 128 B] bf16
+  uint8_t* sA = sC + W8_CBUF * C::C_BYTES;             // [STAGES][128 x 128 B] e4m3
+  uint8_t* sB = sA + STAGES * C::A8_BYTES;             // [STAGES][2 halves][BN x 128 B] bf16
+  float* sws = reinterpret_cast<float*>(sB + STAGES * C::B_BYTES);  // [2][MAX_KB]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sws + 2 * MAX_KB);
+  uint64_t* empty = full + STAGES;
+  uint64_t* cfull = empty + STAGES;
+  uint64_t* cempty = cfull + W8_CBUF;
+  uint64_t* tfull = cempty + W8_CBUF;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* sfull = tempty + 2;
+  uint64_t* sempty = sfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int KB = K / QBLK;
+  const int KBp = kb_pad(KB);
+  const int num_ob = O / 128;
+  const int num_chunks = meta[0];
+  const int num_units = num_chunks * num_ob;
+  unsigned long long* trace =
+      ((mode & EPI_TRACE) && blockIdx.x == 0) ? reinterpret_cast<unsigned long long*>(const_cast<bf16*>(residual))
+                                              : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = clock64();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 5);  // 4 converter warps (A read) + the MMA commit (B read)
+    }
+    for (int c = 0; c < W8_CBUF; ++c) {
+      mbar_init(&cfull[c], 4);
+      mbar_init(&cempty[c], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+      mbar_init(&sfull[a], 1);
+      mbar_init(&sempty[a], 4);
+    }
+    *abort_flag = (KB > MAX_KB || (K % QBLK) || (O % 128)) ? 1 : 0;
+    if (*abort_flag) set_status(FB_KERR_BAD_ARG);
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(tmW);
+    tma_prefetch_desc(tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, j = 0;
+      const uint64_t pol = policy_evict_first();
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++j) {
+        const int c = u % num_chunks, ob = u / num_chunks;
+        const int4 ch = chunks[c];
+        const int wrow = ch.x * O + ob * 128;
+        const uint32_t slot = j & 1;
+        if (!mbar_wait(&sempty[slot], ((j >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&sfull[slot], KBp * 4);
+        bulk_load(sws + slot * MAX_KB, w_scale + (static_cast<size_t>(ch.x) * num_ob + ob) * KBp, KBp * 4,
+                  &sfull[slot]);
+        const int pf = pf_dist(mode);
+        for (int kb = 0; kb < min(pf, KB); ++kb) tma_prefetch_2d(tmW, kb * QBLK, wrow);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (pf && kb + pf < KB) tma_prefetch_2d(tmW, (kb + pf) * QBLK, wrow);
+          if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+            *(volatile int*)abort_flag = 1;
+            break;
+          }
+          if (trace && j == 0 && kb < 16) trace[1 + kb] = clock64();
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          if (mode & EPI_W_STREAM)
+            tma_load_2d_hint(sA + stage * C::A8_BYTES, tmW, &full[stage], kb * QBLK, wrow, pol);
+          else
+            tma_load_2d(sA + stage * C::A8_BYTES, tmW, &full[stage], kb * QBLK, wrow);
+          uint8_t* b = sB + stage * C::B_BYTES;
+          tma_load_2d(b, tmX, &full[stage], kb * QBLK, ch.y);
+          tma_load_2d(b + BN * 128, tmX, &full[stage], kb * QBLK + 64, ch.y);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      for (int s = 0; s < 2; ++s, ++j) mbar_wait(&sempty[j & 1], ((j >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_EMPTY);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16<128, BN>();
+      int stage = 0, cb = 0;
+      uint32_t phase = 0, cphase = 0;
+      int it = 0;
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
+        const int acc = it & 1;
+        if (!mbar_wait(&tempty[acc], ((it >> 1) & 1) ^ 1, FB_KERR_TIMEOUT_TMEM)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          if (trace && it == 0 && kb < 16) trace[20 + kb] = clock64();
+          if (!mbar_wait(&cfull[cb], cphase, FB_KERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          if (trace && it == 0 && kb < 16) trace[40 + kb] = clock64();
+          tc_fence_after();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint64_t adesc = sdesc_sw128(smem_u32(sC + cb * C::C_BYTES + h * (C::C_BYTES / 2)));
+            const uint64_t bdesc = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES + h * BN * 128));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_bf16(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                       (kb > 0 || h > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          mma_commit(&cempty[cb]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++cb == W8_CBUF) {
+            cb = 0;
+            cphase ^= 1;
+          }
+        }
+        mma_commit(&tfull[acc]);
+        if (!ok) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- converters: thread r dequantises weight row r ----------------
+    const int r = threadIdx.x - 64;
+    const int sw7 = r & 7;
+    int stage = 0, cb = 0;
+    uint32_t phase = 0, cphase = 0, j = 0;
+    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++j) {
+      const uint32_t slot = j & 1;
+      if (!mbar_wait(&sfull[slot], (j >> 1) & 1, FB_KERR_TIMEOUT_FULL)) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      const float* wsu = sws + slot * MAX_KB;
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb) {
+        if (!mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL) ||
+            !mbar_wait(&cempty[cb], cphase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+          ok = false;
+          break;
+        }
+        // bf16(sw * 2^120) times the exact bf16 image (value * 2^-120) of each e4m3
+        const bf16 s = __float2bfloat16(wsu[kb] * 1.329227995784916e36f);
+        const bf162 s2 = __halves2bfloat162(s, s);
+        const uint8_t* arow = sA + stage * C::A8_BYTES + r * 128;
+        uint8_t* crow = sC + cb * C::C_BYTES + r * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 in = *reinterpret_cast<const uint4*>(arow + ((q ^ sw7) << 4));
+          const uint32_t wv[4] = {in.x, in.y, in.z, in.w};
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t lo = e4m3x2_bits_to_bf16x2(wv[i], 0x1404u);
+            uint32_t hi = e4m3x2_bits_to_bf16x2(wv[i], 0x3424u);
+            bf162 l2 = __hmul2(*reinterpret_cast<const bf162*>(&lo), s2);
+            bf162 h2 = __hmul2(*reinterpret_cast<const bf162*>(&hi), s2);
+            o[2 * i] = *reinterpret_cast<const uint32_t*>(&l2);
+            o[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          // fp8 chunk q = elements 16q..16q+15 -> bf16 chunks 2q, 2q+1 of half q / 4
+          uint8_t* half = crow + (q >> 2) * (C::C_BYTES / 2);
+          const int c0 = (2 * q) & 7;
+          *reinterpret_cast<uint4*>(half + ((c0 ^ sw7) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(half + (((c0 + 1) ^ sw7) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
+        __syncwarp();
+        if (trace && r == 0 && j == 0 && kb < 16) trace[60 + kb] = clock64();
+        if (lane == 0) {
+          mbar_arrive(&cfull[cb]);
+          mbar_arrive(&empty[stage]);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (++cb == W8_CBUF) {
+          cb = 0;
+          cphase ^= 1;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[slot]);
+      if (!ok) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 6-9) ----------------
+    const int quarter = warp & 3;
+    int it = 0;
+    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
+      const int c = u % num_chunks, ob = u / num_chunks;
+      const int4 ch = chunks[c];
+      const int acc = it & 1;
+      if (!mbar_wait(&tfull[acc], (it >> 1) & 1, FB_KERR_TIMEOUT_TMEM)) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      if (trace && it == 0 && quarter == 0 && lane == 0) trace[80] = clock64();
+      tc_fence_after();
+      const int o = ob * 128 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t rr[16];
+        tmem_ld16(t_row + c0, rr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int t = c0 + i;
+          if (t < ch.z) {
+            const size_t idx = static_cast<size_t>(ch.y + t) * ldo + o;
+            float v = __uint_as_float(rr[i]);
+            if (mode & EPI_RESIDUAL) v += bf2f(residual[idx]);
+            out[idx] = f2bf(v);
+          }
+        }
+      }
+      if (trace && it == 0 && quarter == 0 && lane == 0) trace[81] = clock64();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace
+
+#define FB_W8_GEMM_INSTANCE(BN)                                                                                     \
+  extern "C" __global__ void __launch_bounds__(W8_THREADS, 1) fb_moe_gemm_w8_bn##BN(                               \
+      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const float* w_scale,       \
+      const int4* chunks, const int* meta, bf16* out, const bf16* residual, int O, int K, int ldo, int mode) {      \
+    w8_gemm_body<BN>(&tmW, &tmX, w_scale, chunks, meta, out, residual, O, K, ldo, mode);                           \
+  }
+
+FB_W8_GEMM_INSTANCE(32)
+FB_W8_GEMM_INSTANCE(64)
+FB_W8_GEMM_INSTANCE(128)
+
+// Gather token rows into expert-sorted order: dst[pos[t * k + j]] = src[t]
+// (bf16, H % 8 == 0). One CTA of 256 threads per token.
+extern "C" __global__ void __launch_bounds__(256) fb_moe_scatter_rows(const bf16* __restrict__ src, int lds, int T,
+                                                                     int H, const int* __restrict__ pos, int topk,
+                                                                     bf16* __restrict__ dst) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < H; c += 256 * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(t) * lds + c);
+    for (int j = 0; j < topk; ++j)
+      *reinterpret_cast<uint4*>(dst + static_cast<size_t>(pos[t * topk + j]) * H + c) = v;
   }
 }

@@ -47,6 +47,11 @@ class Qwen3MoeConfig(LlamaConfig):
     moe_inter: int = 768
     norm_topk_prob: bool = True
     arch: str = "qwen3_moe"
+    # fp8 GEMM flavour: "promote" = e4m3 x e4m3 tcgen05 kind::f8f6f4 with
+    # per-128-K promotion (activations quantised per token per 128), "w8" =
+    # e4m3 weights dequantised on chip, bf16 activations, kind::f16
+    fp8_gemm: str = "promote"
+    fp8_prefetch: int = 0  # L2 prefetch distance of weight tiles (k-blocks)
 
     def num_params(self) -> int:
         h, d = self.hidden, self.head_dim
@@ -144,17 +149,28 @@ class Qwen3MoeModel(LlamaModel):
         h, d, k, i = cfg.hidden, cfg.head_dim, cfg.topk, cfg.moe_inter
         p = rows * k
         u8, f32, i32 = torch.uint8, torch.float32, torch.int32
+        sr, kp = M.scale_rows, M.kb_pad
         return {
-            "xq_h": ((rows, h), u8), "xs_h": ((rows, h // 128), f32),
-            "xq_o": ((rows, cfg.n_q * d), u8), "xs_o": ((rows, cfg.n_q * d // 128), f32),
+            "xq_h": ((rows, h), u8), "xs_h": ((sr(rows), kp(h // 128)), f32),
+            "xq_o": ((rows, cfg.n_q * d), u8), "xs_o": ((sr(rows), kp(cfg.n_q * d // 128)), f32),
             "dchunks": ((rows // 32 + 1, 4), i32), "dmeta": ((4,), i32),
             "rlogits": ((rows, cfg.num_experts), torch.bfloat16), "tids": ((rows, k), i32), "tw": ((rows, k), f32),
             "pos": ((p,), i32), "ecounts": ((cfg.num_experts,), i32),
             "chunks": ((M.max_chunks(p, w.e_local, 32), 4), i32), "meta": ((4,), i32),
-            "mxq": ((p, h), u8), "mxs": ((p, h // 128), f32),
-            "y13": ((p, 2 * i), torch.bfloat16), "maq": ((p, i), u8), "mas": ((p, i // 128), f32),
+            "mxq": ((p, h), u8), "mxs": ((sr(p), kp(h // 128)), f32),
+            "y13": ((p, 2 * i), torch.bfloat16), "maq": ((p, i), u8), "mas": ((sr(p), kp(i // 128)), f32),
             "y2": ((p, h), torch.bfloat16),
+            "mx16": ((p, h), torch.bfloat16), "act16": ((p, i), torch.bfloat16),
         }
+
+    def __init__(self, cfg: Qwen3MoeConfig, weights: Qwen3MoeWeights, cos_sin: torch.Tensor):
+        super().__init__(cfg, weights, cos_sin)
+        import os
+
+        self.kind = os.environ.get("FOUNDRY_FP8_GEMM", cfg.fp8_gemm)
+        self.pf = int(os.environ.get("FOUNDRY_FP8_PREFETCH", cfg.fp8_prefetch))
+        if self.kind not in ("promote", "w8"):
+            raise ValueError(f"fp8_gemm must be 'promote' or 'w8', got {self.kind!r}")
 
     def _bn_dense(self, rows: int) -> int:
         return 32 if rows <= 32 else 64
@@ -162,15 +178,22 @@ class Qwen3MoeModel(LlamaModel):
     def _bn_moe(self, pairs: int) -> int:
         return 64 if pairs > 32 * self.w.e_local else 32
 
+    def _gemm(self, w, x, xq, xs, chunks, meta, out, units, bn, residual=None, stream=False):
+        if self.kind == "w8":
+            return M.gemm_w8(w, x, chunks, meta, out, max_units=units, bn=bn, residual=residual,
+                             stream_weights=stream, prefetch=self.pf)
+        return M.gemm_fp8(w, xq, xs, chunks, meta, out, max_units=units, bn=bn, residual=residual,
+                          stream_weights=stream, prefetch=self.pf)
+
     def _begin(self, st, rows) -> None:
         M.dense_chunks(rows, self._bn_dense(rows), st.dchunks, st.dmeta)
 
     def _dense(self, st, x, xq, xs, w, out, rows, residual=None):
-        M.quantize_rows(x, xq, xs)
+        if self.kind == "promote":
+            M.quantize_rows(x, xq, xs)
         bn = self._bn_dense(rows)
-        M.gemm_fp8(w, xq, xs, st.dchunks, st.dmeta, out, max_units=math.ceil(rows / bn) * (w.rows // 128), bn=bn,
-                   residual=residual)
-        return out
+        return self._gemm(w, x, xq, xs, st.dchunks, st.dmeta, out, math.ceil(rows / bn) * (w.rows // 128), bn,
+                          residual=residual)
 
     def _qkv(self, st, x, lw, rows):
         return self._dense(st, x, st.xq_h, st.xs_h, lw["qkv"], st.qkv[:rows], rows)
@@ -189,12 +212,21 @@ class Qwen3MoeModel(LlamaModel):
             return st.ep.moe(self, st, x, h, lw, rows)
         bn = self._bn_moe(p)
         M.plan(st.tids, p, w.e_local, bn, st.pos, st.ecounts, st.chunks, st.meta)
-        M.quantize_rows(x, st.mxq, st.mxs, pos=st.pos, topk=k)
         units = M.max_chunks(p, w.e_local, bn)
-        M.gemm_fp8(lw["w13"], st.mxq, st.mxs, st.chunks, st.meta, st.y13, max_units=units * (2 * cfg.moe_inter // 128),
-                   bn=bn)
-        M.silu_mul_quant(st.y13, p, st.maq, st.mas)
-        M.gemm_fp8(lw["w2"], st.maq, st.mas, st.chunks, st.meta, st.y2, max_units=units * (cfg.hidden // 128), bn=bn)
+        if self.kind == "w8":
+            M.scatter_rows(x, st.pos, k, st.mx16)
+            self._gemm(lw["w13"], st.mx16, None, None, st.chunks, st.meta, st.y13, units * (2 * cfg.moe_inter // 128),
+                       bn, stream=True)
+            ops.silu_mul(st.y13[:p], st.act16[:p])
+            self._gemm(lw["w2"], st.act16, None, None, st.chunks, st.meta, st.y2, units * (cfg.hidden // 128), bn,
+                       stream=True)
+        else:
+            M.quantize_rows(x, st.mxq, st.mxs, pos=st.pos, topk=k)
+            self._gemm(lw["w13"], None, st.mxq, st.mxs, st.chunks, st.meta, st.y13,
+                       units * (2 * cfg.moe_inter // 128), bn, stream=True)
+            M.silu_mul_quant(st.y13, p, st.maq, st.mas)
+            self._gemm(lw["w2"], None, st.maq, st.mas, st.chunks, st.meta, st.y2, units * (cfg.hidden // 128), bn,
+                       stream=True)
 
         def combine(norm_w, x_out, _st=st, _h=h, _k=k):
             M.combine_add_rmsnorm(_st.y2, _st.pos, _st.tw, _k, _h, norm_w, x_out, cfg.eps)

@@ -33,18 +33,39 @@ _U8 = 0  # CU_TENSOR_MAP_DATA_TYPE_UINT8
 _SWIZZLE_128B = 3
 MAX_KB = 32
 EPI_RESIDUAL = 2
+EPI_W_STREAM = 4
+NBUF = 8
 
 
 def gemm_smem(bn: int) -> int:
     stage = 128 * QBLK + bn * QBLK
     stages = min(8, (192 * 1024) // stage)
-    return stages * stage + 4 * bn * MAX_KB * 4 + 256 + 1024
+    return stages * stage + 2 * bn * MAX_KB * 4 + 2 * MAX_KB * 4 + 8 * (2 * stages + 2 * NBUF + 4) + 16 + 1024
+
+
+def kb_pad(kb: int) -> int:
+    """Scale rows are padded to a multiple of 4 floats (16-byte rows for bulk copies)."""
+    return (kb + 3) // 4 * 4
+
+
+def scale_rows(rows: int) -> int:
+    """Rows of an activation-scale buffer for ``rows`` tokens: the GEMM
+    fetches a whole chunk of up to 64 rows of scales at once."""
+    return rows + 64
+
+
+def act_buffers(arena, rows: int, k: int):
+    """(e4m3 [rows, k], fp32 scales [rows + 64, kb_pad(k / 128)]) zeroed activation buffers."""
+    q = arena.zeros((rows, k), torch.uint8)
+    s = arena.zeros((scale_rows(rows), kb_pad(k // QBLK)), torch.float32)
+    return q, s
 
 
 @dataclass
 class Fp8Weight:
     """e4m3 weight ``q`` viewed as [experts * rows, cols] (uint8) with fp32
-    block scales ``scale`` [experts, rows / 128, cols / 128]."""
+    block scales ``scale`` [experts, rows / 128, kb_pad(cols / 128)] (the
+    padding columns are unused)."""
 
     q: torch.Tensor
     scale: torch.Tensor
@@ -57,13 +78,14 @@ class Fp8Weight:
         if rows % 128 or cols % 128:
             raise ValueError(f"fp8 block weights need multiples of 128, got {rows} x {cols}")
         q = arena.empty((experts * rows, cols), torch.uint8)
-        s = arena.empty((experts, rows // 128, cols // 128), torch.float32)
+        s = arena.zeros((experts, rows // 128, kb_pad(cols // 128)), torch.float32)
         return Fp8Weight(q, s, experts, rows, cols)
 
     def dequant(self) -> torch.Tensor:
         """fp32 [experts * rows, cols] (tests, reference forward)."""
         w = self.q.view(torch.float8_e4m3fn).float().view(self.experts, self.rows // 128, 128, self.cols // 128, 128)
-        return (w * self.scale[:, :, None, :, None]).reshape(self.experts * self.rows, self.cols)
+        sc = self.scale[:, :, : self.cols // 128]
+        return (w * sc[:, :, None, :, None]).reshape(self.experts * self.rows, self.cols)
 
 
 _tmaps: dict[tuple, bytes] = {}
@@ -103,12 +125,14 @@ def quantize_block_fp8_(w_bf16: torch.Tensor, w: Fp8Weight) -> None:
 
 def quantize_rows(x: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, pos: torch.Tensor | None = None,
                   topk: int = 1) -> None:
-    """x [T, H] bf16 -> e4m3 rows with per-128 scales. With ``pos`` ([T, topk]
-    int32) row t is written to rows pos[t, :] (MoE dispatch); else to row t."""
+    """x [T, H] bf16 -> e4m3 rows with per-128 scales (``xs`` rows padded to
+    kb_pad(H / 128) floats). With ``pos`` ([T, topk] int32) row t is written
+    to rows pos[t, :] (MoE dispatch); else to row t."""
     t, h = x.shape
-    if h % QBLK or h > 4096:
-        raise ValueError(f"hidden {h} must be a multiple of 128 and <= 4096")
-    _rt.launch(_IMG, "fb_moe_dispatch_local", (math.ceil(t / 8),), (256,), [
+    if h % QBLK:
+        raise ValueError(f"hidden {h} must be a multiple of 128")
+    warps = t * math.ceil(h // QBLK / 4)
+    _rt.launch(_IMG, "fb_moe_dispatch_local", (math.ceil(warps / 8),), (256,), [
         x.data_ptr(), x.stride(0), t, h, pos.data_ptr() if pos is not None else 0, topk, xq.data_ptr(),
         xs.data_ptr()])
 
@@ -118,11 +142,13 @@ def dense_chunks(t: int, bn: int, chunks: torch.Tensor, meta: torch.Tensor) -> N
 
 
 def gemm_fp8(w: Fp8Weight, xq: torch.Tensor, xs: torch.Tensor, chunks: torch.Tensor, meta: torch.Tensor,
-             out: torch.Tensor, max_units: int, bn: int = 64, residual: torch.Tensor | None = None) -> torch.Tensor:
+             out: torch.Tensor, max_units: int, bn: int = 64, residual: torch.Tensor | None = None,
+             stream_weights: bool = False, prefetch: int = 0) -> torch.Tensor:
     """Grouped (or, with one expert, dense) block-scaled fp8 GEMM:
     out[r, :rows] = dequant(W[expert(r)]) @ dequant(xq[r]) for every row r of
     every chunk in the table (+ residual). ``max_units`` bounds the chunks x
-    row-blocks of any step and sizes the persistent grid."""
+    row-blocks of any step and sizes the persistent grid. ``stream_weights``
+    hints weight tiles evict-first in L2 (experts whose tiles are read once)."""
     if bn not in (32, 64):
         raise ValueError("bn must be 32 or 64")
     if w.cols // QBLK > MAX_KB:
@@ -131,12 +157,57 @@ def gemm_fp8(w: Fp8Weight, xq: torch.Tensor, xs: torch.Tensor, chunks: torch.Ten
     if residual is not None:
         assert residual.stride() == out.stride()
         mode |= EPI_RESIDUAL
+    if stream_weights:
+        mode |= EPI_W_STREAM
+    mode |= (min(prefetch, 15) & 15) << 12
     grid = max(1, min(max_units, _rt.sm_count()))
     _rt.launch(_IMG, f"fb_moe_gemm_fp8_bn{bn}", (grid,), (192,), [
         fp8_tmap(w.q, 128), fp8_tmap(xq, bn), w.scale.data_ptr(), xs.data_ptr(), chunks.data_ptr(),
         meta.data_ptr(), out.data_ptr(), residual.data_ptr() if residual is not None else 0, w.rows, w.cols,
         out.stride(0), mode], smem=gemm_smem(bn))
     return out
+
+
+def w8_smem(bn: int) -> int:
+    stage = 128 * 128 + bn * 128 * 2
+    cbuf = 2 * 128 * 128 * 2
+    stages = min(6, (216 * 1024 - cbuf) // stage)
+    return 1024 + cbuf + stages * stage + 2 * MAX_KB * 4 + 8 * (2 * stages + 2 * 2 + 8) + 16
+
+
+def gemm_w8(w: Fp8Weight, x: torch.Tensor, chunks: torch.Tensor, meta: torch.Tensor, out: torch.Tensor,
+            max_units: int, bn: int = 64, residual: torch.Tensor | None = None,
+            stream_weights: bool = False, prefetch: int = 0) -> torch.Tensor:
+    """Weight-only fp8 grouped / dense GEMM: out[r, :rows] = dequant(W[expert(r)]) @ x[r]
+    for every row r of every chunk in the table (+ residual), x in bf16. The
+    e4m3 weight tiles are dequantised on chip into bf16 and multiplied on the
+    tcgen05 bf16 path with the whole K loop accumulated in TMEM."""
+    from .gemm import tmap as bf16_tmap
+
+    if bn not in (32, 64, 128):
+        raise ValueError("bn must be 32, 64 or 128")
+    if w.cols // QBLK > MAX_KB or x.shape[1] != w.cols:
+        raise ValueError(f"bad K: weights {w.cols}, activations {x.shape[1]}")
+    mode = 0
+    if residual is not None:
+        assert residual.stride() == out.stride()
+        mode |= EPI_RESIDUAL
+    if stream_weights:
+        mode |= EPI_W_STREAM
+    mode |= (min(prefetch, 15) & 15) << 12
+    grid = max(1, min(max_units, _rt.sm_count()))
+    _rt.launch(_IMG, f"fb_moe_gemm_w8_bn{bn}", (grid,), (320,), [
+        fp8_tmap(w.q, 128), bf16_tmap(x, bn), w.scale.data_ptr(), chunks.data_ptr(), meta.data_ptr(),
+        out.data_ptr(), residual.data_ptr() if residual is not None else 0, w.rows, w.cols, out.stride(0), mode],
+        smem=w8_smem(bn))
+    return out
+
+
+def scatter_rows(x: torch.Tensor, pos: torch.Tensor, topk: int, dst: torch.Tensor) -> None:
+    """dst[pos[t, j]] = x[t] for every token t and slot j (expert-sorted gather, bf16)."""
+    t, h = x.shape
+    _rt.launch(_IMG, "fb_moe_scatter_rows", (t,), (256,), [x.data_ptr(), x.stride(0), t, h, pos.data_ptr(), topk,
+                                                          dst.data_ptr()])
 
 
 def topk(logits: torch.Tensor, k: int, ids: torch.Tensor, weights: torch.Tensor, renorm: bool = True) -> None:
@@ -179,6 +250,7 @@ def combine_add_rmsnorm(y: torch.Tensor, pos: torch.Tensor, weights: torch.Tenso
 
 
 __all__ = [
-    "Fp8Weight", "combine_add_rmsnorm", "dense_chunks", "fp8_tmap", "gemm_fp8", "gemm_smem", "init_fp8_block_",
+    "Fp8Weight", "combine_add_rmsnorm", "dense_chunks", "fp8_tmap", "gemm_fp8", "gemm_smem", "gemm_w8", "init_fp8_block_",
+    "scatter_rows", "w8_smem",
     "max_chunks", "plan", "quantize_block_fp8_", "quantize_rows", "silu_mul_quant", "topk",
 ]

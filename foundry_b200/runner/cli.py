@@ -36,12 +36,41 @@ def build_engine_config(args):
         raise SystemExit(str(e))
     max_seq = args.prompt_len + args.gen
     pages = -(-max_seq // 64)
-    sizes = default_graph_sizes(args.max_graph_batch)
+    sizes = parse_graph_sizes(args.graph_sizes, args.max_graph_batch)
     return EngineConfig(
-        model=cfg, max_batch=max(args.max_graph_batch, args.prompts), max_seq_len=max_seq,
+        model=cfg, max_batch=max(max(sizes), args.prompts), max_seq_len=max_seq,
         num_blocks=args.prompts * pages + 64, max_prefill_tokens=args.max_prefill_tokens,
         max_prefill_seqs=max(1, args.max_prefill_tokens // args.prompt_len), graph_sizes=sizes,
-        region_base=int(args.region_base, 16), region_size=args.region_size, seed=args.seed)
+        region_base=int(args.region_base, 16), region_size=args.region_size, seed=args.seed,
+        tp=args.tp, ep=args.ep)
+
+
+def parse_graph_sizes(spec: str, max_batch: int) -> list[int]:
+    """``default``: {1,2,4,8} + 16..max step 16; ``start:stop:step`` (inclusive
+    stop), optionally followed by ``+a,b`` extra sizes."""
+    from .engine import default_graph_sizes
+
+    if spec == "default":
+        return default_graph_sizes(max_batch)
+    extra = []
+    if "+" in spec:
+        spec, more = spec.split("+", 1)
+        extra = [int(x) for x in more.split(",") if x]
+    a, b, c = (int(x) for x in spec.split(":"))
+    return sorted(set(list(range(a, b + 1, c)) + extra))
+
+
+def init_dist(args) -> None:
+    """Process group of a multi-rank (TP / EP) engine: gloo over 127.0.0.1
+    bootstraps the symmetric memory; every collective of a step is our own
+    kernel."""
+    if args.world <= 1:
+        return
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{args.dist_port}", rank=args.rank,
+                            world_size=args.world, timeout=timedelta(seconds=300))
 
 
 def add_common(p):
@@ -56,9 +85,30 @@ def add_common(p):
     p.add_argument("--region-size", default="96GB")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--device", type=int, default=None)
+    p.add_argument("--graph-sizes", default="default", help="default | start:stop:step[+a,b]")
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--ep", type=int, default=1)
+    p.add_argument("--rank", type=int, default=0)
+    p.add_argument("--world", type=int, default=1)
+    p.add_argument("--dist-port", type=int, default=29611)
+
+
+_ENGINES = []
 
 
 def main(argv=None):
+    try:
+        return _main(argv)
+    finally:
+        import torch.distributed as dist
+
+        for eng in _ENGINES:
+            eng.close()
+        if dist.is_available() and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _main(argv=None):
     ap = argparse.ArgumentParser(prog="foundry_b200.runner.cli")
     sub = ap.add_subparsers(dest="cmd", required=True)
     for name in ("save", "load", "serve"):
@@ -69,6 +119,7 @@ def main(argv=None):
 
     if args.device is not None:
         torch.cuda.set_device(args.device)
+    init_dist(args)
     from . import persist
 
     if args.cmd == "save":
@@ -76,6 +127,7 @@ def main(argv=None):
 
         t0 = time.perf_counter()
         eng = LLMEngine(build_engine_config(args))
+        _ENGINES.append(eng)
         st = persist.save(eng, args.archive)
         st["engine_setup_s"] = eng.setup_s
         st["wall_s"] = time.perf_counter() - t0
@@ -84,6 +136,7 @@ def main(argv=None):
 
     if args.cmd == "load":
         eng, timings = persist.load(args.archive)
+        _ENGINES.append(eng)
         # First token of a fresh request through the restored engine.
         g = torch.Generator().manual_seed(args.seed + 7)
         prompt = torch.randint(0, eng.ecfg.model.vocab, (args.prompt_len,), generator=g).tolist()
@@ -104,6 +157,7 @@ def main(argv=None):
 
     if args.cmd == "serve":
         eng, timings = persist.load(args.archive)
+        _ENGINES.append(eng)
         g = torch.Generator().manual_seed(args.seed + 11)
         prompts = torch.randint(0, eng.ecfg.model.vocab, (args.prompts, args.prompt_len), generator=g).tolist()
         t0 = time.perf_counter()

@@ -34,7 +34,7 @@ def test_init_fp8_block_statistics_and_shards():
     assert abs(d.mean().item()) < 1e-3 and abs(d.std().item() - 0.02) < 1e-3
     # scales are amax / 448 of each block
     blocks = d.view(4, 2, 128, 4, 128).abs().amax(dim=(2, 4))
-    torch.testing.assert_close(w.scale, blocks / 448.0, rtol=1e-6, atol=0)
+    torch.testing.assert_close(w.scale[..., :4], blocks / 448.0, rtol=1e-6, atol=0)
     # a shard with row_offset reproduces the corresponding rows of the full matrix
     part = M.Fp8Weight.empty(a, 2, 256, 512)
     M.init_fp8_block_(part, seed=11, std=0.02, row_offset=2 * 256)
@@ -50,12 +50,12 @@ def test_quantize_block_and_rows_match_torch():
     w = M.Fp8Weight.empty(a, 1, 384, 640)
     M.quantize_block_fp8_(wb, w)
     s_ref = wb.float().view(3, 128, 5, 128).abs().amax(dim=(1, 3)) / 448.0
-    torch.testing.assert_close(w.scale[0], s_ref, rtol=1e-6, atol=0)
+    torch.testing.assert_close(w.scale[0, :, :5], s_ref, rtol=1e-6, atol=0)
     torch.testing.assert_close(w.dequant(), wb.float(), rtol=0.07, atol=s_ref.max().item())
     x = torch.randn(37, 1024, device="cuda", generator=g).to(torch.bfloat16)
-    xq = torch.zeros(37, 1024, dtype=torch.uint8, device="cuda")
-    xs = torch.zeros(37, 8, dtype=torch.float32, device="cuda")
-    M.quantize_rows(x, xq, xs)
+    xq, xs_full = M.act_buffers(a, 37, 1024)
+    M.quantize_rows(x, xq, xs_full)
+    xs = xs_full[:37, :8]
     deq_ref, s_ref = _q_rows_ref(x)
     torch.testing.assert_close(xs, s_ref, rtol=1e-6, atol=0)
     deq = (xq.view(torch.float8_e4m3fn).float().view(37, 8, 128) * xs[..., None]).view(37, 1024)
@@ -75,15 +75,14 @@ def test_dense_fp8_gemm_matches_fp32(t, o, k, bn):
     w = M.Fp8Weight.empty(a, 1, o, k)
     M.init_fp8_block_(w, seed=t * 7 + 1, std=0.02)
     x = torch.randn(t, k, device="cuda", generator=g).to(torch.bfloat16)
-    xq = torch.zeros(t, k, dtype=torch.uint8, device="cuda")
-    xs = torch.zeros(t, k // 128, dtype=torch.float32, device="cuda")
+    xq, xs = M.act_buffers(a, t, k)
     chunks = torch.zeros(t // 32 + 1, 4, dtype=torch.int32, device="cuda")
     meta = torch.zeros(4, dtype=torch.int32, device="cuda")
     M.quantize_rows(x, xq, xs)
     M.dense_chunks(t, bn, chunks, meta)
     out = torch.full((t, o), float("nan"), dtype=torch.bfloat16, device="cuda")
     M.gemm_fp8(w, xq, xs, chunks, meta, out, max_units=math.ceil(t / bn) * o // 128, bn=bn)
-    xd = (xq.view(torch.float8_e4m3fn).float().view(t, k // 128, 128) * xs[..., None]).view(t, k)
+    xd = (xq.view(torch.float8_e4m3fn).float().view(t, k // 128, 128) * xs[:t, : k // 128, None]).view(t, k)
     ref = xd @ w.dequant().T
     torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * ref.abs().max().item())
     # residual epilogue
@@ -161,12 +160,12 @@ def test_moe_ffn_pipeline_matches_fp32():
     bn = 32
     pos, counts, chunks, meta = z(p), z(e), z(M.max_chunks(p, e, 32), 4), z(4)
     M.plan(ids, p, e, bn, pos, counts, chunks, meta)
-    mxq, mxs = z(p, h, dt=torch.uint8), z(p, h // 128, dt=torch.float32)
+    mxq, mxs = M.act_buffers(a, p, h)
     M.quantize_rows(x, mxq, mxs, pos=pos, topk=k)
     y13 = z(p, 2 * i, dt=torch.bfloat16)
     units = M.max_chunks(p, e, bn)
     M.gemm_fp8(w13, mxq, mxs, chunks, meta, y13, max_units=units * (2 * i // 128), bn=bn)
-    maq, mas = z(p, i, dt=torch.uint8), z(p, i // 128, dt=torch.float32)
+    maq, mas = M.act_buffers(a, p, i)
     M.silu_mul_quant(y13, p, maq, mas)
     y2 = z(p, h, dt=torch.bfloat16)
     M.gemm_fp8(w2, maq, mas, chunks, meta, y2, max_units=units * (h // 128), bn=bn)
@@ -231,3 +230,43 @@ def test_qwen3_moe_engine_matches_reference_and_graphs():
     assert outs_g == outs
     for img in ("moe", "gemm_bf16", "elementwise", "attention_tc"):
         assert ops.status(img) == 0, img
+
+
+@pytest.mark.parametrize("t,o,k,bn,experts", [(5, 1536, 2048, 32, 1), (64, 2048, 768, 64, 1), (200, 5120, 2048, 128, 1),
+                                               (96, 1536, 2048, 32, 8)])
+def test_w8_gemm_matches_fp32(t, o, k, bn, experts):
+    """Weight-only fp8 GEMM (on-chip dequantisation, bf16 activations), dense and grouped."""
+    from foundry_b200 import ops
+    from foundry_b200.ops import moe as M
+
+    a = _arena()
+    g = torch.Generator(device="cuda").manual_seed(t + o + experts)
+    w = M.Fp8Weight.empty(a, experts, o, k)
+    M.init_fp8_block_(w, seed=t + 3, std=0.02)
+    x = torch.randn(t, k, device="cuda", generator=g).to(torch.bfloat16)
+    meta = torch.zeros(4, dtype=torch.int32, device="cuda")
+    if experts == 1:
+        chunks = torch.zeros(t // 32 + 1, 4, dtype=torch.int32, device="cuda")
+        M.dense_chunks(t, bn, chunks, meta)
+        ids = torch.zeros(t, dtype=torch.long, device="cuda")
+        units = math.ceil(t / bn) * o // 128
+    else:
+        ids32 = torch.randint(0, experts, (t, 1), device="cuda", generator=g).to(torch.int32)
+        pos = torch.zeros(t, dtype=torch.int32, device="cuda")
+        counts = torch.zeros(experts, dtype=torch.int32, device="cuda")
+        chunks = torch.zeros(M.max_chunks(t, experts, 32), 4, dtype=torch.int32, device="cuda")
+        M.plan(ids32, t, experts, bn, pos, counts, chunks, meta)
+        xs = torch.zeros_like(x)
+        M.scatter_rows(x, pos, 1, xs)
+        x, ids = xs, torch.sort(ids32.view(-1).long()).values
+        units = M.max_chunks(t, experts, bn) * o // 128
+    out = torch.full((t, o), float("nan"), dtype=torch.bfloat16, device="cuda")
+    M.gemm_w8(w, x, chunks, meta, out, max_units=units, bn=bn)
+    wd = w.dequant().view(experts, o, k)
+    ref = torch.einsum("tk,tok->to", x.float(), wd[ids])
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2 * ref.abs().max().item())
+    res = torch.randn(t, o, device="cuda", generator=g).to(torch.bfloat16)
+    out2 = res.clone()
+    M.gemm_w8(w, x, chunks, meta, out2, max_units=units, bn=bn, residual=out2)
+    torch.testing.assert_close(out2.float(), ref + res.float(), rtol=1e-2, atol=2e-2 * max(1.0, ref.abs().max().item()))
+    assert ops.status("moe") == 0
