@@ -39,6 +39,11 @@ constexpr int QBLK = 128;       // scale block (tokens: 1 x 128, weights: 128 x 
 constexpr float FP8_MAX = 448.f;
 constexpr int EPI_RESIDUAL = 2;
 constexpr int EPI_W_STREAM = 4;  // weights read once per launch: L2 evict-first
+// Expert-parallel combine fused into the epilogue: row R of the output goes to
+// rank (meta[R] >> 24), row (meta[R] & 0xFFFFFF) of that rank's combine buffer
+// (`out` is the buffer's address in rank 0's window, `residual` the row map,
+// peer_stride the byte distance between rank windows). Plain P2P stores.
+constexpr int EPI_PEER_COMBINE = 32;
 constexpr int MAX_KB = 32;       // K <= 4096
 #ifndef FB_MOE_NBUF
 #define FB_MOE_NBUF 8
@@ -109,7 +114,8 @@ template <int BN>
 __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmX,
                                               const float* __restrict__ w_scale, const float* __restrict__ x_scale,
                                               const int4* __restrict__ chunks, const int* __restrict__ meta,
-                                              bf16* out, const bf16* residual, int O, int K, int ldo, int mode) {
+                                              bf16* out, const bf16* residual, int O, int K, int ldo, int mode,
+                                              long long peer_stride) {
   using C = GemmCfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -303,6 +309,18 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
         break;
       }
       const int o = ob * 128 + quarter * 32 + lane;
+      if (mode & EPI_PEER_COMBINE) {
+        const int* rowmap = reinterpret_cast<const int*>(residual);
+#pragma unroll
+        for (int t = 0; t < BN; ++t) {
+          if (t < ch.z) {
+            const int m = rowmap[ch.y + t];
+            bf16* dst = reinterpret_cast<bf16*>(reinterpret_cast<char*>(out) + static_cast<long long>(m >> 24) * peer_stride);
+            dst[static_cast<size_t>(m & 0xFFFFFF) * ldo + o] = f2bf(acc[t]);
+          }
+        }
+        continue;
+      }
 #pragma unroll
       for (int t = 0; t < BN; ++t) {
         if (t < ch.z) {
@@ -327,8 +345,8 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
   extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_moe_gemm_fp8_bn##BN(                             \
       const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const float* w_scale,       \
       const float* x_scale, const int4* chunks, const int* meta, bf16* out, const bf16* residual, int O, int K,     \
-      int ldo, int mode) {                                                                                           \
-    moe_gemm_body<BN>(&tmW, &tmX, w_scale, x_scale, chunks, meta, out, residual, O, K, ldo, mode);                  \
+      int ldo, int mode, long long peer_stride) {                                                                    \
+    moe_gemm_body<BN>(&tmW, &tmX, w_scale, x_scale, chunks, meta, out, residual, O, K, ldo, mode, peer_stride);     \
   }
 
 FB_MOE_GEMM_INSTANCE(32)
@@ -1033,5 +1051,154 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_scatter_rows(const bf16
     const uint4 v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(t) * lds + c);
     for (int j = 0; j < topk; ++j)
       *reinterpret_cast<uint4*>(dst + static_cast<size_t>(pos[t * topk + j]) * H + c) = v;
+  }
+}
+
+// ==== expert parallelism: counts exchange, plan, fused quantise + dispatch ============
+//
+// Every rank owns experts [rank * El, (rank + 1) * El). Per MoE layer:
+//   fb_ep_count     my pair count per global expert -> counts[rank][:] of every
+//                   rank (P2P stores into symmetric memory); then a barrier
+//   fb_ep_plan      from the full counts matrix: where each of my pairs lands in
+//                   its owner's receive buffer (rows grouped by local expert,
+//                   then source rank, then the source's pair order: a
+//                   deterministic layout), and my own chunk table over the rows
+//                   I will receive
+//   fb_ep_dispatch  quantise each token once (e4m3, per-128 scales) and store
+//                   its row + scales + (source rank, pair) into the owner's
+//                   receive buffer over NVLink; then a barrier
+// The expert GEMMs run on the receive buffer; the down projection's epilogue
+// (EPI_PEER_COMBINE) writes each output row straight into the source rank's
+// combine buffer; after a barrier fb_moe_combine_add_rmsnorm sums the k rows.
+
+extern "C" __global__ void __launch_bounds__(256) fb_ep_count(const int* __restrict__ ids, int P, int E, int rank,
+                                                             int world, unsigned long long base,
+                                                             long long stride, long long counts_off) {
+  __shared__ int cnt[256];
+  for (int e = threadIdx.x; e < E; e += 256) cnt[e] = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += 256) atomicAdd(&cnt[ids[p]], 1);
+  __syncthreads();
+  for (int i = threadIdx.x; i < E * world; i += 256) {
+    const int r = i / E, e = i % E;
+    int* dst = reinterpret_cast<int*>(base + r * stride + counts_off);
+    dst[rank * E + e] = cnt[e];
+  }
+}
+
+// One CTA of 1024 threads. counts: [world][E] (this rank's copy).
+extern "C" __global__ void __launch_bounds__(1024) fb_ep_plan(const int* __restrict__ counts,
+                                                             const int* __restrict__ ids, int P, int E, int El,
+                                                             int rank, int world, int bn, int* __restrict__ dst_row,
+                                                             int4* __restrict__ chunks, int* __restrict__ meta) {
+  __shared__ int tot[256], base[256], before[256], run[256], coff[256];
+  __shared__ int wcnt[32][256];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (E > 256) {
+    if (tid == 0) set_status(FB_KERR_BAD_ARG);
+    return;
+  }
+  for (int e = tid; e < E; e += 1024) {
+    int t = 0, b = 0;
+    for (int r = 0; r < world; ++r) {
+      const int c = counts[r * E + e];
+      t += c;
+      if (r < rank) b += c;
+    }
+    tot[e] = t;
+    before[e] = b;
+    run[e] = 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // receive-side row base of every expert inside its owner's buffer, and
+    // my chunk table over my local experts
+    int nch = 0, rows = 0;
+    for (int e = 0; e < E; ++e) {
+      if (e % El == 0) rows = 0;
+      base[e] = rows;
+      rows += tot[e];
+      if (e / El == rank) {
+        coff[e] = nch;
+        nch += (tot[e] + bn - 1) / bn;
+      }
+    }
+    meta[0] = nch;
+    int mine = 0;
+    for (int le = 0; le < El; ++le) mine += tot[rank * El + le];
+    meta[1] = mine;
+  }
+  __syncthreads();
+  for (int le = tid; le < El; le += 1024) {
+    const int e = rank * El + le, n = tot[e];
+    for (int j = 0, r = 0; r < n; ++j, r += bn) chunks[coff[e] + j] = make_int4(le, base[e] + r, min(bn, n - r), 0);
+  }
+  for (int b0 = 0; b0 < P; b0 += 1024) {
+    for (int i = tid; i < 32 * E; i += 1024) wcnt[i / E][i % E] = 0;
+    __syncthreads();
+    const int p = b0 + tid;
+    const int e = p < P ? ids[p] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rk = __popc(same & ((1u << lane) - 1));
+    if (e >= 0 && rk == 0) wcnt[warp][e] = __popc(same);
+    __syncthreads();
+    for (int x = tid; x < E; x += 1024) {
+      int r0 = run[x];
+      for (int w = 0; w < 32; ++w) {
+        const int c = wcnt[w][x];
+        wcnt[w][x] = r0;
+        r0 += c;
+      }
+      run[x] = r0;
+    }
+    __syncthreads();
+    if (e >= 0) dst_row[p] = base[e] + before[e] + wcnt[warp][e] + rk;
+    __syncthreads();
+  }
+}
+
+// Warp per (token, group of 4 scale blocks): quantise once, store to each of
+// the token's k owners: e4m3 row, padded scale row and the row map entry.
+extern "C" __global__ void __launch_bounds__(256) fb_ep_dispatch(
+    const bf16* __restrict__ x, int ldx, int T, int H, const int* __restrict__ ids, const int* __restrict__ dst_row,
+    int topk, int El, int rank, unsigned long long base, long long stride, long long q_off, long long s_off,
+    long long map_off) {
+  constexpr int BPW = 4;
+  const int nb = H / QBLK, nbp = kb_pad(nb);
+  const int groups = (nb + BPW - 1) / BPW;
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= T * groups) return;
+  const int t = w / groups, g = w % groups, b0 = g * BPW;
+  uint32_t q[BPW];
+  float sc[BPW];
+#pragma unroll
+  for (int i = 0; i < BPW; ++i) {
+    const int b = b0 + i;
+    if (b >= nb) break;
+    const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<size_t>(t) * ldx + b * QBLK + lane * 4);
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const bf162*>(&raw.y));
+    const float am = warp_max(fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y))));
+    const float s = fmaxf(am, 1e-12f) / FP8_MAX;
+    const float inv = 1.f / s;
+    q[i] = pack_e4m3x4(f0.x * inv, f0.y * inv, f1.x * inv, f1.y * inv);
+    sc[i] = s;
+  }
+  for (int j = 0; j < topk; ++j) {
+    const int pidx = t * topk + j;
+    const int owner = ids[pidx] / El;
+    const int row = dst_row[pidx];
+    const unsigned long long win = base + owner * stride;
+    uint32_t* dq = reinterpret_cast<uint32_t*>(win + q_off + static_cast<unsigned long long>(row) * H);
+    float* ds = reinterpret_cast<float*>(win + s_off) + static_cast<size_t>(row) * nbp;
+#pragma unroll
+    for (int i = 0; i < BPW; ++i) {
+      const int b = b0 + i;
+      if (b >= nb) break;
+      dq[b * 32 + lane] = q[i];
+      if (lane == i) ds[b] = sc[i];
+    }
+    if (g == 0 && lane == 0) reinterpret_cast<int*>(win + map_off)[row] = (rank << 24) | pidx;
   }
 }

@@ -130,7 +130,8 @@ class Qwen3MoeWeights:
         for idx, (name, t) in enumerate(self.tensors()):
             s = (seed * 1_000_003 + idx * 7_919) & ((1 << 63) - 1)
             if isinstance(t, M.Fp8Weight):
-                M.init_fp8_block_(t, s, std, row_offset=self.e0 * t.rows)
+                expert = name.endswith(("w13", "w2"))  # expert shards draw their rows of the full matrix
+                M.init_fp8_block_(t, s, std, row_offset=self.e0 * t.rows if expert else 0)
             elif t.dim() == 1:
                 ops.fill_(t, 1.0)
             else:

@@ -34,6 +34,7 @@ _SWIZZLE_128B = 3
 MAX_KB = 32
 EPI_RESIDUAL = 2
 EPI_W_STREAM = 4
+EPI_PEER_COMBINE = 32
 NBUF = 8
 
 
@@ -142,13 +143,19 @@ def dense_chunks(t: int, bn: int, chunks: torch.Tensor, meta: torch.Tensor) -> N
 
 
 def gemm_fp8(w: Fp8Weight, xq: torch.Tensor, xs: torch.Tensor, chunks: torch.Tensor, meta: torch.Tensor,
-             out: torch.Tensor, max_units: int, bn: int = 64, residual: torch.Tensor | None = None,
-             stream_weights: bool = False, prefetch: int = 0) -> torch.Tensor:
+             out: torch.Tensor | int, max_units: int, bn: int = 64, residual: torch.Tensor | None = None,
+             stream_weights: bool = False, prefetch: int = 0, peer_rowmap: torch.Tensor | None = None,
+             peer_stride: int = 0, ldo: int | None = None) -> torch.Tensor | int:
     """Grouped (or, with one expert, dense) block-scaled fp8 GEMM:
     out[r, :rows] = dequant(W[expert(r)]) @ dequant(xq[r]) for every row r of
     every chunk in the table (+ residual). ``max_units`` bounds the chunks x
     row-blocks of any step and sizes the persistent grid. ``stream_weights``
-    hints weight tiles evict-first in L2 (experts whose tiles are read once)."""
+    hints weight tiles evict-first in L2 (experts whose tiles are read once).
+
+    Expert-parallel combine: with ``peer_rowmap`` (int32 per output row:
+    source rank << 24 | row) ``out`` is the address of the combine buffer in
+    rank 0's symmetric window and each row is stored over NVLink into rank
+    ``map >> 24``'s window (``peer_stride`` bytes apart), row ``map & 0xFFFFFF``."""
     if bn not in (32, 64):
         raise ValueError("bn must be 32 or 64")
     if w.cols // QBLK > MAX_KB:
@@ -160,11 +167,15 @@ def gemm_fp8(w: Fp8Weight, xq: torch.Tensor, xs: torch.Tensor, chunks: torch.Ten
     if stream_weights:
         mode |= EPI_W_STREAM
     mode |= (min(prefetch, 15) & 15) << 12
+    if peer_rowmap is not None:
+        mode |= EPI_PEER_COMBINE
+        out_ptr, res_ptr, ld = int(out), peer_rowmap.data_ptr(), int(ldo)
+    else:
+        out_ptr, res_ptr, ld = out.data_ptr(), residual.data_ptr() if residual is not None else 0, out.stride(0)
     grid = max(1, min(max_units, _rt.sm_count()))
     _rt.launch(_IMG, f"fb_moe_gemm_fp8_bn{bn}", (grid,), (192,), [
         fp8_tmap(w.q, 128), fp8_tmap(xq, bn), w.scale.data_ptr(), xs.data_ptr(), chunks.data_ptr(),
-        meta.data_ptr(), out.data_ptr(), residual.data_ptr() if residual is not None else 0, w.rows, w.cols,
-        out.stride(0), mode], smem=gemm_smem(bn))
+        meta.data_ptr(), out_ptr, res_ptr, w.rows, w.cols, ld, mode, int(peer_stride)], smem=gemm_smem(bn))
     return out
 
 

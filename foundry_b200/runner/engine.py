@@ -33,6 +33,7 @@ from ..ops.gemm import MAX_SPLITS, PartialBuffer
 from .arena import Arena
 
 PAGE = 64
+EP_PREFILL_CAP = 2048  # prefill tokens per chunk and rank under expert parallelism (sizes the exchange)
 
 
 def default_graph_sizes(max_batch: int = 1024) -> list[int]:
@@ -64,13 +65,18 @@ class EngineConfig:
 
 
 def _model_buffers(obj, cfg, w, arena, rows) -> None:
-    """Allocates the model family's extra scratch (zeroed: padding rows of a
+    """Allocates the model family's extra scratch and, under expert
+    parallelism, the exchange's per-state scratch (zeroed: padding rows of a
     GEMM tile are read, never NaN bit patterns)."""
     spec = getattr(family(cfg)[2], "buffers", None)
-    if spec is None:
-        return
-    for name, (shape, dtype) in spec(cfg, w, rows).items():
+    items = dict(spec(cfg, w, rows)) if spec is not None else {}
+    ep = getattr(obj, "ep", None)
+    if ep is not None:
+        items.update(ep.buffers(rows))
+    for name, (shape, dtype) in items.items():
         setattr(obj, name, arena.zeros(shape, dtype))
+    if ep is not None:
+        obj.ep_ident.copy_(torch.arange(obj.ep_ident.numel(), dtype=torch.int32))
 
 
 class TPContext:
@@ -99,10 +105,11 @@ class DecodeState:
     """Static device buffers of a decode step for up to max_batch rows
     (per-rank shapes under tensor parallelism)."""
 
-    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, w: LlamaWeights, tp=None):
+    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, w: LlamaWeights, tp=None, ep=None):
         cfg = ecfg.model
         b = ecfg.max_batch
         self.tp = tp
+        self.ep = ep
         nq, nkv = w.nq_l, w.nkv_l
         self.page = PAGE
         self.max_pages = ecfg.pages_per_seq
@@ -141,10 +148,11 @@ class DecodeState:
 class PrefillBatch:
     """Static device buffers of one packed prefill chunk."""
 
-    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, w: LlamaWeights, tp=None):
+    def __init__(self, ecfg: EngineConfig, arena: Arena, k_cache, v_cache, w: LlamaWeights, tp=None, ep=None):
         cfg = ecfg.model
         t, n = ecfg.max_prefill_tokens, ecfg.max_prefill_seqs
         self.tp = tp
+        self.ep = ep
         nq, nkv = w.nq_l, w.nkv_l
         i32 = torch.int32
         self.max_tokens, self.max_seqs = t, n
@@ -221,12 +229,17 @@ class LLMEngine:
         # Order matters: it fixes every device address (SAVE == LOAD).
         _, weights_cls, model_cls = family(cfg)
         kw = {}
+        self.ep = None
         if ecfg.ep > 1:
             import torch.distributed as dist
+
+            from ..parallel.ep import EPContext
 
             if ecfg.tp > 1 or not dist.is_initialized() or dist.get_world_size() != ecfg.ep:
                 raise RuntimeError(f"ep={ecfg.ep} needs tp=1 and an initialised process group of that size")
             kw = {"ep_rank": dist.get_rank(), "ep_size": ecfg.ep}
+            ecfg.max_prefill_tokens = min(ecfg.max_prefill_tokens, EP_PREFILL_CAP)
+            self.ep = EPContext(cfg, max(ecfg.max_batch, ecfg.max_prefill_tokens))
         self.weights = weights_cls(cfg, self.arena, seed=ecfg.seed, init=init_weights, tp_rank=tp_rank,
                                    tp_size=ecfg.tp, **kw)
         nb = ecfg.num_blocks or ecfg.max_batch * ecfg.pages_per_seq
@@ -239,12 +252,14 @@ class LLMEngine:
         self.cos_sin = self.arena.empty((ecfg.max_seq_len, cfg.head_dim // 2, 2), torch.float32)
         self.cos_sin.copy_(ops.rope_cos_sin(ecfg.max_seq_len, cfg.rope_theta, cfg.head_dim,
                                             scaling=cfg.rope_scaling))
-        self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp)
-        self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp)
+        self.state = DecodeState(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp, self.ep)
+        self.prefill_buf = PrefillBatch(ecfg, self.arena, self.k_cache, self.v_cache, self.weights, self.tp, self.ep)
         self.model = model_cls(cfg, self.weights, self.cos_sin)
         self.graph_sizes = sorted(ecfg.graph_sizes or default_graph_sizes(ecfg.max_batch))
         self.graphs: dict[int, object] = {}
-        self.free_pages = list(range(nb - 1, -1, -1))
+        # Under expert parallelism page 0 is kept for the padding prefill
+        # chunks that keep every rank's collective steps in step.
+        self.free_pages = list(range(nb - 1, 0 if self.ep is not None else -1, -1))
         self.rows_free = list(range(ecfg.max_batch - 1, -1, -1))
         self.running: list[Request] = []
         self.h_in = torch.zeros(ecfg.max_batch, dtype=torch.int32, pin_memory=True)
@@ -280,9 +295,11 @@ class LLMEngine:
 
     # ---- prefill -------------------------------------------------------------------------------
     def prefill(self, reqs: list[Request]) -> None:
-        """Prefills requests in packed chunks; appends each request's first token."""
+        """Prefills requests in packed chunks; appends each request's first token.
+        Under expert parallelism every rank runs the same number of chunks
+        (padding with one-token chunks) so the exchange steps line up."""
         pb = self.prefill_buf
-        i = 0
+        chunks, i = [], 0
         while i < len(reqs):
             chunk, ntok = [], 0
             while i < len(reqs) and len(chunk) < pb.max_seqs and ntok + len(reqs[i].prompt) <= pb.max_tokens:
@@ -291,7 +308,21 @@ class LLMEngine:
                 i += 1
             if not chunk:
                 raise ValueError("prompt longer than max_prefill_tokens")
-            self._prefill_chunk(chunk)
+            chunks.append(chunk)
+        n = self._max_over_ranks(len(chunks)) if self.ep is not None else len(chunks)
+        for c in chunks:
+            self._prefill_chunk(c)
+        for _ in range(n - len(chunks)):
+            pad = Request(rid=-1, prompt=[0], max_new_tokens=1, pages=[0])
+            self._prefill_chunk([pad])
+
+    def _max_over_ranks(self, v: int) -> int:
+        import torch.distributed as dist
+
+        dev = self.device if dist.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([v], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return int(t.item())
 
     def _prefill_chunk(self, chunk: list[Request]) -> None:
         pb = self.prefill_buf
@@ -385,7 +416,10 @@ class LLMEngine:
         reqs = self.add_requests(prompts, max_new_tokens)
         self.prefill(reqs)
         b = self.start_decode(reqs)
-        while not all(r.done for r in reqs):
+        steps = max_new_tokens - 1
+        if self.ep is not None:  # every rank takes the same decode steps (and graph sizes stay per rank)
+            steps = self._max_over_ranks(steps)
+        for _ in range(steps):
             toks = self.decode_step(b)
             for r in reqs:
                 if not r.done:
@@ -426,3 +460,6 @@ class LLMEngine:
         if self.tp is not None:
             self.tp.close()
             self.tp = None
+        if self.ep is not None:
+            self.ep.close()
+            self.ep = None

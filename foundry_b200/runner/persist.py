@@ -51,7 +51,7 @@ def _layout_fingerprint(eng: LLMEngine) -> dict:
         "k_cache0_ptr": eng.k_cache[0].data_ptr(),
         "arena_used": eng.arena.used,
         "final_alloc_offset": core().get_current_alloc_offset(),
-        "symm": eng.tp.symm.layout() if eng.tp is not None else None,
+        "symm": (eng.tp or eng.ep).symm.layout() if (eng.tp or eng.ep) is not None else None,
     }
 
 
@@ -70,8 +70,8 @@ def rank_dir(archive: str) -> str:
 def save(eng: LLMEngine, archive: str) -> dict:
     """Captures (if needed) and writes every decode graph of ``eng``; a
     tensor-parallel engine writes its rank's graphs under ``rank_<r>``."""
-    if eng.ecfg.tp > 1:
-        archive = os.path.join(archive, f"rank_{eng.tp.rank}")
+    if eng.ecfg.tp > 1 or eng.ecfg.ep > 1:
+        archive = os.path.join(archive, f"rank_{(eng.tp or eng.ep).rank}")
     os.makedirs(archive, exist_ok=True)
     t0 = time.perf_counter()
     capture_s = 0.0
