@@ -125,7 +125,13 @@ class ClockSampler:
 
 
 def run_cli(cmd: list[str], env_extra: dict | None = None, timeout: int = 1800) -> dict:
-    env = dict(os.environ)
+    # The runner gets its rank and rendezvous from its own arguments; the
+    # launcher's variables (TORCHELASTIC_USE_AGENT_STORE in particular, which
+    # makes rank 0 join the agent's store instead of hosting one) must not leak.
+    env = {k: v for k, v in os.environ.items()
+           if not k.startswith(("TORCHELASTIC_", "TORCH_ELASTIC")) and k not in (
+               "RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK", "ROLE_WORLD_SIZE",
+               "MASTER_ADDR", "MASTER_PORT", "GROUP_WORLD_SIZE", "ROLE_NAME")}
     env.update(env_extra or {})
     env["PYTHONPATH"] = ROOT + os.pathsep + env.get("PYTHONPATH", "")
     res = subprocess.run([sys.executable, "-m", "foundry_b200.runner.cli", *cmd], env=env, capture_output=True,
@@ -158,20 +164,27 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     gen = max(args.gen, 1 + args.warmup + 2 * args.steps + 2)
+    mode = args.parallel if world > 1 else "dp"
+    port = int(os.environ.get("MASTER_PORT", 29500))
     workdir = args.workdir or f"/tmp/foundry_bench_{os.environ.get('MASTER_PORT', os.getpid())}"
-    archive = os.path.join(workdir, f"rank_{rank}")
+    # dp: independent engines, one archive per rank; tp / ep: one multi-rank
+    # engine whose archive holds a rank_<r> folder per rank
+    archive = os.path.join(workdir, f"rank_{rank}") if mode == "dp" else workdir
     common = ["--archive", archive, "--model", args.model, "--prompts", str(args.batch), "--prompt-len",
               str(args.prompt_len), "--gen", str(gen), "--device", str(local), "--graph-sizes", args.graph_sizes,
               "--region-size", args.region_size]
+    if mode in ("tp", "ep"):
+        common += [f"--{mode}", str(world), "--rank", str(rank), "--world", str(world)]
 
-    # 1) SAVE in a fresh process: capture the 67 decode graphs and write the archive.
+    # 1) SAVE in a fresh process: capture the decode graphs and write the archive.
     t0 = time.perf_counter()
-    save_info = run_cli(["save", *common])["save"]
+    save_info = run_cli(["save", *common, "--dist-port", str(port + 17)])["save"]
     save_wall = time.perf_counter() - t0
     # 2) LOAD in a fresh process: cold start (spawn -> first token) and restore time.
     cold = {}
     if not args.skip_cold_start:
-        cold = run_cli(["load", *common], {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns())})["load"]
+        cold = run_cli(["load", *common, "--dist-port", str(port + 19)],
+                       {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns())})["load"]
 
     # 3) This process restores the archive and runs the timed decode.
     from foundry_b200 import ops
@@ -179,7 +192,7 @@ def main():
 
     eng, restore = persist.load(archive)
     cfg = eng.ecfg.model
-    g = torch.Generator().manual_seed(1234 + rank)
+    g = torch.Generator().manual_seed(1234 + (0 if mode == "tp" else rank))
     prompts = torch.randint(0, cfg.vocab, (args.batch, args.prompt_len), generator=g).tolist()
     reqs = eng.add_requests(prompts, max_new_tokens=gen)
     torch.cuda.synchronize()
@@ -232,7 +245,8 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
     dev_ms, e2e_ms = t.tolist()
-    tokens = n_active * world * args.steps
+    seq_ranks = 1 if mode == "tp" else world  # tp ranks share one batch of sequences
+    tokens = n_active * seq_ranks * args.steps
     value = tokens / (dev_ms / 1e3)
     e2e = tokens / (e2e_ms / 1e3)
     if rank == 0:
@@ -245,13 +259,13 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": round(dev_ms / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if mode == "tp" else "weak",
             "vs_baseline": None,
             "dtype": "fp8-block (e4m3, 128x128 fp32 scales) + bf16" if "qwen3" in args.model else "bf16",
             "data": "synthetic (uniform random prompt token ids, random-init N(0,0.02) weights)",
             "config": {
-                "model": args.model, "global_batch": n_active * world, "seq_len": args.prompt_len + gen,
-                "prompt_len": args.prompt_len, "gen_len": args.gen, "parallelism": f"dp{world}",
+                "model": args.model, "global_batch": n_active * seq_ranks, "seq_len": args.prompt_len + gen,
+                "prompt_len": args.prompt_len, "gen_len": args.gen, "parallelism": f"{mode}{world}",
                 "decode_batch_per_gpu": b, "graphs_per_rank": restore["num_graphs"],
                 "topology_groups": restore["num_groups"],
                 "l2": "inputs larger than L2 (all weights + the KV cache are read every step)",
@@ -273,7 +287,7 @@ def main():
             },
         }
         print(json.dumps(out))
-    eng.graphs.clear()
+    eng.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
