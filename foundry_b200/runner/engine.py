@@ -310,8 +310,11 @@ class LLMEngine:
                 raise ValueError("prompt longer than max_prefill_tokens")
             chunks.append(chunk)
         n = self._max_over_ranks(len(chunks)) if self.ep is not None else len(chunks)
-        for c in chunks:
-            self._prefill_chunk(c)
+        from ..utils.trace import phase
+
+        with phase("foundry.prefill"):
+            for c in chunks:
+                self._prefill_chunk(c)
         for _ in range(n - len(chunks)):
             pad = Request(rid=-1, prompt=[0], max_new_tokens=1, pages=[0])
             self._prefill_chunk([pad])

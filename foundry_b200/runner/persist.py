@@ -23,6 +23,7 @@ import torch
 
 from .. import core, load_cuda_modules_and_libraries, pack_fatbins_to_folder
 from ..graphs import CUDAGraph, save_graph_manifest
+from ..utils.trace import phase
 from ..models import config_from_dict
 from .engine import EngineConfig, LLMEngine
 
@@ -76,7 +77,8 @@ def save(eng: LLMEngine, archive: str) -> dict:
     t0 = time.perf_counter()
     capture_s = 0.0
     if not eng.graphs:
-        capture_s = eng.capture_graphs()
+        with phase("foundry.save.capture"):
+            capture_s = eng.capture_graphs()
     t1 = time.perf_counter()
     paths = []
     for i, s in enumerate(eng.graph_sizes):
@@ -106,9 +108,11 @@ def load(archive: str, init_weights: bool = True, num_threads: int = 8) -> tuple
         state = json.load(f)
     ecfg = engine_config_from_dict(state["engine"])
     torch.cuda.init()
-    load_cuda_modules_and_libraries(archive)
+    with phase("foundry.load.modules"):
+        load_cuda_modules_and_libraries(archive)
     t_mod = time.perf_counter()
-    eng = LLMEngine(ecfg, init_weights=False)
+    with phase("foundry.load.engine_layout"):
+        eng = LLMEngine(ecfg, init_weights=False)
     lay = _layout_fingerprint(eng)
     for k in ("embed_ptr", "state_ptr", "k_cache0_ptr", "arena_used"):
         if lay[k] != state["layout"][k]:
@@ -117,10 +121,13 @@ def load(archive: str, init_weights: bool = True, num_threads: int = 8) -> tuple
         raise RuntimeError(f"symmetric-memory layout differs from SAVE: {lay['symm']} vs {state['layout'].get('symm')}")
     t_arena = time.perf_counter()
     paths = [os.path.join(archive, f"graph_{i}.json") for i in range(len(state["graph_sizes"]))]
-    pending = CUDAGraph.start_graph_builds(paths, num_threads=num_threads)
+    with phase("foundry.load.start_graph_builds"):
+        pending = CUDAGraph.start_graph_builds(paths, num_threads=num_threads)
     if init_weights:
-        eng.init_weights()  # GPU work overlaps the background template builds
-    loaded = CUDAGraph.finish_graph_loads(pending)
+        with phase("foundry.load.init_weights"):
+            eng.init_weights()  # GPU work overlaps the background template builds
+    with phase("foundry.load.finish_graph_loads"):
+        loaded = CUDAGraph.finish_graph_loads(pending)
     for s, (g, _) in zip(state["graph_sizes"], loaded):
         eng.graphs[s] = g
     t_done = time.perf_counter()

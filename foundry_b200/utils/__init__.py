@@ -1,0 +1,1 @@
+"""Utilities: tracing."""
