@@ -1,0 +1,161 @@
+"""vLLM (V1 engine, 0.22) integration: persist the engine's CUDA graphs.
+
+``install_hooks(config)`` patches, in the current process:
+
+  CUDAGraphWrapper.__call__        capture -> foundry capture + save (SAVE) or
+                                   restore (LOAD) keyed by the batch descriptor
+  Worker.init_device               after the device/communicator init: LOAD
+                                   loads the packed modules, both modes enable
+                                   the region and skip the scratch space
+  Worker.determine_available_memory  SAVE records the KV-cache budget, LOAD
+                                   reuses it (re-profiling could size the KV
+                                   cache differently and move every address)
+  kernel_warmup (gpu_worker)       skipped on LOAD (its kernels are restored)
+  GPUModelRunner.capture_model     LOAD: start all graph builds first; SAVE:
+                                   manifest + packed modules + final offset
+
+Spawned engine processes install the same hooks through the
+``_site/sitecustomize.py`` shim when FOUNDRY_GRAPH_CONFIG names the TOML file
+(``python -m foundry_b200.integration.vllm.serve`` sets it up).
+
+Parity: reference python/foundry/integration/vllm/hooks.py:85-706 (10 patches
+against foundry-org's vLLM fork); these target upstream vLLM.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+
+from .. import graph_ops, runtime
+from ..config import GraphExtensionConfig, GraphExtensionMode, global_rank
+
+log = logging.getLogger("foundry")
+
+_originals: dict = {}
+
+
+def _targets():
+    import vllm.compilation.cuda_graph as cg
+    import vllm.v1.worker.gpu_model_runner as mr
+    import vllm.v1.worker.gpu_worker as gw
+
+    return cg, gw, mr
+
+
+def _wrapper_call(self, *args, **kwargs):
+    from vllm.compilation.cuda_graph import CUDAGraphEntry
+    from vllm.config import CUDAGraphMode
+    from vllm.forward_context import get_forward_context, is_forward_context_available
+
+    if runtime.mode() == GraphExtensionMode.NONE:
+        return _originals["CUDAGraphWrapper.__call__"](self, *args, **kwargs)
+    if not is_forward_context_available():
+        return self.runnable(*args, **kwargs)
+    fc = get_forward_context()
+    bd, rm = fc.batch_descriptor, fc.cudagraph_runtime_mode
+    if rm == CUDAGraphMode.NONE or rm != self.runtime_mode:
+        return self.runnable(*args, **kwargs)
+    entry = self.concrete_cudagraph_entries.get(bd)
+    if entry is None:
+        entry = self.concrete_cudagraph_entries[bd] = CUDAGraphEntry(batch_descriptor=bd)
+    if entry.cudagraph is None:
+        pc = getattr(self.runnable, "piecewise_compile_index", None) if rm == CUDAGraphMode.PIECEWISE else None
+        key = graph_ops.GraphKey(rm.name, bd.num_tokens, bd.num_reqs, bool(bd.uniform), bool(bd.has_lora), pc)
+        import torch
+
+        g, out = graph_ops.capture_or_load(key, self.runnable, args, kwargs, pool=self.graph_pool,
+                                           stream=torch.cuda.current_stream())
+        entry.cudagraph = g
+        entry.output = out
+        return out
+    entry.cudagraph.replay()
+    return entry.output
+
+
+def _init_device(self, *a, **k):
+    r = _originals["Worker.init_device"](self, *a, **k)
+    cfg = _config
+    pc = self.vllm_config.parallel_config
+    grank = global_rank(self.rank, pc.world_size, getattr(pc, "data_parallel_rank", 0) or 0)
+    runtime.setup_graph_extension(cfg, grank)
+    if cfg.mode != GraphExtensionMode.NONE:
+        runtime.skip_to_scratch_boundary()
+    return r
+
+
+def _determine_available_memory(self, *a, **k):
+    st = runtime.state()
+    if st is None or st.config.mode == GraphExtensionMode.NONE:
+        return _originals["Worker.determine_available_memory"](self, *a, **k)
+    ws = st.config.workspace_dir
+    if st.config.mode == GraphExtensionMode.LOAD:
+        saved = runtime.WarmupState.load(ws)
+        if saved is not None and "available_memory" in saved.extra:
+            return int(saved.extra["available_memory"])
+    v = _originals["Worker.determine_available_memory"](self, *a, **k)
+    if st.config.mode == GraphExtensionMode.SAVE:
+        runtime.WarmupState(extra={"available_memory": int(v)}).save(ws)
+    return v
+
+
+def _kernel_warmup(worker, *a, **k):
+    if runtime.mode() == GraphExtensionMode.LOAD:
+        return None
+    return _originals["kernel_warmup"](worker, *a, **k)
+
+
+def _capture_model(self, *a, **k):
+    st = runtime.state()
+    if st is not None and st.config.mode == GraphExtensionMode.LOAD:
+        graph_ops.start_graph_builds(st.config.workspace_dir)
+    r = _originals["GPUModelRunner.capture_model"](self, *a, **k)
+    if st is not None and st.config.mode == GraphExtensionMode.SAVE:
+        graph_ops.finalize_save()
+    if st is not None and st.config.mode != GraphExtensionMode.NONE:
+        runtime.capture_final_alloc_offset()
+    return r
+
+
+_config: GraphExtensionConfig | None = None
+
+
+def install_hooks(config: GraphExtensionConfig | str) -> None:
+    """Patches vLLM in this process (idempotent)."""
+    global _config
+    if isinstance(config, (str, os.PathLike)):
+        config = GraphExtensionConfig.from_toml(config)
+    _config = config
+    if _originals:
+        return
+    cg, gw, mr = _targets()
+    _originals["CUDAGraphWrapper.__call__"] = cg.CUDAGraphWrapper.__call__
+    _originals["Worker.init_device"] = gw.Worker.init_device
+    _originals["Worker.determine_available_memory"] = gw.Worker.determine_available_memory
+    _originals["kernel_warmup"] = gw.kernel_warmup
+    _originals["GPUModelRunner.capture_model"] = mr.GPUModelRunner.capture_model
+    cg.CUDAGraphWrapper.__call__ = _wrapper_call
+    gw.Worker.init_device = _init_device
+    gw.Worker.determine_available_memory = _determine_available_memory
+    gw.kernel_warmup = _kernel_warmup
+    mr.GPUModelRunner.capture_model = _capture_model
+    log.info("[foundry] vLLM hooks installed (mode %s)", config.mode.value)
+
+
+def uninstall_hooks() -> None:
+    if not _originals:
+        return
+    cg, gw, mr = _targets()
+    cg.CUDAGraphWrapper.__call__ = _originals.pop("CUDAGraphWrapper.__call__")
+    gw.Worker.init_device = _originals.pop("Worker.init_device")
+    gw.Worker.determine_available_memory = _originals.pop("Worker.determine_available_memory")
+    gw.kernel_warmup = _originals.pop("kernel_warmup")
+    mr.GPUModelRunner.capture_model = _originals.pop("GPUModelRunner.capture_model")
+    runtime.reset()
+
+
+def installed() -> bool:
+    return bool(_originals)
+
+
+__all__ = ["install_hooks", "installed", "uninstall_hooks"]

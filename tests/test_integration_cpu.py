@@ -1,0 +1,102 @@
+"""Engine integrations on CPU: TOML config, archive file naming, the region
+setup / scratch skip / final-offset check on the mock driver, and the vLLM
+hooks being installable and removable against the installed vLLM."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+MOCK = os.path.join(ROOT, "foundry_b200", "lib", "libfoundry_mockcuda.so")
+
+
+def test_config_from_toml(tmp_path):
+    from foundry_b200.integration.config import GraphExtensionConfig, GraphExtensionMode, global_rank
+
+    p = tmp_path / "c.toml"
+    p.write_text('mode = "save"\nbase_addr = "0x610000000000"\nregion_size = "8GB"\n'
+                 'workspace_root = "arch"\nscratch_space_size = "32MB"\n')
+    c = GraphExtensionConfig.from_toml(p)
+    assert c.mode == GraphExtensionMode.SAVE and c.base_addr == 0x610000000000
+    assert c.workspace_for(global_rank(1, 2, dp_rank=1)) == os.path.join("arch", "rank_3")
+    assert GraphExtensionConfig.from_dict({}).mode == GraphExtensionMode.NONE
+    with pytest.raises(ValueError):
+        GraphExtensionConfig.from_dict({"mode": "save", "bogus": 1})
+    with pytest.raises(ValueError):
+        GraphExtensionConfig.from_dict({"mode": "frobnicate"})
+    with pytest.raises(ValueError):
+        GraphExtensionConfig.from_dict({"region_size": "1GB", "scratch_space_size": "2GB"})
+    recipes = os.path.join(ROOT, "foundry_b200", "integration", "vllm", "recipes")
+    assert GraphExtensionConfig.from_toml(os.path.join(recipes, "foundry_load.toml")).mode == GraphExtensionMode.LOAD
+
+
+def test_graph_filename_codec():
+    from foundry_b200.integration.graph_ops import GraphKey, parse_filename
+
+    keys = [GraphKey("FULL", 256, 256, True, False, None), GraphKey("PIECEWISE", 8, None, False, True, 3),
+            GraphKey("FULL_DECODE_ONLY", 1, 1, True, False, None)]
+    for i, k in enumerate(keys):
+        name = k.filename(i)
+        assert parse_filename(name) == (i, k)
+    assert keys[0].filename(7) == "graph_7_FULL_t256_r256_UX_pcN.json"
+    assert parse_filename("graph_manifest.json") is None
+
+
+RUNTIME = r"""
+import json, os, sys
+sys.path.insert(0, ROOT)
+from foundry_b200 import core, get_current_alloc_offset
+from foundry_b200.integration import runtime
+from foundry_b200.integration.config import GraphExtensionConfig
+ws = os.path.join(TMP, "arch")
+cfg = GraphExtensionConfig.from_dict({"mode": "save", "region_size": "1GB", "scratch_space_size": "64MB",
+                                      "workspace_root": ws, "base_addr": "0x600000000000"})
+runtime.setup_graph_extension(cfg, 0)
+assert runtime.skip_to_scratch_boundary() == 64 << 20
+assert get_current_alloc_offset() == 64 << 20
+p = core().region_alloc(4 << 20)
+assert p >= 0x600000000000 + (64 << 20)
+off = runtime.capture_final_alloc_offset()
+assert json.load(open(os.path.join(ws, "rank_0", "final_alloc_offset.json")))["final_alloc_offset"] == off
+env = runtime.ld_preload_env({"LD_PRELOAD": "/x.so"})
+assert env["LD_PRELOAD"].split(":")[-1] == "/x.so" and "libfoundry_hook.so" in env["LD_PRELOAD"]
+print("RUNTIME_OK")
+"""
+
+
+def test_runtime_region_scratch_and_final_offset_on_mock(tmp_path):
+    env = dict(os.environ, FOUNDRY_CUDA_DRIVER=MOCK, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="")
+    code = f"ROOT={ROOT!r}; TMP={str(tmp_path)!r}\n" + RUNTIME
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=180)
+    assert r.returncode == 0 and "RUNTIME_OK" in r.stdout, r.stdout + r.stderr[-3000:]
+
+
+VLLM_HOOKS = r"""
+import sys
+sys.path.insert(0, ROOT)
+import vllm.compilation.cuda_graph as cg
+import vllm.v1.worker.gpu_worker as gw
+import vllm.v1.worker.gpu_model_runner as mr
+orig = (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, mr.GPUModelRunner.capture_model)
+from foundry_b200.integration.vllm import install_hooks, installed, uninstall_hooks
+from foundry_b200.integration.config import GraphExtensionConfig
+install_hooks(GraphExtensionConfig.from_dict({"mode": "save"}))
+assert installed()
+assert cg.CUDAGraphWrapper.__call__ is not orig[0] and gw.Worker.init_device is not orig[1]
+assert gw.kernel_warmup is not orig[2] and mr.GPUModelRunner.capture_model is not orig[3]
+uninstall_hooks()
+assert (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup,
+        mr.GPUModelRunner.capture_model) == orig
+print("HOOKS_OK")
+"""
+
+
+def test_vllm_hooks_install_and_uninstall():
+    pytest.importorskip("vllm")
+    env = dict(os.environ, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, "-c", f"ROOT={ROOT!r}\n" + VLLM_HOOKS], env=env, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and "HOOKS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]
