@@ -175,6 +175,42 @@ def build_noalloc(force=False) -> Path:
     return out
 
 
+def build_tsan(dest: Path) -> Path:
+    """ThreadSanitizer build of the host libraries (hook, mock driver, _C) in a
+    copy of the Python package under ``dest`` (race detection of the region,
+    registry and parallel-restore threads on the mock driver; run the copy
+    with LD_PRELOAD of libtsan). Returns the folder to put on PYTHONPATH."""
+    import pybind11
+
+    dest = Path(dest)
+    pkg = dest / "foundry_b200"
+    if pkg.exists():
+        shutil.rmtree(pkg)
+    shutil.copytree(PKG, pkg, ignore=shutil.ignore_patterns("*.so", "*.stamp", "__pycache__", "kernels", "*.tmp"))
+    (pkg / "lib").mkdir(exist_ok=True)
+    tsan = ["-fsanitize=thread", "-g", "-O1", "-fno-omit-frame-pointer"]
+    flags = [f for f in CXXFLAGS if f != "-O2"] + tsan
+    hook_srcs = sorted((CSRC / "hook").glob("*.cpp"))
+    _run(["g++", *flags, "-shared", *map(str, hook_srcs), "-o", str(pkg / "lib" / "libfoundry_hook.so"), "-ldl",
+          "-lpthread"])
+    _run(["g++", *flags, "-shared", str(CSRC / "mockcuda" / "mock_cuda.cpp"), "-o",
+          str(pkg / "lib" / "libfoundry_mockcuda.so"), "-ldl", "-lpthread"])
+    inc = [f"-I{sysconfig.get_paths()['include']}", f"-I{pybind11.get_include()}"]
+    objdir = dest / "obj"
+    objdir.mkdir(parents=True, exist_ok=True)
+
+    def compile_one(src: Path) -> Path:
+        obj = objdir / (src.stem + ".o")
+        _run(["g++", *flags, *inc, "-c", str(src), "-o", str(obj)])
+        return obj
+
+    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(compile_one, sorted((CSRC / "core").glob("*.cpp"))))
+    _run(["g++", *tsan, "-shared", *map(str, objs), "-o", str(pkg / f"_C{ext_suffix()}"), f"-L{pkg / 'lib'}",
+          "-lfoundry_hook", "-Wl,-rpath,$ORIGIN/lib", "-ldl", "-lpthread"])
+    return dest
+
+
 def build_all(force=False, kernels=True) -> None:
     build_hook(force)
     build_mock(force)

@@ -20,14 +20,18 @@ import random
 import struct
 import sys
 
-BASE = 0x600000000000
+# FOUNDRY_TEST_REGION_BASE moves the region (ThreadSanitizer reserves the
+# default 0x600000000000 range for itself)
+BASE = int(os.environ.get("FOUNDRY_TEST_REGION_BASE", "0x600000000000"), 0)
 REGION = 64 << 30
 N_GRAPHS, N_GROUPS, CHAIN, N_ARGS = 64, 4, 32, 8
 PARAM_SIZES = [8, 8, 8, 4, 4, 16, 8, 32]  # 8 args: pointers and seeded random bytes
 
 
 def _core():
-    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    # FOUNDRY_PKG_ROOT selects another build of the package (e.g. the
+    # ThreadSanitizer build); default: this repository
+    sys.path.insert(0, os.environ.get("FOUNDRY_PKG_ROOT") or os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import foundry_b200 as fb
 
     c = fb.core()
