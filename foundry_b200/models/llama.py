@@ -76,6 +76,13 @@ def toy() -> LlamaConfig:
 
 CONFIGS = {"llama-3-8b": llama3_8b, "llama-3-70b": llama3_70b}
 
+# Tensor parallel: row counts from which the row-parallel GEMM outputs are
+# summed by an NVLS reduce-scatter + multicast instead of the slot exchange.
+NVLS_MIN_ROWS = 128
+# "auto": NVLS for >= NVLS_MIN_ROWS rows on more than 2 ranks (at 2 ranks one
+# slot copy is all the exchange moves anyway); "nvls": also at 2 ranks (tests)
+_TP_REDUCE = __import__("os").environ.get("FOUNDRY_TP_REDUCE", "auto")
+
 
 class LlamaWeights:
     """All parameters (this rank's tensor-parallel shard), allocated from an
@@ -245,6 +252,12 @@ class LlamaModel:
             from ..parallel import comm
 
             ex = st.tp.slots
+            if rows >= NVLS_MIN_ROWS and ex.symm.multicast and (ex.symm.world > 2 or _TP_REDUCE == "nvls"):
+                # many rows: partial sums reduced in the switch (one copy of the
+                # output crosses NVLink per rank instead of world - 1)
+                ops.linear(inp, weight, out=ex.slot(which, 0)[:rows])
+                ex.nvls_reduce(which, rows)
+                return ("reduced", which)
             target = ex.gemm_target(which)
             if target:
                 ops.linear_multicast(inp, weight, target)
@@ -265,7 +278,10 @@ class LlamaModel:
         elif isinstance(pending, tuple):
             from ..parallel import comm
 
-            comm.add_rmsnorm_slots(st.tp.slots.local_slots(pending[1]), rows, h, weight, x, self.cfg.eps)
+            slots = st.tp.slots.local_slots(pending[1])
+            if pending[0] == "reduced":
+                slots = slots[1:2]  # the reduced sum
+            comm.add_rmsnorm_slots(slots, rows, h, weight, x, self.cfg.eps)
         else:
             ops.add_rmsnorm_partials(pending, h, weight, x, self.cfg.eps)
 

@@ -82,6 +82,26 @@ class SlotExchange:
     def local_slot(self, which: int) -> torch.Tensor:
         return self.local_slots(which)[self.symm.rank]
 
+    def slot(self, which: int, i: int) -> torch.Tensor:
+        """Slot ``i`` of buffer ``which`` in this rank's memory ([rows, cols])."""
+        return self.local_slots(which)[i]
+
+    def nvls_reduce(self, which: int, rows: int) -> None:
+        """Large-row alternative to the slot exchange (same buffers): every rank
+        has written its partial GEMM output into slot 0 of buffer ``which`` (the
+        same offset on every rank); after a barrier each rank reduces 1/world
+        of it in the switch (multimem.ld_reduce, fp32 accumulation) and
+        multicasts the sum into slot 1 of every rank; a second barrier makes
+        slot 1 complete everywhere. NVLink ingress per rank: one copy of the
+        output instead of world - 1 copies."""
+        s = self.symm
+        n = rows * self.cols
+        barrier(s)
+        mc_in = s.mc_ptr + self._buf_off(which)
+        _rt.launch(_IMG, "fb_allreduce_nvls_bf16", (min(132, max(1, math.ceil(n / 8 / 256))),), (256,),
+                   [mc_in, mc_in + self.slot_bytes, n, s.rank, s.world])
+        barrier(s)
+
     def broadcast_local_slot(self, which: int, rows: int) -> None:
         """No-multicast fallback: copy this rank's slot to every rank over P2P."""
         s = self.symm

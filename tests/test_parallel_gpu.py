@@ -54,33 +54,36 @@ if s.multicast:
     comm.all_reduce(s, off, x.numel(), out2, algo="nvls")
     torch.testing.assert_close(out2.float(), ref, atol=3e-2 * W, rtol=2e-2)
     comm.barrier(s)
-# 3) fused GEMM -> multicast slots -> add + RMSNorm (row-parallel layer)
-T, H, Kr = 64, 1024, 512
-ex = comm.SlotExchange(s, CTRL_BYTES + (16 << 20), T, H)
-gw = torch.Generator(device="cuda").manual_seed(7)
-xs = [torch.randn(T, Kr, device="cuda", generator=gw).to(torch.bfloat16) for _ in range(W)]
-ws = [(torch.randn(H, Kr, device="cuda", generator=gw) * 0.05).to(torch.bfloat16) for _ in range(W)]
-h0 = torch.randn(T, H, device="cuda", generator=gw).to(torch.bfloat16)
-nw = torch.randn(H, device="cuda", generator=gw).to(torch.bfloat16)
-tgt = ex.gemm_target(0)
-if tgt:
-    ops.linear_multicast(xs[R], ws[R], tgt)
-else:
-    ops.linear(xs[R], ws[R], out=ex.local_slot(0)[:T])
-    ex.broadcast_local_slot(0, T)
-comm.barrier(s)
-h = h0.clone(); xo = torch.empty_like(h)
-comm.add_rmsnorm_slots(ex.local_slots(0), T, h, nw, xo, 1e-5)
-part = [(xs[r].float() @ ws[r].float().T).to(torch.bfloat16).float() for r in range(W)]
-href = (sum(part) + h0.float())
-torch.testing.assert_close(h.float(), href, atol=6e-2, rtol=2e-2)
-hf = h.float()
-torch.testing.assert_close(xo.float(), hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * nw.float(), atol=3e-2, rtol=2e-2)
+# 3) fused GEMM -> multicast slots -> add + RMSNorm (row-parallel layer);
+#    T = 64 runs the swap-AB (transposed) epilogue, T = 320 the row-major one
+for which, T in ((0, 64), (1, 320)):
+    H, Kr = 1024, 512
+    ex = comm.SlotExchange(s, CTRL_BYTES + (16 << 20), 320, H)
+    gw = torch.Generator(device="cuda").manual_seed(7 + T)
+    xs = [torch.randn(T, Kr, device="cuda", generator=gw).to(torch.bfloat16) for _ in range(W)]
+    ws = [(torch.randn(H, Kr, device="cuda", generator=gw) * 0.05).to(torch.bfloat16) for _ in range(W)]
+    h0 = torch.randn(T, H, device="cuda", generator=gw).to(torch.bfloat16)
+    nw = torch.randn(H, device="cuda", generator=gw).to(torch.bfloat16)
+    tgt = ex.gemm_target(which)
+    if tgt:
+        ops.linear_multicast(xs[R], ws[R], tgt)
+    else:
+        ops.linear(xs[R], ws[R], out=ex.local_slot(which)[:T])
+        ex.broadcast_local_slot(which, T)
+    comm.barrier(s)
+    h = h0.clone(); xo = torch.empty_like(h)
+    comm.add_rmsnorm_slots(ex.local_slots(which), T, h, nw, xo, 1e-5)
+    part = [(xs[r].float() @ ws[r].float().T).to(torch.bfloat16).float() for r in range(W)]
+    href = (sum(part) + h0.float())
+    torch.testing.assert_close(h.float(), href, atol=6e-2, rtol=2e-2)
+    hf = h.float()
+    torch.testing.assert_close(xo.float(), hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * nw.float(), atol=3e-2, rtol=2e-2)
+    comm.barrier(s)
 # 4) vocab-sharded greedy argmax
 V = 4000
 full = torch.randn(T, V * W, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9)).to(torch.bfloat16)
 ids = torch.empty(T, dtype=torch.int32, device="cuda")
-comm.argmax_sharded(s, full[:, R * V:(R + 1) * V].contiguous(), R * V, CTRL_BYTES + (64 << 20), ids)
+comm.argmax_sharded(s, full[:, R * V:(R + 1) * V].contiguous(), R * V, CTRL_BYTES + (128 << 20), ids)
 assert torch.equal(ids.long(), full.float().argmax(-1)), (ids[:8], full.float().argmax(-1)[:8])
 for img in ("comm", "gemm_bf16"):
     assert ops.status(img) == 0, img

@@ -126,7 +126,9 @@ def _free_port():
 
 def _run_ranks(body, world, archive):
     port = _free_port()
-    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0")
+    # FOUNDRY_TP_REDUCE=nvls: prefill rows (>= 128) take the NVLS reduce path
+    # even at 2 ranks, decode rows the multicast slot exchange
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", FOUNDRY_TP_REDUCE="nvls")
     procs = []
     for rank in range(world):
         code = f"ROOT={ROOT!r}; PORT={port}; RANK={rank}; WORLD={world}; ARCHIVE={archive!r}\n" + body
