@@ -79,6 +79,7 @@ CONFIGS = {"llama-3-8b": llama3_8b, "llama-3-70b": llama3_70b}
 # Tensor parallel: row counts from which the row-parallel GEMM outputs are
 # summed by an NVLS reduce-scatter + multicast instead of the slot exchange.
 NVLS_MIN_ROWS = 128
+NVLS_MIN_ROWS_2 = 512  # at 2 ranks (measured: slots faster at 256 rows, NVLS at 1024)
 # "auto": NVLS for >= NVLS_MIN_ROWS rows on more than 2 ranks (at 2 ranks one
 # slot copy is all the exchange moves anyway); "nvls": also at 2 ranks (tests)
 _TP_REDUCE = __import__("os").environ.get("FOUNDRY_TP_REDUCE", "auto")
@@ -252,7 +253,8 @@ class LlamaModel:
             from ..parallel import comm
 
             ex = st.tp.slots
-            if rows >= NVLS_MIN_ROWS and ex.symm.multicast and (ex.symm.world > 2 or _TP_REDUCE == "nvls"):
+            if ex.symm.multicast and (rows >= NVLS_MIN_ROWS_2 or (rows >= NVLS_MIN_ROWS and (
+                    ex.symm.world > 2 or _TP_REDUCE == "nvls"))):
                 # many rows: partial sums reduced in the switch (one copy of the
                 # output crosses NVLink per rank instead of world - 1)
                 ops.linear(inp, weight, out=ex.slot(which, 0)[:rows])
