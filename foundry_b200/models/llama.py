@@ -307,9 +307,11 @@ class LlamaModel:
             ops.rope_kv_write(qkv, pb.positions[:t], self.cos_sin, pb.q[:t], pb.k_cache[li], pb.v_cache[li],
                               pb.slots[:t], w.nq_l, w.nkv_l, lw.get("q_norm"), lw.get("k_norm"), cfg.eps,
                               k_out=pb.k_rot[:t], v_out=pb.v_rot[:t])
+            from ..runner.engine import PREFILL_IMPL
+
             ops.prefill_attention(pb.q[:t].view(t, nqd), pb.k_rot[:t].view(t, nkvd), pb.v_rot[:t].view(t, nkvd),
                                   pb.attn_out[:t], pb.cu_seqlens, pb.tile_seq, pb.tile_start, w.nq_l, w.nkv_l,
-                                  scale=self.scale)
+                                  scale=self.scale, impl=PREFILL_IMPL)
             o = self._o_proj(pb, pb.attn_out[:t], lw, h, t)
             self._norm(pb, o, h, lw["mlp_norm"], x, t)
             pending = self._mlp(pb, x, h, lw, t)

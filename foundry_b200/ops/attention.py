@@ -108,22 +108,48 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out
 
 
-def prefill_tiles(seqlens: list[int]) -> tuple[list[int], list[int]]:
+PREFILL_TILE = {"tc": 128, "simt": 64}
+PREFILL_TC_SMEM = 200 * 1024
+
+
+def prefill_tiles(seqlens: list[int], tile: int = 128) -> tuple[list[int], list[int]]:
+    """(sequence, first query position) of every ``tile``-row query tile."""
     tile_seq, tile_start = [], []
     for i, n in enumerate(seqlens):
-        for s0 in range(0, n, 64):
+        for s0 in range(0, n, tile):
             tile_seq.append(i)
             tile_start.append(s0)
     return tile_seq, tile_start
 
 
+def _rows_tmap(t: torch.Tensor) -> bytes:
+    """TMA map of a [T, heads * 128] bf16 view: 64-dim x 128-row boxes, 128B swizzle."""
+    from .._native import core
+
+    rows, cols = t.shape
+    if t.stride(1) != 1 or (t.stride(0) * 2) % 16 or t.data_ptr() % 16:
+        raise ValueError("prefill q/k/v must be row-contiguous with 16-byte aligned rows")
+    return core().make_tmap_2d(t.data_ptr(), 9, cols, rows, t.stride(0) * 2, 64, 128, 3)
+
+
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
                       cu_seqlens: torch.Tensor, tile_seq: torch.Tensor, tile_start: torch.Tensor,
-                      n_q: int, n_kv: int, scale: float | None = None) -> torch.Tensor:
+                      n_q: int, n_kv: int, scale: float | None = None, impl: str = "tc") -> torch.Tensor:
     """Causal attention over packed prompts. q: [T, *] with head h at columns
-    h*128 (row stride q.stride(0)); k, v likewise with n_kv heads; out [T, n_q*128]."""
+    h*128 (row stride q.stride(0)); k, v likewise with n_kv heads; out [T, n_q*128].
+
+    ``impl="tc"``: tcgen05 kernel (csrc/kernels/prefill_tc.cu), query tiles of
+    128 rows; ``impl="simt"``: CUDA-core kernel, query tiles of 64 rows. The
+    tile tables must come from ``prefill_tiles(seqlens, PREFILL_TILE[impl])``."""
     scale = scale if scale is not None else 1.0 / math.sqrt(128)
     n_tiles = tile_seq.numel()
+    if impl == "tc":
+        t = q.shape[0]
+        _rt.launch("prefill_tc", "fb_prefill_attn_tc", (n_tiles, n_q), (192,), [
+            _rows_tmap(q[:t, : n_q * 128]), _rows_tmap(k[:t, : n_kv * 128]), _rows_tmap(v[:t, : n_kv * 128]),
+            out.data_ptr(), out.stride(0), cu_seqlens.data_ptr(), tile_seq.data_ptr(), tile_start.data_ptr(), n_q,
+            n_kv, float(scale * LOG2E)], smem=PREFILL_TC_SMEM)
+        return out
     _rt.launch(_IMG, "fb_prefill_attn", (n_tiles, n_q), (128,), [
         q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), k.stride(0), v.stride(0), out.data_ptr(),
         out.stride(0),

@@ -28,11 +28,13 @@ import torch
 from .. import ops
 from ..models import family
 from ..models.llama import LlamaConfig, LlamaWeights
-from ..ops.attention import DecodeWorkspace, decode_splits, prefill_tiles
+from ..ops.attention import PREFILL_TILE, DecodeWorkspace, decode_splits, prefill_tiles
 from ..ops.gemm import MAX_SPLITS, PartialBuffer
 from .arena import Arena
 
 PAGE = 64
+# prefill attention kernel: "tc" (tcgen05) or "simt" (CUDA cores)
+PREFILL_IMPL = __import__("os").environ.get("FOUNDRY_PREFILL_ATTN", "tc")
 EP_PREFILL_CAP = 2048  # prefill tokens per chunk and rank under expert parallelism (sizes the exchange)
 
 
@@ -342,7 +344,7 @@ class LLMEngine:
             pb.h_cu[j + 1] = off
             pb.h_last[j] = off - 1
             seqlens.append(n)
-        ts, tst = prefill_tiles(seqlens)
+        ts, tst = prefill_tiles(seqlens, PREFILL_TILE[PREFILL_IMPL])
         pb.h_tile_seq[:len(ts)] = torch.tensor(ts, dtype=torch.int32)
         pb.h_tile_start[:len(ts)] = torch.tensor(tst, dtype=torch.int32)
         n_seq = len(chunk)

@@ -255,20 +255,24 @@ def test_decode_attention_ignores_nan_past_end(impl):
     torch.testing.assert_close(out.float(), ref, atol=2e-2, rtol=2e-2)
 
 
-def test_prefill_attention():
+@pytest.mark.parametrize("impl,nq,nkv,seqlens", [
+    ("simt", 8, 2, [1, 70, 129, 64]), ("tc", 8, 2, [1, 70, 129, 64]), ("tc", 16, 2, [300, 5, 256, 128, 513]),
+    ("tc", 32, 8, [1000])])
+def test_prefill_attention(impl, nq, nkv, seqlens):
     from foundry_b200 import ops
+    from foundry_b200.ops.attention import PREFILL_TILE
 
-    nq, nkv, d = 8, 2, 128
-    seqlens = [1, 70, 129, 64]
+    d = 128
     t = sum(seqlens)
     q = _bf(t, nq * d, seed=19)
     k = _bf(t, nkv * d, seed=20)
     v = _bf(t, nkv * d, seed=21)
     cu = torch.tensor([0] + list(torch.tensor(seqlens).cumsum(0)), dtype=torch.int32, device="cuda")
-    ts, tst = ops.prefill_tiles(seqlens)
-    out = torch.empty(t, nq * d, dtype=torch.bfloat16, device="cuda")
+    ts, tst = ops.prefill_tiles(seqlens, PREFILL_TILE[impl])
+    out = torch.full((t, nq * d), float("nan"), dtype=torch.bfloat16, device="cuda")
     ops.prefill_attention(q, k, v, out, cu, torch.tensor(ts, dtype=torch.int32, device="cuda"),
-                          torch.tensor(tst, dtype=torch.int32, device="cuda"), nq, nkv)
+                          torch.tensor(tst, dtype=torch.int32, device="cuda"), nq, nkv, impl=impl)
+    assert ops.status("prefill_tc" if impl == "tc" else "attention") == 0
     g = nq // nkv
     off = 0
     for n in seqlens:
