@@ -26,7 +26,7 @@ _ALIGN = 256
 
 class Arena:
     def __init__(self, base: int | None, size: int | str, device=None, chunk: int | str = "1GB"):
-        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.base = base
         self.size = parse_size(size)
         self.chunk = parse_size(chunk)
@@ -36,7 +36,8 @@ class Arena:
         self._owned: list[torch.Tensor] = []  # fallback allocations
         self.used = 0
         if base is not None:
-            torch.cuda.init()
+            if self.device.type == "cuda":  # (a CPU device: host-side layout checks on the mock driver)
+                torch.cuda.init()
             c = core()
             c.set_allocation_region(base, self.size)
 
@@ -54,6 +55,17 @@ class Arena:
 
     def alloc_bytes(self, nbytes: int) -> int:
         nbytes = math.ceil(max(nbytes, 1) / _ALIGN) * _ALIGN
+        if nbytes > self._cur_left and nbytes >= self.chunk // 4:
+            # Large tensors (KV-cache layers, weight matrices) get a region
+            # allocation of their own, rounded to the granularity only: carving
+            # them out of fixed-size chunks strands the chunk tails (a 605 MB
+            # KV layer per 1 GB chunk wastes 40% of the device).
+            gran = core().region_granularity()
+            n = math.ceil(nbytes / gran) * gran
+            ptr = core().region_alloc(n)
+            self._chunks.append((ptr, n))
+            self.used += nbytes
+            return ptr
         if nbytes > self._cur_left:
             self._new_chunk(nbytes)
         p = self._cur_ptr
