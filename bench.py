@@ -283,6 +283,8 @@ def main():
                 "restore_s_per_256_graphs": round(restore["restore_s"] * 256 / restore["num_graphs"], 4),
                 "cold_start_first_token_s": cold.get("cold_start_first_token_s"),
                 "cold_start_restore_s": cold.get("restore_s"),
+                "cold_start_breakdown_s": {k: cold.get(k) for k in ("python_import_s", "modules_s", "arena_s",
+                                                                    "restore_s", "load_total_s")},
                 "prefill_s": round(prefill_s, 3),
             },
         }
