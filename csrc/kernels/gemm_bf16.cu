@@ -379,3 +379,287 @@ FB_GEMM_INSTANCE(32, 2)
 FB_GEMM_INSTANCE(64, 2)
 FB_GEMM_INSTANCE(128, 2)
 FB_GEMM_INSTANCE(256, 2)
+
+// ==== stream-K variant (swap-AB decode GEMMs with more tiles than SMs) =================
+//
+// fb_gemm_sk_bn{BN}: the same TMA -> tcgen05 -> TMEM pipeline, but every CTA
+// gets an equal share of the (tile, k-block) iterations instead of whole
+// tiles, so 224 tiles on 148 SMs take 1.51 tile-times instead of 2. A CTA's
+// range is cut into segments at tile boundaries; with at least one tile per
+// CTA a tile is split between at most two neighbouring CTAs (b, b + 1). Both
+// halves meet through slot b of a workspace: per epilogue warp (32 output
+// rows) an atomic ticket decides who arrives first; the first writes its fp32
+// partial and releases a flag, the second adds the partner's partial to its
+// own (a + b == b + a in fp32, so the result does not depend on the order),
+// writes the bf16 output and resets the ticket and flag for the next launch.
+// Nobody waits for a CTA that has not started: the first arriver never waits
+// and the second only waits for a write already in progress (bounded).
+// Output: transposed (out[token][feature]) with optional residual.
+namespace {
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int BN>
+__device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
+                                             const bf16* residual, int M, int N, int K, int ldo, int mode,
+                                             float* __restrict__ ws, int* __restrict__ flags) {
+  using C = Cfg<BN, 1>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::ACC_BUFS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int KB = (K + BK - 1) / BK;
+  const long long total = static_cast<long long>(num_m) * num_n * KB;
+  const long long it0 = total * blockIdx.x / gridDim.x;
+  const long long it1 = total * (blockIdx.x + 1) / gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(tmA);
+    tma_prefetch_desc(tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint64_t pol = policy_evict_first();
+      const int pf_dist = (mode >> 8) & 0xFF;
+      for (long long it = it0; it < it1 && !*(volatile int*)abort_flag;) {
+        const int tile = static_cast<int>(it / KB);
+        const int kb0 = static_cast<int>(it % KB);
+        const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
+        const int m_blk = tile % num_m, n_blk = tile / num_m;
+        for (int kb = kb0; kb < min(kb1, kb0 + pf_dist); ++kb) tma_prefetch_2d(tmA, kb * BK, m_blk * BM);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (pf_dist && kb + pf_dist < kb1) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, m_blk * BM);
+          if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+            *(volatile int*)abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          if (mode & EPI_A_STREAM)
+            tma_load_2d_hint(sA + stage * C::A_BYTES, tmA, &full[stage], kb * BK, m_blk * BM, pol);
+          else
+            tma_load_2d(sA + stage * C::A_BYTES, tmA, &full[stage], kb * BK, m_blk * BM);
+          tma_load_2d(sB + stage * C::B_BYTES, tmB, &full[stage], kb * BK, n_blk * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        it += kb1 - kb0;
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: one accumulator per segment ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16<BM, BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int seg = 0;
+      for (long long it = it0; it < it1 && !*(volatile int*)abort_flag; ++seg) {
+        const int kb0 = static_cast<int>(it % KB);
+        const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
+        const int acc = NBUF == 2 ? (seg & 1) : 0;
+        const uint32_t aphase = NBUF == 2 ? ((seg >> 1) & 1) : (seg & 1);
+        if (!mbar_wait(&tempty[acc], aphase ^ 1, FB_KERR_TIMEOUT_TMEM)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128(smem_u32(sA + stage * C::A_BYTES));
+          const uint64_t bdesc = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                     (kb > kb0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit(&tfull[acc]);
+        if (!ok) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        it += kb1 - kb0;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    int seg = 0;
+    for (long long it = it0; it < it1 && !*(volatile int*)abort_flag; ++seg) {
+      const int tile = static_cast<int>(it / KB);
+      const int kb0 = static_cast<int>(it % KB);
+      const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
+      it += kb1 - kb0;
+      const int m_blk = tile % num_m, n_blk = tile / num_m;
+      const int acc = NBUF == 2 ? (seg & 1) : 0;
+      const uint32_t aphase = NBUF == 2 ? ((seg >> 1) & 1) : (seg & 1);
+      if (!mbar_wait(&tfull[acc], aphase, FB_KERR_TIMEOUT_TMEM)) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int gm = m_blk * BM + quarter * 32 + lane;  // output feature of this thread
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::ACC_COLS;
+      // Split tile: the prefix owner is the CTA whose range ends inside it.
+      const bool split = !(kb0 == 0 && kb1 == KB);
+      const int slot = (kb0 == 0) ? blockIdx.x : blockIdx.x - 1;
+      int* ticket = flags + slot * 8 + quarter;
+      int* ready = flags + slot * 8 + 4 + quarter;
+      float* part = ws + (static_cast<size_t>(slot) * BM + quarter * 32 + lane) * BN;
+      bool first = false;
+      if (split) {
+        int t = 0;
+        if (lane == 0) t = atomicAdd(ticket, 1);
+        first = __shfl_sync(0xffffffffu, t, 0) == 0;
+        if (!first) {
+          // the partner is writing its partial: bounded wait for its flag
+          const uint64_t t0 = globaltimer();
+          uint32_t spins = 0;
+          while (ld_acquire_gpu(ready) == 0) {
+            if ((++spins & 255u) == 0 && globaltimer() - t0 > FB_WAIT_NS) {
+              set_status(FB_KERR_TIMEOUT_PEER);
+              break;
+            }
+          }
+        }
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + c0, r);
+        tmem_ld_wait();
+        if (split && first) {
+          float4* dst = reinterpret_cast<float4*>(part + c0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+          continue;
+        }
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+        if (split) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 p = __ldcg(reinterpret_cast<const float4*>(part + c0) + i);
+            v[4 * i] += p.x;
+            v[4 * i + 1] += p.y;
+            v[4 * i + 2] += p.z;
+            v[4 * i + 3] += p.w;
+          }
+        }
+        if (gm < M) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int gn = n_blk * BN + c0 + i;
+            if (gn < N) {
+              const size_t idx = static_cast<size_t>(gn) * ldo + gm;
+              float x = v[i];
+              if (mode & EPI_RESIDUAL) x += bf2f(residual[idx]);
+              out[idx] = f2bf(x);
+            }
+          }
+        }
+      }
+      if (split) {
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) {
+          if (first) {
+            st_release_gpu(ready, 1);
+          } else {
+            *ticket = 0;  // reset for the next launch (kernel boundary orders it)
+            *ready = 0;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace
+
+#define FB_GEMM_SK_INSTANCE(BN)                                                                                     \
+  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_sk_bn##BN(                                  \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
+      const bf16* residual, int M, int N, int K, int ldo, int mode, float* ws, int* flags) {                        \
+    gemm_sk_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, ws, flags);                                     \
+  }
+
+FB_GEMM_SK_INSTANCE(16)
+FB_GEMM_SK_INSTANCE(32)
+FB_GEMM_SK_INSTANCE(64)
+FB_GEMM_SK_INSTANCE(128)
+FB_GEMM_SK_INSTANCE(256)

@@ -49,10 +49,6 @@ constexpr int MAX_KB = 32;       // K <= 4096
 #define FB_MOE_NBUF 8
 #endif
 constexpr int NBUF = FB_MOE_NBUF;  // TMEM partial buffers (the epilogue may lag the MMAs by NBUF - 1 k-blocks)
-constexpr int EPI_PROBE_NO_PROMOTE = 1 << 8;  // timing probe: skip the TMEM reads and promotion (wrong results)
-constexpr int EPI_PROBE_NO_PEMPTY = 1 << 9;   // timing probe: MMAs do not wait for the epilogue (wrong results)
-constexpr int EPI_TMA16 = 1 << 10;  // tensor maps describe the e4m3 rows as 16-bit elements (K / 2 per row)
-constexpr int EPI_TRACE = 1 << 11;  // timing probe: CTA 0 writes clock64 stamps to `residual` (as uint64[128])
 // mode bits 12..15: L2 prefetch distance for weight tiles, in k-blocks (0 = off)
 __device__ __forceinline__ int pf_dist(int mode) { return (mode >> 12) & 15; }
 
@@ -201,8 +197,8 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          const int kx = (mode & EPI_TMA16) ? kb * (QBLK / 2) : kb * QBLK;  // 128 bytes either way
-          if (pf && kb + pf < KB) tma_prefetch_2d(tmW, (mode & EPI_TMA16) ? (kb + pf) * (QBLK / 2) : (kb + pf) * QBLK, wrow);
+          const int kx = kb * QBLK;
+          if (pf && kb + pf < KB) tma_prefetch_2d(tmW, (kb + pf) * QBLK, wrow);
           if (mode & EPI_W_STREAM)
             tma_load_2d_hint(sA + stage * C::A_BYTES, tmW, &full[stage], kx, wrow, pol);
           else
@@ -235,7 +231,7 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb, ++g) {
           const uint32_t buf = g % NBUF;
-          if ((!(mode & EPI_PROBE_NO_PEMPTY) && !mbar_wait(&pempty[buf], ((g / NBUF) & 1) ^ 1, FB_KERR_TIMEOUT_TMEM)) ||
+          if (!mbar_wait(&pempty[buf], ((g / NBUF) & 1) ^ 1, FB_KERR_TIMEOUT_TMEM) ||
               !mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
             ok = false;
             break;
@@ -285,11 +281,6 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
           break;
         }
         tc_fence_after();
-        if (mode & EPI_PROBE_NO_PROMOTE) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&pempty[buf]);
-          continue;
-        }
         uint32_t r[BN];
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
 #pragma unroll
@@ -772,10 +763,6 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
   const int num_ob = O / 128;
   const int num_chunks = meta[0];
   const int num_units = num_chunks * num_ob;
-  unsigned long long* trace =
-      ((mode & EPI_TRACE) && blockIdx.x == 0) ? reinterpret_cast<unsigned long long*>(const_cast<bf16*>(residual))
-                                              : nullptr;
-  if (trace && threadIdx.x == 0) trace[0] = clock64();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -836,7 +823,6 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
             *(volatile int*)abort_flag = 1;
             break;
           }
-          if (trace && j == 0 && kb < 16) trace[1 + kb] = clock64();
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           if (mode & EPI_W_STREAM)
             tma_load_2d_hint(sA + stage * C::A8_BYTES, tmW, &full[stage], kb * QBLK, wrow, pol);
@@ -881,12 +867,10 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
             ok = false;
             break;
           }
-          if (trace && it == 0 && kb < 16) trace[20 + kb] = clock64();
           if (!mbar_wait(&cfull[cb], cphase, FB_KERR_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
-          if (trace && it == 0 && kb < 16) trace[40 + kb] = clock64();
           tc_fence_after();
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -962,7 +946,6 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
         }
         fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
         __syncwarp();
-        if (trace && r == 0 && j == 0 && kb < 16) trace[60 + kb] = clock64();
         if (lane == 0) {
           mbar_arrive(&cfull[cb]);
           mbar_arrive(&empty[stage]);
@@ -995,7 +978,6 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
         *(volatile int*)abort_flag = 1;
         break;
       }
-      if (trace && it == 0 && quarter == 0 && lane == 0) trace[80] = clock64();
       tc_fence_after();
       const int o = ob * 128 + quarter * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
@@ -1015,7 +997,6 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
           }
         }
       }
-      if (trace && it == 0 && quarter == 0 && lane == 0) trace[81] = clock64();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);

@@ -221,7 +221,7 @@ class LlamaModel:
             self._norm(st, o, h, lw["mlp_norm"], x, b)
             pending = self._mlp(st, x, h, lw, b)
         self._norm(st, pending, h, w.final_norm, x, b)
-        ops.linear(x, w.lm_head, out=st.logits[:b])
+        ops.linear(x, w.lm_head, out=st.logits[:b], streamk=st.sk)
         if st.tp:
             from ..parallel import comm
 
@@ -241,7 +241,7 @@ class LlamaModel:
 
     def _mlp(self, st, x, h, lw, rows):
         """SwiGLU FFN of x; returns the pending output that the next norm adds into h."""
-        gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:rows])
+        gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:rows], streamk=getattr(st, "sk", None))
         ops.silu_mul(gu, st.act[:rows])
         return self._row_parallel(st, st.act[:rows], lw["down"], h, rows, which=1)
 

@@ -59,6 +59,20 @@ class Partial:
         return self.rows * self.cols
 
 
+class StreamKBuffer:
+    """Workspace of the stream-K GEMM: fp32 partial tiles (``ws``, any
+    contents; may share memory with a PartialBuffer whose slices are consumed
+    before and produced after the stream-K GEMM) and ``flags`` (int32, must be
+    zero before the first launch; every launch leaves them zero)."""
+
+    def __init__(self, ws: torch.Tensor, flags: torch.Tensor):
+        assert ws.dtype == torch.float32 and flags.dtype == torch.int32
+        self.ws, self.flags = ws, flags
+
+    def fits(self, grid: int, bn: int) -> bool:
+        return self.ws.numel() >= grid * BM * bn and self.flags.numel() >= grid * 8
+
+
 class PartialBuffer:
     """Scratch for split slices (fp32). Must not be shared by GEMMs whose
     slices are still unconsumed."""
@@ -100,13 +114,15 @@ class Plan:
     est_us: float = 0.0
     mt: int = 1  # 128-row A tiles per work unit (2 = two MMAs share each B tile)
     pf: int = 0  # k-blocks of L2 prefetch lead for streamed A tiles (0 = off)
+    streamk: bool = False  # equal (tile, k-block) shares per CTA (fb_gemm_sk_*)
 
     @property
     def kernel(self) -> str:
-        return f"fb_gemm_bf16_bn{self.bn}_m{self.mt}"
+        return f"fb_gemm_sk_bn{self.bn}" if self.streamk else f"fb_gemm_bf16_bn{self.bn}_m{self.mt}"
 
 
-def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bool = True) -> Plan:
+def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bool = True,
+         allow_streamk: bool = False) -> Plan:
     """Chooses the tile width and split count with a small cost model:
     waves of CTAs x k-blocks per CTA x time per k-block, bounded below by the
     HBM time of the operands, plus the traffic of split slices."""
@@ -148,6 +164,17 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
     # (measured 7-12% on Llama-3-8B decode shapes).
     if best.swap and kb >= 8:
         best.pf = 4
+    # Stream-K: whole-tile plans whose tile count is not a multiple of the SM
+    # count leave the last wave part empty; equal (tile, k-block) shares
+    # remove that tail. Measured on B200 (Llama-3-8B gate_up, 224 tiles):
+    # 47.3 -> 40.8 us at 64 tokens (bn 64), 52.6 -> 51.1 us at 128 (bn 128),
+    # but 71.8 -> 76.3 us at 256 (bn 256: the partial-tile exchange costs more
+    # than the half-empty second wave), so only narrow tiles use it.
+    if allow_streamk and best.swap and best.splits == 1 and best.mt == 1 and best.bn <= 64:
+        tiles = math.ceil(mg / BM) * math.ceil(ng / best.bn)
+        if tiles > sms and tiles % sms:
+            best.streamk = True
+            best.grid = sms
     return best
 
 
@@ -169,7 +196,7 @@ def linear_multicast(x: torch.Tensor, w: torch.Tensor, target: int, plan_overrid
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
            residual: torch.Tensor | None = None, partials: PartialBuffer | None = None,
-           plan_override: Plan | None = None):
+           plan_override: Plan | None = None, streamk: StreamKBuffer | None = None):
     """out = x @ w.T (+ residual). x: [T, K] bf16, w: [N, K] bf16, out: [T, N] bf16.
 
     Returns ``out`` - or, when ``partials`` is given and the plan splits K, a
@@ -180,7 +207,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     t_tok, k = x.shape
     n_out, k2 = w.shape
     assert k == k2, f"K mismatch {k} vs {k2}"
-    p = plan_override or plan(t_tok, n_out, k, allow_split=partials is not None)
+    p = plan_override or plan(t_tok, n_out, k, allow_split=partials is not None, allow_streamk=streamk is not None)
+    if p.streamk and (streamk is None or not streamk.fits(p.grid, p.bn)):
+        p = plan(t_tok, n_out, k, allow_split=partials is not None)
     mode = 0
     if p.swap:
         a, b, mg, ng = w, x, n_out, t_tok
@@ -205,6 +234,11 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     if residual is not None:
         assert residual.shape == out.shape and residual.stride() == out.stride()
         mode |= EPI_RESIDUAL
+    if p.streamk:
+        args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
+                mg, ng, k, out.stride(0), mode, streamk.ws.data_ptr(), streamk.flags.data_ptr()]
+        _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, 1))
+        return out
     args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
             mg, ng, k, out.stride(0), mode, 1, 0, 0]
     _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))

@@ -136,6 +136,10 @@ class DecodeState:
         _model_buffers(self, ecfg.model, w, arena, b)
         # fp32 split-K slices of the decode GEMMs (consumed by the next op)
         self.part = PartialBuffer(buf=arena.empty((MAX_SPLITS * b * max(w.qkv_dim_l, cfg.hidden),), torch.float32))
+        # stream-K GEMMs (gate_up, lm_head) keep their partial tiles in the
+        # split-K slice buffer (free between the ops that use it) and their
+        # tickets in a zeroed flag array that every launch leaves zeroed
+        self.sk = ops.StreamKBuffer(self.part.buf, arena.zeros((1024 * 8,), torch.int32))
         sizes = ecfg.graph_sizes or default_graph_sizes(b)
         self.attn_splits = {s: decode_splits(s, nkv, self.max_pages) for s in sizes}
         for s in range(1, b + 1):

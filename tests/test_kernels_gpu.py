@@ -284,3 +284,34 @@ def test_prefill_attention(impl, nq, nkv, seqlens):
         ref = torch.einsum("hts,shd->thd", att.masked_fill(mask, float("-inf")).softmax(-1), vv)
         torch.testing.assert_close(out[off:off + n].float().view(n, nq, d), ref, atol=2e-2, rtol=2e-2)
         off += n
+
+
+@pytest.mark.parametrize("t,n,k", [(64, 28672, 4096), (16, 28672, 4096), (40, 19000, 1024), (64, 40000, 512)])
+def test_linear_streamk(t, n, k):
+    """Stream-K decode GEMM (tiles split between neighbouring CTAs, fp32
+    partials met through a workspace): matches fp32, with and without the
+    residual epilogue, on repeated launches (the tickets reset themselves)
+    and bit-identically across launches."""
+    from foundry_b200 import ops
+    from foundry_b200.ops.gemm import plan
+
+    p = plan(t, n, k, allow_streamk=True)
+    assert p.streamk, p
+    x = _bf(t, k, seed=31)
+    w = _bf(n, k, seed=32, scale=0.02)
+    sk = ops.StreamKBuffer(torch.empty(148 * 128 * 256, device="cuda"),
+                           torch.zeros(1024 * 8, dtype=torch.int32, device="cuda"))
+    ref = x.float() @ w.float().T
+    outs = []
+    for _ in range(3):
+        out = torch.full((t, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        ops.linear(x, w, out=out, streamk=sk)
+        outs.append(out)
+    torch.testing.assert_close(outs[0].float(), ref, atol=2e-2, rtol=2e-2)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    res = _bf(t, n, seed=33)
+    out = res.clone()
+    ops.linear(x, w, out=out, residual=out, streamk=sk)
+    torch.testing.assert_close(out.float(), ref + res.float(), atol=3e-2, rtol=2e-2)
+    assert int(sk.flags.abs().sum()) == 0
+    assert ops.status("gemm_bf16") == 0
