@@ -95,7 +95,7 @@ struct GemmCfg {
   static constexpr int A_BYTES = 128 * QBLK;  // 128 weight rows x 128 K bytes
   static constexpr int B_BYTES = BN * QBLK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 10 ? 10 : (200 * 1024) / STAGE_BYTES;
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(NBUF * BN);
   static constexpr int XS_FLOATS = BN * MAX_KB;  // token scales of one unit [BN][KBp]
 };

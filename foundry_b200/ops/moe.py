@@ -40,7 +40,7 @@ NBUF = 8
 
 def gemm_smem(bn: int) -> int:
     stage = 128 * QBLK + bn * QBLK
-    stages = min(8, (192 * 1024) // stage)
+    stages = min(10, (200 * 1024) // stage)
     return stages * stage + 2 * bn * MAX_KB * 4 + 2 * MAX_KB * 4 + 8 * (2 * stages + 2 * NBUF + 4) + 16 + 1024
 
 
