@@ -18,7 +18,7 @@
 //    nothing. Kernel params are deep-copied with their declared sizes.
 // The mock is intentionally strict: unknown handles return
 // CUDA_ERROR_INVALID_HANDLE, so host-side bugs surface as statuses.
-// It has no counterpart in the reference (which has no fakes).
+// It has no counterpart in the reference, whose tests use no fakes.
 #include <cuda.h>
 #include <dlfcn.h>
 #include <string.h>

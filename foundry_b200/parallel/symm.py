@@ -13,7 +13,7 @@ the sum over GPUs.
 
 Parity: the reference maps IPC'd VMM memory at the exporter's address
 (csrc/hook.cpp:2864-3080) and relies on NVSHMEM (DeepEP) for symmetric heaps;
-this is our own substrate (SURVEY 2.3, B200-native plan).
+this is our own substrate.
 """
 
 from __future__ import annotations
