@@ -1183,3 +1183,27 @@ extern "C" __global__ void __launch_bounds__(256) fb_ep_dispatch(
     if (g == 0 && lane == 0) reinterpret_cast<int*>(win + map_off)[row] = (rank << 24) | pidx;
   }
 }
+
+// Block-scaled e4m3 [R, C] (scales [R/128, kb_pad(C/128)]) -> bf16 [R, C]:
+// w = q * scale of its 128 x 128 block. One CTA per block, 8 elements per thread.
+extern "C" __global__ void __launch_bounds__(256) fb_dequant_block_fp8(const uint8_t* __restrict__ q,
+                                                                      const float* __restrict__ scales, int R,
+                                                                      int Cc, bf16* __restrict__ out) {
+  const int bc = blockIdx.x, br = blockIdx.y;
+  const float s = scales[static_cast<size_t>(br) * kb_pad(Cc / 128) + bc];
+  const int r0 = threadIdx.x / 16, c0 = (threadIdx.x % 16) * 8;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const size_t row = static_cast<size_t>(br) * 128 + r0 + 16 * i;
+    const uint2 raw = *reinterpret_cast<const uint2*>(q + row * Cc + bc * 128 + c0);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw);
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      __nv_fp8_e4m3 v;
+      v.__x = b[j];
+      f[j] = static_cast<float>(v) * s;
+    }
+    *reinterpret_cast<uint4*>(out + row * Cc + bc * 128 + c0) = pack8(f);
+  }
+}

@@ -1,12 +1,16 @@
 """Qwen3-MoE decoder (Qwen3-30B-A3B shape) with block-scaled fp8 weights.
 
-Per layer: RMSNorm -> fp8 QKV -> per-head q/k RMSNorm + RoPE + paged KV write
--> decode attention (GQA 32/4) -> fp8 O (+= residual) -> RMSNorm -> router
+Per layer: RMSNorm -> QKV -> per-head q/k RMSNorm + RoPE + paged KV write
+-> decode attention (GQA 32/4) -> O (+= residual) -> RMSNorm -> router
 (bf16, 128 experts) -> softmax top-8 (renormalised) -> grouped fp8 expert
 FFN (gate_up, SiLU*up, down) -> top-k weighted combine fused with the next
-RMSNorm. Every linear layer except the router, embedding and lm_head is
-e4m3 with 128 x 128 block scales; activations are quantised per token per
-128 features right before each fp8 GEMM.
+RMSNorm. The expert weights are e4m3 with 128 x 128 block scales and their
+activations are quantised per token per 128 features right before each fp8
+GEMM. The attention projections come from the same block-scaled fp8
+checkpoint; by default they are dequantised once at load into bf16 and run
+on the dense bf16 GEMM (split-K slices consumed by RoPE / the next norm,
+residual epilogue), which at decode batch sizes is faster than the grouped
+fp8 kernel for these 19 MB per layer; ``attn_fp8=True`` keeps them e4m3.
 
 Expert parallelism (``ep_size`` > 1, with DP attention: every rank runs the
 attention of its own sequences) shards the experts; the dispatch/combine
@@ -52,6 +56,9 @@ class Qwen3MoeConfig(LlamaConfig):
     # e4m3 weights dequantised on chip, bf16 activations, kind::f16
     fp8_gemm: str = "promote"
     fp8_prefetch: int = 0  # L2 prefetch distance of weight tiles (k-blocks)
+    # qkv / o projections kept as e4m3 block weights (True) or dequantised
+    # once into bf16 (False: same values up to one bf16 rounding)
+    attn_fp8: bool = False
 
     def num_params(self) -> int:
         h, d = self.hidden, self.head_dim
@@ -98,8 +105,8 @@ class Qwen3MoeWeights:
         for _ in range(cfg.layers):
             self.layers.append({
                 "attn_norm": arena.empty((h,)),
-                "qkv": M.Fp8Weight.empty(arena, 1, cfg.qkv_dim, h),
-                "o": M.Fp8Weight.empty(arena, 1, h, cfg.n_q * d),
+                "qkv": self._proj(arena, cfg.qkv_dim, h),
+                "o": self._proj(arena, h, cfg.n_q * d),
                 "q_norm": arena.empty((d,)),
                 "k_norm": arena.empty((d,)),
                 "mlp_norm": arena.empty((h,)),
@@ -114,6 +121,9 @@ class Qwen3MoeWeights:
 
     vocab_offset = 0
 
+    def _proj(self, arena, rows: int, cols: int):
+        return M.Fp8Weight.empty(arena, 1, rows, cols) if self.cfg.attn_fp8 else arena.empty((rows, cols))
+
     def tensors(self):
         yield "embed", self.embed
         for i, lw in enumerate(self.layers):
@@ -125,13 +135,22 @@ class Qwen3MoeWeights:
     def init(self, seed: int) -> None:
         """N(0, init_std) matrices (fp8 ones quantised per block), ones for norms.
         Seeds depend only on the tensor, and expert shards draw their rows of
-        the full expert matrix, so every EP degree sees the same model."""
+        the full expert matrix, so every EP degree sees the same model. bf16
+        attention projections are the dequantised fp8 block weights that
+        ``attn_fp8`` would hold."""
         std = self.cfg.init_std
         for idx, (name, t) in enumerate(self.tensors()):
             s = (seed * 1_000_003 + idx * 7_919) & ((1 << 63) - 1)
             if isinstance(t, M.Fp8Weight):
                 expert = name.endswith(("w13", "w2"))  # expert shards draw their rows of the full matrix
                 M.init_fp8_block_(t, s, std, row_offset=self.e0 * t.rows if expert else 0)
+            elif name.endswith((".qkv", ".o")):
+                rows, cols = t.shape
+                tmp = M.Fp8Weight(torch.empty((rows, cols), dtype=torch.uint8, device=t.device),
+                                  torch.zeros((1, rows // 128, M.kb_pad(cols // 128)), dtype=torch.float32,
+                                              device=t.device), 1, rows, cols)
+                M.init_fp8_block_(tmp, s, std)
+                M.dequantize_block_fp8_(tmp, t)
             elif t.dim() == 1:
                 ops.fill_(t, 1.0)
             else:
@@ -141,9 +160,6 @@ class Qwen3MoeWeights:
 class Qwen3MoeModel(LlamaModel):
     """Decode / prefill of Qwen3-MoE on the shared attention path of LlamaModel."""
 
-    def __init__(self, cfg: Qwen3MoeConfig, weights: Qwen3MoeWeights, cos_sin: torch.Tensor):
-        super().__init__(cfg, weights, cos_sin)
-
     # scratch buffers a DecodeState / PrefillBatch needs for `rows` tokens
     @staticmethod
     def buffers(cfg: Qwen3MoeConfig, w: Qwen3MoeWeights, rows: int) -> dict:
@@ -151,10 +167,12 @@ class Qwen3MoeModel(LlamaModel):
         p = rows * k
         u8, f32, i32 = torch.uint8, torch.float32, torch.int32
         sr, kp = M.scale_rows, M.kb_pad
-        return {
+        dense = {
             "xq_h": ((rows, h), u8), "xs_h": ((sr(rows), kp(h // 128)), f32),
             "xq_o": ((rows, cfg.n_q * d), u8), "xs_o": ((sr(rows), kp(cfg.n_q * d // 128)), f32),
             "dchunks": ((rows // 32 + 1, 4), i32), "dmeta": ((4,), i32),
+        } if cfg.attn_fp8 else {}
+        return dense | {
             "rlogits": ((rows, cfg.num_experts), torch.bfloat16), "tids": ((rows, k), i32), "tw": ((rows, k), f32),
             "pos": ((p,), i32), "ecounts": ((cfg.num_experts,), i32),
             "chunks": ((M.max_chunks(p, w.e_local, 32), 4), i32), "meta": ((4,), i32),
@@ -187,7 +205,8 @@ class Qwen3MoeModel(LlamaModel):
                           stream_weights=stream, prefetch=self.pf)
 
     def _begin(self, st, rows) -> None:
-        M.dense_chunks(rows, self._bn_dense(rows), st.dchunks, st.dmeta)
+        if self.w.cfg.attn_fp8:
+            M.dense_chunks(rows, self._bn_dense(rows), st.dchunks, st.dmeta)
 
     def _dense(self, st, x, xq, xs, w, out, rows, residual=None):
         if self.kind == "promote":
@@ -197,9 +216,13 @@ class Qwen3MoeModel(LlamaModel):
                           residual=residual)
 
     def _qkv(self, st, x, lw, rows):
+        if not isinstance(lw["qkv"], M.Fp8Weight):
+            return super()._qkv(st, x, lw, rows)
         return self._dense(st, x, st.xq_h, st.xs_h, lw["qkv"], st.qkv[:rows], rows)
 
     def _o_proj(self, st, inp, lw, h, rows):
+        if not isinstance(lw["o"], M.Fp8Weight):
+            return super()._o_proj(st, inp, lw, h, rows)
         self._dense(st, inp, st.xq_o, st.xs_o, lw["o"], h, rows, residual=h)
         return None
 
@@ -241,7 +264,7 @@ def reference_forward(cfg: Qwen3MoeConfig, weights: Qwen3MoeWeights, ids: torch.
     activation quantisation); returns logits [T, vocab]. Needs all experts
     local (ep_size 1)."""
     assert weights.ep_size == 1
-    f = lambda t: t.float()  # noqa: E731
+    f = lambda t: t.dequant() if isinstance(t, M.Fp8Weight) else t.float()  # noqa: E731
     t_len = ids.numel()
     pos = torch.arange(t_len, device=ids.device)
     h = f(weights.embed)[ids.long()]
@@ -250,7 +273,7 @@ def reference_forward(cfg: Qwen3MoeConfig, weights: Qwen3MoeWeights, ids: torch.
     e, i = cfg.num_experts, cfg.moe_inter
     for lw in weights.layers[: layers or cfg.layers]:
         x = _rms(h, f(lw["attn_norm"]), cfg.eps)
-        qkv = x @ lw["qkv"].dequant().T
+        qkv = x @ f(lw["qkv"]).T
         q = qkv[:, : cfg.n_q * d].view(t_len, cfg.n_q, d)
         k = qkv[:, cfg.n_q * d: (cfg.n_q + cfg.n_kv) * d].view(t_len, cfg.n_kv, d)
         v = qkv[:, (cfg.n_q + cfg.n_kv) * d:].view(t_len, cfg.n_kv, d)
@@ -263,7 +286,7 @@ def reference_forward(cfg: Qwen3MoeConfig, weights: Qwen3MoeWeights, ids: torch.
         mask = torch.triu(torch.ones(t_len, t_len, dtype=torch.bool, device=ids.device), 1)
         att = att.masked_fill(mask, float("-inf")).softmax(-1)
         o = torch.einsum("hts,shd->thd", att, v).reshape(t_len, cfg.n_q * d)
-        h = h + o @ lw["o"].dequant().T
+        h = h + o @ f(lw["o"]).T
         x = _rms(h, f(lw["mlp_norm"]), cfg.eps)
         probs = (x @ f(lw["router"]).T).softmax(-1)
         tw, tid = probs.topk(cfg.topk, dim=-1)

@@ -124,6 +124,15 @@ def quantize_block_fp8_(w_bf16: torch.Tensor, w: Fp8Weight) -> None:
                [w_bf16.data_ptr(), r, c, w.q.data_ptr(), w.scale.data_ptr()])
 
 
+def dequantize_block_fp8_(w: Fp8Weight, out: torch.Tensor) -> torch.Tensor:
+    """bf16 [experts * rows, cols] <- e4m3 * block scale (one rounding to bf16)."""
+    r, c = w.experts * w.rows, w.cols
+    assert tuple(out.shape) == (r, c) and out.dtype == torch.bfloat16 and out.is_contiguous()
+    _rt.launch(_IMG, "fb_dequant_block_fp8", (c // 128, r // 128), (256,),
+               [w.q.data_ptr(), w.scale.data_ptr(), r, c, out.data_ptr()])
+    return out
+
+
 def quantize_rows(x: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, pos: torch.Tensor | None = None,
                   topk: int = 1) -> None:
     """x [T, H] bf16 -> e4m3 rows with per-128 scales (``xs`` rows padded to
@@ -262,6 +271,6 @@ def combine_add_rmsnorm(y: torch.Tensor, pos: torch.Tensor, weights: torch.Tenso
 
 __all__ = [
     "Fp8Weight", "combine_add_rmsnorm", "dense_chunks", "fp8_tmap", "gemm_fp8", "gemm_smem", "gemm_w8", "init_fp8_block_",
-    "scatter_rows", "w8_smem",
+    "scatter_rows", "w8_smem", "dequantize_block_fp8_",
     "max_chunks", "plan", "quantize_block_fp8_", "quantize_rows", "silu_mul_quant", "topk",
 ]

@@ -39,6 +39,10 @@ def test_init_fp8_block_statistics_and_shards():
     part = M.Fp8Weight.empty(a, 2, 256, 512)
     M.init_fp8_block_(part, seed=11, std=0.02, row_offset=2 * 256)
     assert torch.equal(part.q, w.q[2 * 256:]) and torch.equal(part.scale, w.scale[2:])
+    # dequantised to bf16 on the device: the fp32 dequant rounded once
+    out = torch.empty(4 * 256, 512, dtype=torch.bfloat16, device="cuda")
+    M.dequantize_block_fp8_(w, out)
+    assert torch.equal(out, d.to(torch.bfloat16))
 
 
 def test_quantize_block_and_rows_match_torch():
@@ -195,22 +199,24 @@ def test_moe_ffn_pipeline_matches_fp32():
                                rtol=2e-2, atol=2e-2)
 
 
-def _moe_engine(layers=2, experts=32, max_batch=32, region=False):
+def _moe_engine(layers=2, experts=32, max_batch=32, region=False, attn_fp8=False):
     from foundry_b200.models.qwen3_moe import tiny_moe
     from foundry_b200.runner.engine import EngineConfig, LLMEngine
 
     cfg = tiny_moe(layers=layers, experts=experts)
+    cfg.attn_fp8 = attn_fp8
     ecfg = EngineConfig(model=cfg, max_batch=max_batch, max_seq_len=256, max_prefill_tokens=1024,
                         max_prefill_seqs=8, graph_sizes=[1, 2, 4, 8, 16, 32],
                         region_base=0x630000000000 if region else None, region_size="16GB")
     return LLMEngine(ecfg)
 
 
-def test_qwen3_moe_engine_matches_reference_and_graphs():
+@pytest.mark.parametrize("attn_fp8", [False, True])
+def test_qwen3_moe_engine_matches_reference_and_graphs(attn_fp8):
     from foundry_b200 import ops
     from foundry_b200.models.qwen3_moe import reference_forward
 
-    eng = _moe_engine()
+    eng = _moe_engine(attn_fp8=attn_fp8)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (5, 70, 130)]
     outs = eng.generate(prompts, max_new_tokens=4)
