@@ -48,7 +48,6 @@ constexpr int MAX_KB = 32;       // K <= 4096
 #ifndef FB_MOE_NBUF
 #define FB_MOE_NBUF 8
 #endif
-constexpr int NBUF = FB_MOE_NBUF;  // TMEM partial buffers (the epilogue may lag the MMAs by NBUF - 1 k-blocks)
 // mode bits 12..15: L2 prefetch distance for weight tiles, in k-blocks (0 = off)
 __device__ __forceinline__ int pf_dist(int mode) { return (mode >> 12) & 15; }
 
@@ -90,12 +89,28 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// Resident CTAs per SM of the promote GEMM, per token-tile width. The
+// per-k-block promotion chain (MMA commit -> TMEM load -> FMA -> release)
+// bounds one CTA's rate, not HBM: at 32-token tiles three CTAs per SM
+// stream the expert weights 1.5x faster than one (same bytes, same result);
+// 64-token tiles gain nothing and keep the deeper single-CTA ring.
+template <int BN>
+struct MoeOcc {
+  static constexpr int CTAS = BN == 32 ? 3 : 1;
+};
+
 template <int BN>
 struct GemmCfg {
+  static constexpr int CTAS = MoeOcc<BN>::CTAS;
   static constexpr int A_BYTES = 128 * QBLK;  // 128 weight rows x 128 K bytes
   static constexpr int B_BYTES = BN * QBLK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 10 ? 10 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int BUDGET = CTAS == 1 ? 200 * 1024 : CTAS == 2 ? 100 * 1024 : 60 * 1024;  // operand ring
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 10 ? 10 : BUDGET / STAGE_BYTES;
+  // TMEM partial buffers: the epilogue may lag the MMAs by NBUF - 1 k-blocks;
+  // the resident CTAs share the SM's 512 columns (power-of-two allocations)
+  static constexpr int CTA_COLS = CTAS == 1 ? 512 : CTAS == 2 ? 256 : 128;
+  static constexpr int NBUF = FB_MOE_NBUF * BN > CTA_COLS ? CTA_COLS / BN : FB_MOE_NBUF;
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(NBUF * BN);
   static constexpr int XS_FLOATS = BN * MAX_KB;  // token scales of one unit [BN][KBp]
 };
@@ -114,6 +129,7 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
                                               long long peer_stride) {
   using C = GemmCfg<BN>;
   constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::NBUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -333,7 +349,7 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
 }  // namespace
 
 #define FB_MOE_GEMM_INSTANCE(BN)                                                                                    \
-  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_moe_gemm_fp8_bn##BN(                             \
+  extern "C" __global__ void __launch_bounds__(NUM_THREADS, MoeOcc<BN>::CTAS) fb_moe_gemm_fp8_bn##BN(                             \
       const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const float* w_scale,       \
       const float* x_scale, const int4* chunks, const int* meta, bf16* out, const bf16* residual, int O, int K,     \
       int ldo, int mode, long long peer_stride) {                                                                    \

@@ -195,6 +195,10 @@ class Qwen3MoeModel(LlamaModel):
         return 32 if rows <= 32 else 64
 
     def _bn_moe(self, pairs: int) -> int:
+        # promote: 32-token tiles at three CTAs per SM beat 64-token tiles at
+        # every decode size measured (512 to 1024 tokens, 64 or 128 experts)
+        if self.kind == "promote":
+            return 32
         return 64 if pairs > 32 * self.w.e_local else 32
 
     def _gemm(self, w, x, xq, xs, chunks, meta, out, units, bn, residual=None, stream=False):

@@ -38,9 +38,15 @@ EPI_PEER_COMBINE = 32
 NBUF = 8
 
 
+# resident CTAs per SM of the promote GEMM per token-tile width (MoeOcc in
+# moe.cu): one CTA's per-k-block promotion chain, not HBM, bounds 32-token tiles
+GEMM_CTAS = {32: 3, 64: 1}
+
+
 def gemm_smem(bn: int) -> int:
     stage = 128 * QBLK + bn * QBLK
-    stages = min(10, (200 * 1024) // stage)
+    budget = {1: 200, 2: 100, 3: 60}[GEMM_CTAS[bn]] * 1024
+    stages = min(10, budget // stage)
     return stages * stage + 2 * bn * MAX_KB * 4 + 2 * MAX_KB * 4 + 8 * (2 * stages + 2 * NBUF + 4) + 16 + 1024
 
 
@@ -181,7 +187,7 @@ def gemm_fp8(w: Fp8Weight, xq: torch.Tensor, xs: torch.Tensor, chunks: torch.Ten
         out_ptr, res_ptr, ld = int(out), peer_rowmap.data_ptr(), int(ldo)
     else:
         out_ptr, res_ptr, ld = out.data_ptr(), residual.data_ptr() if residual is not None else 0, out.stride(0)
-    grid = max(1, min(max_units, _rt.sm_count()))
+    grid = max(1, min(max_units, GEMM_CTAS[bn] * _rt.sm_count()))
     _rt.launch(_IMG, f"fb_moe_gemm_fp8_bn{bn}", (grid,), (192,), [
         fp8_tmap(w.q, 128), fp8_tmap(xq, bn), w.scale.data_ptr(), xs.data_ptr(), chunks.data_ptr(),
         meta.data_ptr(), out_ptr, res_ptr, w.rows, w.cols, ld, mode, int(peer_stride)], smem=gemm_smem(bn))
