@@ -428,34 +428,88 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_topk(const bf16* __rest
 // One CTA of 1024 threads. ids [P] (P = T * topk pairs) -> per-expert counts,
 // expert-sorted position of every pair (stable: pair order within an expert),
 // the chunk table {expert, first row, rows, 0} with chunks of <= bn rows, and
-// meta = {num_chunks, P}.
+// meta = {num_chunks, P}. Warp w owns the pairs [w * S, (w + 1) * S):
+// (1) each warp counts its pairs per expert (match_any leaders, in order);
+// (2) per expert, a shuffle scan over the 32 warps gives each warp its first
+//     row inside the expert, and the total is the expert's count;
+// (3) warp 0 scans counts and chunk counts over the experts;
+// (4) each warp walks its pairs again and assigns positions in order.
 extern "C" __global__ void __launch_bounds__(1024) fb_moe_plan(const int* __restrict__ ids, int P, int E, int bn,
                                                               int* __restrict__ pos, int* __restrict__ counts,
                                                               int4* __restrict__ chunks, int* __restrict__ meta) {
-  __shared__ int cnt[256], off[256], coff[256], run[256];
-  __shared__ int wcnt[32][256];
+  __shared__ int cnt[256], off[256], coff[256];
+  __shared__ int wbase[32][257];  // [warp][expert]; odd stride: the scan in (2) reads a column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (E > 256) {
     if (tid == 0) set_status(FB_KERR_BAD_ARG);
     return;
   }
-  for (int e = tid; e < E; e += 1024) {
-    cnt[e] = 0;
-    run[e] = 0;
+  for (int i = tid; i < 32 * E; i += 1024) wbase[i / E][i % E] = 0;
+  __syncthreads();
+  const int S = ((P + 31) / 32 + 31) / 32 * 32;  // pairs per warp, whole 32-pair rounds
+  const int p0 = warp * S, p1 = min(P, p0 + S);
+  const unsigned lt = (1u << lane) - 1;
+  for (int b = p0; b < p1; b += 128) {
+    int ev[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int p = b + u * 32 + lane;
+      ev[u] = p < p1 ? ids[p] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const unsigned same = __match_any_sync(0xffffffffu, ev[u]);
+      if (ev[u] >= 0 && (same & lt) == 0) wbase[warp][ev[u]] += __popc(same);
+      __syncwarp();
+    }
   }
   __syncthreads();
-  for (int p = tid; p < P; p += 1024) atomicAdd(&cnt[ids[p]], 1);
-  __syncthreads();
-  if (tid == 0) {
-    int a = 0, b = 0;
-    for (int e = 0; e < E; ++e) {
-      off[e] = a;
-      coff[e] = b;
-      a += cnt[e];
-      b += (cnt[e] + bn - 1) / bn;
+  for (int e = warp; e < E; e += 32) {
+    const int v = wbase[lane][e];
+    int inc = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc += n;
     }
-    meta[0] = b;
-    meta[1] = P;
+    wbase[lane][e] = inc - v;
+    if (lane == 31) cnt[e] = inc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int c[8], sa = 0, sb = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane * 8 + i;
+      c[i] = e < E ? cnt[e] : 0;
+      sa += c[i];
+      sb += (c[i] + bn - 1) / bn;
+    }
+    int ia = sa, ib = sb;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int na = __shfl_up_sync(0xffffffffu, ia, d);
+      const int nb = __shfl_up_sync(0xffffffffu, ib, d);
+      if (lane >= d) {
+        ia += na;
+        ib += nb;
+      }
+    }
+    int ea = ia - sa, eb = ib - sb;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane * 8 + i;
+      if (e < E) {
+        off[e] = ea;
+        coff[e] = eb;
+      }
+      ea += c[i];
+      eb += (c[i] + bn - 1) / bn;
+    }
+    if (lane == 31) {
+      meta[0] = ib;
+      meta[1] = P;
+    }
   }
   __syncthreads();
   for (int e = tid; e < E; e += 1024) {
@@ -463,28 +517,22 @@ extern "C" __global__ void __launch_bounds__(1024) fb_moe_plan(const int* __rest
     const int n = cnt[e];
     for (int j = 0, r = 0; r < n; ++j, r += bn) chunks[coff[e] + j] = make_int4(e, off[e] + r, min(bn, n - r), 0);
   }
-  // Stable positions, 1024 pairs per round.
-  for (int base = 0; base < P; base += 1024) {
-    for (int i = tid; i < 32 * E; i += 1024) wcnt[i / E][i % E] = 0;
-    __syncthreads();
-    const int p = base + tid;
-    const int e = p < P ? ids[p] : -1;
-    const unsigned same = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(same & ((1u << lane) - 1));
-    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(same);
-    __syncthreads();
-    for (int x = tid; x < E; x += 1024) {
-      int r0 = run[x];
-      for (int w = 0; w < 32; ++w) {
-        const int c = wcnt[w][x];
-        wcnt[w][x] = r0;
-        r0 += c;
-      }
-      run[x] = r0;
+  for (int b = p0; b < p1; b += 128) {
+    int ev[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int p = b + u * 32 + lane;
+      ev[u] = p < p1 ? ids[p] : -1;
     }
-    __syncthreads();
-    if (e >= 0) pos[p] = off[e] + wcnt[warp][e] + rank;
-    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const unsigned same = __match_any_sync(0xffffffffu, ev[u]);
+      const int rank = __popc(same & lt);
+      if (ev[u] >= 0) pos[b + u * 32 + lane] = off[ev[u]] + wbase[warp][ev[u]] + rank;
+      __syncwarp();
+      if (ev[u] >= 0 && rank == 0) wbase[warp][ev[u]] += __popc(same);
+      __syncwarp();
+    }
   }
 }
 

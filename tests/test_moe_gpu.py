@@ -140,6 +140,34 @@ def test_topk_and_plan():
             assert offs[ex] <= start and start + n <= offs[ex] + ref_counts[ex]
 
 
+@pytest.mark.parametrize("pairs,e", [(0, 32), (1, 8), (40, 32), (4096, 128), (16384, 128), (5000, 256)])
+def test_plan_positions_are_a_stable_expert_sort(pairs, e):
+    from foundry_b200.ops import moe as M
+
+    g = torch.Generator(device="cuda").manual_seed(pairs + e)
+    ids = torch.randint(0, e, (max(pairs, 1),), device="cuda", generator=g, dtype=torch.int32)
+    pos = torch.full((max(pairs, 1),), -1, dtype=torch.int32, device="cuda")
+    counts = torch.full((e,), -1, dtype=torch.int32, device="cuda")
+    chunks = torch.zeros(M.max_chunks(pairs, e, 32), 4, dtype=torch.int32, device="cuda")
+    meta = torch.full((4,), -1, dtype=torch.int32, device="cuda")
+    M.plan(ids, pairs, e, 32, pos, counts, chunks, meta)
+    flat = ids[:pairs].long()
+    ref = torch.bincount(flat, minlength=e)
+    assert torch.equal(counts.long(), ref)
+    order = torch.sort(flat * max(pairs, 1) + torch.arange(pairs, device="cuda")).indices
+    want = torch.empty_like(order)
+    want[order] = torch.arange(pairs, device="cuda")
+    assert torch.equal(pos[:pairs].long(), want)
+    assert int(meta[0]) == int(((ref + 31) // 32).sum()) and int(meta[1]) == pairs
+    assert ops_status_ok()
+
+
+def ops_status_ok():
+    from foundry_b200 import ops
+
+    return ops.status("moe") == 0
+
+
 def test_moe_ffn_pipeline_matches_fp32():
     """router top-k -> plan -> dispatch -> grouped gate_up -> silu*up -> grouped
     down -> combine + residual + RMSNorm, against fp32 math on the same weights."""
