@@ -5,8 +5,8 @@ started by tests/test_interposer_gpu.py with libfoundry_hook.so preloaded
     LD_PRELOAD=.../libfoundry_hook.so python tests/interposer_scenarios.py <name> <workdir>
 
 Parity: reference tests/test_vmm_alloc.py, test_stop_resume.py,
-test_preallocation.py, test_load_graph.py, test_load_cublas_ws.py (same
-checks, our own scripts).
+test_preallocation.py, test_load_graph.py, test_load_cublas_ws.py,
+test_async_load.py (same checks, our own scripts).
 """
 
 from __future__ import annotations
@@ -157,7 +157,101 @@ def scenario_graph_load(workdir):
     print(json.dumps({"ok": True}))
 
 
+# ---- many graphs, shared topologies, asynchronous restore ---------------------------------
+ASYNC_SIZES = [8, 16, 32, 64, 128, 256, 8, 16, 512, 1024, 32, 64]
+
+
+class _Mlp:
+    """4 layers of fp16 GEMM + bias + SiLU (cuBLAS + libtorch elementwise kernels)."""
+
+    def __init__(self, torch, width=384, layers=4):
+        g = torch.Generator(device="cuda").manual_seed(7)
+        self.ws = [(torch.randn(width, width, device="cuda", generator=g) * 0.05).half() for _ in range(layers)]
+        self.bs = [(torch.randn(width, device="cuda", generator=g) * 0.1).half() for _ in range(layers)]
+
+    def __call__(self, torch, x):
+        for w, b in zip(self.ws, self.bs):
+            x = torch.nn.functional.silu(torch.addmm(b, x, w.T))
+        return x
+
+
+def _async_prepare(torch, fb):
+    """Weights, every static input and the warm-up, all before any capture,
+    in the same order in SAVE and LOAD (the region cursor must agree)."""
+    fb.set_allocation_region(BASE, SIZE)
+    fb.preallocate_cublas_workspaces()
+    net = _Mlp(torch)
+    xs = [torch.zeros(bs, 384, device="cuda", dtype=torch.float16) for bs in ASYNC_SIZES]
+    for _ in range(2):
+        for x in xs:
+            net(torch, x)
+    torch.cuda.synchronize()
+    return net, xs
+
+
+def _async_inputs(torch, i):
+    g = torch.Generator(device="cuda").manual_seed(100 + i)
+    return torch.randn(ASYNC_SIZES[i], 384, device="cuda", generator=g).half()
+
+
+def scenario_async_save(workdir):
+    torch, fb = _setup()
+    net, xs = _async_prepare(torch, fb)
+    archive = os.path.join(workdir, "archive")
+    os.makedirs(archive, exist_ok=True)
+    pool = fb.graph_pool_handle()
+    graphs, outs = [], []
+    for x in xs:
+        g = fb.CUDAGraph()
+        with fb.graph(g, pool=pool):
+            y = net(torch, x)
+        graphs.append(g)
+        outs.append(y)
+    for i, (g, y) in enumerate(zip(graphs, outs)):
+        g.save(os.path.join(archive, f"graph_{i}.json"), output_tensors=y)
+    fb.pack_fatbins_to_folder(archive)
+    manifest = fb.save_graph_manifest(archive)
+    results = []
+    for i, (g, x, y) in enumerate(zip(graphs, xs, outs)):
+        x.copy_(_async_inputs(torch, i))
+        g.replay()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(y, net(torch, x), rtol=2e-3, atol=2e-3)
+        results.append(y.cpu().clone())
+    torch.save(results, os.path.join(workdir, "async_out.pt"))
+    groups = len(manifest["topology_groups"]) if manifest else len(ASYNC_SIZES)
+    print(json.dumps({"ok": True, "graphs": len(graphs), "groups": groups}))
+
+
+def scenario_async_load(workdir):
+    import time
+
+    torch, fb = _setup()
+    archive = os.path.join(workdir, "archive")
+    fb.set_skip_fatbin_processing(True)
+    fb.load_cuda_modules_and_libraries(archive)
+    net, xs = _async_prepare(torch, fb)
+    paths = [os.path.join(archive, f"graph_{i}.json") for i in range(len(ASYNC_SIZES))]
+    t0 = time.perf_counter()
+    pending = fb.CUDAGraph.start_graph_builds(paths)
+    started = time.perf_counter() - t0
+    busy = sum(i * i for i in range(200_000))  # host work overlapping the background builds
+    loaded = fb.CUDAGraph.finish_graph_loads(pending)
+    total = time.perf_counter() - t0
+    saved = torch.load(os.path.join(workdir, "async_out.pt"))
+    # replay in an order unlike capture order: on-demand members patch their template
+    for i in [3, 0, 7, 1, 11, 6, 2, 9, 4, 8, 10, 5]:
+        g, y = loaded[i]
+        xs[i].copy_(_async_inputs(torch, i))
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y.cpu(), saved[i]), f"graph {i}: LOAD replay differs from SAVE replay"
+        torch.testing.assert_close(y, net(torch, xs[i]), rtol=2e-3, atol=2e-3)
+    print(json.dumps({"ok": busy > 0, "start_s": started, "restore_s": total}))
+
+
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
     {"region": scenario_region, "prealloc": scenario_prealloc, "graph_save": scenario_graph_save,
-     "graph_load": scenario_graph_load}[name](workdir)
+     "graph_load": scenario_graph_load, "async_save": scenario_async_save,
+     "async_load": scenario_async_load}[name](workdir)

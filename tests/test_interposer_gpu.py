@@ -1,7 +1,7 @@
 """The LD_PRELOAD interposer on the real driver: region placement of torch
-allocations, stop/resume, preallocation, and a torch graph (cuBLAS GEMMs +
+allocations, stop/resume, preallocation, a torch graph (cuBLAS GEMMs +
 elementwise kernels from libtorch) saved in one process and restored in
-another, bit-exact."""
+another, bit-exact, and 12 such graphs restored asynchronously."""
 
 import json
 import os
@@ -37,3 +37,11 @@ def test_torch_graph_save_load(tmp_path):
     info = _run("graph_save", str(tmp_path))
     assert info["nodes"] > 2
     assert _run("graph_load", str(tmp_path))["ok"]
+
+
+def test_async_restore_of_graphs_sharing_topologies(tmp_path):
+    """12 graphs at batch sizes 8..1024 with repeats (members share topology
+    templates), restored with start_graph_builds overlapped with host work."""
+    info = _run("async_save", str(tmp_path))
+    assert info["graphs"] == 12 and info["groups"] < 12, info
+    assert _run("async_load", str(tmp_path))["ok"]
