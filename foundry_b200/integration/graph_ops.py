@@ -65,7 +65,11 @@ class LoadPlan:
 
 def start_graph_builds(workspace: str, num_threads: int = 8) -> LoadPlan:
     """LOAD: parallel read of every graph file of the workspace and background
-    template builds; graphs are finished one by one by ``capture_or_load``."""
+    template builds; graphs are finished one by one by ``capture_or_load``.
+    A second call in the same process returns the plan already started."""
+    st = runtime.state()
+    if st is not None and st.pending is not None:
+        return st.pending
     found = []
     for name in os.listdir(workspace):
         p = parse_filename(name)
@@ -75,7 +79,6 @@ def start_graph_builds(workspace: str, num_threads: int = 8) -> LoadPlan:
     paths = [f[2] for f in found]
     pending = CUDAGraph.start_graph_builds(paths, num_threads=num_threads) if paths else None
     plan = LoadPlan(pending, {f[1]: i for i, f in enumerate(found)}, paths)
-    st = runtime.state()
     if st is not None:
         st.pending = plan
     return plan

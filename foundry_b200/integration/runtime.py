@@ -20,8 +20,8 @@ import logging
 import os
 from dataclasses import asdict, dataclass, field
 
-from .. import (get_current_alloc_offset, load_cuda_modules_and_libraries, set_allocation_region,
-                set_current_alloc_offset, set_skip_fatbin_processing)
+from .. import (get_current_alloc_offset, load_cuda_modules_and_libraries, preallocate_region,
+                set_allocation_region, set_current_alloc_offset, set_skip_fatbin_processing)
 from ..allocation_region import parse_size
 from .config import GraphExtensionConfig, GraphExtensionMode
 
@@ -124,6 +124,28 @@ def capture_final_alloc_offset() -> int:
     return off
 
 
+def preallocate_for_load_mode() -> int:
+    """LOAD: maps the rest of SAVE's working set in one piece, from the cursor
+    to SAVE's final offset, so the weight, KV-cache and graph allocations that
+    follow are sub-allocated from it (same addresses, no map call each).
+    Returns the bytes mapped (0 outside LOAD or without a recorded offset).
+
+    Parity: reference python/foundry/integration/vllm/runtime.py:235-264."""
+    if _state is None or _state.config.mode != GraphExtensionMode.LOAD:
+        return 0
+    path = os.path.join(_state.config.workspace_dir, FINAL_OFFSET)
+    if not os.path.exists(path):
+        return 0
+    with open(path) as f:
+        want = int(json.load(f)["final_alloc_offset"])
+    size = want - get_current_alloc_offset()
+    if size <= 0:
+        return 0
+    preallocate_region(size)
+    log.info("[foundry] LOAD: preallocated %d MiB up to the SAVE final offset", size >> 20)
+    return size
+
+
 def ld_preload_env(env: dict | None = None, config: GraphExtensionConfig | None = None) -> dict:
     """Environment for a spawned engine process: preload the interposer and
     carry the config path."""
@@ -142,5 +164,5 @@ def reset() -> None:
     _state = None
 
 
-__all__ = ["ExtensionState", "WarmupState", "capture_final_alloc_offset", "ld_preload_env", "mode", "reset",
-           "setup_graph_extension", "skip_to_scratch_boundary", "state"]
+__all__ = ["ExtensionState", "WarmupState", "capture_final_alloc_offset", "ld_preload_env", "mode",
+           "preallocate_for_load_mode", "reset", "setup_graph_extension", "skip_to_scratch_boundary", "state"]

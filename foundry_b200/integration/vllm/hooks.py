@@ -11,8 +11,23 @@
                                    reuses it (re-profiling could size the KV
                                    cache differently and move every address)
   kernel_warmup (gpu_worker)       skipped on LOAD (its kernels are restored)
-  GPUModelRunner.capture_model     LOAD: start all graph builds first; SAVE:
-                                   manifest + packed modules + final offset
+  GPUModelRunner.load_model        LOAD: map SAVE's working set in one piece
+                                   before the weights load, start the graph
+                                   builds right after (they overlap the KV
+                                   cache setup and profiling that follow)
+  GPUModelRunner._dummy_run        SAVE/LOAD: the one eager sampler-warm-up
+                                   forward (runtime mode NONE, skip_eplb, no
+                                   profile/capture/attention/decode flag)
+                                   returns zero hidden states instead of
+                                   running the model; every other dummy run
+                                   (profiling, capture, DP padding) runs
+  GPUModelRunner.capture_model     LOAD: start all graph builds first (if not
+                                   already); SAVE: manifest + packed modules +
+                                   final offset
+  torch.cuda.get_device_capability answered from NVML, so importing a kernel
+                                   library in the API-server process does not
+                                   create a CUDA context there (a process that
+                                   has one cannot fork engine workers)
 
 Spawned engine processes install the same hooks through the
 ``_site/sitecustomize.py`` shim when FOUNDRY_GRAPH_CONFIG names the TOML file
@@ -26,6 +41,7 @@ from __future__ import annotations
 
 import logging
 import os
+import time
 
 from .. import graph_ops, runtime
 from ..config import GraphExtensionConfig, GraphExtensionMode, global_rank
@@ -105,6 +121,78 @@ def _kernel_warmup(worker, *a, **k):
     return _originals["kernel_warmup"](worker, *a, **k)
 
 
+def _load_model(self, *a, **k):
+    st = runtime.state()
+    if st is None or st.config.mode != GraphExtensionMode.LOAD:
+        return _originals["GPUModelRunner.load_model"](self, *a, **k)
+    t0 = time.perf_counter()
+    runtime.preallocate_for_load_mode()
+    r = _originals["GPUModelRunner.load_model"](self, *a, **k)
+    graph_ops.start_graph_builds(st.config.workspace_dir)
+    log.info("[foundry TIMING] load_model (preallocate + weights + start graph builds): %.3f s",
+             time.perf_counter() - t0)
+    return r
+
+
+def is_sampler_warmup_run(kwargs: dict) -> bool:
+    """The eager full forward vLLM runs once before the sampler warm-up
+    (Worker.compile_or_warm_up_model): runtime mode NONE with skip_eplb and
+    none of the flags that mark profiling, capture, forced attention or a
+    uniform-decode (DP padding) batch."""
+    mode = kwargs.get("cudagraph_runtime_mode")
+    return (mode is not None and getattr(mode, "name", None) == "NONE" and kwargs.get("skip_eplb") is True
+            and not any(kwargs.get(f) for f in ("is_profile", "is_graph_capturing", "force_attention",
+                                                "uniform_decode")))
+
+
+def _dummy_run(self, *a, **k):
+    if runtime.mode() == GraphExtensionMode.NONE or not is_sampler_warmup_run(k):
+        return _originals["GPUModelRunner._dummy_run"](self, *a, **k)
+    import torch
+
+    n = int(a[0]) if a else int(k.get("num_tokens", 1))
+    hs = torch.zeros(n, self.model_config.get_hidden_size(), device=self.device, dtype=self.model_config.dtype)
+    return hs, hs
+
+
+def nvml_device_capability(device=None, _nvml=None) -> tuple[int, int]:
+    """(major, minor) of ``device`` from NVML (no CUDA context is created)."""
+    nv = _nvml
+    if nv is None:
+        import pynvml as nv
+    if not _nvml_started.get(id(nv)):
+        nv.nvmlInit()
+        _nvml_started[id(nv)] = True
+    if device is None:
+        idx = 0
+    elif isinstance(device, int):
+        idx = device
+    elif isinstance(device, str):
+        idx = int(device.split(":")[-1]) if ":" in device else 0
+    else:  # torch.device
+        idx = device.index or 0
+    major, minor = nv.nvmlDeviceGetCudaComputeCapability(nv.nvmlDeviceGetHandleByIndex(idx))
+    return int(major), int(minor)
+
+
+_nvml_started: dict = {}
+
+
+def _quarantine_capability() -> None:
+    import torch
+
+    orig = torch.cuda.get_device_capability
+    _originals["torch.cuda.get_device_capability"] = orig
+
+    def capability(device=None):
+        try:
+            return nvml_device_capability(device)
+        except Exception:
+            return orig(device)
+
+    torch.cuda.get_device_capability = capability
+
+
 def _capture_model(self, *a, **k):
     st = runtime.state()
     if st is not None and st.config.mode == GraphExtensionMode.LOAD:
@@ -128,17 +216,25 @@ def install_hooks(config: GraphExtensionConfig | str) -> None:
     _config = config
     if _originals:
         return
+    t0 = os.environ.get("FOUNDRY_SPAWN_T0_NS")
+    if t0:
+        log.info("[foundry TIMING] process start -> install_hooks: %.1f ms", (time.time_ns() - int(t0)) / 1e6)
+    _quarantine_capability()
     cg, gw, mr = _targets()
     _originals["CUDAGraphWrapper.__call__"] = cg.CUDAGraphWrapper.__call__
     _originals["Worker.init_device"] = gw.Worker.init_device
     _originals["Worker.determine_available_memory"] = gw.Worker.determine_available_memory
     _originals["kernel_warmup"] = gw.kernel_warmup
     _originals["GPUModelRunner.capture_model"] = mr.GPUModelRunner.capture_model
+    _originals["GPUModelRunner.load_model"] = mr.GPUModelRunner.load_model
+    _originals["GPUModelRunner._dummy_run"] = mr.GPUModelRunner._dummy_run
     cg.CUDAGraphWrapper.__call__ = _wrapper_call
     gw.Worker.init_device = _init_device
     gw.Worker.determine_available_memory = _determine_available_memory
     gw.kernel_warmup = _kernel_warmup
     mr.GPUModelRunner.capture_model = _capture_model
+    mr.GPUModelRunner.load_model = _load_model
+    mr.GPUModelRunner._dummy_run = _dummy_run
     log.info("[foundry] vLLM hooks installed (mode %s)", config.mode.value)
 
 
@@ -151,6 +247,11 @@ def uninstall_hooks() -> None:
     gw.Worker.determine_available_memory = _originals.pop("Worker.determine_available_memory")
     gw.kernel_warmup = _originals.pop("kernel_warmup")
     mr.GPUModelRunner.capture_model = _originals.pop("GPUModelRunner.capture_model")
+    mr.GPUModelRunner.load_model = _originals.pop("GPUModelRunner.load_model")
+    mr.GPUModelRunner._dummy_run = _originals.pop("GPUModelRunner._dummy_run")
+    import torch
+
+    torch.cuda.get_device_capability = _originals.pop("torch.cuda.get_device_capability")
     runtime.reset()
 
 
@@ -158,4 +259,4 @@ def installed() -> bool:
     return bool(_originals)
 
 
-__all__ = ["install_hooks", "installed", "uninstall_hooks"]
+__all__ = ["install_hooks", "installed", "is_sampler_warmup_run", "nvml_device_capability", "uninstall_hooks"]

@@ -16,6 +16,7 @@ import argparse
 import os
 import shutil
 import sys
+import time
 
 from ..config import GraphExtensionConfig
 from ..runtime import ld_preload_env
@@ -32,6 +33,7 @@ def main(argv=None) -> int:
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     env["PYTHONPATH"] = os.pathsep.join([site, root] + [p for p in env.get("PYTHONPATH", "").split(os.pathsep) if p])
     env["FOUNDRY_GRAPH_CONFIG"] = os.path.abspath(a.foundry_config)
+    env["FOUNDRY_SPAWN_T0_NS"] = str(time.time_ns())  # engine processes log their start-up cost from here
     env.setdefault("NCCL_CUMEM_ENABLE", "0")
     env.setdefault("NCCL_NVLS_ENABLE", "0")
     rest = [x for x in a.rest if x != "--"]

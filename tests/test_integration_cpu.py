@@ -59,11 +59,39 @@ assert runtime.skip_to_scratch_boundary() == 64 << 20
 assert get_current_alloc_offset() == 64 << 20
 p = core().region_alloc(4 << 20)
 assert p >= 0x600000000000 + (64 << 20)
+sizes = [3 << 20, 64 << 20, 5 << 20, 300 << 20, 2 << 20]
+addrs = [core().region_alloc(n) for n in sizes]
 off = runtime.capture_final_alloc_offset()
 assert json.load(open(os.path.join(ws, "rank_0", "final_alloc_offset.json")))["final_alloc_offset"] == off
+from foundry_b200 import pack_fatbins_to_folder
+pack_fatbins_to_folder(os.path.join(ws, "rank_0"))
+json.dump({"first": p, "addrs": addrs}, open(os.path.join(TMP, "save_addrs.json"), "w"))
 env = runtime.ld_preload_env({"LD_PRELOAD": "/x.so"})
 assert env["LD_PRELOAD"].split(":")[-1] == "/x.so" and "libfoundry_hook.so" in env["LD_PRELOAD"]
 print("RUNTIME_OK")
+"""
+
+RUNTIME_LOAD = r"""
+import json, os, sys
+sys.path.insert(0, ROOT)
+from foundry_b200 import core
+from foundry_b200.integration import graph_ops, runtime
+from foundry_b200.integration.config import GraphExtensionConfig
+ws = os.path.join(TMP, "arch")
+cfg = GraphExtensionConfig.from_dict({"mode": "load", "region_size": "1GB", "scratch_space_size": "64MB",
+                                      "workspace_root": ws, "base_addr": "0x600000000000"})
+runtime.setup_graph_extension(cfg, 0)
+runtime.skip_to_scratch_boundary()
+want = json.load(open(os.path.join(TMP, "save_addrs.json")))
+mapped = runtime.preallocate_for_load_mode()
+final = json.load(open(os.path.join(ws, "rank_0", "final_alloc_offset.json")))["final_alloc_offset"]
+assert mapped == final - (64 << 20), (mapped, final)
+got = [core().region_alloc(4 << 20)] + [core().region_alloc(n) for n in [3 << 20, 64 << 20, 5 << 20, 300 << 20, 2 << 20]]
+assert got == [want["first"]] + want["addrs"], (got, want)
+runtime.capture_final_alloc_offset()  # raises if the cursor drifted from SAVE's
+plan = graph_ops.start_graph_builds(cfg.workspace_dir)
+assert graph_ops.start_graph_builds(cfg.workspace_dir) is plan and plan.paths == []
+print("RUNTIME_LOAD_OK")
 """
 
 
@@ -72,6 +100,10 @@ def test_runtime_region_scratch_and_final_offset_on_mock(tmp_path):
     code = f"ROOT={ROOT!r}; TMP={str(tmp_path)!r}\n" + RUNTIME
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=180)
     assert r.returncode == 0 and "RUNTIME_OK" in r.stdout, r.stdout + r.stderr[-3000:]
+    # LOAD: one preallocated window up to SAVE's final offset gives the same addresses
+    code = f"ROOT={ROOT!r}; TMP={str(tmp_path)!r}\n" + RUNTIME_LOAD
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=180)
+    assert r.returncode == 0 and "RUNTIME_LOAD_OK" in r.stdout, r.stdout + r.stderr[-3000:]
 
 
 VLLM_HOOKS = r"""
@@ -80,18 +112,65 @@ sys.path.insert(0, ROOT)
 import vllm.compilation.cuda_graph as cg
 import vllm.v1.worker.gpu_worker as gw
 import vllm.v1.worker.gpu_model_runner as mr
-orig = (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, mr.GPUModelRunner.capture_model)
+import types, torch
+from vllm.config import CUDAGraphMode
+R = mr.GPUModelRunner
+orig = (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, R.capture_model, R.load_model,
+        R._dummy_run, torch.cuda.get_device_capability)
+from foundry_b200.integration import runtime
 from foundry_b200.integration.vllm import install_hooks, installed, uninstall_hooks
+from foundry_b200.integration.vllm.hooks import is_sampler_warmup_run
 from foundry_b200.integration.config import GraphExtensionConfig
-install_hooks(GraphExtensionConfig.from_dict({"mode": "save"}))
+cfg = GraphExtensionConfig.from_dict({"mode": "save"})
+install_hooks(cfg)
 assert installed()
-assert cg.CUDAGraphWrapper.__call__ is not orig[0] and gw.Worker.init_device is not orig[1]
-assert gw.kernel_warmup is not orig[2] and mr.GPUModelRunner.capture_model is not orig[3]
+now = (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, R.capture_model, R.load_model,
+       R._dummy_run, torch.cuda.get_device_capability)
+assert all(a is not b for a, b in zip(now, orig)), now
+# only the eager sampler warm-up forward is replaced
+none = CUDAGraphMode.NONE
+assert is_sampler_warmup_run({"cudagraph_runtime_mode": none, "skip_eplb": True})
+for extra in ("is_profile", "is_graph_capturing", "force_attention", "uniform_decode"):
+    assert not is_sampler_warmup_run({"cudagraph_runtime_mode": none, "skip_eplb": True, extra: True})
+assert not is_sampler_warmup_run({"skip_eplb": True})
+assert not is_sampler_warmup_run({"cudagraph_runtime_mode": CUDAGraphMode.FULL, "skip_eplb": True})
+runtime._state = runtime.ExtensionState(cfg, 0)
+fake = types.SimpleNamespace(model_config=types.SimpleNamespace(get_hidden_size=lambda: 16, dtype=torch.float32),
+                             device="cpu")
+hs, last = R._dummy_run(fake, 4, cudagraph_runtime_mode=none, skip_eplb=True)
+assert hs.shape == (4, 16) and not hs.any() and last is hs
 uninstall_hooks()
-assert (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup,
-        mr.GPUModelRunner.capture_model) == orig
+assert (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, R.capture_model, R.load_model,
+        R._dummy_run, torch.cuda.get_device_capability) == orig
 print("HOOKS_OK")
 """
+
+
+def test_nvml_capability_without_cuda_context():
+    from foundry_b200.integration.vllm.hooks import nvml_device_capability
+
+    class FakeNvml:
+        def __init__(self):
+            self.inits, self.asked = 0, []
+
+        def nvmlInit(self):
+            self.inits += 1
+
+        def nvmlDeviceGetHandleByIndex(self, i):
+            self.asked.append(i)
+            return ("h", i)
+
+        def nvmlDeviceGetCudaComputeCapability(self, h):
+            return (10, 0) if h[1] == 0 else (9, 0)
+
+    nv = FakeNvml()
+    assert nvml_device_capability(None, _nvml=nv) == (10, 0)
+    assert nvml_device_capability(1, _nvml=nv) == (9, 0)
+    assert nvml_device_capability("cuda:1", _nvml=nv) == (9, 0)
+    import torch
+
+    assert nvml_device_capability(torch.device("cuda", 0), _nvml=nv) == (10, 0)
+    assert nv.inits == 1 and nv.asked == [0, 1, 1, 0]
 
 
 def test_vllm_hooks_install_and_uninstall():
