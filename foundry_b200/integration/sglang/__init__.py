@@ -1,5 +1,5 @@
 """SGLang integration (SAVE/LOAD of CudaGraphRunner graphs); see hooks.py."""
 
-from .hooks import install_hooks, uninstall_hooks
+from .hooks import install_hooks, installed, uninstall_hooks, workspace_rank
 
-__all__ = ["install_hooks", "uninstall_hooks"]
+__all__ = ["install_hooks", "installed", "uninstall_hooks", "workspace_rank"]
