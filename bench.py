@@ -4,14 +4,16 @@ full engine per GPU, weak scaling), plus the persistence numbers of the same
 run: graph capture + SAVE, fresh-process cold start to first token, and
 restore time of the 67 decode graphs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl foundry|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl foundry|reference|torch]
 
 For N > 1 launch with torch.distributed.run (one rank per GPU). Rank 0 prints
 one JSON line. ``value`` is the device-timed decode rate (CUDA events around
 K back-to-back restored-graph steps, max over ranks, summed over ranks as
 tokens / slowest rank's time); ``e2e`` is the same metric through the public
 engine API with a pinned-host H2D of each step's input tokens and a D2H of
-the sampled tokens every step.
+the sampled tokens every step. ``--impl torch`` runs the same decode step in
+stock PyTorch (cuBLAS GEMMs, SDPA attention) under torch.cuda.graph, as a
+same-box comparison.
 """
 
 from __future__ import annotations
@@ -52,7 +54,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="foundry", choices=["foundry", "reference"])
+    ap.add_argument("--impl", default="foundry", choices=["foundry", "reference", "torch"],
+                    help="torch: the same decode step in stock PyTorch (cuBLAS, SDPA) under torch.cuda.graph")
     ap.add_argument("--model", default="llama-3-8b")
     ap.add_argument("--batch", type=int, default=None, help="prompts per GPU (dp/ep) or per job (tp)")
     ap.add_argument("--prompt-len", type=int, default=None)
@@ -144,6 +147,47 @@ def run_cli(cmd: list[str], env_extra: dict | None = None, timeout: int = 1800) 
     raise RuntimeError(f"runner {cmd[0]} printed no JSON:\n{res.stdout[-2000:]}")
 
 
+def run_torch_baseline(args, rank: int, world: int, local: int) -> int:
+    """Same model, batch and graph sizes as the foundry arm, in stock PyTorch
+    (foundry_b200/runner/torch_baseline.py); data-parallel over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from foundry_b200.runner.cli import parse_graph_sizes
+    from foundry_b200.runner.torch_baseline import run
+
+    gen = max(args.gen, 1 + args.warmup + 2 * args.steps + 2)
+    sizes = parse_graph_sizes(args.graph_sizes, 1024)
+    sampler = ClockSampler(local)
+    sampler.start()
+    r = run(args.model, args.batch, args.prompt_len, gen, args.steps, args.warmup, sizes, device=local)
+    clocks = sampler.stop()
+    t = torch.tensor([r["dev_ms"], r["capture_s"]], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_ms, capture_s = t.tolist()
+    tokens = args.batch * world * args.steps
+    if rank == 0:
+        print(json.dumps({
+            "impl": "torch",
+            "metric": f"graph decode tok/s ({args.model} shape, {r['num_graphs']} torch.cuda.graph decode graphs)",
+            "value": round(tokens / (dev_ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random token ids, random-init N(0,0.02) weights, KV cache filled with random "
+                    "values of the prompt length instead of a prefill)",
+            "config": {"model": args.model, "global_batch": args.batch * world, "seq_len": args.prompt_len + gen,
+                       "prompt_len": args.prompt_len, "parallelism": f"dp{world}", "graphs_per_rank": r["num_graphs"],
+                       "kernels": r["kernels_note"],
+                       "l2": "inputs larger than L2 (all weights + the KV cache are read every step)"},
+            "clocks": clocks,
+            "capture_s": round(capture_s, 2),
+        }))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -162,6 +206,8 @@ def main():
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    if args.impl == "torch":
+        return run_torch_baseline(args, rank, world, local)
 
     gen = max(args.gen, 1 + args.warmup + 2 * args.steps + 2)
     mode = args.parallel if world > 1 else "dp"
