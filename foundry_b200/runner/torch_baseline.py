@@ -146,3 +146,34 @@ def run(model: str, batch: int, prompt_len: int, gen: int, steps: int, warmup: i
 
 
 __all__ = ["TorchLlama", "run"]
+
+
+def _main(argv=None) -> int:
+    """One eager decode step of the baseline (for a kernel launch list):
+    python -m foundry_b200.runner.torch_baseline --model llama-3-8b@2l --batch 256 --ctx 512"""
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="llama-3-8b@2l")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--ctx", type=int, default=512)
+    ap.add_argument("--warmup", type=int, default=2)
+    a = ap.parse_args(argv)
+    cfg = config_by_name(a.model)
+    net = TorchLlama(cfg, a.batch, a.ctx + a.warmup + 2)
+    net.tokens.random_(0, cfg.vocab)
+    net.positions.fill_(a.ctx)
+    for _ in range(a.warmup):
+        net.step(a.batch)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    net.step(a.batch)
+    end.record()
+    torch.cuda.synchronize()
+    print({"eager_step_ms": start.elapsed_time(end), "layers": cfg.layers, "batch": a.batch})
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_main())
