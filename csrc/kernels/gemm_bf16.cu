@@ -663,3 +663,302 @@ FB_GEMM_SK_INSTANCE(32)
 FB_GEMM_SK_INSTANCE(64)
 FB_GEMM_SK_INSTANCE(128)
 FB_GEMM_SK_INSTANCE(256)
+
+// ==== two-SM variant (cta_group::2) ======================================================
+//
+// fb_gemm2_bf16_bn{BN}: a cluster of two CTAs (the two SMs of a TPC) computes
+// one 256-row x BN tile. Each CTA loads its own 128 A rows and half of the BN
+// B rows into its shared memory; the even CTA issues tcgen05.mma.cta_group::2
+// (M = 256), which reads both CTAs' shared memory at the same offsets and
+// accumulates each CTA's 128 rows x BN in that CTA's TMEM. Per SM and k-block
+// that is 16 KB of A + BN/2 x 128 B of B instead of 16 KB + BN x 128 B for the
+// same tensor work, so the ring is deeper at the same shared memory.
+//
+// Cross-CTA synchronisation (addresses of the other CTA come from mapa):
+//   full[s]   even CTA only: one arrival (its producer, expecting both CTAs'
+//             bytes); both CTAs' TMA loads complete_tx on it
+//   empty[s]  each CTA: the even CTA's MMA commits arrive on both
+//   tfull[a]  each CTA: the even CTA commits on both after a unit's last k-block
+//   tempty[a] even CTA only: 8 arrivals, the 4 epilogue warps of each CTA
+// Every mbarrier wait is bounded; the cluster barriers at start (barrier
+// initialisation visible to the peer) and end (no CTA leaves while the pair's
+// MMAs or remote arrivals may still touch it) are reached on every path.
+// No TMA multicast: loads carry .cta_group::2 only.
+namespace {
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa_cta(const void* p, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, uint32_t bar, int32_t c0, int32_t c1,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+
+template <int BN>
+struct PairCfg {
+  static constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 A rows per K step
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's half of the B rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int ACC_BUFS = (2 * BN <= 512) ? 2 : 1;
+  static constexpr uint32_t TMEM_COLS = tmem_cols_for(ACC_BUFS * BN);
+};
+
+template <int BN>
+__device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
+                                               const bf16* residual, int M, int N, int K, int ldo, int mode,
+                                               int splits, float* __restrict__ ws, long long split_stride) {
+  using C = PairCfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::ACC_BUFS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                           // [STAGES][128 x 64]
+  uint8_t* sB = smem + STAGES * C::A_BYTES;     // [STAGES][BN/2 x 64]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: issues the MMAs; 1: its peer
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  const int num_m = (M + 2 * BM - 1) / (2 * BM);
+  const int num_n = (N + BN - 1) / BN;
+  const int KB = (K + BK - 1) / BK;
+  const int kb_per = (KB + splits - 1) / splits;
+  const int num_units = num_m * num_n * splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(tmA);
+    tma_prefetch_desc(tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised before either signals the other
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint64_t pol_a = (mode & EPI_A_STREAM) ? policy_evict_first() : policy_evict_last();
+      const uint64_t pol_b = (mode & EPI_B_STREAM) ? policy_evict_first() : policy_evict_last();
+      const int pf_dist = (mode >> 8) & 0xFF;
+      for (int u = pair; u < num_units && !*(volatile int*)abort_flag; u += num_pairs) {
+        const int mn = u / splits, sp = u % splits;
+        const int m_blk = mn % num_m, n_blk = mn / num_m;
+        const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
+        const int a_row = m_blk * 2 * BM + rank * BM;
+        const int b_row = n_blk * BN + rank * (BN / 2);
+        for (int kb = kb0; kb < min(kb1, kb0 + pf_dist); ++kb) tma_prefetch_2d(tmA, kb * BK, a_row);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (pf_dist && kb + pf_dist < kb1) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, a_row);
+          if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+            *(volatile int*)abort_flag = 1;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          const uint32_t bar = mapa_cta(&full[stage], 0);
+          tma_load_2d_pair(sA + stage * C::A_BYTES, tmA, bar, kb * BK, a_row, pol_a);
+          tma_load_2d_pair(sB + stage * C::B_BYTES, tmB, bar, kb * BK, b_row, pol_b);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: every stage this CTA armed is consumed before it may leave.
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16<2 * BM, BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int u = pair; u < num_units && !*(volatile int*)abort_flag; u += num_pairs, ++it) {
+        const int sp = u % splits;
+        const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
+        const int acc = NBUF == 2 ? (it & 1) : 0;
+        const uint32_t aphase = NBUF == 2 ? ((it >> 1) & 1) : (it & 1);
+        if (!mbar_wait(&tempty[acc], aphase ^ 1, FB_KERR_TIMEOUT_TMEM)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_sw128(smem_u32(sA + stage * C::A_BYTES));
+          const uint64_t bdesc = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16_pair(d_tmem, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                          (kb > kb0 || k > 0) ? 1u : 0u);
+          mma_commit_pair(mapa_cta(&empty[stage], 0));
+          mma_commit_pair(mapa_cta(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit_pair(mapa_cta(&tfull[acc], 0));
+        mma_commit_pair(mapa_cta(&tfull[acc], 1));
+        if (!ok) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int quarter = warp & 3;
+    const uint32_t tempty0 = mapa_cta(&tempty[0], 0), tempty1 = mapa_cta(&tempty[1], 0);
+    int it = 0;
+    for (int u = pair; u < num_units && !*(volatile int*)abort_flag; u += num_pairs, ++it) {
+      const int mn = u / splits, sp = u % splits;
+      const int m_blk = mn % num_m, n_blk = mn / num_m;
+      const int acc = NBUF == 2 ? (it & 1) : 0;
+      const uint32_t aphase = NBUF == 2 ? ((it >> 1) & 1) : (it & 1);
+      if (!mbar_wait(&tfull[acc], aphase, FB_KERR_TIMEOUT_TMEM)) {
+        *(volatile int*)abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      float* part = splits > 1 ? ws + static_cast<size_t>(sp) * split_stride : nullptr;
+      const int gm = m_blk * 2 * BM + rank * BM + quarter * 32 + lane;  // D row of this thread
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + c0, r);
+        tmem_ld_wait();
+        const int gn0 = n_blk * BN + c0;
+        if (gm >= M) continue;
+        if (mode & EPI_TRANSPOSE) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int gn = gn0 + i;
+            if (gn < N) {
+              const size_t idx = static_cast<size_t>(gn) * ldo + gm;
+              float v = __uint_as_float(r[i]);
+              if (part) {
+                part[idx] = v;
+              } else {
+                if (mode & EPI_RESIDUAL) v += bf2f(residual[idx]);
+                out[idx] = f2bf(v);
+              }
+            }
+          }
+        } else {
+          const size_t base = static_cast<size_t>(gm) * ldo + gn0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (gn0 + i < N) {
+              float v = __uint_as_float(r[i]);
+              if (part) {
+                part[base + i] = v;
+              } else {
+                if (mode & EPI_RESIDUAL) v += bf2f(residual[base + i]);
+                out[base + i] = f2bf(v);
+              }
+            }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // the pair's MMAs, commits and remote arrivals are done
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace
+
+#define FB_GEMM_PAIR_INSTANCE(BN)                                                                                   \
+  extern "C" __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1) fb_gemm2_bf16_bn##BN(      \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
+      const bf16* residual, int M, int N, int K, int ldo, int mode, int splits, float* ws,                          \
+      long long split_stride) {                                                                                      \
+    gemm_pair_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);                   \
+  }
+
+FB_GEMM_PAIR_INSTANCE(64)
+FB_GEMM_PAIR_INSTANCE(128)
+FB_GEMM_PAIR_INSTANCE(256)

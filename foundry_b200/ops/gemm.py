@@ -16,6 +16,7 @@ while it reads its input. Callers that cannot consume slices pass no
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -43,6 +44,22 @@ def smem_bytes(bn: int, mt: int = 1) -> int:
     stage = mt * BM * BK * 2 + bn * BK * 2
     stages = min(8, (200 * 1024) // stage)
     return stages * stage + 1024 + 256
+
+
+def smem_bytes_pair(bn: int) -> int:
+    """Shared memory of one CTA of the two-SM kernel (its 128 A rows + bn/2 B rows per stage)."""
+    stage = BM * BK * 2 + (bn // 2) * BK * 2
+    stages = min(8, (200 * 1024) // stage)
+    return stages * stage + 1024 + 256
+
+
+# Two-SM (cta_group::2) tiles for swap-AB decode GEMMs: "1" uses them for
+# every swap plan with tiles of 64+ tokens, "0" (default) never. Measured on
+# B200 at 256 tokens (us, one-SM -> two-SM): gate_up 4096->28672 72.8 -> 68.3,
+# lm_head 4096->128256 243.8 -> 232.6, but qkv 21.9 -> 25.4, o 19.2 -> 23.0,
+# down 33.6 -> 37.1 and 64/128-token gate_up 48.2 -> 53.0 / 53.9 -> 58.0:
+# halving each SM's token-operand traffic is not what bounds these GEMMs.
+_PAIR = os.environ.get("FOUNDRY_GEMM_PAIR", "0")
 
 
 @dataclass
@@ -115,10 +132,21 @@ class Plan:
     mt: int = 1  # 128-row A tiles per work unit (2 = two MMAs share each B tile)
     pf: int = 0  # k-blocks of L2 prefetch lead for streamed A tiles (0 = off)
     streamk: bool = False  # equal (tile, k-block) shares per CTA (fb_gemm_sk_*)
+    pair: bool = False  # two-SM 256-row tiles (fb_gemm2_*); grid counts CTAs (two per pair)
 
     @property
     def kernel(self) -> str:
+        if self.pair:
+            return f"fb_gemm2_bf16_bn{self.bn}"
         return f"fb_gemm_sk_bn{self.bn}" if self.streamk else f"fb_gemm_bf16_bn{self.bn}_m{self.mt}"
+
+    @property
+    def smem(self) -> int:
+        return smem_bytes_pair(self.bn) if self.pair else smem_bytes(self.bn, self.mt)
+
+    @property
+    def b_box(self) -> int:
+        return self.bn // 2 if self.pair else self.bn
 
 
 def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bool = True,
@@ -170,12 +198,38 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
     # 47.3 -> 40.8 us at 64 tokens (bn 64), 52.6 -> 51.1 us at 128 (bn 128),
     # but 71.8 -> 76.3 us at 256 (bn 256: the partial-tile exchange costs more
     # than the half-empty second wave), so only narrow tiles use it.
+    if _PAIR == "1" and best.swap and best.bn >= 64 and mg >= 2 * BM:
+        return pair_plan(mg, ng, k, best.bn, sms, allow_split, best.pf)
     if allow_streamk and best.swap and best.splits == 1 and best.mt == 1 and best.bn <= 64:
         tiles = math.ceil(mg / BM) * math.ceil(ng / best.bn)
         if tiles > sms and tiles % sms:
             best.streamk = True
             best.grid = sms
     return best
+
+
+def pair_plan(mg: int, ng: int, k: int, bn: int, sms: int, allow_split: bool = True, pf: int = 4) -> Plan:
+    """Two-SM plan for a swap-AB GEMM (mg weight rows, ng tokens): 256-row
+    tiles, split K while more splits shorten the waves of CTA pairs."""
+    pairs = sms // 2
+    kb = math.ceil(k / BK)
+    tiles = math.ceil(mg / (2 * BM)) * math.ceil(ng / bn)
+    stage = BM * BK * 2 + (bn // 2) * BK * 2  # per SM
+    stages = min(8, (200 * 1024) // stage)
+    mma = 2 * BM * bn * BK / _SM_MMA_FLOPS
+    t_kb = max((_TMA_LATENCY + mma) / stages, stage / _CTA_FILL_BPS_MAX, mma)
+    dram = (mg * k + ng * k) * 2 / _HBM_BPS
+    best_s, best_t = 1, None
+    for s in range(1, (MAX_SPLITS if allow_split else 1) + 1):
+        if s > 1 and kb // s < 4:
+            break
+        t = max(math.ceil(tiles * s / pairs) * math.ceil(kb / s) * t_kb, dram)
+        if s > 1:
+            t += 2 * s * mg * ng * 4 / _HBM_BPS
+        if best_t is None or t < best_t * 0.97:
+            best_s, best_t = s, t
+    units = tiles * best_s
+    return Plan(bn=bn, splits=best_s, grid=2 * min(units, pairs), swap=True, est_us=best_t * 1e6, pf=pf, pair=True)
 
 
 def linear_multicast(x: torch.Tensor, w: torch.Tensor, target: int, plan_override: Plan | None = None) -> None:
@@ -224,9 +278,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         need = p.splits * t_tok * n_out
         if need > partials.numel:
             raise RuntimeError(f"split-K slice buffer too small: need {need} floats, have {partials.numel}")
-        args = [tmap(a, BM), tmap(b, p.bn), 0, 0, mg, ng, k, n_out, mode, p.splits,
+        args = [tmap(a, BM), tmap(b, p.b_box), 0, 0, mg, ng, k, n_out, mode, p.splits,
                 partials.buf.data_ptr(), t_tok * n_out]
-        _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))
+        _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)
         return Partial(partials.buf, p.splits, t_tok, n_out)
     if out is None:
         out = torch.empty(t_tok, n_out, dtype=torch.bfloat16, device=x.device)
@@ -239,7 +293,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
                 mg, ng, k, out.stride(0), mode, streamk.ws.data_ptr(), streamk.flags.data_ptr()]
         _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, 1))
         return out
-    args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
+    args = [tmap(a, BM), tmap(b, p.b_box), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
             mg, ng, k, out.stride(0), mode, 1, 0, 0]
-    _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))
+    _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)
     return out

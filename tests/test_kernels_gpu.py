@@ -60,6 +60,36 @@ def test_linear_all_tile_configs(bn, mt, splits, t, n, k, swap):
         torch.testing.assert_close(total, ref, atol=4e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("bn,splits,t,n,k,residual", [
+    (64, 1, 64, 512, 256, False), (128, 2, 200, 4224, 4160, True), (256, 1, 256, 2304, 1024, True),
+    (256, 3, 256, 1536, 4096, False),
+])
+def test_linear_pair_tiles(bn, splits, t, n, k, residual):
+    """Two-SM (cta_group::2) 256-row tiles against fp32: M, N and K tails,
+    residual epilogue and split-K slices."""
+    from foundry_b200 import ops
+    from foundry_b200.ops import gemm as G
+
+    x = _bf(t, k, seed=31)
+    w = _bf(n, k, scale=0.05, seed=32)
+    p = G.pair_plan(n, t, k, bn, G._rt.sm_count(), allow_split=splits > 1)
+    p.splits = splits
+    p.grid = 2 * min(math.ceil(n / 256) * math.ceil(t / bn) * splits, G._rt.sm_count() // 2)
+    assert p.pair and p.kernel == f"fb_gemm2_bf16_bn{bn}"
+    ref = x.float() @ w.float().T
+    if splits > 1:
+        pb = ops.PartialBuffer(splits * t * n)
+        r = ops.linear(x, w, partials=pb, plan_override=p)
+        total = r.buf[: splits * t * n].view(splits, t, n).sum(0)
+        torch.testing.assert_close(total, ref, atol=4e-2, rtol=2e-2)
+        return
+    res = _bf(t, n, seed=33) if residual else None
+    out = res.clone() if residual else torch.empty(t, n, dtype=torch.bfloat16, device="cuda")
+    ops.linear(x, w, out=out, residual=out if residual else None, plan_override=p)
+    want = ref + (res.float() if residual else 0)
+    torch.testing.assert_close(out.float(), want, atol=4e-2, rtol=2e-2)
+
+
 @pytest.mark.parametrize("t,n,k", [(8, 4096, 4096), (64, 1024, 14336), (600, 512, 1024)])
 def test_linear_residual(t, n, k):
     from foundry_b200 import ops
