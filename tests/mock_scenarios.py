@@ -161,6 +161,85 @@ def scenario_load(workdir: str) -> None:
     print("LOAD OK", len(graphs), templates, pending.phase1_ms, pending.phase2_ms)
 
 
+def _cluster_graph_json(img_hash: int, ptrs: list[int], cluster: int | None, seed: int) -> str:
+    """Four kernels; node 2 launches with a (cluster, 1, 1) cluster when
+    ``cluster`` is set (the shape of the two-SM GEMM's launch)."""
+    rnd = random.Random(seed)
+    nodes = []
+    for n in range(4):
+        params, off = [], 0
+        for i, sz in enumerate(PARAM_SIZES):
+            val = struct.pack("<Q", ptrs[rnd.randrange(len(ptrs))]) if (sz == 8 and i < 3) else \
+                bytes(rnd.getrandbits(8) for _ in range(sz))
+            params.append({"index": i, "offset": off, "size": sz, "value_hex": val.hex()})
+            off += sz
+        node = {"id": n, "type": "KernelNode", "params": {
+            "blockDimX": 192, "blockDimY": 1, "blockDimZ": 1, "gridDimX": 2 * (1 + rnd.randrange(74)),
+            "gridDimY": 1, "gridDimZ": 1, "sharedMemBytes": 0, "kernelParams": params,
+            "function_name": f"fbmock_k{n}", "kernel_source_binary_hash": f"{img_hash:016x}"}}
+        if n == 2 and cluster:
+            node["params"]["kernel_node_attrs"] = {"attrQueryAvailable": 1, "clusterDimX": cluster,
+                                                   "clusterDimY": 1, "clusterDimZ": 1}
+        nodes.append(node)
+    deps = [{"from": i, "to": i + 1} for i in range(3)]
+    return json.dumps({"nodes": nodes, "dependencies": deps, "topology_key": "", "generators": []})
+
+
+def scenario_cluster(workdir: str) -> None:
+    """Cluster launch dimensions survive analysis, JSON and .cugraph, restore
+    onto the rebuilt node, and split topology groups: graphs 0 and 2 (node 2
+    in 2-CTA clusters) share a template, graph 1 (no cluster) does not."""
+    fb, c = _core()
+    phase = sys.argv[3]
+    archive = os.path.join(workdir, "cluster_archive")
+    img = os.path.join(workdir, "mock.cubin")
+    if phase == "save":
+        os.makedirs(archive, exist_ok=True)
+        c.set_allocation_region(BASE, REGION)
+        ptrs = [c.region_alloc(1 << 20) for _ in range(8)]
+        with open(img, "wb") as f:
+            f.write(_image_bytes(0))
+        _, h = c.load_image_file(img)
+        keys = []
+        for gi, cl in enumerate((2, None, 2)):
+            desc = c.graph_from_json_text(_cluster_graph_json(h, ptrs, cl, 50 + gi))
+            c.recompute_topology_key(desc)
+            live = c.build_live_graph(desc)
+            analyzed = c.analyze_graph(live)
+            c.destroy_graph(live)
+            node2 = json.loads(analyzed.to_json())["nodes"][2]["params"]
+            if cl:
+                attrs = node2.get("kernel_node_attrs") or json.loads(analyzed.to_json()).get("common_kernel_node_attrs")
+                assert attrs and attrs["clusterDimX"] == 2, node2
+            keys.append(analyzed.topology_key)
+            analyzed.save(os.path.join(archive, f"graph_{gi}.json"))
+        assert ":C2_1_1" in keys[0] and ":C2_1_1" not in keys[1] and keys[0] == keys[2], keys
+        fb.pack_fatbins_to_folder(archive)
+        from foundry_b200.graphs import save_graph_manifest
+
+        m = save_graph_manifest(archive)
+        assert len(m["topology_groups"]) == 2, m
+        with open(os.path.join(workdir, "cluster_keys.json"), "w") as f:
+            json.dump(keys, f)
+        print("CLUSTER SAVE OK")
+        return
+    keys = json.load(open(os.path.join(workdir, "cluster_keys.json")))
+    fb.load_cuda_modules_and_libraries(archive)
+    c.set_allocation_region(BASE, REGION)
+    paths = [os.path.join(archive, f"graph_{i}.json") for i in range(3)]
+    for p, k in zip(paths, keys):
+        d = c.read_binary_graph(p.replace(".json", ".cugraph"))
+        assert d.topology_key == k
+    pending = c.start_graph_builds(paths, 2)
+    pending.wait()
+    assert pending.num_groups == 2, pending.num_groups
+    graphs = [pending.finish_one(i) for i in range(3)]
+    for g, k in zip(graphs, keys):
+        assert g.desc.topology_key == k
+        g.launch(0)
+    print("CLUSTER LOAD OK")
+
+
 def scenario_numeric(workdir: str) -> None:
     """A graph of axpy/fill kernels on region memory: SAVE runs it, LOAD restores
     and runs it again; results must be bit-identical."""
@@ -293,4 +372,5 @@ def scenario_faults(workdir: str) -> None:
 
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
-    {"save": scenario_save, "load": scenario_load, "numeric": scenario_numeric, "faults": scenario_faults}[name](workdir)
+    {"save": scenario_save, "load": scenario_load, "numeric": scenario_numeric, "faults": scenario_faults,
+     "cluster": scenario_cluster}[name](workdir)

@@ -69,3 +69,12 @@ def test_numeric_save_load_bit_exact(saved):
 
 def test_fault_injection(saved):
     assert "FAULTS OK" in _run("faults", saved)
+
+
+def test_cluster_launch_dims_round_trip(tmp_path):
+    """Kernel nodes launched in thread-block clusters (the two-SM GEMM's shape)
+    keep their cluster dims through analysis, JSON, .cugraph and restore, and
+    only graphs with the same cluster shapes share a topology template."""
+    wd = str(tmp_path)
+    assert "CLUSTER SAVE OK" in _run("cluster", wd, "save")
+    assert "CLUSTER LOAD OK" in _run("cluster", wd, "load")
