@@ -253,6 +253,7 @@ def main():
 
     for _ in range(args.warmup):
         eng.decode_step(b)
+    eng.wait_materialized()  # restored graphs get their own executables after the first step
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()

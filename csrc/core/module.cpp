@@ -508,10 +508,11 @@ PYBIND11_MODULE(_C, m) {
       .def_property_readonly("path", [](const RestoredGraph& g) { return g.path; })
       .def_property_readonly("is_template", [](const RestoredGraph& g) { return g.is_template; })
       .def_property_readonly("num_diff_nodes", [](const RestoredGraph& g) { return g.diff_nodes.size(); })
-      .def_property_readonly("materialized", [](const RestoredGraph& g) { return g.own_exec != nullptr; })
+      .def_property_readonly("materialized", [](const RestoredGraph& g) { return g.own_exec.load() != nullptr; })
       .def_property_readonly("last_switch_ns", [](const RestoredGraph& g) { return g.last_switch_ns; })
       .def_property_readonly("exec_handle", [](const RestoredGraph& g) {
-        return reinterpret_cast<uintptr_t>(g.own_exec ? g.own_exec : (g.shared ? g.shared->exec : nullptr));
+        CUgraphExec e = g.own_exec.load();
+        return reinterpret_cast<uintptr_t>(e ? e : (g.shared ? g.shared->exec : nullptr));
       })
       .def_property_readonly("output_tensors_json", [](const RestoredGraph& g) { return g.desc->output_tensors_json; });
   m.def("load_graph", [](const std::string& path) {

@@ -76,7 +76,8 @@ SharedExec::~SharedExec() {
 }
 
 RestoredGraph::~RestoredGraph() {
-  if (own_exec && fb_driver()->cuGraphExecDestroy) fb_driver()->cuGraphExecDestroy(own_exec);
+  CUgraphExec e = own_exec.load(std::memory_order_acquire);
+  if (e && fb_driver()->cuGraphExecDestroy) fb_driver()->cuGraphExecDestroy(e);
   if (shared) {
     std::lock_guard<std::mutex> lk(shared->mu);
     if (shared->current == this) shared->current = nullptr;
@@ -105,8 +106,8 @@ std::vector<uint32_t> diff_against(const GraphDesc& tmpl, const GraphDesc& membe
 
 void RestoredGraph::launch(CUstream stream) {
   const FbDriver* d = fb_driver();
-  if (own_exec) {
-    check_drv(d->cuGraphLaunch(own_exec, stream), "cuGraphLaunch");
+  if (CUgraphExec e = own_exec.load(std::memory_order_acquire)) {
+    check_drv(d->cuGraphLaunch(e, stream), "cuGraphLaunch");
     return;
   }
   if (!shared || !shared->exec) throw std::runtime_error("graph has no executable (load failed?)");
@@ -134,14 +135,16 @@ void RestoredGraph::launch(CUstream stream) {
 }
 
 void RestoredGraph::materialize() {
-  if (own_exec) return;
+  std::lock_guard<std::mutex> lk(materialize_mu);
+  if (own_exec.load(std::memory_order_acquire)) return;
+  if (ctx) check_drv(fb_driver()->cuCtxSetCurrent(ctx), "cuCtxSetCurrent");
   GraphDesc g = *desc;
   if (!g.has_deps && shared && shared->template_desc) {
     g.deps = shared->template_desc->deps;
     g.has_deps = true;
   }
   own_built = build_graph(g);
-  own_exec = instantiate(own_built->graph);
+  own_exec.store(instantiate(own_built->graph), std::memory_order_release);
 }
 
 std::shared_ptr<RestoredGraph> restore_single(std::shared_ptr<GraphDesc> desc, const std::string& path) {
@@ -155,6 +158,7 @@ std::shared_ptr<RestoredGraph> restore_single(std::shared_ptr<GraphDesc> desc, c
   r->shared = shared;
   r->path = path;
   r->is_template = true;
+  fb_driver()->cuCtxGetCurrent(&r->ctx);
   shared->current = r.get();
   return r;
 }
@@ -317,6 +321,7 @@ std::shared_ptr<RestoredGraph> PendingLoads::finish_one(size_t index) {
   r->path = paths[index];
   r->is_template = group_template[group_of[index]] == static_cast<int>(index);
   r->diff_nodes = diffs[index];
+  r->ctx = ctx;
   if (r->is_template) {
     std::lock_guard<std::mutex> lk(r->shared->mu);
     if (!r->shared->current) r->shared->current = r.get();

@@ -47,13 +47,17 @@ class RestoredGraph {
   std::vector<uint32_t> diff_nodes;  // positions that differ from the template
   std::string path;
   bool is_template = false;
-  // Own exec after materialize().
+  // Own exec after materialize(). Published with release ordering once fully
+  // instantiated, so a launch on another thread either sees nothing (and
+  // uses the shared exec) or the finished exec.
   std::unique_ptr<BuiltGraph> own_built;
-  CUgraphExec own_exec = nullptr;
+  std::atomic<CUgraphExec> own_exec{nullptr};
+  std::mutex materialize_mu;
+  CUcontext ctx = nullptr;  // context of the restoring thread (made current by materialize)
 
   ~RestoredGraph();
   void launch(CUstream stream);
-  void materialize();
+  void materialize();  // safe on any thread, concurrently with launch()
   size_t num_nodes() const { return desc ? desc->nodes.size() : 0; }
   uint64_t last_switch_ns = 0;
 };

@@ -20,6 +20,7 @@ python/foundry/integration/vllm/graph_ops.py:123-205 capture-or-load loop).
 from __future__ import annotations
 
 import math
+import threading
 import time
 from dataclasses import dataclass, field
 
@@ -263,6 +264,13 @@ class LLMEngine:
         self.model = model_cls(cfg, self.weights, self.cos_sin)
         self.graph_sizes = sorted(ecfg.graph_sizes or default_graph_sizes(ecfg.max_batch))
         self.graphs: dict[int, object] = {}
+        # Restored graphs share one executable per topology group and patch
+        # their differing nodes in when the batch size changes. After the
+        # first decode step a background thread gives every graph its own
+        # executable (largest batch first), so later switches cost nothing.
+        self.materialize_after_first_step = False
+        self._materializer: threading.Thread | None = None
+        self._stop_materializing = False
         # Under expert parallelism page 0 is kept for the padding prefill
         # chunks that keep every rank's collective steps in step.
         self.free_pages = list(range(nb - 1, 0 if self.ep is not None else -1, -1))
@@ -410,6 +418,9 @@ class LLMEngine:
             self.graphs[b].replay()
         else:
             self._decode_body(b)
+        if self.materialize_after_first_step:
+            self.materialize_after_first_step = False
+            self.materialize_graphs(background=True)
         self.h_out[:b].copy_(st.next_ids[:b], non_blocking=True)
         if sync_tokens:
             torch.cuda.current_stream().synchronize()
@@ -461,9 +472,39 @@ class LLMEngine:
         torch.cuda.synchronize()
         return time.perf_counter() - t0
 
+    def materialize_graphs(self, sizes: list[int] | None = None, background: bool = True):
+        """Gives restored decode graphs their own executables (largest batch
+        first); with ``background`` on a daemon thread, returned. Graphs that
+        are not restored ones (captured here) are skipped."""
+        order = sorted(sizes if sizes is not None else list(self.graphs), reverse=True)
+
+        def run():
+            for s in order:
+                if self._stop_materializing:
+                    return
+                g = self.graphs.get(s)
+                if g is not None and hasattr(g, "materialize"):
+                    g.materialize()
+
+        if not background:
+            run()
+            return None
+        self.wait_materialized()
+        self._materializer = threading.Thread(target=run, name="foundry-materialize", daemon=True)
+        self._materializer.start()
+        return self._materializer
+
+    def wait_materialized(self) -> None:
+        """Blocks until a background materialisation (if any) has finished."""
+        if self._materializer is not None:
+            self._materializer.join()
+            self._materializer = None
+
     def close(self) -> None:
         """Drops the decode graphs and unmaps the tensor-parallel buffers (graphs
         that reference the symmetric memory go first)."""
+        self._stop_materializing = True
+        self.wait_materialized()
         torch.cuda.synchronize()
         self.graphs.clear()
         if self.tp is not None:

@@ -130,6 +130,7 @@ def load(archive: str, init_weights: bool = True, num_threads: int = 8) -> tuple
         loaded = CUDAGraph.finish_graph_loads(pending)
     for s, (g, _) in zip(state["graph_sizes"], loaded):
         eng.graphs[s] = g
+    eng.materialize_after_first_step = True
     t_done = time.perf_counter()
     timings = {
         "modules_s": t_mod - t0,

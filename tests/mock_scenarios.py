@@ -154,6 +154,29 @@ def scenario_load(workdir: str) -> None:
     # every member's launch state equals its own saved parameters
     for g, rec in zip(graphs, record["graphs"]):
         g.launch(0)
+    # a background thread gives every member its own executable while the
+    # main thread keeps launching them (template patching or own exec)
+    import threading
+
+    errors = []
+
+    def materialize_all():
+        try:
+            for g in graphs:
+                g.materialize()
+        except Exception as e:  # noqa: BLE001 - reported below
+            errors.append(e)
+
+    t = threading.Thread(target=materialize_all)
+    t.start()
+    for _ in range(10):
+        for g in graphs:
+            g.launch(0)
+    t.join()
+    assert not errors, errors
+    assert all(g.materialized for g in graphs)
+    for g in graphs:
+        g.launch(0)
     # the image came back byte-identical (same CRC-64 hash re-registered)
     _, h = c.load_image_file(os.path.join(workdir, "mock.cubin"))
     assert h == record["image_hash"]
