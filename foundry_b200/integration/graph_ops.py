@@ -114,6 +114,31 @@ def capture_or_load(key: GraphKey, runnable: Callable, args: tuple = (), kwargs:
     return g, out
 
 
+def materialize_loaded(background: bool = True):
+    """LOAD: gives every graph restored so far its own executable (largest
+    token count first), so the engine's later batch-size switches patch
+    nothing. With ``background`` on a daemon thread, which is returned;
+    launches may run concurrently."""
+    import threading
+
+    st = runtime.state()
+    if st is None or not st.loaded:
+        return None
+    graphs = [g for _, (g, _) in sorted(st.loaded.items(), key=lambda kv: -kv[0].num_tokens)]
+
+    def run():
+        for g in graphs:
+            if hasattr(g, "materialize"):
+                g.materialize()
+
+    if not background:
+        run()
+        return None
+    t = threading.Thread(target=run, name="foundry-materialize", daemon=True)
+    t.start()
+    return t
+
+
 def finalize_save(workspace: str | None = None) -> None:
     """SAVE: graph manifest (topology groups) + packed modules of the workspace."""
     st = runtime.state()
@@ -122,4 +147,5 @@ def finalize_save(workspace: str | None = None) -> None:
     pack_fatbins_to_folder(ws)
 
 
-__all__ = ["GraphKey", "LoadPlan", "capture_or_load", "finalize_save", "parse_filename", "start_graph_builds"]
+__all__ = ["GraphKey", "LoadPlan", "capture_or_load", "finalize_save", "materialize_loaded", "parse_filename",
+           "start_graph_builds"]

@@ -26,7 +26,9 @@ required. The patches, in the order an SGLang worker reaches them:
                                        offset after the capture loop; LOAD:
                                        replaces the loop: preallocate, start
                                        all builds, finish them in SAVE order
-                                       into ``graphs`` / ``output_buffers``
+                                       into ``graphs`` / ``output_buffers``,
+                                       then give each its own executable on a
+                                       background thread
   Engine._launch_scheduler_processes,
   DataParallelController.launch_tensor_parallel_group
                                        export LD_PRELOAD (interposer) and the
@@ -245,6 +247,7 @@ def _capture(orig):
             t0 = time.perf_counter()
             n = _load_all_graphs(self)
             runtime.capture_final_alloc_offset()
+            graph_ops.materialize_loaded(background=True)
             log.info("[foundry TIMING] SGLang LOAD of %d graphs: %.3f s", n, time.perf_counter() - t0)
             return None
         r = orig(self, *a, **k)

@@ -22,7 +22,9 @@
                                    running the model; every other dummy run
                                    (profiling, capture, DP padding) runs
   GPUModelRunner.capture_model     LOAD: start all graph builds first (if not
-                                   already); SAVE: manifest + packed modules +
+                                   already), afterwards give every restored
+                                   graph its own executable on a background
+                                   thread; SAVE: manifest + packed modules +
                                    final offset
   torch.cuda.get_device_capability answered from NVML, so importing a kernel
                                    library in the API-server process does not
@@ -202,6 +204,8 @@ def _capture_model(self, *a, **k):
         graph_ops.finalize_save()
     if st is not None and st.config.mode != GraphExtensionMode.NONE:
         runtime.capture_final_alloc_offset()
+    if st is not None and st.config.mode == GraphExtensionMode.LOAD:
+        graph_ops.materialize_loaded(background=True)
     return r
 
 

@@ -179,3 +179,32 @@ def test_vllm_hooks_install_and_uninstall():
     r = subprocess.run([sys.executable, "-c", f"ROOT={ROOT!r}\n" + VLLM_HOOKS], env=env, capture_output=True,
                        text=True, timeout=600)
     assert r.returncode == 0 and "HOOKS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]
+
+
+def test_materialize_loaded_graphs_in_background():
+    """LOAD: every restored graph gets its own executable, largest first, on a
+    background thread (fake graphs record the order)."""
+    from foundry_b200.integration import graph_ops, runtime
+    from foundry_b200.integration.config import GraphExtensionConfig
+
+    order = []
+
+    class FakeGraph:
+        def __init__(self, n):
+            self.n = n
+
+        def materialize(self):
+            order.append(self.n)
+
+    st = runtime.ExtensionState(GraphExtensionConfig.from_dict({"mode": "load"}), 0)
+    for n in (8, 256, 1, 64):
+        st.loaded[graph_ops.GraphKey("FULL", n, n, True, False, None)] = (FakeGraph(n), None)
+    runtime._state = st
+    try:
+        t = graph_ops.materialize_loaded(background=True)
+        t.join(timeout=30)
+        assert order == [256, 64, 8, 1]
+        runtime._state = runtime.ExtensionState(GraphExtensionConfig.from_dict({"mode": "load"}), 0)
+        assert graph_ops.materialize_loaded() is None  # nothing restored yet
+    finally:
+        runtime.reset()
