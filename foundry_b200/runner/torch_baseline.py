@@ -145,8 +145,6 @@ def run(model: str, batch: int, prompt_len: int, gen: int, steps: int, warmup: i
             "kernels_note": "cuBLAS GEMMs, torch SDPA and elementwise kernels (none of this package's)"}
 
 
-__all__ = ["TorchLlama", "run"]
-
 
 def _main(argv=None) -> int:
     """One eager decode step of the baseline (for a kernel launch list):
@@ -173,6 +171,9 @@ def _main(argv=None) -> int:
     torch.cuda.synchronize()
     print({"eager_step_ms": start.elapsed_time(end), "layers": cfg.layers, "batch": a.batch})
     return 0
+
+
+__all__ = ["TorchLlama", "run"]
 
 
 if __name__ == "__main__":
