@@ -36,6 +36,15 @@ def test_public_names():
         assert hasattr(foundry, n), n
     for n in ("start_graph_builds", "finish_graph_loads", "finish_one_graph_load", "load", "save"):
         assert hasattr(foundry.CUDAGraph, n), n
+    # the extension-module names engine integrations use as `import foundry.ops as fops`
+    import foundry.ops as fops
+
+    for n in ("get_current_alloc_offset", "set_current_alloc_offset", "stop_allocation_region",
+              "resume_allocation_region", "set_allocation_region", "preallocate_region", "preallocate_cublas_workspaces",
+              "load_cuda_modules_and_libraries", "pack_fatbins_to_folder", "set_pack_fatbins_on_exit",
+              "set_skip_fatbin_processing", "init_nvshmem_for_loaded_modules", "graph_pool_handle", "get_graph_ptr",
+              "CUDAGraph"):
+        assert hasattr(fops, n), n
 
 
 def test_model_configs():
