@@ -45,6 +45,13 @@ def test_public_names():
               "set_skip_fatbin_processing", "init_nvshmem_for_loaded_modules", "graph_pool_handle", "get_graph_ptr",
               "CUDAGraph"):
         assert hasattr(fops, n), n
+    # reference module paths; the package attributes stay the context managers
+    from foundry.allocation_region import parse_size
+    from foundry.graph import save_graph_manifest
+    import foundry.graph  # noqa: F401
+
+    assert parse_size("1.5GB") == 3 << 29 and callable(save_graph_manifest)
+    assert foundry.graph is foundry_b200.graph and foundry.allocation_region is foundry_b200.allocation_region
 
 
 def test_model_configs():
