@@ -1,0 +1,106 @@
+"""Times the bf16 decode GEMM variants on the shapes of a model's decode step.
+
+    python -m foundry_b200.runner.profile_gemm --model llama-3-8b --tokens 256
+    python -m foundry_b200.runner.profile_gemm --model llama-3-8b --tokens 256 --variants plan,pair --check
+
+For every linear layer of one decoder layer (+ lm_head) at ``--tokens``
+tokens it prints one JSON line per variant:
+- ``plan``: the planner's choice (one-SM tiles, split-K, stream-K);
+- ``pair``: two-SM ``cta_group::2`` tiles with the same tile width;
+- ``pf<N>``: the planner's plan with an L2 prefetch lead of N k-blocks.
+
+Each line gives the plan (tile width, splits, grid) and the mean time of
+``--iters`` back-to-back launches (CUDA events, after ``--warmup``).
+Weights larger than the 126 MB L2 (Llama-3-8B gate_up, down, lm_head) stream
+from HBM on every launch. Smaller ones (qkv 50 MB, o 34 MB) may partly stay
+in L2 across back-to-back launches, which they do not inside a decode step.
+With ``--check`` each variant's output is compared against fp32.
+"""
+
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import json
+import sys
+
+
+def shapes(cfg, tokens: int):
+    h, d = cfg.hidden, cfg.head_dim
+    out = [("qkv", tokens, cfg.qkv_dim, h), ("o", tokens, h, cfg.n_q * d)]
+    if getattr(cfg, "inter", 0):
+        out += [("gate_up", tokens, 2 * cfg.inter, h), ("down", tokens, h, cfg.inter)]
+    out.append(("lm_head", tokens, cfg.vocab, h))
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="foundry_b200.runner.profile_gemm")
+    ap.add_argument("--model", default="llama-3-8b")
+    ap.add_argument("--tokens", type=int, default=256)
+    ap.add_argument("--variants", default="plan,pair")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--check", action="store_true")
+    ap.add_argument("--device", type=int, default=0)
+    a = ap.parse_args(argv)
+
+    import torch
+
+    from .. import ops
+    from ..models import config_by_name
+    from ..ops import gemm as G
+
+    torch.cuda.set_device(a.device)
+    cfg = config_by_name(a.model)
+    sms = G._rt.sm_count()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    for name, t, n, k in shapes(cfg, a.tokens):
+        x = (torch.randn(t, k, device="cuda", generator=gen) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(n, k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+        pb = G.PartialBuffer(G.MAX_SPLITS * t * n)
+        out = torch.empty(t, n, dtype=torch.bfloat16, device="cuda")
+        ref = (x.float() @ w.float().T) if a.check else None
+        base = G.plan(t, n, k)
+        for v in a.variants.split(","):
+            if v == "plan":
+                p = base
+            elif v == "pair":
+                if not base.swap or n < 256:
+                    continue
+                p = G.pair_plan(n, t, k, max(64, base.bn), sms, pf=base.pf)
+            elif v.startswith("pf"):
+                p = dataclasses.replace(base, pf=int(v[2:]))
+            else:
+                raise SystemExit(f"unknown variant {v!r}")
+
+            def run():
+                return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p)
+
+            for _ in range(a.warmup):
+                run()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(a.iters):
+                r = run()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1000 / a.iters
+            line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v, "bn": p.bn, "splits": p.splits,
+                    "grid": p.grid, "us": round(us, 1),
+                    "weight_tbps": round(n * k * 2 / (us * 1e-6) / 1e12, 2),
+                    "tflops": round(2 * t * n * k / (us * 1e-6) / 1e12, 1)}
+            if a.check:
+                y = (r.buf[: r.splits * r.stride].view(r.splits, t, n).sum(0) if isinstance(r, G.Partial)
+                     else r.float())
+                line["max_err"] = round((y - ref).abs().max().item(), 4)
+            line["status"] = ops.status("gemm_bf16")
+            print(json.dumps(line), flush=True)
+            if line["status"]:
+                return 1
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

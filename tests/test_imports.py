@@ -11,6 +11,7 @@ MODULES = [
     "foundry_b200.models", "foundry_b200.models.llama", "foundry_b200.models.qwen3_moe", "foundry_b200.parallel.symm",
     "foundry_b200.parallel.comm", "foundry_b200.parallel.ep", "foundry_b200.runner.engine",
     "foundry_b200.runner.persist", "foundry_b200.runner.cli", "foundry_b200.runner.arena",
+    "foundry_b200.runner.profile_gemm", "foundry_b200.runner.torch_baseline",
 ]
 
 PUBLIC = [
