@@ -54,8 +54,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="foundry", choices=["foundry", "reference", "torch"],
-                    help="torch: the same decode step in stock PyTorch (cuBLAS, SDPA) under torch.cuda.graph")
+    ap.add_argument("--impl", default="foundry", choices=["foundry", "reference", "torch", "vllm"],
+                    help="torch: the same decode step in stock PyTorch (cuBLAS, SDPA) under torch.cuda.graph; "
+                         "vllm: upstream vLLM on the same shape (dummy weights, no tokenizer)")
     ap.add_argument("--model", default="llama-3-8b")
     ap.add_argument("--batch", type=int, default=None, help="prompts per GPU (dp/ep) or per job (tp)")
     ap.add_argument("--prompt-len", type=int, default=None)
@@ -188,6 +189,47 @@ def run_torch_baseline(args, rank: int, world: int, local: int) -> int:
     return 0
 
 
+def run_vllm_baseline(args, rank: int, world: int, local: int) -> int:
+    """Upstream vLLM on the same model shape, batch and graph sizes, one engine
+    per GPU (data parallel over the ranks; foundry_b200/runner/vllm_baseline.py)."""
+    import torch
+    import torch.distributed as dist
+
+    from foundry_b200.runner.cli import parse_graph_sizes
+    from foundry_b200.runner.vllm_baseline import run
+
+    workdir = args.workdir or f"/tmp/foundry_vllm_{os.environ.get('MASTER_PORT', os.getpid())}_{rank}"
+    # vLLM's engine process is spawned with this environment: show it this rank's GPU only
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    ids = [x for x in visible.split(",") if x] if visible else [str(i) for i in range(torch.cuda.device_count())]
+    os.environ["CUDA_VISIBLE_DEVICES"] = ids[local]
+    sampler = ClockSampler(local)
+    sampler.start()
+    r = run(args.model, args.batch, args.prompt_len, args.gen, parse_graph_sizes(args.graph_sizes, 1024), workdir)
+    clocks = sampler.stop()
+    t = torch.tensor([r["decode_s"]], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    decode_s = float(t.item())
+    if rank == 0:
+        tokens = r["decode_tokens"] * world
+        print(json.dumps({
+            "impl": "vllm", "metric": f"decode tok/s ({args.model} shape, upstream vLLM, FULL_DECODE_ONLY graphs)",
+            "value": round(tokens / decode_s, 1), "unit": "tokens/s", "n_gpus": world,
+            "ms_per_step": round(r["ms_per_step"], 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8-block + bf16" if "qwen3" in args.model else "bf16",
+            "data": "synthetic (random token-id prompts, dummy weights)",
+            "timing": "host wall clock around blocking generate() calls with device syncs: decode = generate(gen) "
+                      "- generate(1)",
+            "config": {"model": args.model, "global_batch": args.batch * world, "prompt_len": args.prompt_len,
+                       "gen_len": args.gen, "parallelism": f"dp{world}"},
+            "startup_s": round(r["startup_s"], 2), "prefill_s": round(r["prefill_s"], 3), "clocks": clocks,
+        }))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -208,6 +250,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     if args.impl == "torch":
         return run_torch_baseline(args, rank, world, local)
+    if args.impl == "vllm":
+        return run_vllm_baseline(args, rank, world, local)
 
     gen = max(args.gen, 1 + args.warmup + 2 * args.steps + 2)
     mode = args.parallel if world > 1 else "dp"
