@@ -191,3 +191,24 @@ def test_missing_required_target_patches_nothing(tmp_path):
     env = dict(os.environ, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="", FOUNDRY_CUDA_DRIVER=MOCK)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=180)
     assert r.returncode == 0 and "MISSING_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+def test_serve_launcher_environment(tmp_path):
+    """The SGLang launcher preloads the interposer, exports the config and the
+    engine selector, puts the shim first on PYTHONPATH and turns NCCL's cuMem
+    and NVLS paths off; the recipes parse."""
+    from foundry_b200.integration.config import GraphExtensionConfig, GraphExtensionMode
+    from foundry_b200.integration.sglang.serve import build_command
+
+    recipes = os.path.join(ROOT, "foundry_b200", "integration", "sglang", "recipes")
+    toml = os.path.join(recipes, "foundry_save.toml")
+    assert GraphExtensionConfig.from_toml(toml).mode == GraphExtensionMode.SAVE
+    assert GraphExtensionConfig.from_toml(os.path.join(recipes, "foundry_load.toml")).mode == GraphExtensionMode.LOAD
+    cmd, env = build_command(["--foundry-config", toml, "--", "--model-path", "m", "--tp-size", "2"],
+                             environ={"PYTHONPATH": "/x", "NCCL_NVLS_ENABLE": "1"})
+    assert cmd[1:3] == ["-m", "sglang.launch_server"] and cmd[3:] == ["--model-path", "m", "--tp-size", "2"]
+    assert env["FOUNDRY_GRAPH_ENGINE"] == "sglang" and env["FOUNDRY_GRAPH_CONFIG"] == os.path.abspath(toml)
+    assert env["PYTHONPATH"].split(os.pathsep)[0].endswith(os.path.join("vllm", "_site"))
+    assert env["PYTHONPATH"].split(os.pathsep)[-1] == "/x"
+    assert env["NCCL_CUMEM_ENABLE"] == "0" and env["NCCL_NVLS_ENABLE"] == "1"  # explicit settings win
+    assert "libfoundry_hook.so" in env.get("LD_PRELOAD", "")
