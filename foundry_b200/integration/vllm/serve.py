@@ -22,13 +22,14 @@ from ..config import GraphExtensionConfig
 from ..runtime import ld_preload_env
 
 
-def main(argv=None) -> int:
+def build_command(argv=None, environ=None) -> tuple[list[str], dict]:
+    """(command, environment) of the launch; nothing is started."""
     ap = argparse.ArgumentParser(prog="foundry_b200.integration.vllm.serve")
     ap.add_argument("--foundry-config", required=True)
     ap.add_argument("rest", nargs=argparse.REMAINDER)
     a = ap.parse_args(argv)
     cfg = GraphExtensionConfig.from_toml(a.foundry_config)
-    env = ld_preload_env(os.environ, cfg)
+    env = ld_preload_env(os.environ if environ is None else environ, cfg)
     site = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_site")
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     env["PYTHONPATH"] = os.pathsep.join([site, root] + [p for p in env.get("PYTHONPATH", "").split(os.pathsep) if p])
@@ -39,6 +40,11 @@ def main(argv=None) -> int:
     rest = [x for x in a.rest if x != "--"]
     vllm = shutil.which("vllm")
     cmd = [vllm, "serve", *rest] if vllm else [sys.executable, "-m", "vllm.entrypoints.cli.main", "serve", *rest]
+    return cmd, env
+
+
+def main(argv=None) -> int:
+    cmd, env = build_command(argv)
     os.execvpe(cmd[0], cmd, env)
     return 0
 

@@ -208,3 +208,18 @@ def test_materialize_loaded_graphs_in_background():
         assert graph_ops.materialize_loaded() is None  # nothing restored yet
     finally:
         runtime.reset()
+
+
+def test_vllm_serve_launcher_environment():
+    """The vLLM launcher preloads the interposer, exports the config, puts the
+    shim first on PYTHONPATH and turns NCCL's cuMem and NVLS paths off."""
+    from foundry_b200.integration.vllm.serve import build_command
+
+    toml = os.path.join(ROOT, "foundry_b200", "integration", "vllm", "recipes", "foundry_load.toml")
+    cmd, env = build_command(["--foundry-config", toml, "--", "Qwen/Qwen3-30B-A3B-FP8", "--data-parallel-size", "2"],
+                             environ={})
+    assert "serve" in cmd and cmd[-3:] == ["Qwen/Qwen3-30B-A3B-FP8", "--data-parallel-size", "2"]
+    assert env["FOUNDRY_GRAPH_CONFIG"] == os.path.abspath(toml) and "FOUNDRY_SPAWN_T0_NS" in env
+    assert env["PYTHONPATH"].split(os.pathsep)[0].endswith(os.path.join("vllm", "_site"))
+    assert env["NCCL_CUMEM_ENABLE"] == "0" and env["NCCL_NVLS_ENABLE"] == "0"
+    assert "libfoundry_hook.so" in env.get("LD_PRELOAD", "")
