@@ -1,0 +1,82 @@
+"""The interposer's driver entry points on the mock driver, called the way a
+library would call them (ctypes on the preloaded libfoundry_hook.so):
+cuMemAlloc_v2 / cuMemFree_v2 inside and outside the region, and
+cuMemAddressReserve carving. Reservations below 2 GiB are carved from the
+cursor and logged as Reserve events; larger ones are placed past the span;
+freeing a carved range is a no-op that leaves the cursor where it is."""
+
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "foundry_b200", "lib")
+
+SCRIPT = r"""
+import ctypes, json, sys
+sys.path.insert(0, ROOT)
+import foundry_b200 as fb
+c = fb.core()
+assert c.hook_is_preloaded() and c.driver_is_mock()
+cu = ctypes.CDLL(None)
+U64 = ctypes.c_uint64
+for name, args in (("cuMemAlloc_v2", [ctypes.POINTER(U64), ctypes.c_size_t]), ("cuMemFree_v2", [U64]),
+                   ("cuMemAddressReserve", [ctypes.POINTER(U64), ctypes.c_size_t, ctypes.c_size_t, U64,
+                                            ctypes.c_ulonglong]),
+                   ("cuMemAddressFree", [U64, ctypes.c_size_t])):
+    getattr(cu, name).argtypes = args
+    getattr(cu, name).restype = ctypes.c_int
+
+base, size = 0x6b0000000000, 8 << 30
+c.set_allocation_region(base, size)
+gran = c.region_granularity()
+
+# cuMemAlloc_v2 from "a library": lands at the cursor, cursor moves forward
+p = U64(0)
+assert cu.cuMemAlloc_v2(ctypes.byref(p), 3 << 20) == 0
+assert base <= p.value < base + size, hex(p.value)
+off1 = fb.get_current_alloc_offset()
+assert off1 >= (3 << 20) and off1 % gran == 0
+ctypes.memset(p.value, 7, 4096)                       # mock device memory is host memory
+assert cu.cuMemFree_v2(p) == 0
+assert fb.get_current_alloc_offset() == off1          # frees never rewind the cursor
+
+# reservations: carved (< 2 GiB) and recorded
+c.start_hook_record()
+r = U64(0)
+assert cu.cuMemAddressReserve(ctypes.byref(r), 64 << 20, 0, 0, 0) == 0
+assert r.value == base + off1, (hex(r.value), hex(base + off1))
+off2 = fb.get_current_alloc_offset()
+assert off2 == off1 + (64 << 20)
+c.end_hook_record()
+ev = json.loads(c.hook_events_json())["events"]
+assert [e["type"] for e in ev] == ["reserve"] and ev[0]["ptr"] == r.value and ev[0]["size"] == 64 << 20, ev
+assert cu.cuMemAddressFree(r, 64 << 20) == 0          # carved: a no-op
+assert fb.get_current_alloc_offset() == off2
+
+# a large reservation (symmetric heaps, expandable segments) goes past the span
+big = U64(0)
+assert cu.cuMemAddressReserve(ctypes.byref(big), 4 << 30, 0, 0, 0) == 0
+assert not (base <= big.value < base + size), hex(big.value)
+assert fb.get_current_alloc_offset() == off2
+assert cu.cuMemAddressFree(big, 4 << 30) == 0
+
+# region stopped: allocations bypass it; resumed: back at the cursor
+c.stop_allocation_region()
+q = U64(0)
+assert cu.cuMemAlloc_v2(ctypes.byref(q), 1 << 20) == 0
+assert not (base <= q.value < base + size), hex(q.value)
+assert cu.cuMemFree_v2(q) == 0
+c.resume_allocation_region()
+assert cu.cuMemAlloc_v2(ctypes.byref(q), 1 << 20) == 0
+assert q.value == base + off2, (hex(q.value), hex(base + off2))
+print("HOOK_OK")
+"""
+
+
+def test_hook_entry_points_on_mock():
+    env = dict(os.environ, FOUNDRY_CUDA_DRIVER=os.path.join(LIB, "libfoundry_mockcuda.so"), PYTHONPATH=ROOT,
+               CUDA_VISIBLE_DEVICES="", LD_PRELOAD=os.path.join(LIB, "libfoundry_hook.so"))
+    r = subprocess.run([sys.executable, "-c", f"ROOT={ROOT!r}\n" + SCRIPT], env=env, capture_output=True, text=True,
+                       timeout=180)
+    assert r.returncode == 0 and "HOOK_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
