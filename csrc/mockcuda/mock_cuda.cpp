@@ -848,9 +848,28 @@ CUresult cuIpcOpenMemHandle_v2(CUdeviceptr*, CUipcMemHandle, unsigned int) {
 }
 CUresult cuIpcCloseMemHandle(CUdeviceptr) { return CUDA_ERROR_NOT_SUPPORTED; }
 
+// Like the driver: a base name resolves to its newest versioned entry point of
+// this library. Lookups use libc's dlsym on this library's own handle, so an
+// interposer's dlsym override (which redirects driver symbols) is not involved.
 CUresult cuGetProcAddress_v2(const char* symbol, void** pfn, int, cuuint64_t,
                              CUdriverProcAddressQueryResult* status) {
-  *pfn = dlsym(RTLD_DEFAULT, symbol);
+  using RealDlsym = void* (*)(void*, const char*);
+  static RealDlsym real = reinterpret_cast<RealDlsym>(dlvsym(RTLD_DEFAULT, "dlsym", "GLIBC_2.2.5"));
+  // The address of an internal object names this library; an exported
+  // function's address may resolve to an interposer's definition of it.
+  static const int anchor = 0;
+  static void* self = [] {
+    Dl_info info;
+    dladdr(&anchor, &info);
+    return dlopen(info.dli_fname, RTLD_NOW | RTLD_NOLOAD);
+  }();
+  *pfn = nullptr;
+  if (real && self && symbol) {
+    for (const char* suffix : {"_v3", "_v2", ""}) {
+      *pfn = real(self, (std::string(symbol) + suffix).c_str());
+      if (*pfn) break;
+    }
+  }
   if (status) *status = *pfn ? CU_GET_PROC_ADDRESS_SUCCESS : CU_GET_PROC_ADDRESS_SYMBOL_NOT_FOUND;
   return *pfn ? CUDA_SUCCESS : CUDA_ERROR_NOT_FOUND;
 }

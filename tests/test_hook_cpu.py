@@ -80,3 +80,50 @@ def test_hook_entry_points_on_mock():
     r = subprocess.run([sys.executable, "-c", f"ROOT={ROOT!r}\n" + SCRIPT], env=env, capture_output=True, text=True,
                        timeout=180)
     assert r.returncode == 0 and "HOOK_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+FRONT_DOOR = r"""
+import ctypes, sys
+sys.path.insert(0, ROOT)
+import foundry_b200 as fb
+c = fb.core()
+assert c.hook_is_preloaded() and c.driver_is_mock()
+hook = ctypes.CDLL(HOOK)
+addr = lambda f: ctypes.cast(f, ctypes.c_void_p).value
+libdl = ctypes.CDLL(None)
+libdl.dlopen.restype = ctypes.c_void_p
+libdl.dlopen.argtypes = [ctypes.c_char_p, ctypes.c_int]
+libdl.dlsym.restype = ctypes.c_void_p
+libdl.dlsym.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
+drv = libdl.dlopen(MOCK.encode(), 2)  # RTLD_NOW, local: how a runtime opens the driver
+assert drv
+# dlsym on the driver handle: overridden entry points resolve to the interposer
+for name in ("cuMemAlloc_v2", "cuMemFree_v2", "cuMemAddressReserve", "cuLibraryLoadData", "cuIpcGetMemHandle"):
+    assert libdl.dlsym(drv, name.encode()) == addr(getattr(hook, name)), name
+# others stay the driver's, unknown names stay unknown
+assert libdl.dlsym(drv, b"cuCtxGetDevice") == addr(ctypes.CDLL(MOCK).cuCtxGetDevice)
+assert not libdl.dlsym(drv, b"cuNoSuchEntryPoint")
+# cuGetProcAddress(base name, version) -> the versioned override
+pfn = ctypes.c_void_p(0)
+status = ctypes.c_int(0)
+gpa = hook.cuGetProcAddress_v2
+gpa.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_uint64,
+                ctypes.POINTER(ctypes.c_int)]
+assert gpa(b"cuMemAlloc", ctypes.byref(pfn), 12080, 0, ctypes.byref(status)) == 0
+assert pfn.value == addr(hook.cuMemAlloc_v2)
+assert gpa(b"cuMemAlloc", ctypes.byref(pfn), 3000, 0, ctypes.byref(status)) == 0
+assert pfn.value != addr(hook.cuMemAlloc_v2)          # pre-_v2 callers keep the driver's entry point
+assert gpa(b"cuCtxGetDevice", ctypes.byref(pfn), 12080, 0, ctypes.byref(status)) == 0
+assert pfn.value == addr(ctypes.CDLL(MOCK).cuCtxGetDevice)
+print("FRONT_DOOR_OK")
+"""
+
+
+def test_symbol_front_door_on_mock():
+    """dlsym and cuGetProcAddress route the overridden driver entry points to
+    the interposer and leave every other symbol alone."""
+    mock, hook = os.path.join(LIB, "libfoundry_mockcuda.so"), os.path.join(LIB, "libfoundry_hook.so")
+    env = dict(os.environ, FOUNDRY_CUDA_DRIVER=mock, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="", LD_PRELOAD=hook)
+    code = f"ROOT={ROOT!r}; MOCK={mock!r}; HOOK={hook!r}\n" + FRONT_DOOR
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=180)
+    assert r.returncode == 0 and "FRONT_DOOR_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
