@@ -263,6 +263,88 @@ def scenario_cluster(workdir: str) -> None:
     print("CLUSTER LOAD OK")
 
 
+def _mixed_graph_json(img_hash: int, ptrs: list[int]) -> str:
+    """kernel -> memcpy (device to device) -> event record -> empty -> event
+    wait -> memset -> kernel: every node type the graph store handles."""
+    def kernel(i, seed):
+        rnd = random.Random(seed)
+        params, off = [], 0
+        for j, sz in enumerate(PARAM_SIZES):
+            val = struct.pack("<Q", ptrs[j % len(ptrs)]) if (sz == 8 and j < 3) else \
+                bytes(rnd.getrandbits(8) for _ in range(sz))
+            params.append({"index": j, "offset": off, "size": sz, "value_hex": val.hex()})
+            off += sz
+        return {"id": i, "type": "KernelNode", "params": {
+            "blockDimX": 64, "blockDimY": 1, "blockDimZ": 1, "gridDimX": 8, "gridDimY": 1, "gridDimZ": 1,
+            "sharedMemBytes": 0, "kernelParams": params, "function_name": "fbmock_k1",
+            "kernel_source_binary_hash": f"{img_hash:016x}"}}
+    memcpy = {k: 0 for k in ("Depth", "Height", "WidthInBytes", "dstDevice", "dstHeight", "dstLOD", "dstPitch",
+                             "dstXInBytes", "dstY", "dstZ", "srcDevice", "srcHeight", "srcLOD", "srcPitch",
+                             "srcXInBytes", "srcY", "srcZ")}
+    memcpy.update({"Depth": 1, "Height": 1, "WidthInBytes": 4096, "dstDevice": ptrs[1], "srcDevice": ptrs[0],
+                   "dstMemoryType": 2, "srcMemoryType": 2})
+    nodes = [kernel(0, 7), {"id": 1, "type": "MemcpyNode", "params": memcpy},
+             {"id": 2, "type": "EventRecordNode", "params": {"event_id": 0}},
+             {"id": 3, "type": "EmptyNode", "params": {}},
+             {"id": 4, "type": "EventWaitNode", "params": {"event_id": 0}},
+             {"id": 5, "type": "MemsetNode", "params": {"dst": ptrs[2], "elementSize": 4, "height": 1, "pitch": 0,
+                                                        "value": 0xABCD, "width": 256}},
+             kernel(6, 8)]
+    deps = [{"from": i, "to": i + 1} for i in range(6)]
+    return json.dumps({"nodes": nodes, "dependencies": deps, "topology_key": "", "generators": [],
+                       "num_events": 1})
+
+
+def scenario_mixed(workdir: str) -> None:
+    """Memcpy, event record / wait, empty and memset nodes next to kernels:
+    analysis reads them back, JSON and .cugraph round-trip them, and a fresh
+    process restores and launches the graph."""
+    fb, c = _core()
+    phase = sys.argv[3]
+    archive = os.path.join(workdir, "mixed_archive")
+    img = os.path.join(workdir, "mock.cubin")
+    if phase == "save":
+        os.makedirs(archive, exist_ok=True)
+        c.set_allocation_region(BASE, REGION)
+        ptrs = [c.region_alloc(1 << 20) for _ in range(3)]
+        with open(img, "wb") as f:
+            f.write(_image_bytes(0))
+        _, h = c.load_image_file(img)
+        desc = c.graph_from_json_text(_mixed_graph_json(h, ptrs))
+        c.recompute_topology_key(desc)
+        live = c.build_live_graph(desc)
+        analyzed = c.analyze_graph(live)
+        c.destroy_graph(live)
+        got = json.loads(analyzed.to_json())
+        types = [n["type"] for n in got["nodes"]]
+        assert types == ["KernelNode", "MemcpyNode", "EventRecordNode", "EmptyNode", "EventWaitNode", "MemsetNode",
+                         "KernelNode"], types
+        assert got["nodes"][1]["params"]["WidthInBytes"] == 4096 and got["nodes"][1]["params"]["srcDevice"] == ptrs[0]
+        assert got["nodes"][5]["params"]["value"] == 0xABCD and got["num_events"] == 1
+        assert got["nodes"][2]["params"]["event_id"] == got["nodes"][4]["params"]["event_id"]
+        path = os.path.join(archive, "graph_0.json")
+        analyzed.save(path)
+        fb.pack_fatbins_to_folder(archive)
+        with open(os.path.join(workdir, "mixed.json"), "w") as f:
+            json.dump({"json": analyzed.to_json(), "key": analyzed.topology_key}, f)
+        print("MIXED SAVE OK")
+        return
+    rec = json.load(open(os.path.join(workdir, "mixed.json")))
+    fb.load_cuda_modules_and_libraries(archive)
+    c.set_allocation_region(BASE, REGION)
+    for _ in range(3):
+        c.region_alloc(1 << 20)
+    path = os.path.join(archive, "graph_0.json")
+    assert c.read_binary_graph(path.replace(".json", ".cugraph")).to_json() == rec["json"]
+    pending = c.start_graph_builds([path], 1)
+    g = pending.finish_one(0)
+    assert g.desc.topology_key == rec["key"]
+    g.launch(0)
+    g.materialize()
+    g.launch(0)
+    print("MIXED LOAD OK")
+
+
 def scenario_numeric(workdir: str) -> None:
     """A graph of axpy/fill kernels on region memory: SAVE runs it, LOAD restores
     and runs it again; results must be bit-identical."""
@@ -396,4 +478,4 @@ def scenario_faults(workdir: str) -> None:
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
     {"save": scenario_save, "load": scenario_load, "numeric": scenario_numeric, "faults": scenario_faults,
-     "cluster": scenario_cluster}[name](workdir)
+     "cluster": scenario_cluster, "mixed": scenario_mixed}[name](workdir)

@@ -78,3 +78,11 @@ def test_cluster_launch_dims_round_trip(tmp_path):
     wd = str(tmp_path)
     assert "CLUSTER SAVE OK" in _run("cluster", wd, "save")
     assert "CLUSTER LOAD OK" in _run("cluster", wd, "load")
+
+
+def test_memcpy_event_empty_nodes_round_trip(tmp_path):
+    """Every node type of the graph store (kernel, memcpy, memset, event
+    record / wait, empty) through analysis, JSON, .cugraph and restore."""
+    wd = str(tmp_path)
+    assert "MIXED SAVE OK" in _run("mixed", wd, "save")
+    assert "MIXED LOAD OK" in _run("mixed", wd, "load")
