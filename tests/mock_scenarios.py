@@ -342,6 +342,12 @@ def scenario_mixed(workdir: str) -> None:
     g.launch(0)
     g.materialize()
     g.launch(0)
+    # without the binary file the JSON is read instead, to the same description
+    os.remove(path.replace(".json", ".cugraph"))
+    assert c.read_graph_file(path).to_json() == rec["json"]
+    g2 = c.start_graph_builds([path], 1).finish_one(0)
+    assert g2.desc.topology_key == rec["key"]
+    g2.launch(0)
     print("MIXED LOAD OK")
 
 
