@@ -2,7 +2,8 @@
 serving load (256 prompts x 512 random tokens, greedy) on N GPUs (DP: one
 full engine per GPU, weak scaling), plus the persistence numbers of the same
 run: graph capture + SAVE, fresh-process cold start to first token, and
-restore time of the 67 decode graphs.
+restore time of the 67 decode graphs, and a second SAVE / fresh-process
+LOAD of 256 decode graphs per rank (restore time measured, not scaled).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl foundry|reference|torch]
 
@@ -31,9 +32,11 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-REF_UNAVAILABLE = (
-    "reference build needs Boost>=1.83 (CMakeLists.txt:9 find_package(Boost)); Boost is not on this image and "
-    "there is no network; pip install of the reference fails at its CMake configure step"
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+REF_INSTALL_FAILURE = (
+    "the offline install (pip install --no-index --no-deps --target baseline/_ref <reference copy>) fails at the "
+    "reference's CMake configure step: CMakeLists.txt:9 find_package(Boost) finds no Boost>=1.83 on this image "
+    "and there is no network"
 )
 
 
@@ -66,6 +69,8 @@ def parse():
     ap.add_argument("--parallel", default=None, choices=["dp", "tp", "ep"])
     ap.add_argument("--workdir", default=None)
     ap.add_argument("--skip-cold-start", action="store_true")
+    ap.add_argument("--restore-graphs", default="4:1024:4",
+                    help="graph sizes of the restore-at-scale SAVE/LOAD (default: 256 graphs); 'none' skips it")
     args = ap.parse_args()
     base = args.model.split("@")[0]
     preset = PRESETS.get(base, PRESETS["llama-3-8b"])
@@ -230,15 +235,39 @@ def run_vllm_baseline(args, rank: int, world: int, local: int) -> int:
     return 0
 
 
+def run_reference(rank: int) -> int:
+    """The reference arm: imports the reference's own package from
+    baseline/_ref in a clean interpreter (this repository's ``foundry`` alias
+    package must not shadow it). The reference persists graphs of the vLLM /
+    SGLang forks it patches, neither of which is on the image, so even an
+    importable build would have no engine to serve the benchmark; the import
+    is still tried so that the reason printed is the one observed."""
+    reason = None
+    if not os.path.isdir(REF_DIR):
+        reason = f"baseline/_ref is absent: {REF_INSTALL_FAILURE}"
+    else:
+        res = subprocess.run([sys.executable, "-c", "import foundry, foundry.ops; print(foundry.__file__)"],
+                             cwd="/tmp", env={**{k: v for k, v in os.environ.items() if k != "PYTHONPATH"},
+                                              "PYTHONPATH": REF_DIR},
+                             capture_output=True, text=True, timeout=300)
+        if res.returncode != 0:
+            err = (res.stderr.strip().splitlines() or ["no output"])[-1]
+            reason = f"importing the reference from baseline/_ref failed: {err}"
+        else:
+            reason = ("the reference imports, but its decode path is the foundry-org vLLM/SGLang forks, which are "
+                      "not on the image; upstream vLLM 0.22 lacks the graph-extension hooks it patches")
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}))
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE}))
-        return 0
+        return run_reference(rank)
 
     import torch
     import torch.distributed as dist
@@ -276,6 +305,24 @@ def main():
         cold = run_cli(["load", *common, "--dist-port", str(port + 19)],
                        {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns())})["load"]
 
+    # 2b) Restore at scale: a second archive of 256 decode graphs per rank,
+    # SAVE and fresh-process LOAD; the LOAD times until every graph of the
+    # archive also has its own executable (the cost if each graph were its own
+    # topology group).
+    scale = {}
+    if args.restore_graphs != "none":
+        archive256 = os.path.join(workdir, f"scale_rank_{rank}") if mode == "dp" else workdir + "_scale"
+        common256 = list(common)
+        common256[common256.index("--archive") + 1] = archive256
+        common256[common256.index("--graph-sizes") + 1] = args.restore_graphs
+        save256 = run_cli(["save", *common256, "--dist-port", str(port + 23)])["save"]
+        load256 = run_cli(["load", *common256, "--dist-port", str(port + 29), "--materialize-all"],
+                          {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns())})["load"]
+        scale = {"graphs": load256["num_graphs"], "topology_groups": load256["num_groups"],
+                 "capture_s": save256.get("capture_s"), "restore_s": load256["restore_s"],
+                 "cold_start_first_token_s": load256["cold_start_first_token_s"],
+                 "materialize_all_s_after_first_token": load256.get("materialize_all_s_after_first_token")}
+
     # 3) This process restores the archive and runs the timed decode.
     from foundry_b200 import ops
     from foundry_b200.runner import persist
@@ -295,6 +342,7 @@ def main():
     st = eng.state
     kernels_per_step = len(graph.desc.kernel_names())
 
+    ctx0 = args.prompt_len + 1  # tokens in the cache at the first decode step
     for _ in range(args.warmup):
         eng.decode_step(b)
     eng.wait_materialized()  # restored graphs get their own executables after the first step
@@ -329,17 +377,44 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_end)
     clocks = sampler.stop()
+    dev_ctx = [ctx0 + args.warmup, ctx0 + args.warmup + args.steps - 1]
+    e2e_ctx = [dev_ctx[1] + 1, dev_ctx[1] + args.steps]
 
-    n_active = len(reqs)
-    t = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    # Whole serving load through the public API: fresh requests, prefill, then
+    # every decode step of the args.gen-token generation (context prompt_len+1
+    # .. prompt_len+gen-1), each with its H2D input and D2H token copy.
+    n_full = len(reqs)
+    eng.release(reqs)
+    freqs = eng.add_requests(prompts, max_new_tokens=args.gen)
+    eng.prefill(freqs)
+    fb = eng.start_decode(freqs)
     if world > 1:
+        dist.barrier()
+    f_start, f_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    f_start.record()
+    for _ in range(args.gen - 1):
+        eng.decode_step(fb)
+    f_end.record()
+    torch.cuda.synchronize()
+    full_ms = f_start.elapsed_time(f_end)
+    eng.release(freqs)
+
+    n_active = n_full
+    per_rank = [dev_ms, e2e_ms, full_ms, restore["restore_s"], cold.get("cold_start_first_token_s") or 0.0,
+                scale.get("restore_s") or 0.0, scale.get("cold_start_first_token_s") or 0.0,
+                scale.get("materialize_all_s_after_first_token") or 0.0]
+    t = torch.tensor(per_rank, dtype=torch.float64, device="cuda")
+    if world > 1:  # every time below is the maximum over ranks
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
-    dev_ms, e2e_ms = t.tolist()
+    (dev_ms, e2e_ms, full_ms, restore_max, cold_max, scale_restore_max, scale_cold_max,
+     scale_mat_max) = t.tolist()
     seq_ranks = 1 if mode == "tp" else world  # tp ranks share one batch of sequences
     tokens = n_active * seq_ranks * args.steps
     value = tokens / (dev_ms / 1e3)
     e2e = tokens / (e2e_ms / 1e3)
+    full_tokens = n_active * seq_ranks * (args.gen - 1)
     if rank == 0:
         out = {
             "metric": f"restored decode tok/s ({args.model} shape, {restore['num_graphs']} persisted decode graphs)",
@@ -359,24 +434,39 @@ def main():
                 "prompt_len": args.prompt_len, "gen_len": args.gen, "parallelism": f"{mode}{world}",
                 "decode_batch_per_gpu": b, "graphs_per_rank": restore["num_graphs"],
                 "topology_groups": restore["num_groups"],
+                "decode_context_timed": dev_ctx, "decode_context_e2e": e2e_ctx,
                 "l2": "inputs larger than L2 (all weights + the KV cache are read every step)",
             },
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * b,
-                    "d2h_bytes_per_step": 4 * b, "ms_per_step": round(e2e_ms / args.steps, 4)},
+                    "d2h_bytes_per_step": 4 * b, "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "decode_context": e2e_ctx},
+            "full_generation": {
+                "value": round(full_tokens / (full_ms / 1e3), 1), "unit": "tokens/s",
+                "decode_steps": args.gen - 1, "decode_context": [ctx0, args.prompt_len + args.gen - 1],
+                "ms_per_step": round(full_ms / (args.gen - 1), 4), "h2d_bytes_per_step": 4 * fb,
+                "d2h_bytes_per_step": 4 * fb,
+                "how": "public API decode_step for every step of the generation after prefill, CUDA events, "
+                       "max over ranks"},
             "gpu_launches": (kernels_per_step + 1) * args.steps,
             "persistence": {
-                "capture_s_67_graphs": save_info.get("capture_s"), "save_s": save_info.get("save_s"),
+                "capture_s": save_info.get("capture_s"), "captured_graphs": restore["num_graphs"],
+                "save_s": save_info.get("save_s"),
                 "save_process_wall_s": round(save_wall, 2),
-                "restore_s": round(restore["restore_s"], 4),
+                "restore_s": round(restore_max, 4),
                 "restore_phase1_ms": restore["restore_phase1_ms"],
                 "restore_phase2_ms": restore["restore_phase2_ms"],
-                "restore_s_per_256_graphs": round(restore["restore_s"] * 256 / restore["num_graphs"], 4),
-                "cold_start_first_token_s": cold.get("cold_start_first_token_s"),
+                "cold_start_first_token_s": round(cold_max, 3) if cold else None,
                 "cold_start_restore_s": cold.get("restore_s"),
                 "cold_start_breakdown_s": {k: cold.get(k) for k in ("python_import_s", "modules_s", "arena_s",
                                                                     "restore_s", "load_total_s")},
                 "prefill_s": round(prefill_s, 3),
+                "restore_at_scale": dict(scale, restore_s=round(scale_restore_max, 4),
+                                         cold_start_first_token_s=round(scale_cold_max, 3),
+                                         materialize_all_s_after_first_token=round(scale_mat_max, 3),
+                                         ranks=world, how="max over ranks; fresh-process LOAD of a "
+                                                           "separately saved archive") if scale else None,
+                "times": "max over ranks",
             },
         }
         print(json.dumps(out))

@@ -256,7 +256,7 @@ std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>&
   pl->groups.resize(pl->group_template.size());
   pl->diffs.resize(paths.size());
   pl->results.resize(paths.size());
-  pl->finished.assign(paths.size(), false);
+  pl->finished.assign(paths.size(), 0);
   pl->phase1_ms = ms_since(t0);
   pl->start_phase2();
   return pl;
@@ -283,9 +283,13 @@ void PendingLoads::start_phase2() {
       parallel_for(descs.size(), num_threads, [&](size_t i) {
         const int tmpl = group_template[group_of[i]];
         if (static_cast<size_t>(tmpl) == i) return;
-        if (descs[i]->topology_key != descs[tmpl]->topology_key &&
+        // Exec patching only rewrites node parameters: a member must have its
+        // template's node types, edges and cluster shapes, which is what the
+        // topology key encodes. A manifest that groups it otherwise is stale.
+        if (descs[i]->topology_key != descs[tmpl]->topology_key ||
             descs[i]->nodes.size() != descs[tmpl]->nodes.size())
-          throw std::runtime_error("manifest groups " + paths[i] + " with a template of another topology");
+          throw std::runtime_error("manifest groups " + paths[i] + " with a template of another topology (" +
+                                   paths[tmpl] + ")");
         diffs[i] = diff_against(*descs[tmpl], *descs[i]);
       });
     } catch (...) {
@@ -308,6 +312,7 @@ void PendingLoads::wait() {
 std::shared_ptr<RestoredGraph> PendingLoads::finish_one(size_t index) {
   if (index >= descs.size()) throw std::out_of_range("graph index out of range");
   wait();
+  std::lock_guard<std::mutex> lk(finish_mu_);
   if (finished[index]) return results[index];
   // Allocator events are replayed in capture order: the cursor must walk the
   // same trajectory it walked on SAVE.
@@ -327,7 +332,7 @@ std::shared_ptr<RestoredGraph> PendingLoads::finish_one(size_t index) {
     if (!r->shared->current) r->shared->current = r.get();
   }
   results[index] = r;
-  finished[index] = true;
+  finished[index] = 1;
   return r;
 }
 

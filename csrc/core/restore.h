@@ -77,7 +77,7 @@ class PendingLoads {
   std::vector<int> group_template;  // graph index of each group's template
   std::vector<std::vector<uint32_t>> diffs;
   std::vector<std::shared_ptr<RestoredGraph>> results;
-  std::vector<bool> finished;
+  std::vector<char> finished;  // not vector<bool>: elements are written by finish_one
   double phase1_ms = 0, phase2_ms = 0;
   int num_threads = 4;
   CUcontext ctx = nullptr;
@@ -91,6 +91,9 @@ class PendingLoads {
   std::thread worker_;
   std::mutex mu_;
   std::condition_variable cv_;
+  // Serialises finish_one: the finished check, the allocator-event replay and
+  // the result store must happen once per graph and in one thread at a time.
+  std::mutex finish_mu_;
   bool done_ = false;
   std::exception_ptr error_;
 };

@@ -27,10 +27,14 @@
 // (sequence, head, split) row it owns before the combine reads it - a split
 // past a sequence's end writes m = -inf, l = 0 - so no clearing is needed.
 //
-// Setup: the first call on each device (with that device current) resolves
-// g_scratch's device address with cudaGetSymbolAddress and raises the
-// kernels' dynamic shared-memory limit; make that first call before any
-// stream capture. Later calls on that device only launch.
+// Setup: the first call in each CUDA context resolves g_scratch's device
+// address with cudaGetSymbolAddress, raises the split kernels' dynamic
+// shared-memory limit and loads the combine kernel; make that first call
+// before any stream capture. The set-up is cached per context, keyed by the
+// driver's context ID (cuCtxGetId), which is never reused within a process:
+// a second context on the same device, a non-primary context or a context
+// re-created after cudaDeviceReset gets its own set-up instead of a stale
+// address from another context. Later calls in a context only launch.
 //
 // Concurrency: every call on a device uses the same g_scratch. Calls that
 // overlap on the device (different streams, or different host threads with
@@ -38,15 +42,18 @@
 // partials; calls on one stream are ordered and safe.
 //
 // Allocation: the entry point makes no cudaMalloc/cudaFree call and calls no
-// library that allocates; its only CUDA calls are cudaGetDevice,
-// cudaGetSymbolAddress, cudaFuncSetAttribute, two kernel launches and
-// cudaGetLastError.
+// library that allocates; its only CUDA calls are
+// cudaGetDriverEntryPointByVersion, cuCtxGetCurrent, cuCtxGetId,
+// cudaGetSymbolAddress, cudaFuncSetAttribute, cudaFuncGetAttributes, two
+// kernel launches and cudaGetLastError.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
 #include <mutex>
 
 #include "../kernels/attention.cu"
+#include "decode_attn_noalloc.h"
 
 #define FB_NOALLOC_EXPORT extern "C" __attribute__((visibility("default")))
 
@@ -54,19 +61,27 @@ namespace {
 
 constexpr int kHeadDim = 128;
 constexpr int kPage = 64;
-constexpr long long kMaxPartialRows = 16384;  // (sequence, query head, split) rows
+constexpr long long kMaxPartialRows = FB_NOALLOC_MAX_PARTIAL_ROWS;  // (sequence, query head, split) rows
 constexpr size_t FB_NOALLOC_SCRATCH_BYTES = kMaxPartialRows * (kHeadDim + 2) * sizeof(float);
-constexpr int kMaxDevices = 64;
+static_assert(FB_NOALLOC_SCRATCH_BYTES == 8519680, "documented scratch size");
+constexpr int kMaxContexts = 64;
 
 // o partials first ([rows][128] fp32), then (m, l) pairs ([rows][2] fp32).
 static __device__ __align__(256) float g_scratch[FB_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
-struct DeviceSetup {
-  bool ready = false;
+// One entry per CUDA context that has called the entry point.
+struct ContextSetup {
+  unsigned long long ctx_id = 0;
   float* scratch = nullptr;
 };
-DeviceSetup g_setup[kMaxDevices];
+ContextSetup g_setup[kMaxContexts];
+int g_setup_count = 0;
 std::mutex g_setup_mu;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
 
 int decode_smem_bytes(int group) {
   return 2 * 2 * kPage * kHeadDim * 2 + (group * kPage * 2 + group + group * kHeadDim) * 4;
@@ -82,35 +97,75 @@ int fail_cuda(char* err, int err_len, const char* what, cudaError_t e) {
   return 3;
 }
 
-// Once per device, with the device current.
-int setup_device(int dev, float** scratch, char* err, int err_len) {
-  std::lock_guard<std::mutex> lock(g_setup_mu);
-  DeviceSetup& s = g_setup[dev];
-  if (!s.ready) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
-    if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaGetSymbolAddress(g_scratch)", e);
-    e = cudaFuncSetAttribute(fb_decode_attn_g4, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem_bytes(4));
-    if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaFuncSetAttribute(fb_decode_attn_g4)", e);
-    e = cudaFuncSetAttribute(fb_decode_attn_g8, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem_bytes(8));
-    if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaFuncSetAttribute(fb_decode_attn_g8)", e);
-    s.scratch = static_cast<float*>(p);
-    s.ready = true;
+int driver_entry(const char* name, void** fn, char* err, int err_len) {
+  cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+  cudaError_t e = cudaGetDriverEntryPointByVersion(name, fn, 12000, cudaEnableDefault, &q);
+  if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaGetDriverEntryPointByVersion", e);
+  if (q != cudaDriverEntryPointSuccess || !*fn) {
+    if (err && err_len > 0) snprintf(err, static_cast<size_t>(err_len), "driver entry point %s not found", name);
+    return 3;
   }
-  *scratch = s.scratch;
+  return 0;
+}
+
+// ID of the context current on this thread; a runtime call is made first when
+// none is current, so that the runtime binds the device's primary context.
+int current_context_id(unsigned long long* id, char* err, int err_len) {
+  if (!g_ctx_get_current) {
+    void* a = nullptr;
+    void* b = nullptr;
+    if (int rc = driver_entry("cuCtxGetCurrent", &a, err, err_len)) return rc;
+    if (int rc = driver_entry("cuCtxGetId", &b, err, err_len)) return rc;
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(b);
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(a);
+  }
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) return fail(err, err_len, 3, "cuCtxGetCurrent failed");
+  if (!ctx) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);  // initialises the primary context
+    if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaGetSymbolAddress(g_scratch)", e);
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx) return fail(err, err_len, 3, "no current CUDA context");
+  }
+  if (g_ctx_get_id(ctx, id) != CUDA_SUCCESS) return fail(err, err_len, 3, "cuCtxGetId failed");
+  return 0;
+}
+
+// Once per context, with that context current.
+int setup_context(float** scratch, char* err, int err_len) {
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  unsigned long long id = 0;
+  if (int rc = current_context_id(&id, err, err_len)) return rc;
+  for (int i = 0; i < g_setup_count; ++i) {
+    if (g_setup[i].ctx_id == id) {
+      *scratch = g_setup[i].scratch;
+      return 0;
+    }
+  }
+  if (g_setup_count == kMaxContexts)
+    return fail(err, err_len, 2, "more than %lld CUDA contexts called this entry point", kMaxContexts);
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+  if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaGetSymbolAddress(g_scratch)", e);
+  e = cudaFuncSetAttribute(fb_decode_attn_g4, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem_bytes(4));
+  if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaFuncSetAttribute(fb_decode_attn_g4)", e);
+  e = cudaFuncSetAttribute(fb_decode_attn_g8, cudaFuncAttributeMaxDynamicSharedMemorySize, decode_smem_bytes(8));
+  if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaFuncSetAttribute(fb_decode_attn_g8)", e);
+  // Under lazy module loading the combine kernel would otherwise load on the
+  // first call with splits > 1, which may come during a stream capture.
+  cudaFuncAttributes attrs;
+  e = cudaFuncGetAttributes(&attrs, fb_decode_attn_combine);
+  if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaFuncGetAttributes(fb_decode_attn_combine)", e);
+  g_setup[g_setup_count].ctx_id = id;
+  g_setup[g_setup_count].scratch = static_cast<float*>(p);
+  ++g_setup_count;
+  *scratch = static_cast<float*>(p);
   return 0;
 }
 
 }  // namespace
 
-// out[b, h, :] = softmax(q[b, h] . K^T * scale) V over the first seq_lens[b]
-// tokens of sequence b's pages. q: [batch, n_q, 128] bf16; k_cache, v_cache:
-// [blocks, n_kv, 64, 128] bf16; block_tables: [batch, max_blocks] int32;
-// seq_lens: [batch] int32; out: [batch, n_q, 128] bf16. n_q / n_kv must be 4
-// or 8; splits * pages_per_split must cover max_blocks. stream is a
-// cudaStream_t (0 = the legacy default stream).
-// Returns 0 on success; 1 = the partials do not fit the static scratch,
-// 2 = invalid argument, 3 = CUDA error. A message goes to err (if given).
+// Declared and documented in decode_attn_noalloc.h.
 FB_NOALLOC_EXPORT int fb_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                                   const int* block_tables, int max_blocks, const int* seq_lens,
                                                   void* out, int batch, int n_q, int n_kv, int splits,
@@ -130,18 +185,15 @@ FB_NOALLOC_EXPORT int fb_decode_attention_noalloc(const void* q, const void* k_c
     return fail(err, err_len, 1,
                 "batch * n_q * splits = %lld partial rows exceed the static scratch (%lld rows, 8,519,680 bytes)",
                 rows, kMaxPartialRows);
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail_cuda(err, err_len, "cudaGetDevice", e);
-  if (dev < 0 || dev >= kMaxDevices) return fail(err, err_len, 2, "device ordinal %lld out of range", dev);
   float* scratch = nullptr;
-  if (int rc = setup_device(dev, &scratch, err, err_len)) return rc;
+  if (int rc = setup_context(&scratch, err, err_len)) return rc;
   float* o_part = scratch;
   float* ml_part = scratch + kMaxPartialRows * kHeadDim;
   const int group = n_q / n_kv;
   const float scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaGetLastError();  // start from a clean launch-error state of this runtime
+  cudaError_t e;
   const dim3 grid(splits, n_kv, batch);
   const auto* qb = static_cast<const bf16*>(q);
   const auto* kb = static_cast<const bf16*>(k_cache);

@@ -162,7 +162,8 @@ def build_noalloc(force=False) -> Path:
     static scratch buffer (runtime API, static cudart, one exported symbol)."""
     out = LIB / "libfoundry_noalloc.so"
     src = CSRC / "noalloc" / "decode_attn_noalloc.cu"
-    headers = [CSRC / "kernels" / "attention.cu", *sorted((CSRC / "kernels").glob("*.cuh"))]
+    headers = [CSRC / "noalloc" / "decode_attn_noalloc.h", CSRC / "kernels" / "attention.cu",
+               *sorted((CSRC / "kernels").glob("*.cuh"))]
     flags = [f for f in NVCCFLAGS if f != "-Xptxas=-v"] + ["-rdc=true", "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden"]
     d = _digest([src, *headers], " ".join(flags))
     if not force and _up_to_date(out, d):

@@ -30,9 +30,8 @@ def parse_size(size: int | str) -> int:
         return size
     m = _SIZE_RE.match(size.strip().upper())
     if not m:
-        raise ValueError(
-            f"Invalid size format: {size}. Expected format like '1GB', '16MB', '24KB', or integer bytes"
-        )
+        raise ValueError(f"cannot read {size!r} as a size: use a byte count or a number with a binary "
+                         "unit (B, KB, MB, GB, TB; KiB..TiB also accepted)")
     return int(float(m.group(1)) * _UNITS[m.group(2) or "B"])
 
 

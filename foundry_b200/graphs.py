@@ -277,46 +277,66 @@ def _graph_index(name: str) -> int:
         return 1 << 30
 
 
-def save_graph_manifest(archive_dir: str) -> dict[str, Any] | None:
-    """Groups ``graph_*.json`` in ``archive_dir`` by topology key, marks the
-    first of each group as its template, strips the dependency table from the
-    other members' JSON (the binary keeps it) and writes graph_manifest.json.
+def _manifest_candidates(archive_dir: str) -> list[str]:
+    names = [f for f in os.listdir(archive_dir)
+             if f.startswith("graph_") and f.endswith(".json") and f != "graph_manifest.json"]
+    return sorted(names, key=lambda f: (_graph_index(f), f))
 
-    Parity: reference python/foundry/graph.py:170-242.
+
+def save_graph_manifest(archive_dir: str) -> dict[str, Any] | None:
+    """Writes ``graph_manifest.json`` for the graphs saved in ``archive_dir``.
+
+    Graphs with equal topology keys form one group; the lowest-numbered graph
+    of a group is its template (restored as a real executable) and the others
+    are restored as parameter patches onto it. A member's JSON no longer
+    needs its dependency table, so it is dropped there (the ``.cugraph``
+    binary keeps it). Returns the manifest, or None when the folder holds no
+    graph. Raises ``ValueError`` when a graph has no topology key: such an
+    archive could only be restored one graph at a time, and a manifest that
+    silently left graphs out would hide that.
+
+    Manifest schema (kept from reference python/foundry/graph.py:170-242 so
+    either side reads the other's archives):
+    ``{"topology_groups": [{"topology_key", "template", "members"}]}``.
     """
-    files = sorted(
-        (f for f in os.listdir(archive_dir) if f.startswith("graph_") and f.endswith(".json")
-         and f != "graph_manifest.json"),
-        key=_graph_index,
-    )
-    if not files:
+    names = _manifest_candidates(archive_dir)
+    if not names:
         return None
-    groups: dict[str, list[str]] = {}
-    for fname in files:
-        with open(os.path.join(archive_dir, fname)) as f:
-            key = json.load(f).get("topology_key", "")
-        if not key:
-            return None
-        groups.setdefault(key, []).append(fname)
-    manifest = {"topology_groups": [
-        {"topology_key": k, "template": v[0], "members": v} for k, v in groups.items()
-    ]}
-    with open(os.path.join(archive_dir, "graph_manifest.json"), "w") as f:
-        json.dump(manifest, f, indent=2)
-    templates = {v[0] for v in groups.values()}
-    stripped = 0
-    for fname in files:
-        if fname in templates:
-            continue
-        path = os.path.join(archive_dir, fname)
-        with open(path) as f:
-            data = json.load(f)
-        if "dependencies" in data:
-            del data["dependencies"]
-            with open(path, "w") as f:
-                json.dump(data, f)
-            stripped += 1
-    n_on_demand = sum(len(v) - 1 for v in groups.values())
-    print(f"[foundry] Saved graph_manifest.json: {len(groups)} topology groups "
-          f"({len(groups)} templates, {n_on_demand} on-demand, {stripped} stripped)", file=sys.stderr)
+    docs = {}
+    for name in names:
+        with open(os.path.join(archive_dir, name)) as f:
+            docs[name] = json.load(f)
+    keyless = [n for n in names if not docs[n].get("topology_key")]
+    if keyless:
+        raise ValueError(f"{archive_dir}: {len(keyless)} graph(s) have no topology_key "
+                         f"(first: {keyless[0]}); re-save them with this version")
+    order: list[str] = []
+    members: dict[str, list[str]] = {}
+    for name in names:
+        key = docs[name]["topology_key"]
+        if key not in members:
+            order.append(key)
+            members[key] = []
+        members[key].append(name)
+    manifest = {"topology_groups": [{"topology_key": k, "template": members[k][0], "members": members[k]}
+                                    for k in order]}
+    dropped = 0
+    for group in manifest["topology_groups"]:
+        for name in group["members"][1:]:
+            if docs[name].pop("dependencies", None) is None:
+                continue
+            _write_json_atomic(os.path.join(archive_dir, name), docs[name], indent=None)
+            dropped += 1
+    _write_json_atomic(os.path.join(archive_dir, "graph_manifest.json"), manifest, indent=2)
+    patched = len(names) - len(order)
+    print(f"[foundry_b200] manifest: {len(names)} graphs, {len(order)} topology groups, "
+          f"{patched} restored by patching a template; edge lists dropped from {dropped} member JSON files",
+          file=sys.stderr)
     return manifest
+
+
+def _write_json_atomic(path: str, obj: Any, indent: int | None) -> None:
+    tmp = f"{path}.tmp.{os.getpid()}"
+    with open(tmp, "w") as f:
+        json.dump(obj, f, indent=indent)
+    os.replace(tmp, path)

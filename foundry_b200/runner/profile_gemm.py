@@ -7,7 +7,12 @@ For every linear layer of one decoder layer (+ lm_head) at ``--tokens``
 tokens it prints one JSON line per variant:
 - ``plan``: the planner's choice (one-SM tiles, split-K, stream-K);
 - ``pair``: two-SM ``cta_group::2`` tiles with the same tile width;
-- ``pf<N>``: the planner's plan with an L2 prefetch lead of N k-blocks.
+- ``pf<N>``: the planner's plan with an L2 prefetch lead of N k-blocks;
+- ``bn<B>s<S>[m<T>]``: one-SM tiles of B tokens, S splits, T weight tiles per
+  unit (default 1);
+- ``pair<B>s<S>``: two-SM tiles of B tokens with S splits;
+- ``sk<B>``: stream-K over one-SM tiles of B tokens.
+``--ops`` restricts the run to some layers (e.g. ``gate_up,lm_head``).
 
 Each line gives the plan (tile width, splits, grid) and the mean time of
 ``--iters`` back-to-back launches (CUDA events, after ``--warmup``).
@@ -43,6 +48,10 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--check", action="store_true")
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--ops", default="", help="comma-separated subset of qkv,o,gate_up,down,lm_head")
+    ap.add_argument("--graph", action="store_true",
+                    help="time one CUDA-graph replay of --iters launches (no host launch overhead)")
+    ap.add_argument("--shape", default="", help="n,k: one custom weight shape instead of the model's layers")
     a = ap.parse_args(argv)
 
     import torch
@@ -55,7 +64,14 @@ def main(argv=None) -> int:
     cfg = config_by_name(a.model)
     sms = G._rt.sm_count()
     gen = torch.Generator(device="cuda").manual_seed(0)
-    for name, t, n, k in shapes(cfg, a.tokens):
+    only = set(filter(None, a.ops.split(",")))
+    todo = shapes(cfg, a.tokens)
+    if a.shape:
+        n_, k_ = (int(v) for v in a.shape.split(","))
+        todo = [("custom", a.tokens, n_, k_)]
+    for name, t, n, k in todo:
+        if only and name not in only:
+            continue
         x = (torch.randn(t, k, device="cuda", generator=gen) * 0.5).to(torch.bfloat16)
         w = (torch.randn(n, k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
         pb = G.PartialBuffer(G.MAX_SPLITS * t * n)
@@ -71,24 +87,54 @@ def main(argv=None) -> int:
                 p = G.pair_plan(n, t, k, max(64, base.bn), sms, pf=base.pf)
             elif v.startswith("pf"):
                 p = dataclasses.replace(base, pf=int(v[2:]))
+            elif v.startswith("bn"):
+                bn, rest = v[2:].split("s")
+                sp, mt = (rest.split("m") + ["1"])[:2]
+                bn, sp, mt = int(bn), int(sp), int(mt)
+                units = -(-n // (128 * mt)) * -(-t // bn) * sp if base.swap else 0
+                p = dataclasses.replace(base, bn=bn, splits=sp, mt=mt, grid=min(units, sms), streamk=False,
+                                        pair=False)
+            elif v.startswith("pair") and v != "pair":
+                bn, sp = (int(x) for x in v[4:].split("s"))
+                tiles = -(-n // 256) * -(-t // bn)
+                p = G.Plan(bn=bn, splits=sp, grid=2 * min(tiles * sp, sms // 2), swap=True, pf=base.pf,
+                           pair=True)
+            elif v.startswith("sk"):
+                bn = int(v[2:])
+                p = dataclasses.replace(base, bn=bn, splits=1, mt=1, grid=sms, streamk=True, pair=False)
             else:
                 raise SystemExit(f"unknown variant {v!r}")
 
+            skb = G.StreamKBuffer(torch.empty(sms * 128 * 256, dtype=torch.float32, device="cuda"),
+                                  torch.zeros(sms * 8, dtype=torch.int32, device="cuda")) if p.streamk else None
+
             def run():
-                return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p)
+                return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p,
+                                streamk=skb)
 
             for _ in range(a.warmup):
                 run()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
-            e0.record()
-            for _ in range(a.iters):
-                r = run()
-            e1.record()
+            if a.graph:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for _ in range(a.iters):
+                        r = run()
+                g.replay()
+                torch.cuda.synchronize()
+                e0.record()
+                g.replay()
+                e1.record()
+            else:
+                e0.record()
+                for _ in range(a.iters):
+                    r = run()
+                e1.record()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000 / a.iters
-            line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v, "bn": p.bn, "splits": p.splits,
-                    "grid": p.grid, "us": round(us, 1),
+            line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v, "kernel": p.kernel, "bn": p.bn,
+                    "splits": p.splits, "grid": p.grid, "us": round(us, 1),
                     "weight_tbps": round(n * k * 2 / (us * 1e-6) / 1e12, 2),
                     "tflops": round(2 * t * n * k / (us * 1e-6) / 1e12, 1)}
             if a.check:

@@ -478,6 +478,23 @@ def scenario_faults(workdir: str) -> None:
         raise AssertionError("backwards offset accepted")
     except RuntimeError as e:
         assert "forward" in str(e), e
+    # (h) a stale manifest that groups two graphs with the same node count but
+    # different topology keys (groups 0 and 1 put their memset at different
+    # positions) must be refused, not patched onto the wrong template
+    stale = os.path.join(workdir, "stale_manifest")
+    shutil.copytree(archive, stale)
+    k0 = c.read_binary_graph(os.path.join(stale, "graph_0.cugraph")).topology_key
+    k1 = c.read_binary_graph(os.path.join(stale, "graph_1.cugraph")).topology_key
+    assert k0 != k1
+    with open(os.path.join(stale, "graph_manifest.json"), "w") as f:
+        json.dump({"topology_groups": [{"topology_key": k0, "template": "graph_0.json",
+                                        "members": ["graph_0.json", "graph_1.json"]}]}, f)
+    pending = c.start_graph_builds([os.path.join(stale, "graph_0.json"), os.path.join(stale, "graph_1.json")], 2)
+    try:
+        pending.wait()
+        raise AssertionError("stale manifest accepted")
+    except RuntimeError as e:
+        assert "another topology" in str(e), e
     print("FAULTS OK")
 
 

@@ -86,3 +86,23 @@ def test_memcpy_event_empty_nodes_round_trip(tmp_path):
     wd = str(tmp_path)
     assert "MIXED SAVE OK" in _run("mixed", wd, "save")
     assert "MIXED LOAD OK" in _run("mixed", wd, "load")
+
+
+def test_manifest_refuses_graphs_without_topology_key(tmp_path):
+    """A graph without a topology key cannot join a group: writing a manifest
+    that silently leaves it out would hide that, so the call raises."""
+    from foundry_b200.graphs import save_graph_manifest
+
+    (tmp_path / "graph_0.json").write_text(json.dumps({"topology_key": "k", "nodes": [], "dependencies": []}))
+    (tmp_path / "graph_1.json").write_text(json.dumps({"nodes": []}))
+    with pytest.raises(ValueError, match="topology_key"):
+        save_graph_manifest(str(tmp_path))
+    assert not (tmp_path / "graph_manifest.json").exists()
+    (tmp_path / "graph_1.json").write_text(json.dumps({"topology_key": "k", "nodes": [], "dependencies": [1]}))
+    (tmp_path / "graph_10.json").write_text(json.dumps({"topology_key": "j", "nodes": []}))
+    m = save_graph_manifest(str(tmp_path))
+    assert m["topology_groups"] == [
+        {"topology_key": "k", "template": "graph_0.json", "members": ["graph_0.json", "graph_1.json"]},
+        {"topology_key": "j", "template": "graph_10.json", "members": ["graph_10.json"]}]
+    assert "dependencies" in json.loads((tmp_path / "graph_0.json").read_text())
+    assert "dependencies" not in json.loads((tmp_path / "graph_1.json").read_text())

@@ -1,8 +1,11 @@
 """The allocation-free decode-attention entry point (lib/libfoundry_noalloc.so,
-exported C symbol fb_decode_attention_noalloc) against the cubin entry point
+exported C symbol fb_decode_attention_noalloc, declared in
+csrc/noalloc/decode_attn_noalloc.h) against the cubin entry point
 (ops.decode_attention, impl="simt", same kernels with a caller-owned
-workspace), on two calls in a row; plus its size and argument rejections.
-Named to be collected last; it must also pass alone in a fresh process."""
+workspace), on two calls in a row; the second call must leave the device's
+free memory and torch's allocator untouched. Plus its size and argument
+rejections. Named to be collected last; it must also pass alone in a fresh
+process."""
 
 import ctypes
 import os
@@ -14,6 +17,8 @@ pytestmark = pytest.mark.gpu
 
 LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "foundry_b200", "lib",
                    "libfoundry_noalloc.so")
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "csrc", "noalloc",
+                      "decode_attn_noalloc.h")
 MAX_PARTIAL_ROWS = 16384
 
 
@@ -65,12 +70,24 @@ def test_no_alloc_matches_workspace_entry_point(batch, n_q, n_kv, max_pages, spl
     ops.decode_attention(q, kc, vc, tables, lens, want, max_pages, ws, scale=scale, splits=(splits, pps),
                          impl="simt")
     assert ops.status("attention") == 0
-    for _ in range(2):  # the first call does the per-device setup; the second reuses it
+    for call in range(2):  # the first call does the per-context setup; the second reuses it
         out = torch.full_like(q, float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        torch_before = torch.cuda.memory_allocated()
         rc, msg = _call(fn, q, kc, vc, tables, lens, out, splits, pps, scale)
         assert rc == 0, msg
         torch.cuda.synchronize()
+        if call == 1:
+            assert torch.cuda.mem_get_info()[0] == free_before, "the entry point allocated device memory"
+            assert torch.cuda.memory_allocated() == torch_before
         torch.testing.assert_close(out.float(), want.float(), atol=2e-2, rtol=2e-2)
+
+
+def test_no_alloc_header_declares_the_entry_point():
+    text = open(HEADER).read()
+    assert "int fb_decode_attention_noalloc(" in text
+    assert f"#define FB_NOALLOC_MAX_PARTIAL_ROWS {MAX_PARTIAL_ROWS}" in text
 
 
 def test_no_alloc_rejects_oversize_and_bad_args():
