@@ -38,6 +38,10 @@ enum HeaderFlag : uint32_t {
   HF_ALLOC_EVENTS = 1u << 2,
   HF_OUTPUTS = 1u << 3,
   HF_GENERATORS = 1u << 4,
+  // Generator records carry the device addresses of the generator's graph
+  // seed/offset words (GeneratorPtrRec) so a LOAD can relocate them; an
+  // addition to v1, set only when a graph consumed random numbers.
+  HF_GENERATOR_PTRS = 1u << 5,
 };
 
 #pragma pack(push, 1)
@@ -155,6 +159,12 @@ struct GeneratorRec {
   uint64_t wholegraph_increment;
 };
 
+struct GeneratorPtrRec {
+  GeneratorRec base;
+  uint64_t seed_ptr;
+  uint64_t offset_ptr;
+};
+
 struct DepRec {
   uint32_t from;
   uint32_t to;
@@ -169,6 +179,7 @@ static_assert(sizeof(MemcpyRec) == 152, "memcpy record is 152 bytes");
 static_assert(sizeof(NodeRec) == 168, "node record is 168 bytes");
 static_assert(sizeof(ParamRec) == 8, "param record is 8 bytes");
 static_assert(sizeof(GeneratorRec) == 24, "generator record is 24 bytes");
+static_assert(sizeof(GeneratorPtrRec) == 40, "generator record with pointers is 40 bytes");
 static_assert(sizeof(DepRec) == 8, "dependency record is 8 bytes");
 
 }  // namespace bin

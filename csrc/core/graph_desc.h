@@ -81,8 +81,14 @@ struct Node {
   int32_t event_id = -1;
 };
 
+// A random-number generator whose state the graph's kernels read. The
+// kernels hold the device addresses of the generator's graph seed and offset
+// words (seed_ptr, offset_ptr; 0 when unknown); before every replay the host
+// writes the generator's seed and current offset there and advances the
+// offset by wholegraph_increment.
 struct Generator {
   uint64_t id = 0, seed = 0, wholegraph_increment = 0;
+  uint64_t seed_ptr = 0, offset_ptr = 0;
 };
 
 struct GraphDesc {
@@ -137,6 +143,12 @@ void make_kernel_params(const KernelNode& k, CUDA_KERNEL_NODE_PARAMS* p, std::ve
                         std::vector<void*>* extra);
 
 bool kernel_launch_equal(const KernelNode& a, const KernelNode& b);
+
+// Moves the generators' seed/offset words to seed_slot / seed_slot + 8: every
+// 8-byte-aligned word of a kernel parameter (or packed argument buffer) that
+// equals a generator's seed_ptr or offset_ptr is rewritten, and the generator
+// records take the new addresses. Returns the number of words rewritten.
+size_t relocate_generator_words(GraphDesc& g, uint64_t seed_slot);
 
 void check_drv(CUresult r, const char* what);
 

@@ -418,6 +418,43 @@ bool kernel_launch_equal(const KernelNode& a, const KernelNode& b) {
          a.params == b.params && a.has_extra == b.has_extra && a.extra_buffer == b.extra_buffer;
 }
 
+namespace {
+
+size_t rewrite_words(std::vector<uint8_t>& bytes, uint64_t from_seed, uint64_t from_off, uint64_t to_seed,
+                     uint64_t to_off) {
+  size_t n = 0;
+  for (size_t o = 0; o + 8 <= bytes.size(); o += 8) {
+    uint64_t w;
+    memcpy(&w, bytes.data() + o, 8);
+    const uint64_t to = w == from_seed ? to_seed : w == from_off ? to_off : 0;
+    if (to) {
+      memcpy(bytes.data() + o, &to, 8);
+      ++n;
+    }
+  }
+  return n;
+}
+
+}  // namespace
+
+size_t relocate_generator_words(GraphDesc& g, uint64_t seed_slot) {
+  size_t n = 0;
+  for (Generator& gen : g.generators) {
+    if (!gen.seed_ptr || !gen.offset_ptr) continue;
+    const uint64_t to_seed = seed_slot, to_off = seed_slot + 8;
+    if (gen.seed_ptr == to_seed && gen.offset_ptr == to_off) continue;
+    for (Node& node : g.nodes) {
+      if (node.type != NodeType::Kernel) continue;
+      KernelNode& k = node.kernel;
+      for (auto& p : k.params) n += rewrite_words(p, gen.seed_ptr, gen.offset_ptr, to_seed, to_off);
+      if (k.has_extra) n += rewrite_words(k.extra_buffer, gen.seed_ptr, gen.offset_ptr, to_seed, to_off);
+    }
+    gen.seed_ptr = to_seed;
+    gen.offset_ptr = to_off;
+  }
+  return n;
+}
+
 BuiltGraph::~BuiltGraph() {
   const FbDriver* d = fb_driver();
   if (graph && d->cuGraphDestroy) d->cuGraphDestroy(graph);

@@ -455,6 +455,36 @@ PYBIND11_MODULE(_C, m) {
         for (const auto& p : n.kernel.params) out.append(py::bytes(reinterpret_cast<const char*>(p.data()), p.size()));
         return out;
       })
+      .def_property(
+          "generators",
+          [](const GraphDesc& g) {
+            py::list out;
+            for (const auto& gen : g.generators) {
+              py::dict d;
+              d["id"] = gen.id;
+              d["seed"] = gen.seed;
+              d["wholegraph_increment"] = gen.wholegraph_increment;
+              d["seed_ptr"] = gen.seed_ptr;
+              d["offset_ptr"] = gen.offset_ptr;
+              out.append(d);
+            }
+            return out;
+          },
+          [](GraphDesc& g, const py::list& gens) {
+            std::vector<Generator> v;
+            for (const auto& item : gens) {
+              const py::dict d = item.cast<py::dict>();
+              Generator gen;
+              gen.id = d.contains("id") ? d["id"].cast<uint64_t>() : 0;
+              gen.seed = d["seed"].cast<uint64_t>();
+              gen.wholegraph_increment = d["wholegraph_increment"].cast<uint64_t>();
+              gen.seed_ptr = d.contains("seed_ptr") ? d["seed_ptr"].cast<uint64_t>() : 0;
+              gen.offset_ptr = d.contains("offset_ptr") ? d["offset_ptr"].cast<uint64_t>() : 0;
+              v.push_back(gen);
+            }
+            g.generators = std::move(v);
+          })
+      .def("relocate_generator_words", [](GraphDesc& g, uint64_t slot) { return relocate_generator_words(g, slot); })
       .def("to_json", [](const GraphDesc& g) { return to_json(g).dump(); })
       .def("save", [](GraphDesc& g, const std::string& json_path) {
         py::gil_scoped_release rel;
@@ -515,14 +545,15 @@ PYBIND11_MODULE(_C, m) {
         return reinterpret_cast<uintptr_t>(e ? e : (g.shared ? g.shared->exec : nullptr));
       })
       .def_property_readonly("output_tensors_json", [](const RestoredGraph& g) { return g.desc->output_tensors_json; });
-  m.def("load_graph", [](const std::string& path) {
+  m.def("load_graph", [](const std::string& path, uint64_t rng_slot) {
     py::gil_scoped_release rel;
     auto desc = read_graph_file(path);
+    if (rng_slot) relocate_generator_words(*desc, rng_slot);
     const auto& ev = desc->allocator_events_json;
     if (!ev.empty() && fb_events_replay_json(ev.data(), ev.size()) != FB_OK)
       throw std::runtime_error(fb_last_error());
     return restore_single(desc, path);
-  });
+  }, py::arg("path"), py::arg("rng_slot") = 0);
 
   py::class_<PendingLoads, std::shared_ptr<PendingLoads>>(m, "PendingGraphLoads")
       .def_property_readonly("num_graphs", [](const PendingLoads& p) { return p.paths.size(); })
@@ -537,8 +568,8 @@ PYBIND11_MODULE(_C, m) {
         py::gil_scoped_release rel;
         return p.finish_one(i);
       });
-  m.def("start_graph_builds", [](const std::vector<std::string>& paths, int num_threads) {
+  m.def("start_graph_builds", [](const std::vector<std::string>& paths, int num_threads, uint64_t rng_slot) {
     py::gil_scoped_release rel;
-    return start_graph_builds(paths, num_threads);
-  }, py::arg("paths"), py::arg("num_threads") = 4);
+    return start_graph_builds(paths, num_threads, rng_slot);
+  }, py::arg("paths"), py::arg("num_threads") = 4, py::arg("rng_slot") = 0);
 }

@@ -204,7 +204,8 @@ void parallel_for(size_t n, int threads, F&& f) {
 
 }  // namespace
 
-std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>& paths, int num_threads) {
+std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>& paths, int num_threads,
+                                                 uint64_t rng_slot) {
   auto pl = std::make_shared<PendingLoads>();
   pl->paths = paths;
   pl->num_threads = num_threads;
@@ -212,7 +213,10 @@ std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>&
   const auto t0 = std::chrono::steady_clock::now();
   // Phase 1: read every graph file in parallel (binary fast path).
   pl->descs.resize(paths.size());
-  parallel_for(paths.size(), num_threads, [&](size_t i) { pl->descs[i] = read_graph_file(paths[i]); });
+  parallel_for(paths.size(), num_threads, [&](size_t i) {
+    pl->descs[i] = read_graph_file(paths[i]);
+    if (rng_slot) relocate_generator_words(*pl->descs[i], rng_slot);
+  });
   // Grouping: the manifest when present, else topology keys in file order.
   std::map<std::string, int> by_name;
   for (size_t i = 0; i < paths.size(); ++i) by_name[basename_of(paths[i])] = static_cast<int>(i);

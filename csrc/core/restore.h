@@ -98,6 +98,9 @@ class PendingLoads {
   std::exception_ptr error_;
 };
 
-std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>& paths, int num_threads);
+// rng_slot != 0: the generators' seed/offset words of every graph are moved to
+// rng_slot / rng_slot + 8 (relocate_generator_words) as the graphs are read.
+std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>& paths, int num_threads,
+                                                 uint64_t rng_slot = 0);
 
 }  // namespace fbc

@@ -250,6 +250,10 @@ J::Value to_json(const GraphDesc& g) {
     o["id"] = static_cast<unsigned long long>(gen.id);
     o["seed"] = static_cast<unsigned long long>(gen.seed);
     o["wholegraph_increment"] = static_cast<unsigned long long>(gen.wholegraph_increment);
+    if (gen.seed_ptr) {
+      o["seed_ptr"] = static_cast<unsigned long long>(gen.seed_ptr);
+      o["offset_ptr"] = static_cast<unsigned long long>(gen.offset_ptr);
+    }
     gens.push_back(J::Value(std::move(o)));
   }
   root["generators"] = J::Value(std::move(gens));
@@ -323,8 +327,10 @@ std::shared_ptr<GraphDesc> from_json(const J::Value& v) {
   if (const J::Value* gens = root.find("generators"))
     for (const J::Value& gv : gens->as_array()) {
       const J::Object& o = gv.as_object();
-      g->generators.push_back(Generator{o.at("id").as_u64(), o.at("seed").as_u64(),
-                                        o.at("wholegraph_increment").as_u64()});
+      Generator gen{o.at("id").as_u64(), o.at("seed").as_u64(), o.at("wholegraph_increment").as_u64()};
+      if (const J::Value* sp = o.find("seed_ptr")) gen.seed_ptr = sp->as_u64();
+      if (const J::Value* op = o.find("offset_ptr")) gen.offset_ptr = op->as_u64();
+      g->generators.push_back(gen);
     }
   if (const J::Value* ne = root.find("num_events")) g->num_events = static_cast<int>(ne->as_i64());
   if (const J::Value* ae = root.find("allocator_events")) g->allocator_events_json = ae->dump();
@@ -485,8 +491,17 @@ void write_binary(const GraphDesc& g, const std::string& path) {
     common.attr_query_available = tmp.attr_query_available;
     common.preferred_smem_carveout = tmp.preferred_smem_carveout;
   }
+  bool gen_ptrs = false;
+  for (const auto& gen : g.generators) gen_ptrs = gen_ptrs || gen.seed_ptr != 0;
   std::vector<bin::GeneratorRec> gens;
-  for (const auto& gen : g.generators) gens.push_back(bin::GeneratorRec{gen.id, gen.seed, gen.wholegraph_increment});
+  std::vector<bin::GeneratorPtrRec> gens_p;
+  for (const auto& gen : g.generators) {
+    const bin::GeneratorRec r{gen.id, gen.seed, gen.wholegraph_increment};
+    if (gen_ptrs)
+      gens_p.push_back(bin::GeneratorPtrRec{r, gen.seed_ptr, gen.offset_ptr});
+    else
+      gens.push_back(r);
+  }
 
   // Assemble sections.
   struct Blob {
@@ -501,7 +516,8 @@ void write_binary(const GraphDesc& g, const std::string& path) {
       {pdata.data(), pdata.size()},
       {argbuf.data(), argbuf.size()},
       {&common, g.has_common_attrs ? sizeof(common) : 0},
-      {gens.data(), gens.size() * sizeof(bin::GeneratorRec)},
+      {gen_ptrs ? static_cast<const void*>(gens_p.data()) : static_cast<const void*>(gens.data()),
+       gen_ptrs ? gens_p.size() * sizeof(bin::GeneratorPtrRec) : gens.size() * sizeof(bin::GeneratorRec)},
       {g.allocator_events_json.data(), g.allocator_events_json.size()},
       {g.output_tensors_json.data(), g.output_tensors_json.size()},
       {g.topology_key.data(), g.topology_key.size()},
@@ -513,10 +529,10 @@ void write_binary(const GraphDesc& g, const std::string& path) {
   h.flags = (g.has_common_attrs ? bin::HF_COMMON_ATTRS : 0) | (g.has_deps ? bin::HF_DEPS : 0) |
             (!g.allocator_events_json.empty() ? bin::HF_ALLOC_EVENTS : 0) |
             (!g.output_tensors_json.empty() ? bin::HF_OUTPUTS : 0) |
-            (!g.generators.empty() ? bin::HF_GENERATORS : 0);
+            (!g.generators.empty() ? bin::HF_GENERATORS : 0) | (gen_ptrs ? bin::HF_GENERATOR_PTRS : 0);
   h.num_nodes = static_cast<uint32_t>(nodes.size());
   h.num_deps = static_cast<uint32_t>(deps.size());
-  h.num_generators = static_cast<uint32_t>(gens.size());
+  h.num_generators = static_cast<uint32_t>(g.generators.size());
   h.num_sections = bin::S_COUNT;
   h.num_strings = strings.count;
   // num_events has no header field in v1; it is stored in the reserved bytes.
@@ -679,11 +695,14 @@ std::shared_ptr<GraphDesc> read_binary(const std::string& path) {
     a.attr_query_available = c.attr_query_available;
     a.preferred_carveout = c.preferred_smem_carveout;
   }
-  if (dir[bin::S_GENERATORS].size != h.num_generators * sizeof(bin::GeneratorRec)) fail("generator table size");
+  const bool gen_ptrs = (h.flags & bin::HF_GENERATOR_PTRS) != 0;
+  const size_t gen_rec = gen_ptrs ? sizeof(bin::GeneratorPtrRec) : sizeof(bin::GeneratorRec);
+  if (dir[bin::S_GENERATORS].size != h.num_generators * gen_rec) fail("generator table size");
   for (uint32_t i = 0; i < h.num_generators; ++i) {
-    bin::GeneratorRec r;
-    memcpy(&r, sec(bin::S_GENERATORS) + i * sizeof(r), sizeof(r));
-    g->generators.push_back(Generator{r.id, r.seed, r.wholegraph_increment});
+    bin::GeneratorPtrRec r{};
+    memcpy(&r, sec(bin::S_GENERATORS) + i * gen_rec, gen_rec);
+    g->generators.push_back(
+        Generator{r.base.id, r.base.seed, r.base.wholegraph_increment, r.seed_ptr, r.offset_ptr});
   }
   g->allocator_events_json.assign(reinterpret_cast<const char*>(sec(bin::S_ALLOC_EVENTS)),
                                   dir[bin::S_ALLOC_EVENTS].size);

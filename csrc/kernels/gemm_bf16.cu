@@ -14,9 +14,12 @@
 //   warp 1      allocates TMEM; one elected lane issues tcgen05.mma (M=128,
 //               N=BN, K=16) and tcgen05.commit to release smem stages and to
 //               publish finished accumulators
-//   warps 2-5   epilogue: tcgen05.ld (32 lanes x 16 columns) -> registers ->
-//               global stores; when TMEM has room the accumulators are double
-//               buffered so the epilogue of one unit overlaps the next unit's MMAs
+//   warps 2-5   epilogue: tcgen05.ld (32 lanes x 16 columns, four per wait) ->
+//               registers -> a shared-memory tile -> TMA store (transposed
+//               decode outputs, residual tile loaded by TMA) or direct global
+//               stores (prefill layout, multicast); when TMEM has room the
+//               accumulators are double buffered so the epilogue of one unit
+//               overlaps the next unit's MMAs
 // A work unit is MT (1 or 2) 128-row A tiles x one BN-column B tile: with
 // MT = 2 the B tile in shared memory feeds two MMAs per K step, halving the
 // B bytes each SM has to pull per A byte (decode GEMMs are bound by how fast
@@ -46,27 +49,58 @@ constexpr int EPI_A_STREAM = 4;  // L2 evict-first hint on A loads
 constexpr int EPI_B_STREAM = 8;  // L2 evict-first hint on B loads
 // mode bits 8..15: how many k-blocks ahead of the ring A tiles are prefetched into L2
 constexpr int EPI_MCAST = 1 << 16;  // `out` is an NVLS multicast address: stores reach every rank
+constexpr int EPI_TMA_OUT = 1 << 17;  // transposed output written by TMA stores through tmO (and tmR)
 constexpr int NUM_THREADS = 192;
+
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// At most one store group may still be reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
+
+// TMA-store epilogue of the transposed (swap-AB) output: per chunk of 32
+// output columns (tokens) the epilogue threads convert their TMEM rows into a
+// [32 tokens][128 features] tile in shared memory (bf16 output, or fp32 for a
+// split-K slice) and one thread stores it with cp.async.bulk.tensor; two
+// buffers alternate so the conversion of a chunk overlaps the store of the
+// previous one. A residual tile comes in by TMA the same way. The epilogue
+// threads then issue about one shared-memory store per output element and no
+// global stores (the scalar-store epilogue left the last tile's stores on the
+// critical path of every launch).
+constexpr int EPI_COLS = 32;
+constexpr int STG_BYTES = 2 * EPI_COLS * BM * 4;  // two fp32 buffers, or two bf16 + two residual buffers
 
 template <int BN, int MT>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;         // one 128-row A tile per K step
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = MT * A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
   static constexpr int ACC_COLS = MT * BN;             // TMEM columns of one accumulator set
   static constexpr int ACC_BUFS = (2 * ACC_COLS <= 512) ? 2 : 1;
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(ACC_BUFS * ACC_COLS);
 };
 
 template <int BN, int MT>
-__device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
-                                          const bf16* residual, int M, int N, int K, int ldo, int mode, int splits,
-                                          float* __restrict__ ws, long long split_stride) {
+__device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmO,
+                                          const CUtensorMap* tmR, bf16* __restrict__ out, const bf16* residual, int M,
+                                          int N, int K, int ldo, int mode, int splits, float* __restrict__ ws,
+                                          long long split_stride) {
   using C = Cfg<BN, MT>;
   constexpr int STAGES = C::STAGES;
   constexpr int NBUF = C::ACC_BUFS;
@@ -74,11 +108,14 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                               // [STAGES][MT][128 x 64]
   uint8_t* sB = smem + STAGES * MT * C::A_BYTES;     // [STAGES][BN x 64]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* stg = smem + STAGES * C::STAGE_BYTES;  // epilogue tiles (STG_BYTES)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* ebar = tempty + 2;  // the four epilogue warps' rendezvous (staging buffer hand-over)
+  uint64_t* rbar = ebar + 1;    // residual tile loads, one per buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -98,6 +135,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
+    mbar_init(ebar, 4);
+    mbar_init(&rbar[0], 1);
+    mbar_init(&rbar[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async();
@@ -105,6 +145,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(tmA);
     tma_prefetch_desc(tmB);
+    if (mode & EPI_TMA_OUT) {
+      tma_prefetch_desc(tmO);
+      if (mode & EPI_RESIDUAL) tma_prefetch_desc(tmR);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -222,8 +266,22 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int et = threadIdx.x - 64;  // 0..127 over the four epilogue warps; 0 issues the tile stores
+    const bool tma_out = (mode & EPI_TMA_OUT) && (mode & EPI_TRANSPOSE) && !(mode & EPI_MCAST);
+    uint32_t ephase = 0, rphase = 0;  // rphase bit b: parity of residual buffer b
+    uint32_t chunk = 0;  // epilogue chunks so far: buffer = chunk & 1
+    bool ok = true;
+    // Bounded rendezvous of the four epilogue warps: a warp that gave up on a
+    // wait never leaves the others blocked.
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ebar);
+      const bool done = mbar_wait(ebar, ephase, FB_KERR_TIMEOUT_TMEM);
+      ephase ^= 1;
+      return done;
+    };
     int it = 0;
-    for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
+    for (int u = blockIdx.x; ok && u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
       const int mn = u / splits, sp = u % splits;
       const int m_blk = mn % num_m, n_blk = mn / num_m;
       const int acc = NBUF == 2 ? (it & 1) : 0;
@@ -235,15 +293,72 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       tc_fence_after();
       float* part = splits > 1 ? ws + static_cast<size_t>(sp) * split_stride : nullptr;
 #pragma unroll 1
-      for (int mt = 0; mt < MT; ++mt) {
+      for (int mt = 0; mt < MT && ok; ++mt) {
         const int gm = (m_blk * MT + mt) * BM + quarter * 32 + lane;  // D row of this thread
         const uint32_t t_row =
             tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::ACC_COLS + mt * BN;
+        // 64 columns (four 16-column TMEM loads) per wait: one TMEM round trip
+        // per 64 columns instead of per 16.
+        if (tma_out) {
+          constexpr int EC = BN < EPI_COLS ? BN : EPI_COLS;
+          const int gm0 = (m_blk * MT + mt) * BM;
+          const int f = quarter * 32 + lane;  // feature (row of D) this thread holds
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(t_row + c0, r);
+          for (int c1 = 0; c1 < BN && ok; c1 += EC, ++chunk) {
+            const int buf = chunk & 1;
+            const int gn0 = n_blk * BN + c1;
+            float* sf = reinterpret_cast<float*>(stg) + buf * (EPI_COLS * BM);          // fp32 tile
+            bf16* sb = reinterpret_cast<bf16*>(stg) + buf * (EPI_COLS * BM);            // bf16 tile
+            bf16* sr = reinterpret_cast<bf16*>(stg + STG_BYTES / 2) + buf * (EPI_COLS * BM);  // residual
+            uint32_t rr[EC];
+#pragma unroll
+            for (int j = 0; j < EC / 16; ++j)
+              tmem_ld16(t_row + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(rr + 16 * j));
+            tmem_ld_wait();
+            if (et == 0 && chunk >= 2) bulk_wait_read_1();  // this buffer's previous store has read it
+            if (!(ok = epi_sync())) break;
+            if (!part && (mode & EPI_RESIDUAL)) {
+              if (et == 0) {
+                mbar_arrive_expect_tx(&rbar[buf], EC * BM * 2);
+                tma_load_2d(sr, tmR, &rbar[buf], gm0, gn0);
+              }
+              if (!(ok = mbar_wait(&rbar[buf], (rphase >> buf) & 1u, FB_KERR_TIMEOUT_FULL))) break;
+              rphase ^= 1u << buf;
+            }
+            if (part) {
+#pragma unroll
+              for (int t = 0; t < EC; ++t) sf[t * BM + f] = __uint_as_float(rr[t]);
+            } else if (mode & EPI_RESIDUAL) {
+#pragma unroll
+              for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(__uint_as_float(rr[t]) + bf2f(sr[t * BM + f]));
+            } else {
+#pragma unroll
+              for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(__uint_as_float(rr[t]));
+            }
+            fence_proxy_async();  // generic-proxy writes -> visible to the TMA engine
+            if (!(ok = epi_sync())) break;
+            if (et == 0) {
+              if (part)
+                tma_store_3d(tmO, sf, gm0, gn0, sp);
+              else
+                tma_store_2d(tmO, sb, gm0, gn0);
+              bulk_commit();
+            }
+          }
+          continue;
+        }
+        constexpr int CH = BN < 64 ? BN : 64;
+#pragma unroll 1
+        for (int c1 = 0; c1 < BN; c1 += CH) {
+          uint32_t rr[CH];
+#pragma unroll
+          for (int j = 0; j < CH / 16; ++j)
+            tmem_ld16(t_row + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(rr + 16 * j));
           tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < CH / 16; ++j) {
+          const uint32_t* r = rr + 16 * j;
+          const int c0 = c1 + 16 * j;
           const int gn0 = n_blk * BN + c0;
           if ((mode & EPI_MCAST) && (mode & EPI_TRANSPOSE)) {
             // Multicast store of bf16 pairs: lanes hold consecutive output
@@ -345,12 +460,18 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
                 }
             }
           }
+          }
         }
+      }
+      if (!ok) {
+        *(volatile int*)abort_flag = 1;
+        break;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (et == 0 && tma_out) bulk_wait_all();  // the tile stores have read shared memory and landed
   }
 
   tc_fence_before();
@@ -363,10 +484,11 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
 
 #define FB_GEMM_INSTANCE(BN, MT)                                                                                    \
   extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_bf16_bn##BN##_m##MT(                         \
-      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,                             \
+      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, bf16* out,                  \
       const bf16* residual, int M, int N, int K, int ldo, int mode, int splits, float* ws,                          \
       long long split_stride) {                                                                                      \
-    gemm_body<BN, MT>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);                    \
+    gemm_body<BN, MT>(&tmA, &tmB, &tmO, &tmR, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);        \
   }
 
 FB_GEMM_INSTANCE(16, 1)

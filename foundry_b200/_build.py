@@ -130,6 +130,31 @@ def build_core(force=False) -> Path:
     return out
 
 
+def build_torchrng(force=False) -> Path:
+    """``foundry_b200/_torchrng*.so``: reads the graph-capture state of torch's
+    default CUDA generators (links libtorch; loaded only when a graph that
+    draws random numbers is saved or restored)."""
+    import torch
+
+    tdir = Path(torch.__file__).resolve().parent
+    out = PKG / f"_torchrng{ext_suffix()}"
+    src = CSRC / "torchrng" / "rng_state.cpp"
+    abi = int(bool(torch._C._GLIBCXX_USE_CXX11_ABI))
+    inc = [f"-I{sysconfig.get_paths()['include']}", f"-I{tdir / 'include'}",
+           f"-I{tdir / 'include' / 'torch' / 'csrc' / 'api' / 'include'}", f"-I{CUDA_HOME / 'include'}"]
+    flags = ["-std=c++17", "-O2", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_torchrng",
+             "-w"]
+    d = _digest([src], " ".join(flags + inc + [torch.__version__]))
+    if not force and _up_to_date(out, d):
+        return out
+    tmp = out.with_name(out.name + ".tmp")
+    _run(["g++", *flags, *inc, "-shared", str(src), "-o", str(tmp), f"-L{tdir / 'lib'}", "-lc10", "-lc10_cuda",
+          "-ltorch_cpu", "-ltorch_cuda", f"-Wl,-rpath,{tdir / 'lib'}"])
+    os.replace(tmp, out)
+    _stamp(out, d)
+    return out
+
+
 def kernel_sources():
     return sorted((CSRC / "kernels").glob("*.cu"))
 
@@ -216,6 +241,7 @@ def build_all(force=False, kernels=True) -> None:
     build_hook(force)
     build_mock(force)
     build_core(force)
+    build_torchrng(force)
     if kernels:
         if shutil.which(NVCC) is None and not Path(NVCC).exists():
             raise RuntimeError(f"nvcc not found at {NVCC}")

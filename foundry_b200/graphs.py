@@ -101,6 +101,76 @@ def _decode_outputs(text: str) -> OutputTensors | None:
     return tensors if meta["type"] == "list" else tuple(tensors)
 
 
+# ---- random-number generator state ------------------------------------------------------
+#
+# A captured kernel that draws random numbers reads the Philox seed and offset
+# from two device words of its generator's graph state. SAVE records their
+# addresses and the graph's whole-graph increment (the offsets one replay
+# consumes). LOAD moves those words into a per-device slot owned by this
+# module (the restore rewrites the matching pointer words in the kernels'
+# parameters), and every replay of a restored graph first writes the
+# generator's seed and current offset into the slot and advances the offset,
+# which is what torch's own replay does for a captured graph. Restored and
+# captured graphs of one process therefore draw the same sequence as the SAVE
+# process when the generator starts from the same seed and offset.
+# Only the device's default CUDA generator is recorded.
+
+_RNG_SLOTS: dict[int, torch.Tensor] = {}
+_RNG_POOLS: dict[int, Any] = {}
+
+
+def _graph_rng_records(device: int) -> list[dict]:
+    """Generator records of the graph whose capture just ended on ``device``."""
+    try:
+        from . import _torchrng
+    except ImportError:  # built by foundry_b200._build; absent only in a partial build
+        return []
+    st = _torchrng.default_generator_graph_state(device)
+    if st["offset_intragraph"] == 0 or not st["seed_ptr"]:
+        return []
+    return [{"id": 0, "seed": st["seed"], "wholegraph_increment": st["offset_intragraph"],
+             "seed_ptr": st["seed_ptr"], "offset_ptr": st["offset_ptr"]}]
+
+
+def rng_slot(device: int | None = None) -> int:
+    """Device address of this process's generator slot (two int64 words) on
+    ``device``. Allocated once, from a private pool and outside any active
+    allocation region, so it moves neither the region cursor nor the blocks
+    of torch's default pool (a LOAD must reproduce SAVE's addresses)."""
+    dev = torch.cuda.current_device() if device is None else device
+    t = _RNG_SLOTS.get(dev)
+    if t is None:
+        c = core()
+        paused = c.region_active()
+        if paused:
+            c.stop_allocation_region()
+        try:
+            pool = torch.cuda.MemPool()
+            with torch.cuda.use_mem_pool(pool, device=dev):
+                t = torch.zeros(2, dtype=torch.int64, device=dev)
+        finally:
+            if paused:
+                c.resume_allocation_region()
+        _RNG_POOLS[dev] = pool
+        _RNG_SLOTS[dev] = t
+    return t.data_ptr()
+
+
+def _as_i64(v: int) -> int:
+    return v - (1 << 64) if v >= (1 << 63) else v
+
+
+def _rng_prologue(device: int, increments: list[int]) -> None:
+    """Seed/offset words for one replay of a restored graph, then advance."""
+    gen = torch.cuda.default_generators[device]
+    slot = _RNG_SLOTS[device]
+    for inc in increments:
+        off = gen.get_offset()
+        slot[0].fill_(_as_i64(gen.initial_seed()))
+        slot[1].fill_(_as_i64(off))
+        gen.set_offset(off + inc)
+
+
 # ---- CUDAGraph ---------------------------------------------------------------------------
 
 class CUDAGraph:
@@ -119,6 +189,8 @@ class CUDAGraph:
         self._analysis_error: str | None = None
         self._restored = None
         self._events_json = ""
+        self._rng_device = 0
+        self._rng_increments: list[int] = []
 
     # -- capture ----------------------------------------------------------------------------
     def capture_begin(self, pool=None, capture_error_mode: str = "global") -> None:
@@ -129,6 +201,7 @@ class CUDAGraph:
     def capture_end(self) -> None:
         assert self._torch is not None, "capture_begin was not called"
         self._torch.capture_end()
+        rng = _graph_rng_records(torch.cuda.current_device())
         c = core()
         c.end_hook_record()
         self._events_json = c.hook_events_json() if c.region_active() else ""
@@ -138,6 +211,8 @@ class CUDAGraph:
                 ev = json.loads(self._events_json)
                 if ev.get("events"):
                     self._desc.allocator_events_json = self._events_json
+            if rng:
+                self._desc.generators = rng
         except RuntimeError as e:  # persisted later only if save() is called
             self._desc = None
             self._analysis_error = str(e)
@@ -154,6 +229,8 @@ class CUDAGraph:
 
     def replay(self) -> None:
         if self._restored is not None:
+            if self._rng_increments:
+                _rng_prologue(self._rng_device, self._rng_increments)
             self._restored.launch(_stream_handle())
         elif self._torch is not None:
             self._torch.replay()
@@ -210,12 +287,14 @@ class CUDAGraph:
     def _from_restored(cls, restored) -> tuple["CUDAGraph", OutputTensors | None]:
         g = cls()
         g._restored = restored
+        g._rng_device = torch.cuda.current_device()
+        g._rng_increments = [r["wholegraph_increment"] for r in restored.desc.generators if r["seed_ptr"]]
         return g, _decode_outputs(restored.output_tensors_json)
 
     @staticmethod
     def load(json_path: str, pool=None) -> "CUDAGraph | tuple[CUDAGraph, OutputTensors]":
         torch.cuda.synchronize()
-        restored = core().load_graph(json_path)
+        restored = core().load_graph(json_path, rng_slot())
         g, outputs = CUDAGraph._from_restored(restored)
         return g if outputs is None else (g, outputs)
 
@@ -224,7 +303,7 @@ class CUDAGraph:
         """Reads every graph (in parallel) and starts building templates on a
         background thread; returns immediately with a pending handle."""
         torch.cuda.synchronize()
-        return core().start_graph_builds(list(json_paths), num_threads)
+        return core().start_graph_builds(list(json_paths), num_threads, rng_slot())
 
     @staticmethod
     def finish_one_graph_load(pending, index: int) -> tuple["CUDAGraph", OutputTensors | None]:

@@ -27,7 +27,11 @@ from . import _rt
 BM, BK = 128, 64
 EPI_TRANSPOSE, EPI_RESIDUAL, EPI_A_STREAM, EPI_B_STREAM = 1, 2, 4, 8
 EPI_MCAST = 1 << 16
+EPI_TMA_OUT = 1 << 17
+EPI_COLS = 32  # tokens per epilogue store chunk of the one-SM kernel
 _BF16 = 9  # CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+_F32 = 7  # CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+_NO_MAP = bytes(128)  # placeholder for tensor-map parameters a launch does not use
 _SWIZZLE_128B = 3
 _BNS = (16, 32, 64, 128, 256)
 # Cost model constants (measured on B200): per-CTA shared-memory fill rate of
@@ -40,10 +44,15 @@ _HBM_BPS = 6.0e12
 MAX_SPLITS = 8
 
 
+STG_BYTES = 64 * BM * 4  # fp32 staging of the transposed epilogue (csrc/kernels/gemm_bf16.cu)
+
+
 def smem_bytes(bn: int, mt: int = 1) -> int:
+    """Dynamic shared memory of the one-SM kernels (and the stream-K ones,
+    which use the same ring): ring of 192 KB at most, staging, barriers."""
     stage = mt * BM * BK * 2 + bn * BK * 2
-    stages = min(8, (200 * 1024) // stage)
-    return stages * stage + 1024 + 256
+    stages = min(8, (192 * 1024) // stage)
+    return stages * stage + STG_BYTES + 1024 + 256
 
 
 def smem_bytes_pair(bn: int) -> int:
@@ -122,6 +131,45 @@ def tmap(t: torch.Tensor, box_rows: int) -> bytes:
     return m
 
 
+_omaps: dict[tuple, bytes] = {}
+
+
+def _cached_map(key: tuple, make) -> bytes:
+    m = _omaps.get(key)
+    if m is None:
+        m = make()
+        if len(_omaps) > 8192:
+            _omaps.clear()
+        _omaps[key] = m
+    return m
+
+
+def out_maps(out_ptr: int, res_ptr: int, n_out: int, t_tok: int, ldo: int, bn: int) -> tuple[bytes, bytes] | None:
+    """TMA-store maps of a transposed bf16 output [t_tok, ldo] (and of its
+    residual), 128 features x min(bn, 32) tokens per box; None when the rows
+    are not 16-byte aligned (the kernel then stores element by element)."""
+    if (ldo * 2) % 16 or out_ptr % 16 or (res_ptr and res_ptr % 16):
+        return None
+    rows = min(bn, EPI_COLS)
+
+    def make(ptr):
+        return lambda: core().make_tmap_2d(ptr, _BF16, n_out, t_tok, ldo * 2, BM, rows, 0)
+
+    o = _cached_map(("o", out_ptr, n_out, t_tok, ldo, rows), make(out_ptr))
+    r = _cached_map(("o", res_ptr, n_out, t_tok, ldo, rows), make(res_ptr)) if res_ptr else _NO_MAP
+    return o, r
+
+
+def partial_map(buf_ptr: int, n_out: int, t_tok: int, splits: int, bn: int) -> bytes | None:
+    """TMA-store map of fp32 split-K slices [splits][t_tok][n_out]."""
+    if (n_out * 4) % 16 or buf_ptr % 16:
+        return None
+    rows = min(bn, EPI_COLS)
+    return _cached_map(("p", buf_ptr, n_out, t_tok, splits, rows),
+                       lambda: core().make_tmap_3d(buf_ptr, _F32, n_out, t_tok, splits, n_out * 4,
+                                                   t_tok * n_out * 4, BM, rows, 1, 0))
+
+
 @dataclass
 class Plan:
     bn: int
@@ -173,7 +221,7 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
         for bn in cands:
             tn = math.ceil(ng / bn)
             stage = mt * BM * BK * 2 + bn * BK * 2
-            stages = min(8, (200 * 1024) // stage)
+            stages = min(8, (192 * 1024) // stage)
             mma = mt * 2 * BM * bn * BK / _SM_MMA_FLOPS
             t_kb = max((_TMA_LATENCY + mma) / stages, stage / _CTA_FILL_BPS_MAX, mma)
             for s in range(1, (MAX_SPLITS if allow_split else 1) + 1):
@@ -244,7 +292,7 @@ def linear_multicast(x: torch.Tensor, w: torch.Tensor, target: int, plan_overrid
         a, b, mg, ng, mode = w, x, n_out, t_tok, EPI_TRANSPOSE | EPI_MCAST
     else:
         a, b, mg, ng, mode = x, w, t_tok, n_out, EPI_MCAST
-    args = [tmap(a, BM), tmap(b, p.bn), target, 0, mg, ng, k, n_out, mode, 1, 0, 0]
+    args = [tmap(a, BM), tmap(b, p.bn), _NO_MAP, _NO_MAP, target, 0, mg, ng, k, n_out, mode, 1, 0, 0]
     _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, p.mt))
 
 
@@ -278,7 +326,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         need = p.splits * t_tok * n_out
         if need > partials.numel:
             raise RuntimeError(f"split-K slice buffer too small: need {need} floats, have {partials.numel}")
-        args = [tmap(a, BM), tmap(b, p.b_box), 0, 0, mg, ng, k, n_out, mode, p.splits,
+        maps = []
+        if not p.pair:
+            pm = partial_map(partials.buf.data_ptr(), n_out, t_tok, p.splits, p.bn) if p.swap else None
+            if pm is not None:
+                mode |= EPI_TMA_OUT
+            maps = [pm or _NO_MAP, _NO_MAP]
+        args = [tmap(a, BM), tmap(b, p.b_box), *maps, 0, 0, mg, ng, k, n_out, mode, p.splits,
                 partials.buf.data_ptr(), t_tok * n_out]
         _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)
         return Partial(partials.buf, p.splits, t_tok, n_out)
@@ -289,11 +343,24 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         assert residual.shape == out.shape and residual.stride() == out.stride()
         mode |= EPI_RESIDUAL
     if p.streamk:
+        # A tile may be split between two neighbouring CTAs only: stream-K
+        # needs at least one whole tile per CTA.
+        if math.ceil(mg / BM) * math.ceil(ng / p.bn) < p.grid:
+            raise ValueError(f"stream-K plan has fewer tiles than its {p.grid} CTAs")
         args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
                 mg, ng, k, out.stride(0), mode, streamk.ws.data_ptr(), streamk.flags.data_ptr()]
         _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, 1))
         return out
-    args = [tmap(a, BM), tmap(b, p.b_box), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
+    maps = []
+    if not p.pair:
+        om = None
+        if p.swap:
+            om = out_maps(out.data_ptr(), residual.data_ptr() if residual is not None else 0, n_out, t_tok,
+                          out.stride(0), p.bn)
+        if om is not None:
+            mode |= EPI_TMA_OUT
+        maps = list(om) if om is not None else [_NO_MAP, _NO_MAP]
+    args = [tmap(a, BM), tmap(b, p.b_box), *maps, out.data_ptr(), residual.data_ptr() if residual is not None else 0,
             mg, ng, k, out.stride(0), mode, 1, 0, 0]
     _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)
     return out

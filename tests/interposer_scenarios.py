@@ -250,8 +250,77 @@ def scenario_async_load(workdir):
     print(json.dumps({"ok": busy > 0, "start_s": started, "restore_s": total}))
 
 
+# ---- random numbers inside a persisted graph -------------------------------------------
+RNG_N = 1 << 16
+
+
+def _rng_prepare(torch, fb):
+    """Same allocations in SAVE and LOAD, before any capture."""
+    fb.set_allocation_region(BASE, SIZE)
+    x = torch.zeros(RNG_N, device="cuda")
+    for _ in range(2):  # load the RNG kernels outside capture
+        _rng_body(torch, x)
+    torch.cuda.synchronize()
+    return x
+
+
+def _rng_body(torch, x):
+    return x + torch.rand_like(x) + torch.nn.functional.dropout(torch.ones_like(x), p=0.5)
+
+
+def scenario_rng_save(workdir):
+    torch, fb = _setup()
+    x = _rng_prepare(torch, fb)
+    g = fb.CUDAGraph()
+    with fb.graph(g):
+        y = _rng_body(torch, x)
+    gens = g.desc.generators
+    assert len(gens) == 1 and gens[0]["wholegraph_increment"] > 0 and gens[0]["seed_ptr"], gens
+    archive = os.path.join(workdir, "archive")
+    os.makedirs(archive, exist_ok=True)
+    g.save(os.path.join(archive, "graph_0.json"), output_tensors=y)
+    fb.pack_fatbins_to_folder(archive)
+    fb.save_graph_manifest(archive)
+    torch.cuda.manual_seed(1234)
+    gen = torch.cuda.default_generators[0]
+    off0 = gen.get_offset()
+    outs = []
+    for i in range(3):
+        x.fill_(float(i))
+        g.replay()
+        outs.append(y.cpu().clone())
+    inc = gens[0]["wholegraph_increment"]
+    # the recorded increment is the one torch's replay applies
+    assert gen.get_offset() - off0 == 3 * inc, (gen.get_offset(), off0, inc)
+    assert not torch.equal(outs[0], outs[1] - 1), "replays drew the same random numbers"
+    torch.save(outs, os.path.join(workdir, "rng_out.pt"))
+    print(json.dumps({"ok": True, "increment": inc}))
+
+
+def scenario_rng_load(workdir):
+    torch, fb = _setup()
+    archive = os.path.join(workdir, "archive")
+    fb.set_skip_fatbin_processing(True)
+    fb.load_cuda_modules_and_libraries(archive)
+    x = _rng_prepare(torch, fb)
+    g, y = fb.CUDAGraph.load(os.path.join(archive, "graph_0.json"))
+    saved = torch.load(os.path.join(workdir, "rng_out.pt"))
+    torch.cuda.manual_seed(1234)
+    for i in range(3):
+        x.fill_(float(i))
+        g.replay()
+        assert torch.equal(y.cpu(), saved[i]), f"replay {i}: restored graph drew other random numbers"
+    # another seed gives another sequence
+    torch.cuda.manual_seed(99)
+    x.fill_(0.0)
+    g.replay()
+    assert not torch.equal(y.cpu(), saved[0])
+    print(json.dumps({"ok": True}))
+
+
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
     {"region": scenario_region, "prealloc": scenario_prealloc, "graph_save": scenario_graph_save,
      "graph_load": scenario_graph_load, "async_save": scenario_async_save,
-     "async_load": scenario_async_load}[name](workdir)
+     "async_load": scenario_async_load, "rng_save": scenario_rng_save,
+     "rng_load": scenario_rng_load}[name](workdir)

@@ -498,7 +498,55 @@ def scenario_faults(workdir: str) -> None:
     print("FAULTS OK")
 
 
+def scenario_rng(workdir: str) -> None:
+    """Generator records with seed/offset word addresses survive JSON and
+    .cugraph, and relocation rewrites exactly the kernel-parameter words that
+    hold those addresses (in the template and in a restore)."""
+    fb, c = _core()
+    archive = os.path.join(workdir, "archive")
+    with open(os.path.join(archive, "graph_1.json")) as f:
+        j = json.load(f)
+    # graph_1's first kernel node: its first parameter is a region pointer
+    k = next(n for n in j["nodes"] if n["type"] == "KernelNode")
+    seed_ptr = struct.unpack("<Q", bytes.fromhex(k["params"]["kernelParams"][0]["value_hex"]))[0]
+    offset_ptr = struct.unpack("<Q", bytes.fromhex(k["params"]["kernelParams"][1]["value_hex"]))[0]
+    assert seed_ptr != offset_ptr
+    hits = sum(1 for n in j["nodes"] if n["type"] == "KernelNode" for prm in n["params"]["kernelParams"]
+               if prm["size"] == 8 and struct.unpack("<Q", bytes.fromhex(prm["value_hex"]))[0] in (seed_ptr, offset_ptr))
+    d = c.graph_from_json_text(json.dumps(j))
+    d.generators = [{"id": 0, "seed": 42, "wholegraph_increment": 8, "seed_ptr": seed_ptr, "offset_ptr": offset_ptr}]
+    out = os.path.join(workdir, "rng", "graph_0.json")
+    os.makedirs(os.path.dirname(out), exist_ok=True)
+    d.save(out)
+    for rd in (c.read_binary_graph(out.replace(".json", ".cugraph")),
+               c.graph_from_json_text(open(out).read())):
+        assert rd.generators == [{"id": 0, "seed": 42, "wholegraph_increment": 8, "seed_ptr": seed_ptr,
+                                  "offset_ptr": offset_ptr}], rd.generators
+    slot = 0x7F0000001000
+    rd = c.read_binary_graph(out.replace(".json", ".cugraph"))
+    n = rd.relocate_generator_words(slot)
+    assert n == hits and n >= 2, (n, hits)
+    assert rd.generators[0]["seed_ptr"] == slot and rd.generators[0]["offset_ptr"] == slot + 8
+    rel = json.loads(rd.to_json())
+    for a, b in zip(j["nodes"], rel["nodes"]):
+        if a["type"] != "KernelNode":
+            continue
+        for pa, pb in zip(a["params"]["kernelParams"], b["params"]["kernelParams"]):
+            va, vb = bytes.fromhex(pa["value_hex"]), bytes.fromhex(pb["value_hex"])
+            if pa["size"] == 8 and struct.unpack("<Q", va)[0] == seed_ptr:
+                assert struct.unpack("<Q", vb)[0] == slot
+            elif pa["size"] == 8 and struct.unpack("<Q", va)[0] == offset_ptr:
+                assert struct.unpack("<Q", vb)[0] == slot + 8
+            else:
+                assert va == vb
+    # a graph without generator addresses keeps the 24-byte v1 records
+    d.generators = [{"id": 0, "seed": 1, "wholegraph_increment": 4}]
+    d.save(out)
+    assert c.read_binary_graph(out.replace(".json", ".cugraph")).generators[0]["seed_ptr"] == 0
+    print("RNG OK", n)
+
+
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
     {"save": scenario_save, "load": scenario_load, "numeric": scenario_numeric, "faults": scenario_faults,
-     "cluster": scenario_cluster, "mixed": scenario_mixed}[name](workdir)
+     "cluster": scenario_cluster, "mixed": scenario_mixed, "rng": scenario_rng}[name](workdir)

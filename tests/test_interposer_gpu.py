@@ -45,3 +45,13 @@ def test_async_restore_of_graphs_sharing_topologies(tmp_path):
     info = _run("async_save", str(tmp_path))
     assert info["graphs"] == 12 and info["groups"] < 12, info
     assert _run("async_load", str(tmp_path))["ok"]
+
+
+def test_random_numbers_in_a_restored_graph(tmp_path):
+    """torch.rand and dropout inside a captured graph: the restored graph,
+    replayed from the same seed, draws the same numbers as the SAVE process's
+    replays (the generator's seed/offset words are relocated and rewritten
+    before each replay)."""
+    info = _run("rng_save", str(tmp_path))
+    assert info["increment"] > 0
+    assert _run("rng_load", str(tmp_path))["ok"]

@@ -67,6 +67,10 @@ def test_numeric_save_load_bit_exact(saved):
     assert a[1] == pytest.approx(1 + 2 * 5.25 * 0.5 * 97)
 
 
+def test_generator_records_and_relocation(saved):
+    assert "RNG OK" in _run("rng", saved)
+
+
 def test_fault_injection(saved):
     assert "FAULTS OK" in _run("faults", saved)
 
