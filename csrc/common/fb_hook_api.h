@@ -76,6 +76,12 @@ fb_status fb_events_replay_json(const char* json, size_t len);
 // kernels enumerated. Loading the same bytes twice returns the same library.
 fb_status fb_registry_load_image(const void* data, size_t size, const char* tag,
                                  CUlibrary* out_lib, uint64_t* out_hash);
+// Adopts a module that another component loaded from bytes it compiled in
+// this process (a JIT compiler such as Triton): data/size are exactly the
+// image handed to cuModuleLoadData. The image is hashed and kept like an own
+// image (packed by bytes, reloaded with cuLibraryLoadData on LOAD) and the
+// module's functions resolve to it. The bytes are stored, never parsed.
+fb_status fb_registry_adopt_module(CUmodule mod, const void* data, size_t size, uint64_t* out_hash);
 // Look up the library handle of an image by hash (after load or archive load).
 fb_status fb_registry_library(uint64_t hash, CUlibrary* out_lib);
 // Resolve an entry point of a registered image to a function of the current context.
@@ -88,6 +94,12 @@ fb_status fb_registry_mark_used(uint64_t hash);
 fb_status fb_registry_pack(const char* folder);
 fb_status fb_registry_load_archive(const char* folder);
 void fb_registry_set_skip_processing(int enabled);
+// Initialises, with the process's NVSHMEM host library, every image reloaded
+// from an archive that needs NVSHMEM (flag bit 1 of the pack, or one of
+// NVSHMEM's device symbols found by driver lookup). Returns the number of
+// images initialised (0 when none is pending), or -1 with a message in err
+// (nothing is retried automatically; pending images stay queued).
+int fb_registry_init_nvshmem(char* err, size_t err_cap);
 void fb_registry_set_pack_on_exit(const char* folder_or_null);
 size_t fb_registry_count(void);
 

@@ -368,6 +368,26 @@ PYBIND11_MODULE(_C, m) {
   });
   m.def("registry_count", []() { return fb_registry_count(); });
   m.def("mark_binary_used", [](uint64_t h) { check(fb_registry_mark_used(h)); });
+  m.def("init_nvshmem_modules", []() {
+    char err[512] = {0};
+    const int n = fb_registry_init_nvshmem(err, sizeof(err));
+    if (n < 0) throw std::runtime_error(err);
+    return n;
+  });
+  m.def("adopt_jit_function", [](uintptr_t fn, py::bytes image) {
+    CUmodule mod = nullptr;
+    check_drv(fb_driver()->cuFuncGetModule(&mod, reinterpret_cast<CUfunction>(fn)), "cuFuncGetModule");
+    std::string b = image;
+    uint64_t h = 0;
+    check(fb_registry_adopt_module(mod, b.data(), b.size(), &h));
+    return h;
+  }, py::arg("function"), py::arg("image"));
+  m.def("adopt_jit_module", [](uintptr_t mod, py::bytes image) {
+    std::string b = image;
+    uint64_t h = 0;
+    check(fb_registry_adopt_module(reinterpret_cast<CUmodule>(mod), b.data(), b.size(), &h));
+    return h;
+  }, py::arg("module"), py::arg("image"));
   m.def("query_function_handle", [](uint64_t hash, const std::string& name) {
     CUfunction f = nullptr;
     check(fb_registry_function(hash, name.c_str(), &f, nullptr));

@@ -1,6 +1,10 @@
 // Internal declarations shared by the translation units of libfoundry_hook.
 #pragma once
 
+#include <cstdint>
+#include <utility>
+#include <vector>
+
 #include <cuda.h>
 
 #include <cstdint>
@@ -21,6 +25,8 @@ bool debug_enabled();
 // Returns true and fills *out if the region for the current device served the
 // request; false means "not handled, call the real driver".
 bool region_try_alloc(size_t size, CUdeviceptr* out, CUresult* result);
+// True when the current device has an enabled (not stopped) region.
+bool region_active_for_current();
 bool region_try_free(CUdeviceptr ptr, CUresult* result);
 bool region_try_reserve(CUdeviceptr* ptr, size_t size, size_t alignment, CUdeviceptr addr,
                         CUresult* result);
@@ -30,8 +36,15 @@ bool region_lookup_chunk(CUdeviceptr ptr, CUdeviceptr* base, size_t* size,
                          CUmemGenericAllocationHandle* handle);
 
 // Registry hooks called after a successful real load by a foreign caller.
-void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag);
-void registry_on_module_loaded(CUmodule mod, const void* code, const char* tag);
+// Scalar load options of a foreign image (JIT options and library options
+// whose value is passed by value); pointer and output options are not kept.
+struct LoadOptions {
+  std::vector<std::pair<int, uint64_t>> jit, lib;
+};
+LoadOptions capture_load_options(unsigned int num_jit, const CUjit_option* jit, void* const* jit_values,
+                                 unsigned int num_lib, const CUlibraryOption* lib, void* const* lib_values);
+void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag, const LoadOptions& opts);
+void registry_on_module_loaded(CUmodule mod, const void* code, const char* tag, const LoadOptions& opts);
 void registry_on_library_file_loaded(CUlibrary lib, const char* path);
 void registry_on_module_file_loaded(CUmodule mod, const char* path);
 bool registry_in_own_load();  // true while fb_registry_load_image runs on this thread

@@ -24,6 +24,8 @@ extern "C" {
 // Forward declarations of our overrides (defined below / in ipc.cpp).
 CUresult cuMemAlloc_v2(CUdeviceptr* dptr, size_t bytesize);
 CUresult cuMemFree_v2(CUdeviceptr dptr);
+CUresult cuMemAllocPitch_v2(CUdeviceptr* dptr, size_t* pPitch, size_t WidthInBytes, size_t Height,
+                            unsigned int ElementSizeBytes);
 CUresult cuMemAddressReserve(CUdeviceptr* ptr, size_t size, size_t alignment, CUdeviceptr addr,
                              unsigned long long flags);
 CUresult cuMemAddressFree(CUdeviceptr ptr, size_t size);
@@ -56,6 +58,7 @@ const std::unordered_map<std::string, void*>& base_overrides() {
   static const std::unordered_map<std::string, void*> m = {
       {"cuMemAlloc", reinterpret_cast<void*>(&cuMemAlloc_v2)},
       {"cuMemFree", reinterpret_cast<void*>(&cuMemFree_v2)},
+      {"cuMemAllocPitch", reinterpret_cast<void*>(&cuMemAllocPitch_v2)},
       {"cuMemAddressReserve", reinterpret_cast<void*>(&cuMemAddressReserve)},
       {"cuMemAddressFree", reinterpret_cast<void*>(&cuMemAddressFree)},
       {"cuLibraryLoadData", reinterpret_cast<void*>(&cuLibraryLoadData)},
@@ -77,6 +80,7 @@ const std::unordered_map<std::string, void*>& symbol_overrides() {
   static const std::unordered_map<std::string, void*> m = {
       {"cuMemAlloc_v2", reinterpret_cast<void*>(&cuMemAlloc_v2)},
       {"cuMemFree_v2", reinterpret_cast<void*>(&cuMemFree_v2)},
+      {"cuMemAllocPitch_v2", reinterpret_cast<void*>(&cuMemAllocPitch_v2)},
       {"cuMemAddressReserve", reinterpret_cast<void*>(&cuMemAddressReserve)},
       {"cuMemAddressFree", reinterpret_cast<void*>(&cuMemAddressFree)},
       {"cuLibraryLoadData", reinterpret_cast<void*>(&cuLibraryLoadData)},
@@ -119,6 +123,34 @@ CUresult cuMemFree_v2(CUdeviceptr dptr) {
   return FB_CALL(cuMemFree, dptr);
 }
 
+// Pitched 2-D allocation inside the region. The pitch is chosen here, not by
+// a throw-away driver allocation: the row width rounded up to the device's
+// texture pitch alignment (at least 128 bytes), so a 2-D texture can be bound
+// to the rows and SAVE and LOAD get the same pitch and the same address.
+// Outside an active region the driver's own call runs.
+CUresult cuMemAllocPitch_v2(CUdeviceptr* dptr, size_t* pPitch, size_t WidthInBytes, size_t Height,
+                            unsigned int ElementSizeBytes) {
+  if (!dptr || !pPitch || WidthInBytes == 0 || Height == 0 ||
+      (ElementSizeBytes != 4 && ElementSizeBytes != 8 && ElementSizeBytes != 16))
+    return CUDA_ERROR_INVALID_VALUE;
+  if (region_active_for_current()) {
+    size_t align = 128;
+    CUdevice dev = 0;
+    int attr = 0;
+    if (FB_CALL(cuCtxGetDevice, &dev) == CUDA_SUCCESS &&
+        FB_CALL(cuDeviceGetAttribute, &attr, CU_DEVICE_ATTRIBUTE_TEXTURE_PITCH_ALIGNMENT, dev) == CUDA_SUCCESS &&
+        attr > static_cast<int>(align))
+      align = static_cast<size_t>(attr);
+    const size_t pitch = (WidthInBytes + align - 1) / align * align;
+    CUresult rc;
+    if (region_try_alloc(pitch * Height, dptr, &rc)) {
+      if (rc == CUDA_SUCCESS) *pPitch = pitch;
+      return rc;
+    }
+  }
+  return FB_CALL(cuMemAllocPitch, dptr, pPitch, WidthInBytes, Height, ElementSizeBytes);
+}
+
 CUresult cuMemAddressReserve(CUdeviceptr* ptr, size_t size, size_t alignment, CUdeviceptr addr,
                              unsigned long long flags) {
   CUresult rc;
@@ -139,7 +171,9 @@ CUresult cuLibraryLoadData(CUlibrary* library, const void* code, CUjit_option* j
   CUresult rc = FB_CALL(cuLibraryLoadData, library, code, jitOptions, jitOptionsValues,
                         numJitOptions, libraryOptions, libraryOptionValues, numLibraryOptions);
   if (rc == CUDA_SUCCESS && !registry_in_own_load())
-    registry_on_library_loaded(*library, code, "cuLibraryLoadData");
+    registry_on_library_loaded(*library, code, "cuLibraryLoadData",
+                               capture_load_options(numJitOptions, jitOptions, jitOptionsValues, numLibraryOptions,
+                                                    libraryOptions, libraryOptionValues));
   return rc;
 }
 
@@ -155,20 +189,22 @@ CUresult cuLibraryLoadFromFile(CUlibrary* library, const char* fileName, CUjit_o
 
 CUresult cuModuleLoadData(CUmodule* module, const void* image) {
   CUresult rc = FB_CALL(cuModuleLoadData, module, image);
-  if (rc == CUDA_SUCCESS) registry_on_module_loaded(*module, image, "cuModuleLoadData");
+  if (rc == CUDA_SUCCESS) registry_on_module_loaded(*module, image, "cuModuleLoadData", LoadOptions{});
   return rc;
 }
 
 CUresult cuModuleLoadDataEx(CUmodule* module, const void* image, unsigned int numOptions,
                             CUjit_option* options, void** optionValues) {
   CUresult rc = FB_CALL(cuModuleLoadDataEx, module, image, numOptions, options, optionValues);
-  if (rc == CUDA_SUCCESS) registry_on_module_loaded(*module, image, "cuModuleLoadDataEx");
+  if (rc == CUDA_SUCCESS)
+    registry_on_module_loaded(*module, image, "cuModuleLoadDataEx",
+                              capture_load_options(numOptions, options, optionValues, 0, nullptr, nullptr));
   return rc;
 }
 
 CUresult cuModuleLoadFatBinary(CUmodule* module, const void* fatCubin) {
   CUresult rc = FB_CALL(cuModuleLoadFatBinary, module, fatCubin);
-  if (rc == CUDA_SUCCESS) registry_on_module_loaded(*module, fatCubin, "cuModuleLoadFatBinary");
+  if (rc == CUDA_SUCCESS) registry_on_module_loaded(*module, fatCubin, "cuModuleLoadFatBinary", LoadOptions{});
   return rc;
 }
 
@@ -188,7 +224,7 @@ CUresult cuGetProcAddress_v2(const char* symbol, void** pfn, int cudaVersion, cu
     // Only the versions we implement: modern cuMemAlloc/cuMemFree (_v2) and
     // cuIpcOpenMemHandle (_v2); older callers keep the driver's function.
     std::string s(symbol);
-    if ((s == "cuMemAlloc" || s == "cuMemFree") && cudaVersion < 3020) return rc;
+    if ((s == "cuMemAlloc" || s == "cuMemFree" || s == "cuMemAllocPitch") && cudaVersion < 3020) return rc;
     if (s == "cuIpcOpenMemHandle" && cudaVersion < 11000) return rc;
     if (s == "cuGetProcAddress" && cudaVersion < 12000)
       *pfn = reinterpret_cast<void*>(&cuGetProcAddress);

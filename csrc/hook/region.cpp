@@ -193,6 +193,11 @@ CUresult region_free_locked(Region& r, uint64_t ptr, bool* handled) {
 
 bool g_preloaded = false;
 
+bool region_active_for_current() {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return region_for_current(true) != nullptr;
+}
+
 bool region_try_alloc(size_t size, CUdeviceptr* out, CUresult* result) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   Region* r = region_for_current(true);

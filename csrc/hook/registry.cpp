@@ -50,11 +50,13 @@ struct Image {
   bool own = false;
   bool used = false;
   bool byname = false;          // foreign kernel found by entry name among loaded images
+  bool nvshmem = false;         // device code reads NVSHMEM's device state (needs module init)
   std::vector<uint8_t> bytes;   // own images only
   std::string src_file;         // foreign: shared object path
   uint64_t src_offset = 0;      // foreign: image pointer - object load base
   CUlibrary lib = nullptr;
   CUmodule mod = nullptr;
+  LoadOptions options;          // foreign: scalar JIT / library options of the original load
   std::vector<std::string> names;
   std::unordered_map<std::string, CUkernel> kernels;
   std::unordered_map<std::string, CUfunction> functions;  // module-loaded images
@@ -65,8 +67,26 @@ struct FnKey {
   std::string name;
 };
 
+// binary_flags bits of the pack's text blocks (same meanings as the
+// reference's pack, csrc/hook.cpp:157-162): bit 0 would mark an image that
+// still needs a device link (never written here), bit 1 an image that needs
+// NVSHMEM module initialisation.
+constexpr unsigned kFlagNeedsNvshmem = 1u << 1;
+
+// Device symbols of NVSHMEM's device-side runtime: an image that defines or
+// references one needs nvshmemx_cumodule_init / nvshmemx_culibrary_init
+// before its kernels run (the probe set of reference csrc/hook.cpp:993-1012).
+const char* const kNvshmemSymbols[] = {
+    "nvshmemi_device_state_d", "nvshmemi_team_pool_d", "nvshmemi_team_same_mype_node_pool_d",
+    "nvshmemi_mype_d",         "nvshmemi_npes_d",      "nvshmemi_node_mype_d",
+    "nvshmemi_node_npes_d",    "nvshmemi_heap_base_d",
+};
+
 std::recursive_mutex g_mu;
 std::map<uint64_t, std::unique_ptr<Image>> g_images;
+// LOAD: reloaded images that need NVSHMEM initialisation, flushed by
+// fb_registry_init_nvshmem once the NVSHMEM runtime is up.
+std::vector<uint64_t> g_nvshmem_pending;
 std::unordered_map<CUlibrary, uint64_t> g_lib_to_hash;
 std::unordered_map<CUmodule, uint64_t> g_mod_to_hash;
 std::unordered_map<CUfunction, FnKey> g_fn_to_key;
@@ -158,6 +178,21 @@ void enumerate_module(Image& img) {
   g_mod_to_hash[img.mod] = img.hash;
 }
 
+// Driver-API probe (no byte of the image is read): does the image carry one
+// of NVSHMEM's device symbols?
+bool probe_nvshmem(const Image& img) {
+  const FbDriver* d = fb_driver();
+  for (const char* sym : kNvshmemSymbols) {
+    CUdeviceptr p = 0;
+    size_t sz = 0;
+    if (img.lib && d->cuLibraryGetGlobal && d->cuLibraryGetGlobal(&p, &sz, img.lib, sym) == CUDA_SUCCESS)
+      return true;
+    if (!img.lib && img.mod && d->cuModuleGetGlobal && d->cuModuleGetGlobal(&p, &sz, img.mod, sym) == CUDA_SUCCESS)
+      return true;
+  }
+  return false;
+}
+
 // Identify a foreign image pointer by the loaded object that contains it.
 bool identify_foreign(const void* code, std::string* file, uint64_t* offset) {
   Dl_info info;
@@ -212,31 +247,85 @@ void pack_at_exit() {
   if (!g_pack_on_exit.empty()) fb_registry_pack(g_pack_on_exit.c_str());
 }
 
+bool jit_option_is_scalar(int o) {
+  switch (o) {
+    case CU_JIT_MAX_REGISTERS:
+    case CU_JIT_THREADS_PER_BLOCK:
+    case CU_JIT_OPTIMIZATION_LEVEL:
+    case CU_JIT_TARGET_FROM_CUCONTEXT:
+    case CU_JIT_TARGET:
+    case CU_JIT_FALLBACK_STRATEGY:
+    case CU_JIT_GENERATE_DEBUG_INFO:
+    case CU_JIT_LOG_VERBOSE:
+    case CU_JIT_GENERATE_LINE_INFO:
+    case CU_JIT_CACHE_MODE:
+    case CU_JIT_POSITION_INDEPENDENT_CODE:
+    case CU_JIT_MIN_CTA_PER_SM:
+    case CU_JIT_MAX_THREADS_PER_BLOCK:
+    case CU_JIT_OVERRIDE_DIRECTIVE_VALUES:
+      return true;
+    default:
+      return false;  // log buffers, wall time, symbol tables: pointers or outputs
+  }
+}
+
+void append_options(std::ostream& txt, const LoadOptions& o) {
+  for (const auto& kv : o.jit) txt << ",jit" << kv.first << "=" << kv.second;
+  for (const auto& kv : o.lib) txt << ",libopt" << kv.first << "=" << kv.second;
+}
+
+LoadOptions options_from(const std::map<std::string, std::string>& opts) {
+  LoadOptions o;
+  for (const auto& kv : opts) {
+    if (kv.first.rfind("jit", 0) == 0 && kv.first.size() > 3 && isdigit(static_cast<unsigned char>(kv.first[3])))
+      o.jit.emplace_back(atoi(kv.first.c_str() + 3), strtoull(kv.second.c_str(), nullptr, 10));
+    else if (kv.first.rfind("libopt", 0) == 0 && kv.first.size() > 6)
+      o.lib.emplace_back(atoi(kv.first.c_str() + 6), strtoull(kv.second.c_str(), nullptr, 10));
+  }
+  return o;
+}
+
 }  // namespace
+
+LoadOptions capture_load_options(unsigned int num_jit, const CUjit_option* jit, void* const* jit_values,
+                                 unsigned int num_lib, const CUlibraryOption* lib, void* const* lib_values) {
+  LoadOptions o;
+  for (unsigned i = 0; jit && jit_values && i < num_jit; ++i)
+    if (jit_option_is_scalar(jit[i]))
+      o.jit.emplace_back(static_cast<int>(jit[i]), static_cast<uint64_t>(reinterpret_cast<uintptr_t>(jit_values[i])));
+  for (unsigned i = 0; lib && lib_values && i < num_lib; ++i)
+    if (lib[i] == CU_LIBRARY_BINARY_IS_PRESERVED)
+      o.lib.emplace_back(static_cast<int>(lib[i]), static_cast<uint64_t>(reinterpret_cast<uintptr_t>(lib_values[i])));
+  return o;
+}
 
 bool registry_in_own_load() { return t_own_load_depth > 0; }
 
-void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag) {
+void registry_on_library_loaded(CUlibrary lib, const void* code, const char* tag, const LoadOptions& opts) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (t_own_load_depth > 0) return;
   g_foreign.push_back(ForeignHandle{lib, nullptr});
   if (g_skip_processing) return;
   Image* img = register_foreign(code, tag);
   if (!img) return;
+  img->options = opts;
   img->lib = lib;
   g_lib_to_hash[lib] = img->hash;
   enumerate_library(*img);
+  img->nvshmem = probe_nvshmem(*img);
 }
 
-void registry_on_module_loaded(CUmodule mod, const void* code, const char* tag) {
+void registry_on_module_loaded(CUmodule mod, const void* code, const char* tag, const LoadOptions& opts) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (t_own_load_depth > 0) return;
   g_foreign.push_back(ForeignHandle{nullptr, mod});
   if (g_skip_processing) return;
   Image* img = register_foreign(code, tag);
   if (!img) return;
+  img->options = opts;
   img->mod = mod;
   enumerate_module(*img);
+  img->nvshmem = probe_nvshmem(*img);
 }
 
 void registry_on_library_file_loaded(CUlibrary lib, const char* path) {
@@ -254,6 +343,7 @@ void registry_on_library_file_loaded(CUlibrary lib, const char* path) {
   slot->lib = lib;
   g_lib_to_hash[lib] = h;
   enumerate_library(*slot);
+  slot->nvshmem = probe_nvshmem(*slot);
 }
 
 void registry_on_module_file_loaded(CUmodule mod, const char* path) {
@@ -270,6 +360,7 @@ void registry_on_module_file_loaded(CUmodule mod, const char* path) {
   slot->loader = "cuModuleLoad";
   slot->mod = mod;
   enumerate_module(*slot);
+  slot->nvshmem = probe_nvshmem(*slot);
 }
 
 }  // namespace fbh
@@ -311,7 +402,39 @@ fb_status fb_registry_load_image(const void* data, size_t size, const char* tag,
   if (rc != CUDA_SUCCESS) return drv_error(rc, "cuLibraryLoadData(own image)");
   g_lib_to_hash[img.lib] = h;
   enumerate_library(img);
+  img.nvshmem = probe_nvshmem(img);
   if (out_lib) *out_lib = img.lib;
+  if (out_hash) *out_hash = h;
+  return FB_OK;
+}
+
+fb_status fb_registry_adopt_module(CUmodule mod, const void* data, size_t size, uint64_t* out_hash) {
+  if (!mod || !data || size == 0) {
+    fb_set_error(FB_ERR_INVALID, "adopt_module: null module or empty image");
+    return FB_ERR_INVALID;
+  }
+  const uint64_t h = fb::crc64(data, size);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto& slot = g_images[h];
+  if (!slot) {
+    slot.reset(new Image());
+    slot->hash = h;
+    slot->own = true;
+    slot->loader = "cuLibraryLoadData";
+    slot->bytes.assign(static_cast<const uint8_t*>(data), static_cast<const uint8_t*>(data) + size);
+  }
+  Image& img = *slot;
+  if (!img.own) {
+    fb_set_error(FB_ERR_INVALID, "adopt_module: image %016llx is registered as foreign", (unsigned long long)h);
+    return FB_ERR_INVALID;
+  }
+  // The same bytes may be loaded as several modules (e.g. one per context);
+  // every module's functions map to the one image.
+  CUmodule keep = img.mod;
+  img.mod = mod;
+  enumerate_module(img);
+  img.nvshmem = img.nvshmem || probe_nvshmem(img);
+  if (keep && keep != mod) img.mod = keep;
   if (out_hash) *out_hash = h;
   return FB_OK;
 }
@@ -477,9 +600,10 @@ fb_status fb_registry_pack(const char* folder) {
   for (auto& kv : g_images) {
     const Image& im = *kv.second;
     if (!im.used) continue;
+    const unsigned flags = im.nvshmem ? kFlagNeedsNvshmem : 0u;
     txt << hex16(im.hash) << "\n" << im.loader;
     if (im.byname) {
-      txt << ",binary_flags=2\n" << im.names.size() << "\n";
+      txt << ",binary_flags=" << flags << "\n" << im.names.size() << "\n";
       for (const auto& n : im.names) txt << n << "\n";
       txt << "---\n";
       continue;
@@ -490,10 +614,11 @@ fb_status fb_registry_pack(const char* folder) {
       img.write(reinterpret_cast<const char*>(&n), 8);
       img.write(reinterpret_cast<const char*>(im.bytes.data()), static_cast<std::streamsize>(n));
     } else {
-      // Foreign image: identified, not copied.
+      // Foreign image: identified, not copied; its load options replayed on LOAD.
+      append_options(txt, im.options);
       txt << ",source=" << im.src_file << ",source_offset=" << im.src_offset;
     }
-    txt << ",binary_flags=" << (im.own ? 0 : 1) << "\n" << im.names.size() << "\n";
+    txt << ",binary_flags=" << flags << "\n" << im.names.size() << "\n";
     for (const auto& n : im.names) txt << n << "\n";
     txt << "---\n";
   }
@@ -612,10 +737,27 @@ fb_status fb_registry_load_archive(const char* folder) {
           return FB_ERR_NOT_FOUND;
         }
         const void* code = base + im.src_offset;
-        if (loader.rfind("cuModule", 0) == 0)
+        im.options = options_from(opts);
+        std::vector<CUjit_option> jk;
+        std::vector<void*> jv;
+        for (const auto& kv : im.options.jit) {
+          jk.push_back(static_cast<CUjit_option>(kv.first));
+          jv.push_back(reinterpret_cast<void*>(static_cast<uintptr_t>(kv.second)));
+        }
+        std::vector<CUlibraryOption> lk2;
+        std::vector<void*> lv;
+        for (const auto& kv : im.options.lib) {
+          lk2.push_back(static_cast<CUlibraryOption>(kv.first));
+          lv.push_back(reinterpret_cast<void*>(static_cast<uintptr_t>(kv.second)));
+        }
+        const unsigned nj = static_cast<unsigned>(jk.size()), nl = static_cast<unsigned>(lk2.size());
+        if (loader == "cuModuleLoadDataEx")
+          rc = d->cuModuleLoadDataEx(&im.mod, code, nj, nj ? jk.data() : nullptr, nj ? jv.data() : nullptr);
+        else if (loader.rfind("cuModule", 0) == 0)
           rc = d->cuModuleLoadData(&im.mod, code);
         else
-          rc = d->cuLibraryLoadData(&im.lib, code, nullptr, nullptr, 0, nullptr, nullptr, 0);
+          rc = d->cuLibraryLoadData(&im.lib, code, nj ? jk.data() : nullptr, nj ? jv.data() : nullptr, nj,
+                                    nl ? lk2.data() : nullptr, nl ? lv.data() : nullptr, nl);
       }
     } else {
       auto bit = blobs.find(h);
@@ -642,8 +784,51 @@ fb_status fb_registry_load_archive(const char* folder) {
                    (unsigned long long)h, im.names.size(), count);
       return FB_ERR_IO;
     }
+    const unsigned flags = static_cast<unsigned>(strtoul(opts["binary_flags"].c_str(), nullptr, 10));
+    im.nvshmem = (flags & kFlagNeedsNvshmem) != 0 || probe_nvshmem(im);
+    if (im.nvshmem) g_nvshmem_pending.push_back(h);
   }
   return FB_OK;
+}
+
+int fb_registry_init_nvshmem(char* err, size_t err_cap) {
+  using ModuleInit = int (*)(CUmodule);
+  using LibraryInit = int (*)(CUlibrary);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g_nvshmem_pending.empty()) return 0;
+  // The NVSHMEM host library is whatever the process loaded (preloaded, or
+  // linked by an extension such as DeepEP); it is looked up, never loaded here.
+  auto mod_init = reinterpret_cast<ModuleInit>(real_dlsym()(RTLD_DEFAULT, "nvshmemx_cumodule_init"));
+  auto lib_init = reinterpret_cast<LibraryInit>(real_dlsym()(RTLD_DEFAULT, "nvshmemx_culibrary_init"));
+  if (!mod_init && !lib_init) {
+    snprintf(err, err_cap, "%zu loaded image(s) need NVSHMEM, but no NVSHMEM host library is loaded",
+             g_nvshmem_pending.size());
+    return -1;
+  }
+  int done = 0;
+  std::vector<uint64_t> left;
+  for (uint64_t h : g_nvshmem_pending) {
+    auto it = g_images.find(h);
+    if (it == g_images.end()) continue;
+    const Image& im = *it->second;
+    int rc = -1;
+    if (im.lib && lib_init) {
+      rc = lib_init(im.lib);
+    } else if (mod_init) {
+      CUmodule m = im.mod;
+      if (!m && im.lib && fb_driver()->cuLibraryGetModule) fb_driver()->cuLibraryGetModule(&m, im.lib);
+      if (m) rc = mod_init(m);
+    }
+    if (rc != 0) {
+      left.push_back(h);
+      snprintf(err, err_cap, "NVSHMEM initialisation of image %016llx failed (%d)", (unsigned long long)h, rc);
+      continue;
+    }
+    ++done;
+  }
+  const bool failed = !left.empty();
+  g_nvshmem_pending.swap(left);
+  return failed ? -1 : done;
 }
 
 void fb_registry_set_skip_processing(int enabled) {

@@ -10,7 +10,7 @@
 //    memfd; cuMemMap maps it MAP_SHARED|MAP_FIXED; cuMemSetAccess mprotects.
 //    Addresses therefore behave exactly like VMM addresses (fixed, shareable).
 //  * a code image is a blob that starts with the header
-//        "FBMOCK\n" { "<entry>:<param sizes comma separated>\n" }* "\n"
+//        "FBMOCK\n" { "<entry>:<param sizes comma separated>\n" | "@<global>:<bytes>\n" }* "\n"
 //    followed by arbitrary payload bytes (tests append 1 MB of random data).
 //  * graphs are node lists with edges; launching a graph (or a kernel) runs
 //    the built-in host implementation of the entry point when it has one
@@ -62,6 +62,7 @@ std::map<uint64_t, size_t> g_plain_allocs;  // cuMemAlloc blocks
 struct MockFunc;
 struct MockLib {
   std::vector<std::unique_ptr<MockFunc>> funcs;
+  std::map<std::string, std::vector<uint8_t>> globals;  // "@name:size" lines: zeroed host storage
   int module_tag;  // address used as the CUmodule of this library
 };
 struct MockFunc {
@@ -72,6 +73,9 @@ struct MockFunc {
 };
 std::set<MockLib*> g_libs;
 std::set<MockFunc*> g_funcs;
+// Options of every image load, in order: "<loader> <key>=<value> ..." (tests
+// check that a LOAD replays the options of the original load).
+std::vector<std::string> g_load_log;
 
 enum NodeKind { KERNEL, MEMSET, MEMCPY, EMPTY, EV_RECORD, EV_WAIT };
 struct MockNode {
@@ -107,6 +111,11 @@ bool parse_image(const void* code, MockLib* lib) {
     std::string line(p, eol);
     p = eol + 1;
     auto colon = line.find(':');
+    if (!line.empty() && line[0] == '@') {
+      const size_t n = colon == std::string::npos ? 8 : strtoull(line.c_str() + colon + 1, nullptr, 10);
+      lib->globals[line.substr(1, colon == std::string::npos ? std::string::npos : colon - 1)].assign(n, 0);
+      continue;
+    }
     std::unique_ptr<MockFunc> f(new MockFunc());
     f->name = line.substr(0, colon);
     memset(f->attrs, 0, sizeof(f->attrs));
@@ -253,6 +262,7 @@ CUresult cuDeviceGetAttribute(int* v, CUdevice_attribute a, CUdevice) {
     case CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT: *v = 148; break;
     case CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MAJOR: *v = 10; break;
     case CU_DEVICE_ATTRIBUTE_COMPUTE_CAPABILITY_MINOR: *v = 0; break;
+    case CU_DEVICE_ATTRIBUTE_TEXTURE_PITCH_ALIGNMENT: *v = 32; break;
     default: *v = 0;
   }
   return CUDA_SUCCESS;
@@ -435,14 +445,41 @@ CUresult cuMulticastCreate(CUmemGenericAllocationHandle*, const CUmulticastObjec
 }
 
 // ---- code images ----------------------------------------------------------------
-CUresult cuLibraryLoadData(CUlibrary* lib, const void* code, CUjit_option*, void**, unsigned int,
-                           CUlibraryOption*, void**, unsigned int) {
+namespace {
+void log_load(const char* loader, unsigned nj, CUjit_option* jk, void** jv, unsigned nl, CUlibraryOption* lk,
+              void** lv) {
+  std::string e = loader;
+  for (unsigned i = 0; jk && jv && i < nj; ++i)
+    e += " jit" + std::to_string(static_cast<int>(jk[i])) + "=" +
+         std::to_string(static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(jv[i])));
+  for (unsigned i = 0; lk && lv && i < nl; ++i)
+    e += " lib" + std::to_string(static_cast<int>(lk[i])) + "=" +
+         std::to_string(static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(lv[i])));
+  g_load_log.push_back(e);
+}
+}  // namespace
+CUresult load_image(CUlibrary* lib, const void* code) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   std::unique_ptr<MockLib> l(new MockLib());
   if (!parse_image(code, l.get())) return CUDA_ERROR_INVALID_IMAGE;
   *lib = reinterpret_cast<CUlibrary>(l.get());
   g_libs.insert(l.release());
   return CUDA_SUCCESS;
+}
+CUresult cuLibraryLoadData(CUlibrary* lib, const void* code, CUjit_option* jitOptions, void** jitOptionsValues,
+                           unsigned int numJitOptions, CUlibraryOption* libraryOptions, void** libraryOptionValues,
+                           unsigned int numLibraryOptions) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  log_load("cuLibraryLoadData", numJitOptions, jitOptions, jitOptionsValues, numLibraryOptions, libraryOptions,
+           libraryOptionValues);
+  return load_image(lib, code);
+}
+// Test hook: entry i of the load log (returns its length, or -1 past the end).
+extern "C" int fbmock_load_log(int i, char* buf, int cap) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (i < 0 || static_cast<size_t>(i) >= g_load_log.size()) return -1;
+  snprintf(buf, static_cast<size_t>(cap), "%s", g_load_log[static_cast<size_t>(i)].c_str());
+  return static_cast<int>(g_load_log[static_cast<size_t>(i)].size());
 }
 CUresult cuLibraryLoadFromFile(CUlibrary*, const char*, CUjit_option*, void**, unsigned int,
                                CUlibraryOption*, void**, unsigned int) {
@@ -458,13 +495,20 @@ CUresult cuLibraryUnload(CUlibrary lib) {
   return CUDA_SUCCESS;
 }
 CUresult cuModuleLoadData(CUmodule* mod, const void* image) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  log_load("cuModuleLoadData", 0, nullptr, nullptr, 0, nullptr, nullptr);
   CUlibrary lib;
-  CUresult rc = cuLibraryLoadData(&lib, image, nullptr, nullptr, 0, nullptr, nullptr, 0);
+  CUresult rc = load_image(&lib, image);
   if (rc == CUDA_SUCCESS) *mod = reinterpret_cast<CUmodule>(lib);
   return rc;
 }
-CUresult cuModuleLoadDataEx(CUmodule* mod, const void* image, unsigned int, CUjit_option*, void**) {
-  return cuModuleLoadData(mod, image);
+CUresult cuModuleLoadDataEx(CUmodule* mod, const void* image, unsigned int n, CUjit_option* o, void** v) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  log_load("cuModuleLoadDataEx", n, o, v, 0, nullptr, nullptr);
+  CUlibrary lib;
+  CUresult rc = load_image(&lib, image);
+  if (rc == CUDA_SUCCESS) *mod = reinterpret_cast<CUmodule>(lib);
+  return rc;
 }
 CUresult cuModuleLoadFatBinary(CUmodule* mod, const void* image) { return cuModuleLoadData(mod, image); }
 CUresult cuModuleLoad(CUmodule*, const char*) { return CUDA_ERROR_NOT_SUPPORTED; }
@@ -508,11 +552,18 @@ CUresult cuLibraryGetModule(CUmodule* m, CUlibrary lib) {
   *m = reinterpret_cast<CUmodule>(lib);
   return CUDA_SUCCESS;
 }
-CUresult cuLibraryGetGlobal(CUdeviceptr*, size_t*, CUlibrary, const char*) {
-  return CUDA_ERROR_NOT_FOUND;
+CUresult cuLibraryGetGlobal(CUdeviceptr* ptr, size_t* size, CUlibrary lib, const char* name) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto* l = reinterpret_cast<MockLib*>(lib);
+  if (!g_libs.count(l)) return CUDA_ERROR_INVALID_HANDLE;
+  auto it = l->globals.find(name);
+  if (it == l->globals.end()) return CUDA_ERROR_NOT_FOUND;
+  if (ptr) *ptr = reinterpret_cast<CUdeviceptr>(it->second.data());
+  if (size) *size = it->second.size();
+  return CUDA_SUCCESS;
 }
-CUresult cuModuleGetGlobal_v2(CUdeviceptr*, size_t*, CUmodule, const char*) {
-  return CUDA_ERROR_NOT_FOUND;
+CUresult cuModuleGetGlobal_v2(CUdeviceptr* ptr, size_t* size, CUmodule m, const char* name) {
+  return cuLibraryGetGlobal(ptr, size, reinterpret_cast<CUlibrary>(m), name);
 }
 CUresult cuKernelGetFunction(CUfunction* f, CUkernel k) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);

@@ -42,12 +42,21 @@ def pack_fatbins_to_folder(folder_path: str) -> None:
 
 
 def load_cuda_modules_and_libraries(archive_dir: str) -> None:
-    """Re-loads every image of an archive so saved graphs can resolve their kernels."""
+    """Re-loads every image of an archive so saved graphs can resolve their
+    kernels. Images that need NVSHMEM are queued for
+    ``init_nvshmem_for_loaded_modules``; with auto-init on (the default) they
+    are initialised right away when the process has already loaded an NVSHMEM
+    host library, and otherwise stay queued."""
     import torch
 
     if torch.cuda.is_available():
         torch.cuda.init()
     core().load_cuda_modules_and_libraries(archive_dir)
+    if _nvshmem_auto_init:
+        try:
+            core().init_nvshmem_modules()
+        except RuntimeError:
+            pass  # NVSHMEM not up yet: init_nvshmem_for_loaded_modules() after its bootstrap
 
 
 def set_skip_fatbin_processing(enabled: bool) -> None:
@@ -65,15 +74,22 @@ _nvshmem_auto_init = True
 
 
 def set_nvshmem_auto_init(enabled: bool) -> None:
-    """Kept for API parity. foundry_b200's kernels use their own symmetric memory
-    (foundry_b200.parallel), never NVSHMEM, so there is nothing to initialise."""
+    """Whether ``load_cuda_modules_and_libraries`` tries to initialise
+    NVSHMEM-dependent images itself (foundry_b200's own kernels use their own
+    symmetric memory and never need it; images of libraries such as DeepEP do)."""
     global _nvshmem_auto_init
     _nvshmem_auto_init = bool(enabled)
 
 
 def init_nvshmem_for_loaded_modules() -> int:
-    """API parity: returns the number of NVSHMEM-dependent modules initialised (always 0)."""
-    return 0
+    """Initialises every reloaded image that needs NVSHMEM with the process's
+    NVSHMEM host library (``nvshmemx_cumodule_init`` /
+    ``nvshmemx_culibrary_init``, looked up in the process, never loaded here);
+    call it after the NVSHMEM runtime is bootstrapped. Returns how many images
+    were initialised (0 when none was pending); raises RuntimeError when some
+    are pending but no NVSHMEM host library is loaded, or an init fails.
+    Parity: reference csrc/hook.cpp:1193-1365."""
+    return core().init_nvshmem_modules()
 
 
 def preallocate_cublas_workspaces() -> None:
@@ -89,6 +105,11 @@ def preallocate_cublas_workspaces() -> None:
 # Same names as the reference package: `graph` is the capture context manager
 # (the implementation module is foundry_b200.graphs).
 from .graphs import CUDAGraph, graph, graph_pool_handle, save_graph_manifest  # noqa: E402
+from . import jit as _jit  # noqa: E402
+
+# Kernels Triton compiles in this process (torch.compile / Inductor) are
+# adopted by the registry as they load, so graphs that use them persist.
+_jit.install()
 
 
 __all__ = [

@@ -318,9 +318,70 @@ def scenario_rng_load(workdir):
     print(json.dumps({"ok": True}))
 
 
+# ---- torch.compile (Inductor / Triton) kernels in a persisted graph -------------------------
+def _compile_inputs(torch):
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(1 << 16, device="cuda", generator=g)
+    y = torch.randn(1 << 16, device="cuda", generator=g)
+    return x, y
+
+
+def _eager(torch, x, y):
+    return torch.sin(x * 1.5 + y) * y - torch.relu(x)
+
+
+def scenario_compile_save(workdir):
+    torch, fb = _setup()
+    from foundry_b200 import jit
+
+    fb.set_allocation_region(BASE, SIZE)
+    x, y = _compile_inputs(torch)
+    fn = torch.compile(lambda a, b: _eager(torch, a, b), dynamic=False)
+    for _ in range(3):  # compile + warm-up: Triton loads (and foundry adopts) the kernel here
+        fn(x, y)
+    torch.cuda.synchronize()
+    assert jit.installed() and jit.adopted, "no Triton kernel was adopted"
+    g = fb.CUDAGraph()
+    with fb.graph(g):
+        z = fn(x, y)
+    names = g.desc.kernel_names()
+    assert any("triton" in n for n in names), names
+    archive = os.path.join(workdir, "archive")
+    os.makedirs(archive, exist_ok=True)
+    g.save(os.path.join(archive, "graph_0.json"), output_tensors=z)
+    fb.pack_fatbins_to_folder(archive)
+    fb.save_graph_manifest(archive)
+    g.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(z, _eager(torch, x, y), rtol=1e-5, atol=1e-5)
+    torch.save(z.cpu(), os.path.join(workdir, "compile_out.pt"))
+    print(json.dumps({"ok": True, "kernels": names, "adopted": len(jit.adopted)}))
+
+
+def scenario_compile_load(workdir):
+    torch, fb = _setup()
+    archive = os.path.join(workdir, "archive")
+    fb.set_skip_fatbin_processing(True)
+    fb.load_cuda_modules_and_libraries(archive)
+    fb.set_allocation_region(BASE, SIZE)
+    x, y = _compile_inputs(torch)
+    g, z = fb.CUDAGraph.load(os.path.join(archive, "graph_0.json"))
+    g.replay()
+    torch.cuda.synchronize()
+    saved = torch.load(os.path.join(workdir, "compile_out.pt"))
+    assert torch.equal(z.cpu(), saved), "restored torch.compile graph differs from SAVE"
+    x.mul_(0.5)
+    g.replay()
+    torch.testing.assert_close(z, _eager(torch, x, y), rtol=1e-5, atol=1e-5)
+    # nothing was compiled in this process
+    assert "torch._inductor.compile_fx" not in sys.modules
+    print(json.dumps({"ok": True}))
+
+
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
     {"region": scenario_region, "prealloc": scenario_prealloc, "graph_save": scenario_graph_save,
      "graph_load": scenario_graph_load, "async_save": scenario_async_save,
      "async_load": scenario_async_load, "rng_save": scenario_rng_save,
-     "rng_load": scenario_rng_load}[name](workdir)
+     "rng_load": scenario_rng_load, "compile_save": scenario_compile_save,
+     "compile_load": scenario_compile_load}[name](workdir)

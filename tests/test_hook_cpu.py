@@ -70,6 +70,19 @@ assert cu.cuMemFree_v2(q) == 0
 c.resume_allocation_region()
 assert cu.cuMemAlloc_v2(ctypes.byref(q), 1 << 20) == 0
 assert q.value == base + off2, (hex(q.value), hex(base + off2))
+
+# pitched 2-D allocations land at the cursor; the pitch is the row width
+# rounded up to the texture pitch alignment (mock: 32, raised to 128)
+cu.cuMemAllocPitch_v2.argtypes = [ctypes.POINTER(U64), ctypes.POINTER(ctypes.c_size_t), ctypes.c_size_t,
+                                  ctypes.c_size_t, ctypes.c_uint]
+cu.cuMemAllocPitch_v2.restype = ctypes.c_int
+off3 = fb.get_current_alloc_offset()
+pp, pitch = U64(0), ctypes.c_size_t(0)
+assert cu.cuMemAllocPitch_v2(ctypes.byref(pp), ctypes.byref(pitch), 1000, 64, 4) == 0
+assert pitch.value == 1024 and pp.value == base + off3, (pitch.value, hex(pp.value))
+ctypes.memset(pp.value + 63 * pitch.value, 1, 1000)  # the last row is mapped
+assert fb.get_current_alloc_offset() > off3
+assert cu.cuMemAllocPitch_v2(ctypes.byref(pp), ctypes.byref(pitch), 1000, 64, 3) != 0  # element size 3
 print("HOOK_OK")
 """
 
@@ -98,7 +111,8 @@ libdl.dlsym.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
 drv = libdl.dlopen(MOCK.encode(), 2)  # RTLD_NOW, local: how a runtime opens the driver
 assert drv
 # dlsym on the driver handle: overridden entry points resolve to the interposer
-for name in ("cuMemAlloc_v2", "cuMemFree_v2", "cuMemAddressReserve", "cuLibraryLoadData", "cuIpcGetMemHandle"):
+for name in ("cuMemAlloc_v2", "cuMemFree_v2", "cuMemAllocPitch_v2", "cuMemAddressReserve", "cuLibraryLoadData",
+             "cuIpcGetMemHandle"):
     assert libdl.dlsym(drv, name.encode()) == addr(getattr(hook, name)), name
 # others stay the driver's, unknown names stay unknown
 assert libdl.dlsym(drv, b"cuCtxGetDevice") == addr(ctypes.CDLL(MOCK).cuCtxGetDevice)
@@ -113,6 +127,8 @@ assert gpa(b"cuMemAlloc", ctypes.byref(pfn), 12080, 0, ctypes.byref(status)) == 
 assert pfn.value == addr(hook.cuMemAlloc_v2)
 assert gpa(b"cuMemAlloc", ctypes.byref(pfn), 3000, 0, ctypes.byref(status)) == 0
 assert pfn.value != addr(hook.cuMemAlloc_v2)          # pre-_v2 callers keep the driver's entry point
+assert gpa(b"cuMemAllocPitch", ctypes.byref(pfn), 12080, 0, ctypes.byref(status)) == 0
+assert pfn.value == addr(hook.cuMemAllocPitch_v2)
 assert gpa(b"cuCtxGetDevice", ctypes.byref(pfn), 12080, 0, ctypes.byref(status)) == 0
 assert pfn.value == addr(ctypes.CDLL(MOCK).cuCtxGetDevice)
 print("FRONT_DOOR_OK")

@@ -55,3 +55,12 @@ def test_random_numbers_in_a_restored_graph(tmp_path):
     info = _run("rng_save", str(tmp_path))
     assert info["increment"] > 0
     assert _run("rng_load", str(tmp_path))["ok"]
+
+
+def test_torch_compile_graph_save_load(tmp_path):
+    """A torch.compile'd function (Inductor fuses it into a Triton kernel) is
+    captured and saved; a fresh process that compiles nothing restores it
+    from the archive's packed image and replays it bit-exact."""
+    info = _run("compile_save", str(tmp_path), timeout=600)
+    assert info["adopted"] >= 1
+    assert _run("compile_load", str(tmp_path))["ok"]
