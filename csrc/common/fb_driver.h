@@ -94,6 +94,7 @@
   X(cuGraphDestroy)                        \
   X(cuGraphGetNodes)                       \
   X(cuGraphGetEdges)                       \
+  X(cuGraphGetEdges_v2)                    \
   X(cuGraphNodeGetType)                    \
   X(cuGraphKernelNodeGetParams)            \
   X(cuGraphKernelNodeGetAttribute)         \
@@ -109,6 +110,7 @@
   X(cuGraphAddEventRecordNode)             \
   X(cuGraphAddEventWaitNode)               \
   X(cuGraphAddDependencies)                \
+  X(cuGraphAddDependencies_v2)             \
   X(cuGraphInstantiate)                    \
   X(cuGraphExecDestroy)                    \
   X(cuGraphLaunch)                         \

@@ -42,6 +42,9 @@ enum HeaderFlag : uint32_t {
   // seed/offset words (GeneratorPtrRec) so a LOAD can relocate them; an
   // addition to v1, set only when a graph consumed random numbers.
   HF_GENERATOR_PTRS = 1u << 5,
+  // Dependency records carry edge data (DepDataRec) because some edge is not
+  // a plain full-completion dependency (programmatic dependent launch).
+  HF_EDGE_DATA = 1u << 6,
 };
 
 #pragma pack(push, 1)
@@ -153,6 +156,15 @@ struct CommonAttrsRec {
   uint32_t preferred_smem_carveout;
 };
 
+struct DepDataRec {
+  uint32_t from;
+  uint32_t to;
+  uint8_t from_port;
+  uint8_t to_port;
+  uint8_t type;
+  uint8_t reserved;
+};
+
 struct GeneratorRec {
   uint64_t id;
   uint64_t seed;
@@ -181,6 +193,7 @@ static_assert(sizeof(ParamRec) == 8, "param record is 8 bytes");
 static_assert(sizeof(GeneratorRec) == 24, "generator record is 24 bytes");
 static_assert(sizeof(GeneratorPtrRec) == 40, "generator record with pointers is 40 bytes");
 static_assert(sizeof(DepRec) == 8, "dependency record is 8 bytes");
+static_assert(sizeof(DepDataRec) == 12, "dependency record with edge data is 12 bytes");
 
 }  // namespace bin
 }  // namespace fbc

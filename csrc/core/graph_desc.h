@@ -91,9 +91,21 @@ struct Generator {
   uint64_t seed_ptr = 0, offset_ptr = 0;
 };
 
+// Data of one dependency edge (CUgraphEdgeData): all zero for a plain
+// full-completion dependency; programmatic dependent launch edges set the
+// ports and type.
+struct EdgeData {
+  uint8_t from_port = 0, to_port = 0, type = 0;
+  bool is_default() const { return from_port == 0 && to_port == 0 && type == 0; }
+  bool operator==(const EdgeData& o) const {
+    return from_port == o.from_port && to_port == o.to_port && type == o.type;
+  }
+};
+
 struct GraphDesc {
   std::vector<Node> nodes;
   std::vector<std::pair<uint32_t, uint32_t>> deps;  // (from, to) node ids
+  std::vector<EdgeData> edge_data;  // parallel to deps; empty when every edge is a plain dependency
   bool has_deps = true;     // false for on-demand members stripped by the manifest
   std::string topology_key;
   bool has_common_attrs = false;

@@ -292,11 +292,30 @@ std::shared_ptr<GraphDesc> analyze_graph(CUgraph graph) {
   }
   g->num_events = static_cast<int>(event_ids.size());
   size_t ne = 0;
-  check_drv(d->cuGraphGetEdges(graph, nullptr, nullptr, &ne), "cuGraphGetEdges");
-  if (ne) {
-    std::vector<CUgraphNode> from(ne), to(ne);
-    check_drv(d->cuGraphGetEdges(graph, from.data(), to.data(), &ne), "cuGraphGetEdges");
-    for (size_t i = 0; i < ne; ++i) g->deps.emplace_back(index.at(from[i]), index.at(to[i]));
+  if (d->cuGraphGetEdges_v2) {
+    // Edge data (ports, type) as well: graphs with programmatic dependent
+    // launch edges cannot be described by the plain query (it reports
+    // CUDA_ERROR_LOSSY_QUERY for them).
+    check_drv(d->cuGraphGetEdges_v2(graph, nullptr, nullptr, nullptr, &ne), "cuGraphGetEdges_v2");
+    if (ne) {
+      std::vector<CUgraphNode> from(ne), to(ne);
+      std::vector<CUgraphEdgeData> data(ne);
+      check_drv(d->cuGraphGetEdges_v2(graph, from.data(), to.data(), data.data(), &ne), "cuGraphGetEdges_v2");
+      bool plain = true;
+      for (size_t i = 0; i < ne; ++i) {
+        g->deps.emplace_back(index.at(from[i]), index.at(to[i]));
+        g->edge_data.push_back(EdgeData{data[i].from_port, data[i].to_port, data[i].type});
+        plain = plain && g->edge_data.back().is_default();
+      }
+      if (plain) g->edge_data.clear();
+    }
+  } else {
+    check_drv(d->cuGraphGetEdges(graph, nullptr, nullptr, &ne), "cuGraphGetEdges");
+    if (ne) {
+      std::vector<CUgraphNode> from(ne), to(ne);
+      check_drv(d->cuGraphGetEdges(graph, from.data(), to.data(), &ne), "cuGraphGetEdges");
+      for (size_t i = 0; i < ne; ++i) g->deps.emplace_back(index.at(from[i]), index.at(to[i]));
+    }
   }
   g->topology_key = compute_topology_key(*g);
   hoist_common_attrs(*g);
@@ -332,9 +351,14 @@ std::string compute_topology_key(const GraphDesc& g) {
   // Edge structure must match too for exec updates to apply.
   if (g.has_deps) {
     uint64_t h = ~0ull;
-    for (const auto& e : g.deps) {
-      uint32_t v[2] = {e.first, e.second};
+    for (size_t i = 0; i < g.deps.size(); ++i) {
+      uint32_t v[2] = {g.deps[i].first, g.deps[i].second};
       h = fb::crc64_update(h, v, sizeof(v));
+      if (!g.edge_data.empty() && !g.edge_data[i].is_default()) {
+        const EdgeData& e = g.edge_data[i];
+        const uint8_t w[3] = {e.from_port, e.to_port, e.type};
+        h = fb::crc64_update(h, w, sizeof(w));
+      }
     }
     char buf[32];
     snprintf(buf, sizeof(buf), "|E%zu:%016llx", g.deps.size(), static_cast<unsigned long long>(~h));
@@ -524,8 +548,23 @@ std::unique_ptr<BuiltGraph> build_graph(const GraphDesc& g) {
       from.push_back(b->nodes[e.first]);
       to.push_back(b->nodes[e.second]);
     }
-    check_drv(d->cuGraphAddDependencies(b->graph, from.data(), to.data(), from.size()),
-              "cuGraphAddDependencies");
+    if (!g.edge_data.empty()) {
+      if (g.edge_data.size() != g.deps.size()) throw std::runtime_error("edge data does not match the edge list");
+      if (!d->cuGraphAddDependencies_v2)
+        throw std::runtime_error("graph has programmatic dependency edges; this driver cannot add them");
+      std::vector<CUgraphEdgeData> data(g.edge_data.size());
+      for (size_t i = 0; i < data.size(); ++i) {
+        memset(&data[i], 0, sizeof(data[i]));
+        data[i].from_port = g.edge_data[i].from_port;
+        data[i].to_port = g.edge_data[i].to_port;
+        data[i].type = g.edge_data[i].type;
+      }
+      check_drv(d->cuGraphAddDependencies_v2(b->graph, from.data(), to.data(), data.data(), from.size()),
+                "cuGraphAddDependencies_v2");
+    } else {
+      check_drv(d->cuGraphAddDependencies(b->graph, from.data(), to.data(), from.size()),
+                "cuGraphAddDependencies");
+    }
   }
   return b;
 }

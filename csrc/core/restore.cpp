@@ -141,6 +141,7 @@ void RestoredGraph::materialize() {
   GraphDesc g = *desc;
   if (!g.has_deps && shared && shared->template_desc) {
     g.deps = shared->template_desc->deps;
+    g.edge_data = shared->template_desc->edge_data;
     g.has_deps = true;
   }
   own_built = build_graph(g);
@@ -261,6 +262,9 @@ std::shared_ptr<PendingLoads> start_graph_builds(const std::vector<std::string>&
   pl->diffs.resize(paths.size());
   pl->results.resize(paths.size());
   pl->finished.assign(paths.size(), 0);
+  pl->resolved.assign(paths.size(), 0);
+  pl->diff_ready.assign(paths.size(), 0);
+  pl->deferred_reason.assign(paths.size(), std::string());
   pl->phase1_ms = ms_since(t0);
   pl->start_phase2();
   return pl;
@@ -272,10 +276,20 @@ void PendingLoads::start_phase2() {
     try {
       const FbDriver* d = fb_driver();
       if (ctx) d->cuCtxSetCurrent(ctx);
-      // Resolve functions (driver lookups, cached per image) for every graph.
-      for (auto& g : descs) resolve_functions(*g);
-      // Templates: build + instantiate, one per group.
+      // Resolve functions (driver lookups, cached per image) for every graph;
+      // a kernel persisted by entry name whose library has not loaded it yet
+      // defers that graph to finish_one.
+      for (size_t i = 0; i < descs.size(); ++i) {
+        try {
+          resolve_functions(*descs[i]);
+          resolved[i] = 1;
+        } catch (const std::exception& e) {
+          deferred_reason[i] = e.what();
+        }
+      }
+      // Templates: build + instantiate, one per group (resolved ones only).
       for (size_t gi = 0; gi < group_template.size(); ++gi) {
+        if (!resolved[group_template[gi]]) continue;
         const auto& tdesc = descs[group_template[gi]];
         auto se = std::make_shared<SharedExec>();
         se->template_desc = tdesc;
@@ -294,7 +308,9 @@ void PendingLoads::start_phase2() {
             descs[i]->nodes.size() != descs[tmpl]->nodes.size())
           throw std::runtime_error("manifest groups " + paths[i] + " with a template of another topology (" +
                                    paths[tmpl] + ")");
+        if (!resolved[i] || !resolved[tmpl]) return;
         diffs[i] = diff_against(*descs[tmpl], *descs[i]);
+        diff_ready[i] = 1;
       });
     } catch (...) {
       std::lock_guard<std::mutex> lk(mu_);
@@ -318,6 +334,29 @@ std::shared_ptr<RestoredGraph> PendingLoads::finish_one(size_t index) {
   wait();
   std::lock_guard<std::mutex> lk(finish_mu_);
   if (finished[index]) return results[index];
+  // Graphs deferred by the background builds: resolve now (the engine has run
+  // the warm-up that loads their kernels by the time it asks for them).
+  const int gi = group_of[index];
+  const int tmpl = group_template[gi];
+  if (!resolved[tmpl]) {
+    resolve_functions(*descs[tmpl]);
+    resolved[tmpl] = 1;
+  }
+  if (!groups[gi]) {
+    auto se = std::make_shared<SharedExec>();
+    se->template_desc = descs[tmpl];
+    se->built = build_graph(*descs[tmpl]);
+    se->exec = instantiate(se->built->graph);
+    groups[gi] = se;
+  }
+  if (!resolved[index]) {
+    resolve_functions(*descs[index]);
+    resolved[index] = 1;
+  }
+  if (static_cast<int>(index) != tmpl && !diff_ready[index]) {
+    diffs[index] = diff_against(*descs[tmpl], *descs[index]);
+    diff_ready[index] = 1;
+  }
   // Allocator events are replayed in capture order: the cursor must walk the
   // same trajectory it walked on SAVE.
   const auto& ev = descs[index]->allocator_events_json;

@@ -78,6 +78,13 @@ class PendingLoads {
   std::vector<std::vector<uint32_t>> diffs;
   std::vector<std::shared_ptr<RestoredGraph>> results;
   std::vector<char> finished;  // not vector<bool>: elements are written by finish_one
+  // Kernels a graph names by entry only (images another library loads on
+  // first use, e.g. cuBLAS kernels) may not be loaded yet when the background
+  // builds run. Such graphs are resolved, and their group's template built,
+  // when finish_one asks for them.
+  std::vector<char> resolved;
+  std::vector<char> diff_ready;
+  std::vector<std::string> deferred_reason;
   double phase1_ms = 0, phase2_ms = 0;
   int num_threads = 4;
   CUcontext ctx = nullptr;

@@ -234,10 +234,15 @@ J::Value to_json(const GraphDesc& g) {
   root["nodes"] = J::Value(std::move(nodes));
   if (g.has_deps) {
     J::Array deps;
-    for (const auto& e : g.deps) {
+    for (size_t i = 0; i < g.deps.size(); ++i) {
       J::Object d;
-      d["from"] = e.first;
-      d["to"] = e.second;
+      d["from"] = g.deps[i].first;
+      d["to"] = g.deps[i].second;
+      if (!g.edge_data.empty() && !g.edge_data[i].is_default()) {
+        d["from_port"] = static_cast<int>(g.edge_data[i].from_port);
+        d["to_port"] = static_cast<int>(g.edge_data[i].to_port);
+        d["type"] = static_cast<int>(g.edge_data[i].type);
+      }
       deps.push_back(J::Value(std::move(d)));
     }
     root["dependencies"] = J::Value(std::move(deps));
@@ -313,9 +318,18 @@ std::shared_ptr<GraphDesc> from_json(const J::Value& v) {
     g->nodes.push_back(std::move(n));
   }
   if (const J::Value* deps = root.find("dependencies")) {
-    for (const J::Value& dv : deps->as_array())
-      g->deps.emplace_back(static_cast<uint32_t>(dv.as_object().at("from").as_u64()),
-                           static_cast<uint32_t>(dv.as_object().at("to").as_u64()));
+    bool plain = true;
+    for (const J::Value& dv : deps->as_array()) {
+      const J::Object& o = dv.as_object();
+      g->deps.emplace_back(static_cast<uint32_t>(o.at("from").as_u64()), static_cast<uint32_t>(o.at("to").as_u64()));
+      EdgeData e;
+      if (const J::Value* v = o.find("from_port")) e.from_port = static_cast<uint8_t>(v->as_u64());
+      if (const J::Value* v = o.find("to_port")) e.to_port = static_cast<uint8_t>(v->as_u64());
+      if (const J::Value* v = o.find("type")) e.type = static_cast<uint8_t>(v->as_u64());
+      g->edge_data.push_back(e);
+      plain = plain && e.is_default();
+    }
+    if (plain) g->edge_data.clear();
   } else {
     g->has_deps = false;
   }
@@ -471,8 +485,17 @@ void write_binary(const GraphDesc& g, const std::string& path) {
       case NodeType::Empty: break;
     }
   }
+  const bool edge_data = !g.edge_data.empty();
   std::vector<bin::DepRec> deps;
-  for (const auto& e : g.deps) deps.push_back(bin::DepRec{e.first, e.second});
+  std::vector<bin::DepDataRec> deps_d;
+  for (size_t i = 0; i < g.deps.size(); ++i) {
+    if (edge_data) {
+      const EdgeData& e = g.edge_data.at(i);
+      deps_d.push_back(bin::DepDataRec{g.deps[i].first, g.deps[i].second, e.from_port, e.to_port, e.type, 0});
+    } else {
+      deps.push_back(bin::DepRec{g.deps[i].first, g.deps[i].second});
+    }
+  }
   bin::CommonAttrsRec common;
   memset(&common, 0, sizeof(common));
   if (g.has_common_attrs) {
@@ -511,7 +534,8 @@ void write_binary(const GraphDesc& g, const std::string& path) {
   Blob blobs[bin::S_COUNT] = {
       {strings.data.data(), strings.data.size()},
       {nodes.data(), nodes.size() * sizeof(bin::NodeRec)},
-      {deps.data(), deps.size() * sizeof(bin::DepRec)},
+      {edge_data ? static_cast<const void*>(deps_d.data()) : static_cast<const void*>(deps.data()),
+       edge_data ? deps_d.size() * sizeof(bin::DepDataRec) : deps.size() * sizeof(bin::DepRec)},
       {pindex.data(), pindex.size() * sizeof(bin::ParamRec)},
       {pdata.data(), pdata.size()},
       {argbuf.data(), argbuf.size()},
@@ -529,9 +553,10 @@ void write_binary(const GraphDesc& g, const std::string& path) {
   h.flags = (g.has_common_attrs ? bin::HF_COMMON_ATTRS : 0) | (g.has_deps ? bin::HF_DEPS : 0) |
             (!g.allocator_events_json.empty() ? bin::HF_ALLOC_EVENTS : 0) |
             (!g.output_tensors_json.empty() ? bin::HF_OUTPUTS : 0) |
-            (!g.generators.empty() ? bin::HF_GENERATORS : 0) | (gen_ptrs ? bin::HF_GENERATOR_PTRS : 0);
+            (!g.generators.empty() ? bin::HF_GENERATORS : 0) | (gen_ptrs ? bin::HF_GENERATOR_PTRS : 0) |
+            (edge_data ? bin::HF_EDGE_DATA : 0);
   h.num_nodes = static_cast<uint32_t>(nodes.size());
-  h.num_deps = static_cast<uint32_t>(deps.size());
+  h.num_deps = static_cast<uint32_t>(g.deps.size());
   h.num_generators = static_cast<uint32_t>(g.generators.size());
   h.num_sections = bin::S_COUNT;
   h.num_strings = strings.count;
@@ -671,11 +696,14 @@ std::shared_ptr<GraphDesc> read_binary(const std::string& path) {
     }
   }
   g->has_deps = (h.flags & bin::HF_DEPS) != 0;
-  if (dir[bin::S_DEPS].size != h.num_deps * sizeof(bin::DepRec)) fail("dependency table size");
+  const bool edge_data = (h.flags & bin::HF_EDGE_DATA) != 0;
+  const size_t dep_rec = edge_data ? sizeof(bin::DepDataRec) : sizeof(bin::DepRec);
+  if (dir[bin::S_DEPS].size != h.num_deps * dep_rec) fail("dependency table size");
   for (uint32_t i = 0; i < h.num_deps; ++i) {
-    bin::DepRec d;
-    memcpy(&d, sec(bin::S_DEPS) + i * sizeof(d), sizeof(d));
+    bin::DepDataRec d{};
+    memcpy(&d, sec(bin::S_DEPS) + i * dep_rec, dep_rec);
     g->deps.emplace_back(d.from, d.to);
+    if (edge_data) g->edge_data.push_back(EdgeData{d.from_port, d.to_port, d.type});
   }
   if (h.flags & bin::HF_COMMON_ATTRS) {
     if (dir[bin::S_COMMON_ATTRS].size < sizeof(bin::CommonAttrsRec)) fail("common attrs size");

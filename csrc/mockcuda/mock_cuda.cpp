@@ -92,6 +92,7 @@ struct MockNode {
 struct MockGraph {
   std::vector<std::unique_ptr<MockNode>> nodes;
   std::vector<std::pair<MockNode*, MockNode*>> edges;
+  std::vector<CUgraphEdgeData> edge_data;  // parallel to edges
 };
 std::set<MockGraph*> g_graphs;
 struct MockExec {
@@ -687,8 +688,12 @@ static CUresult add_node(CUgraph g, const CUgraphNode* deps, size_t ndeps, MockN
     return CUDA_ERROR_INVALID_HANDLE;
   }
   mg->nodes.emplace_back(n);
-  for (size_t i = 0; i < ndeps; ++i)
+  for (size_t i = 0; i < ndeps; ++i) {
     mg->edges.emplace_back(reinterpret_cast<MockNode*>(deps[i]), n);
+    CUgraphEdgeData e;
+    memset(&e, 0, sizeof(e));
+    mg->edge_data.push_back(e);
+  }
   *out = reinterpret_cast<CUgraphNode>(n);
   return CUDA_SUCCESS;
 }
@@ -744,14 +749,23 @@ CUresult cuGraphAddEventWaitNode(CUgraphNode* out, CUgraph g, const CUgraphNode*
   n->ev = e;
   return add_node(g, deps, nd, n, out);
 }
-CUresult cuGraphAddDependencies(CUgraph g, const CUgraphNode* from, const CUgraphNode* to,
-                                size_t n) {
+CUresult cuGraphAddDependencies_v2(CUgraph g, const CUgraphNode* from, const CUgraphNode* to,
+                                   const CUgraphEdgeData* data, size_t n) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   MockGraph* mg = as_graph(g);
   if (!mg) return CUDA_ERROR_INVALID_HANDLE;
-  for (size_t i = 0; i < n; ++i)
+  for (size_t i = 0; i < n; ++i) {
     mg->edges.emplace_back(reinterpret_cast<MockNode*>(from[i]), reinterpret_cast<MockNode*>(to[i]));
+    CUgraphEdgeData e;
+    memset(&e, 0, sizeof(e));
+    if (data) e = data[i];
+    mg->edge_data.push_back(e);
+  }
   return CUDA_SUCCESS;
+}
+CUresult cuGraphAddDependencies(CUgraph g, const CUgraphNode* from, const CUgraphNode* to,
+                                size_t n) {
+  return cuGraphAddDependencies_v2(g, from, to, nullptr, n);
 }
 CUresult cuGraphGetNodes(CUgraph g, CUgraphNode* nodes, size_t* n) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
@@ -763,17 +777,27 @@ CUresult cuGraphGetNodes(CUgraph g, CUgraphNode* nodes, size_t* n) {
   *n = mg->nodes.size();
   return CUDA_SUCCESS;
 }
-CUresult cuGraphGetEdges(CUgraph g, CUgraphNode* from, CUgraphNode* to, size_t* n) {
+CUresult cuGraphGetEdges_v2(CUgraph g, CUgraphNode* from, CUgraphNode* to, CUgraphEdgeData* data, size_t* n) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   MockGraph* mg = as_graph(g);
   if (!mg) return CUDA_ERROR_INVALID_HANDLE;
+  bool lossy = false;
   if (from && to)
     for (size_t i = 0; i < *n && i < mg->edges.size(); ++i) {
       from[i] = reinterpret_cast<CUgraphNode>(mg->edges[i].first);
       to[i] = reinterpret_cast<CUgraphNode>(mg->edges[i].second);
+      const CUgraphEdgeData& e = mg->edge_data[i];
+      if (data)
+        data[i] = e;
+      else if (e.from_port || e.to_port || e.type)
+        lossy = true;
     }
   *n = mg->edges.size();
-  return CUDA_SUCCESS;
+  // Like the driver: a query without edge data cannot describe such edges.
+  return lossy ? CUDA_ERROR_LOSSY_QUERY : CUDA_SUCCESS;
+}
+CUresult cuGraphGetEdges(CUgraph g, CUgraphNode* from, CUgraphNode* to, size_t* n) {
+  return cuGraphGetEdges_v2(g, from, to, nullptr, n);
 }
 CUresult cuGraphNodeGetType(CUgraphNode node, CUgraphNodeType* t) {
   auto* n = reinterpret_cast<MockNode*>(node);
@@ -840,6 +864,7 @@ CUresult cuGraphInstantiateWithFlags(CUgraphExec* out, CUgraph g, unsigned long 
     ex->from_orig[n.get()] = c;
   }
   for (auto& e : mg->edges) ex->g->edges.emplace_back(ex->from_orig[e.first], ex->from_orig[e.second]);
+  ex->g->edge_data = mg->edge_data;
   g_execs.insert(ex);
   *out = reinterpret_cast<CUgraphExec>(ex);
   return CUDA_SUCCESS;

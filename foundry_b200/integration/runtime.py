@@ -82,6 +82,7 @@ def setup_graph_extension(config: GraphExtensionConfig, global_rank: int) -> Ext
         return _state
     if config.mode == GraphExtensionMode.SAVE:
         os.makedirs(ws, exist_ok=True)
+        clear_saved_graphs(ws)
     else:
         if not os.path.isdir(ws):
             raise FileNotFoundError(f"LOAD workspace {ws} does not exist (run SAVE first)")
@@ -92,6 +93,19 @@ def setup_graph_extension(config: GraphExtensionConfig, global_rank: int) -> Ext
     log.info("[foundry] %s rank %d: region %#x + %s, workspace %s", config.mode.value, global_rank,
              config.base_addr, config.region_size, ws)
     return _state
+
+
+def clear_saved_graphs(workspace: str) -> int:
+    """SAVE: removes the graphs, manifest and packed modules of an earlier SAVE
+    pass in ``workspace`` (the warm-up state and final offset stay: a second
+    pass reuses them to allocate exactly as LOAD will). Returns files removed."""
+    n = 0
+    for name in os.listdir(workspace):
+        if (name.startswith("graph_") and name.endswith((".json", ".cugraph"))) or name in (
+                "fatbin_image_packed.img", "fatbin_entrypoint_packed.txt"):
+            os.remove(os.path.join(workspace, name))
+            n += 1
+    return n
 
 
 def skip_to_scratch_boundary() -> int:
@@ -164,5 +178,6 @@ def reset() -> None:
     _state = None
 
 
-__all__ = ["ExtensionState", "WarmupState", "capture_final_alloc_offset", "ld_preload_env", "mode",
+__all__ = ["ExtensionState", "WarmupState", "capture_final_alloc_offset", "clear_saved_graphs", "ld_preload_env",
+           "mode",
            "preallocate_for_load_mode", "reset", "setup_graph_extension", "skip_to_scratch_boundary", "state"]

@@ -4,13 +4,19 @@
 
   CUDAGraphWrapper.__call__        capture -> foundry capture + save (SAVE) or
                                    restore (LOAD) keyed by the batch descriptor
-  Worker.init_device               after the device/communicator init: LOAD
+  init_worker_distributed_environment  (first step of Worker.init_device)
+                                   right after the communicator is up: LOAD
                                    loads the packed modules, both modes enable
-                                   the region and skip the scratch space
-  Worker.determine_available_memory  SAVE records the KV-cache budget, LOAD
-                                   reuses it (re-profiling could size the KV
-                                   cache differently and move every address)
-  kernel_warmup (gpu_worker)       skipped on LOAD (its kernels are restored)
+                                   the region and skip the scratch space, before
+                                   the workspace manager and the model runner's
+                                   persistent buffers are allocated
+  Worker.determine_available_memory  the first SAVE pass profiles and records
+                                   the KV-cache budget; a second SAVE pass and
+                                   LOAD reuse it without profiling, so they
+                                   allocate identically (save twice, then load)
+  GPUModelRunner.initialize_kv_cache SAVE records the KV-cache addresses, LOAD
+                                   checks them before any graph is restored
+  kernel_warmup (gpu_worker)       skipped in SAVE and LOAD (it allocates)
   GPUModelRunner.load_model        LOAD: map SAVE's working set in one piece
                                    before the weights load, start the graph
                                    builds right after (they overlap the KV
@@ -91,11 +97,15 @@ def _wrapper_call(self, *args, **kwargs):
     return entry.output
 
 
-def _init_device(self, *a, **k):
-    r = _originals["Worker.init_device"](self, *a, **k)
+def _init_distributed(vllm_config, rank, *a, **k):
+    """Worker.init_device calls this first; the workspace manager and the model
+    runner's persistent input buffers are allocated right after it, so the
+    region (and, on LOAD, the packed modules) is set up as soon as the
+    communicator is up, before any of those allocations."""
+    r = _originals["init_worker_distributed_environment"](vllm_config, rank, *a, **k)
     cfg = _config
-    pc = self.vllm_config.parallel_config
-    grank = global_rank(self.rank, pc.world_size, getattr(pc, "data_parallel_rank", 0) or 0)
+    pc = vllm_config.parallel_config
+    grank = global_rank(rank, pc.world_size, getattr(pc, "data_parallel_rank", 0) or 0)
     runtime.setup_graph_extension(cfg, grank)
     if cfg.mode != GraphExtensionMode.NONE:
         runtime.skip_to_scratch_boundary()
@@ -103,22 +113,71 @@ def _init_device(self, *a, **k):
 
 
 def _determine_available_memory(self, *a, **k):
+    """KV-cache budget. The first SAVE pass measures it (vLLM's profiling
+    allocates and captures graphs of its own) and records it; a second SAVE
+    pass and every LOAD reuse it without profiling, so they allocate the
+    same buffers in the same order and the KV cache lands at the same
+    address. Parity: reference vllm/hooks.py:536-642."""
     st = runtime.state()
     if st is None or st.config.mode == GraphExtensionMode.NONE:
         return _originals["Worker.determine_available_memory"](self, *a, **k)
     ws = st.config.workspace_dir
+    saved = runtime.WarmupState.load(ws)
+    if saved is not None and "available_memory" in saved.extra:
+        return int(saved.extra["available_memory"])
     if st.config.mode == GraphExtensionMode.LOAD:
-        saved = runtime.WarmupState.load(ws)
-        if saved is not None and "available_memory" in saved.extra:
-            return int(saved.extra["available_memory"])
+        raise RuntimeError(f"LOAD needs {ws}/warmup_state.json from a SAVE run")
     v = _originals["Worker.determine_available_memory"](self, *a, **k)
-    if st.config.mode == GraphExtensionMode.SAVE:
-        runtime.WarmupState(extra={"available_memory": int(v)}).save(ws)
+    runtime.WarmupState(extra={"available_memory": int(v)}).save(ws)
+    log.info("[foundry] SAVE pass 1 recorded the KV-cache budget (%d bytes); run SAVE again for the "
+             "deterministic pass that LOAD reproduces", int(v))
     return v
 
 
+def _kv_cache_ptrs(runner) -> list[int]:
+    out: list[int] = []
+
+    def walk(x):
+        if hasattr(x, "data_ptr"):
+            out.append(int(x.data_ptr()))
+        elif isinstance(x, (list, tuple)):
+            for y in x:
+                walk(y)
+        elif isinstance(x, dict):
+            for y in x.values():
+                walk(y)
+
+    walk(getattr(runner, "kv_caches", []))
+    return out
+
+
+def _initialize_kv_cache(self, *a, **k):
+    """SAVE records the KV-cache tensors' addresses; LOAD checks them before
+    any graph is restored (a restored graph reads the KV cache at SAVE's
+    address, so a different layout must stop here, not in a kernel)."""
+    r = _originals["GPUModelRunner.initialize_kv_cache"](self, *a, **k)
+    st = runtime.state()
+    if st is None or st.config.mode == GraphExtensionMode.NONE or k.get("is_profiling"):
+        return r
+    ptrs = _kv_cache_ptrs(self)
+    ws = st.config.workspace_dir
+    saved = runtime.WarmupState.load(ws) or runtime.WarmupState()
+    if st.config.mode == GraphExtensionMode.SAVE:
+        saved.extra["kv_cache_ptrs"] = ptrs
+        saved.save(ws)
+    elif saved.extra.get("kv_cache_ptrs") is not None and saved.extra["kv_cache_ptrs"] != ptrs:
+        want = saved.extra["kv_cache_ptrs"]
+        raise RuntimeError(f"LOAD placed the KV cache at {hex(ptrs[0]) if ptrs else None}, SAVE at "
+                           f"{hex(want[0]) if want else None} ({len(ptrs)} vs {len(want)} tensors): this run "
+                           "allocated differently before the KV cache (SAVE twice so the archive comes from the "
+                           "deterministic second pass)")
+    return r
+
+
 def _kernel_warmup(worker, *a, **k):
-    if runtime.mode() == GraphExtensionMode.LOAD:
+    # Kernel warm-up (autotuning) allocates as it goes: skipped whenever graphs
+    # are persisted, in SAVE as in LOAD (reference vllm/hooks.py:187-198).
+    if runtime.mode() != GraphExtensionMode.NONE:
         return None
     return _originals["kernel_warmup"](worker, *a, **k)
 
@@ -226,19 +285,21 @@ def install_hooks(config: GraphExtensionConfig | str) -> None:
     _quarantine_capability()
     cg, gw, mr = _targets()
     _originals["CUDAGraphWrapper.__call__"] = cg.CUDAGraphWrapper.__call__
-    _originals["Worker.init_device"] = gw.Worker.init_device
+    _originals["init_worker_distributed_environment"] = gw.init_worker_distributed_environment
     _originals["Worker.determine_available_memory"] = gw.Worker.determine_available_memory
     _originals["kernel_warmup"] = gw.kernel_warmup
     _originals["GPUModelRunner.capture_model"] = mr.GPUModelRunner.capture_model
     _originals["GPUModelRunner.load_model"] = mr.GPUModelRunner.load_model
     _originals["GPUModelRunner._dummy_run"] = mr.GPUModelRunner._dummy_run
+    _originals["GPUModelRunner.initialize_kv_cache"] = mr.GPUModelRunner.initialize_kv_cache
     cg.CUDAGraphWrapper.__call__ = _wrapper_call
-    gw.Worker.init_device = _init_device
+    gw.init_worker_distributed_environment = _init_distributed
     gw.Worker.determine_available_memory = _determine_available_memory
     gw.kernel_warmup = _kernel_warmup
     mr.GPUModelRunner.capture_model = _capture_model
     mr.GPUModelRunner.load_model = _load_model
     mr.GPUModelRunner._dummy_run = _dummy_run
+    mr.GPUModelRunner.initialize_kv_cache = _initialize_kv_cache
     log.info("[foundry] vLLM hooks installed (mode %s)", config.mode.value)
 
 
@@ -247,12 +308,13 @@ def uninstall_hooks() -> None:
         return
     cg, gw, mr = _targets()
     cg.CUDAGraphWrapper.__call__ = _originals.pop("CUDAGraphWrapper.__call__")
-    gw.Worker.init_device = _originals.pop("Worker.init_device")
+    gw.init_worker_distributed_environment = _originals.pop("init_worker_distributed_environment")
     gw.Worker.determine_available_memory = _originals.pop("Worker.determine_available_memory")
     gw.kernel_warmup = _originals.pop("kernel_warmup")
     mr.GPUModelRunner.capture_model = _originals.pop("GPUModelRunner.capture_model")
     mr.GPUModelRunner.load_model = _originals.pop("GPUModelRunner.load_model")
     mr.GPUModelRunner._dummy_run = _originals.pop("GPUModelRunner._dummy_run")
+    mr.GPUModelRunner.initialize_kv_cache = _originals.pop("GPUModelRunner.initialize_kv_cache")
     import torch
 
     torch.cuda.get_device_capability = _originals.pop("torch.cuda.get_device_capability")

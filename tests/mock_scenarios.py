@@ -351,6 +351,56 @@ def scenario_mixed(workdir: str) -> None:
     print("MIXED LOAD OK")
 
 
+def scenario_pdl(workdir: str) -> None:
+    """Programmatic dependent launch edges (edge data: ports and type) are read
+    with the v2 edge query, kept in JSON and .cugraph, enter the topology key
+    and are re-created on restore; a graph of such edges is not grouped with
+    the same graph of plain edges."""
+    fb, c = _core()
+    archive = os.path.join(workdir, "pdl_archive")
+    os.makedirs(archive, exist_ok=True)
+    c.set_allocation_region(BASE, REGION)
+    ptrs = [c.region_alloc(1 << 20) for _ in range(3)]
+    img = os.path.join(workdir, "mock.cubin")
+    with open(img, "wb") as f:
+        f.write(_image_bytes(0))
+    _, h = c.load_image_file(img)
+    base = json.loads(_mixed_graph_json(h, ptrs))
+    nodes = [base["nodes"][0], dict(base["nodes"][6], id=1), dict(base["nodes"][0], id=2)]
+    # kernel 0 -> kernel 1: programmatic (from_port 1 = programmatic port, type 1 = programmatic);
+    # kernel 1 -> kernel 2: plain
+    pdl = {"nodes": nodes, "dependencies": [{"from": 0, "to": 1, "from_port": 1, "to_port": 0, "type": 1},
+                                            {"from": 1, "to": 2}], "topology_key": "", "generators": [],
+           "num_events": 0}
+    plain = dict(pdl, dependencies=[{"from": 0, "to": 1}, {"from": 1, "to": 2}])
+    keys = {}
+    for name, doc in (("pdl", pdl), ("plain", plain)):
+        desc = c.graph_from_json_text(json.dumps(doc))
+        c.recompute_topology_key(desc)
+        live = c.build_live_graph(desc)
+        analyzed = c.analyze_graph(live)
+        c.destroy_graph(live)
+        got = json.loads(analyzed.to_json())
+        deps = sorted((d["from"], d["to"], d.get("from_port", 0), d.get("type", 0)) for d in got["dependencies"])
+        want = [(0, 1, 1, 1), (1, 2, 0, 0)] if name == "pdl" else [(0, 1, 0, 0), (1, 2, 0, 0)]
+        assert deps == want, (name, deps)
+        keys[name] = analyzed.topology_key
+        path = os.path.join(archive, f"graph_{len(keys) - 1}.json")
+        analyzed.save(path)
+        assert c.read_binary_graph(path.replace(".json", ".cugraph")).to_json() == analyzed.to_json()
+    assert keys["pdl"] != keys["plain"], keys
+    paths = [os.path.join(archive, "graph_0.json"), os.path.join(archive, "graph_1.json")]
+    pending = c.start_graph_builds(paths, 2)
+    pending.wait()
+    assert pending.num_groups == 2
+    for i in range(2):
+        g = pending.finish_one(i)
+        g.launch(0)
+        g.materialize()
+        g.launch(0)
+    print("PDL OK")
+
+
 def scenario_numeric(workdir: str) -> None:
     """A graph of axpy/fill kernels on region memory: SAVE runs it, LOAD restores
     and runs it again; results must be bit-identical."""
@@ -549,4 +599,4 @@ def scenario_rng(workdir: str) -> None:
 if __name__ == "__main__":
     name, workdir = sys.argv[1], sys.argv[2]
     {"save": scenario_save, "load": scenario_load, "numeric": scenario_numeric, "faults": scenario_faults,
-     "cluster": scenario_cluster, "mixed": scenario_mixed, "rng": scenario_rng}[name](workdir)
+     "cluster": scenario_cluster, "mixed": scenario_mixed, "rng": scenario_rng, "pdl": scenario_pdl}[name](workdir)

@@ -320,3 +320,87 @@ def test_foreign_load_options_are_replayed(tmp_path):
         r = subprocess.run([sys.executable, "-c", head + script], env=env, capture_output=True, text=True,
                            timeout=120)
         assert r.returncode == 0 and ok in r.stdout, r.stdout + r.stderr
+
+
+LAZY_SAVE = r"""
+import ctypes, json, os, sys
+sys.path.insert(0, ROOT)
+import foundry_b200 as fb
+c = fb.core()
+# a library that loads its kernels on first use, from heap memory (cuBLAS does)
+image = b"FBMOCK\nfblazy_k:8,4\n\n" + bytes(64)
+buf = ctypes.create_string_buffer(image, len(image))
+drv = ctypes.CDLL(None)
+mod = ctypes.c_void_p(0)
+drv.cuModuleLoadData.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+assert drv.cuModuleLoadData(ctypes.byref(mod), buf) == 0
+mock = ctypes.CDLL(MOCK)
+mock.cuModuleGetFunction.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_char_p]
+fn = ctypes.c_void_p(0)
+assert mock.cuModuleGetFunction(ctypes.byref(fn), mod, b"fblazy_k") == 0
+h, name = c.identify_function(fn.value)
+c.mark_binary_used(h)
+fb.pack_fatbins_to_folder(ARCH)
+c.set_allocation_region(0x600000000000, 1 << 30)
+p = c.region_alloc(1 << 20)
+prm = [{"index": 0, "offset": 0, "size": 8, "value_hex": p.to_bytes(8, "little").hex()},
+       {"index": 1, "offset": 8, "size": 4, "value_hex": "07000000"}]
+node = {"id": 0, "type": "KernelNode", "params": {"blockDimX": 32, "blockDimY": 1, "blockDimZ": 1, "gridDimX": 1,
+        "gridDimY": 1, "gridDimZ": 1, "sharedMemBytes": 0, "kernelParams": prm, "function_name": name,
+        "kernel_source_binary_hash": f"{h:016x}"}}
+d = c.graph_from_json_text(json.dumps({"nodes": [node], "dependencies": [], "topology_key": "", "generators": [],
+                                       "num_events": 0}))
+c.recompute_topology_key(d)
+d.save(os.path.join(ARCH, "graph_0.json"))
+print("SAVE_OK")
+"""
+
+LAZY_LOAD = r"""
+import ctypes, os, sys
+sys.path.insert(0, ROOT)
+import foundry_b200 as fb
+c = fb.core()
+fb.set_skip_fatbin_processing(True)
+fb.load_cuda_modules_and_libraries(ARCH)
+c.set_allocation_region(0x600000000000, 1 << 30)
+c.region_alloc(1 << 20)
+path = os.path.join(ARCH, "graph_0.json")
+pending = c.start_graph_builds([path], 1)  # the library has not loaded its kernel yet
+pending.wait()                             # background builds defer the graph instead of failing
+if LOAD_LIBRARY:
+    image = b"FBMOCK\nfblazy_k:8,4\n\n" + bytes(64)
+    buf = ctypes.create_string_buffer(image, len(image))
+    drv = ctypes.CDLL(None)
+    mod = ctypes.c_void_p(0)
+    drv.cuModuleLoadData.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+    assert drv.cuModuleLoadData(ctypes.byref(mod), buf) == 0
+    g = pending.finish_one(0)
+    g.launch(0)
+    print("LOAD_OK")
+else:
+    try:
+        pending.finish_one(0)
+        raise AssertionError("resolved a kernel no library loaded")
+    except RuntimeError as e:
+        assert "persisted by name" in str(e), e
+    print("LOAD_REFUSED_OK")
+"""
+
+
+def test_by_name_kernels_resolve_when_the_graph_is_finished(tmp_path):
+    """A graph whose kernel a library loads lazily (persisted by entry name)
+    restores when its library has loaded the kernel by finish time, even if
+    the background builds started earlier; without it, finish_one fails with
+    a clear message."""
+    arch = str(tmp_path / "arch")
+    os.makedirs(arch)
+    mock = os.path.join(LIB, "libfoundry_mockcuda.so")
+    env = dict(os.environ, FOUNDRY_CUDA_DRIVER=mock, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="",
+               LD_PRELOAD=os.path.join(LIB, "libfoundry_hook.so"))
+    head = f"ROOT={ROOT!r}; ARCH={arch!r}; MOCK={mock!r}\n"
+    runs = ((LAZY_SAVE, "SAVE_OK", ""), (LAZY_LOAD, "LOAD_OK", "LOAD_LIBRARY = True\n"),
+            (LAZY_LOAD, "LOAD_REFUSED_OK", "LOAD_LIBRARY = False\n"))
+    for script, ok, extra in runs:
+        r = subprocess.run([sys.executable, "-c", head + extra + script], env=env, capture_output=True, text=True,
+                           timeout=120)
+        assert r.returncode == 0 and ok in r.stdout, r.stdout + r.stderr

@@ -115,8 +115,8 @@ import vllm.v1.worker.gpu_model_runner as mr
 import types, torch
 from vllm.config import CUDAGraphMode
 R = mr.GPUModelRunner
-orig = (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, R.capture_model, R.load_model,
-        R._dummy_run, torch.cuda.get_device_capability)
+orig = (cg.CUDAGraphWrapper.__call__, gw.init_worker_distributed_environment, gw.kernel_warmup, R.capture_model,
+        R.load_model, R._dummy_run, R.initialize_kv_cache, torch.cuda.get_device_capability)
 from foundry_b200.integration import runtime
 from foundry_b200.integration.vllm import install_hooks, installed, uninstall_hooks
 from foundry_b200.integration.vllm.hooks import is_sampler_warmup_run
@@ -124,8 +124,8 @@ from foundry_b200.integration.config import GraphExtensionConfig
 cfg = GraphExtensionConfig.from_dict({"mode": "save"})
 install_hooks(cfg)
 assert installed()
-now = (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, R.capture_model, R.load_model,
-       R._dummy_run, torch.cuda.get_device_capability)
+now = (cg.CUDAGraphWrapper.__call__, gw.init_worker_distributed_environment, gw.kernel_warmup, R.capture_model,
+       R.load_model, R._dummy_run, R.initialize_kv_cache, torch.cuda.get_device_capability)
 assert all(a is not b for a, b in zip(now, orig)), now
 # only the eager sampler warm-up forward is replaced
 none = CUDAGraphMode.NONE
@@ -140,8 +140,8 @@ fake = types.SimpleNamespace(model_config=types.SimpleNamespace(get_hidden_size=
 hs, last = R._dummy_run(fake, 4, cudagraph_runtime_mode=none, skip_eplb=True)
 assert hs.shape == (4, 16) and not hs.any() and last is hs
 uninstall_hooks()
-assert (cg.CUDAGraphWrapper.__call__, gw.Worker.init_device, gw.kernel_warmup, R.capture_model, R.load_model,
-        R._dummy_run, torch.cuda.get_device_capability) == orig
+assert (cg.CUDAGraphWrapper.__call__, gw.init_worker_distributed_environment, gw.kernel_warmup, R.capture_model,
+        R.load_model, R._dummy_run, R.initialize_kv_cache, torch.cuda.get_device_capability) == orig
 print("HOOKS_OK")
 """
 

@@ -67,6 +67,13 @@ def test_numeric_save_load_bit_exact(saved):
     assert a[1] == pytest.approx(1 + 2 * 5.25 * 0.5 * 97)
 
 
+def test_programmatic_dependency_edges_round_trip(tmp_path):
+    """Graphs captured with programmatic dependent launch (vLLM's and
+    FlashInfer's kernels use it) carry edge data that the plain edge query
+    cannot return; it is persisted and restored."""
+    assert "PDL OK" in _run("pdl", str(tmp_path))
+
+
 def test_generator_records_and_relocation(saved):
     assert "RNG OK" in _run("rng", saved)
 
