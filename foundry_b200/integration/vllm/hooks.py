@@ -32,6 +32,11 @@
                                    graph its own executable on a background
                                    thread; SAVE: manifest + packed modules +
                                    final offset
+  prepare_communication_buffer_for_model  LOAD: initialise the reloaded
+                                   images that need NVSHMEM once DeepEP has
+                                   bootstrapped it (when the target exists)
+  DeepEPLLAll2AllManager._make_all2all_kwargs  fabric-handle buffers, no
+                                   NVLink buffer (when DeepEP is present)
   torch.cuda.get_device_capability answered from NVML, so importing a kernel
                                    library in the API-server process does not
                                    create a CUDA context there (a process that
@@ -268,6 +273,52 @@ def _capture_model(self, *a, **k):
     return r
 
 
+def _prepare_comm_buffer(model, *a, **k):
+    """After vLLM builds its communication buffers (DeepEP's Buffer bootstraps
+    NVSHMEM there), LOAD initialises the reloaded images that need NVSHMEM;
+    earlier, the NVSHMEM runtime is not up. Parity: reference
+    vllm/hooks.py:350-374."""
+    r = _originals["prepare_communication_buffer_for_model"](model, *a, **k)
+    if runtime.mode() == GraphExtensionMode.LOAD:
+        from ... import init_nvshmem_for_loaded_modules
+
+        t = time.perf_counter()
+        n = init_nvshmem_for_loaded_modules()
+        log.info("[foundry TIMING] init_nvshmem_for_loaded_modules: %.3f s (%d images)", time.perf_counter() - t, n)
+    return r
+
+
+def _deepep_kwargs(self, *a, **k):
+    """DeepEP low-latency buffers: fabric-handle memory (which the region
+    sees and maps like its own) and no NVLink buffer, whenever graphs are
+    persisted. Parity: reference vllm/hooks.py:682-706."""
+    out = _originals["DeepEPLLAll2AllManager._make_all2all_kwargs"](self, *a, **k)
+    if isinstance(out, dict) and runtime.mode() != GraphExtensionMode.NONE:
+        out["use_fabric"] = True
+        out["num_nvl_bytes"] = 0
+    return out
+
+
+def _optional_targets() -> list[tuple[str, object, str, object]]:
+    """(key, owner, attribute, replacement) of patches whose targets vLLM
+    builds may not have (absent targets are skipped)."""
+    out = []
+    import vllm.v1.worker.gpu_model_runner as mr
+
+    if hasattr(mr, "prepare_communication_buffer_for_model"):
+        out.append(("prepare_communication_buffer_for_model", mr, "prepare_communication_buffer_for_model",
+                     _prepare_comm_buffer))
+    try:
+        from vllm.distributed.device_communicators import all2all
+    except Exception:  # noqa: BLE001 - optional component
+        all2all = None
+    cls = getattr(all2all, "DeepEPLLAll2AllManager", None) if all2all is not None else None
+    if cls is not None and hasattr(cls, "_make_all2all_kwargs"):
+        out.append(("DeepEPLLAll2AllManager._make_all2all_kwargs", cls, "_make_all2all_kwargs", _deepep_kwargs))
+    return out
+
+
+_optional_installed: list[tuple[str, object, str]] = []
 _config: GraphExtensionConfig | None = None
 
 
@@ -300,6 +351,10 @@ def install_hooks(config: GraphExtensionConfig | str) -> None:
     mr.GPUModelRunner.load_model = _load_model
     mr.GPUModelRunner._dummy_run = _dummy_run
     mr.GPUModelRunner.initialize_kv_cache = _initialize_kv_cache
+    for key, owner, attr, repl in _optional_targets():
+        _originals[key] = getattr(owner, attr)
+        setattr(owner, attr, repl)
+        _optional_installed.append((key, owner, attr))
     log.info("[foundry] vLLM hooks installed (mode %s)", config.mode.value)
 
 
@@ -315,6 +370,9 @@ def uninstall_hooks() -> None:
     mr.GPUModelRunner.load_model = _originals.pop("GPUModelRunner.load_model")
     mr.GPUModelRunner._dummy_run = _originals.pop("GPUModelRunner._dummy_run")
     mr.GPUModelRunner.initialize_kv_cache = _originals.pop("GPUModelRunner.initialize_kv_cache")
+    while _optional_installed:
+        key, owner, attr = _optional_installed.pop()
+        setattr(owner, attr, _originals.pop(key))
     import torch
 
     torch.cuda.get_device_capability = _originals.pop("torch.cuda.get_device_capability")

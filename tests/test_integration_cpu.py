@@ -223,3 +223,41 @@ def test_vllm_serve_launcher_environment():
     assert env["PYTHONPATH"].split(os.pathsep)[0].endswith(os.path.join("vllm", "_site"))
     assert env["NCCL_CUMEM_ENABLE"] == "0" and env["NCCL_NVLS_ENABLE"] == "0"
     assert "libfoundry_hook.so" in env.get("LD_PRELOAD", "")
+
+
+def test_vllm_deepep_and_nvshmem_flush_patches():
+    """The DeepEP kwargs patch forces fabric buffers whenever graphs are
+    persisted; the communication-buffer patch initialises NVSHMEM images on
+    LOAD only, after the original ran."""
+    import types
+
+    from foundry_b200.integration import runtime
+    from foundry_b200.integration.config import GraphExtensionConfig
+    from foundry_b200.integration.vllm import hooks
+
+    saved = dict(hooks._originals)
+    calls = []
+    try:
+        hooks._originals["DeepEPLLAll2AllManager._make_all2all_kwargs"] = lambda self: {"use_fabric": False,
+                                                                                          "num_nvl_bytes": 1 << 30}
+        hooks._originals["prepare_communication_buffer_for_model"] = lambda model: calls.append(("orig", model))
+        runtime._state = runtime.ExtensionState(GraphExtensionConfig.from_dict({"mode": "save"}), 0)
+        assert hooks._deepep_kwargs(object()) == {"use_fabric": True, "num_nvl_bytes": 0}
+        hooks._prepare_comm_buffer("m")
+        assert calls == [("orig", "m")]  # SAVE: no NVSHMEM init
+        runtime._state = runtime.ExtensionState(GraphExtensionConfig.from_dict({"mode": "none"}), 0)
+        assert hooks._deepep_kwargs(object())["use_fabric"] is False
+        runtime._state = runtime.ExtensionState(GraphExtensionConfig.from_dict({"mode": "load"}), 0)
+        import foundry_b200
+
+        orig_init = foundry_b200.init_nvshmem_for_loaded_modules
+        foundry_b200.init_nvshmem_for_loaded_modules = lambda: calls.append("nvshmem") or 3
+        try:
+            hooks._prepare_comm_buffer("m2")
+        finally:
+            foundry_b200.init_nvshmem_for_loaded_modules = orig_init
+        assert calls[-2:] == [("orig", "m2"), "nvshmem"]
+    finally:
+        hooks._originals.clear()
+        hooks._originals.update(saved)
+        runtime.reset()
