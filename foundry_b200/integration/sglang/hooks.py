@@ -22,13 +22,22 @@ required. The patches, in the order an SGLang worker reaches them:
                                        each capture return None instead of
                                        running; the captured graph is saved
                                        under its batch size (and stream index)
-  CudaGraphRunner.capture              SAVE: manifest + packed modules + final
-                                       offset after the capture loop; LOAD:
-                                       replaces the loop: preallocate, start
-                                       all builds, finish them in SAVE order
-                                       into ``graphs`` / ``output_buffers``,
-                                       then give each its own executable on a
-                                       background thread
+  CudaGraphRunner.capture              both: create the DeepEP buffer first
+                                       (when DeepEP is the MoE all-to-all);
+                                       SAVE: with DeepEP one uncaptured
+                                       forward per batch size, then the
+                                       FlashInfer per-batch-size metadata
+                                       pre-pass and the capture loop reusing
+                                       it; manifest + packed modules + final
+                                       offset after the loop. LOAD: replaces
+                                       the loop: graph pool, preallocate, the
+                                       same pre-pass, start all builds,
+                                       finish them in SAVE order into
+                                       ``graphs`` / ``output_buffers``, set
+                                       DeepEP's captured dispatch mode, then
+                                       give each graph its own executable on
+                                       a background thread (pre-pass and
+                                       DeepEP: prepass.py)
   Engine._launch_scheduler_processes,
   DataParallelController.launch_tensor_parallel_group
                                        export LD_PRELOAD (interposer) and the
@@ -38,9 +47,7 @@ Parity: reference python/foundry/integration/sglang/hooks.py:67-594 and
 config.py:134-142 (workspace rank with and without DP attention). SGLang is
 not installed on this build's image: the patches are tested against a fake
 SGLang package with the same class and method names
-(tests/test_sglang_hooks_cpu.py), not against SGLang itself. Not built: the
-FlashInfer per-batch-size metadata pre-pass and the DeepEP buffer bootstrap
-of the reference (both need SGLang's attention and MoE internals).
+(tests/test_sglang_hooks_cpu.py), not against SGLang itself.
 """
 
 from __future__ import annotations
@@ -53,7 +60,9 @@ import time
 from dataclasses import dataclass
 from typing import Callable
 
+from ...allocation_region import resume_allocation_region, stop_allocation_region
 from .. import graph_ops, runtime
+from . import prepass
 from ..config import GraphExtensionConfig, GraphExtensionMode
 
 log = logging.getLogger("foundry")
@@ -190,8 +199,14 @@ def _create_device_graph(orig):
     return wrapped
 
 
+# True while SAVE's DeepEP warm-up pass runs the capture loop without capturing.
+_warmup_pass = [False]
+
+
 def _capture_graph(orig):
     def wrapped(self, graph, pool, stream, run_once_fn):
+        if _warmup_pass[0]:
+            return run_once_fn()  # one plain forward: lazy initialisation happens outside any capture
         if _mode() == GraphExtensionMode.SAVE:
             from ...graphs import graph as foundry_graph
 
@@ -208,6 +223,8 @@ def _capture_one_batch_size(orig):
         if _mode() != GraphExtensionMode.SAVE:
             return orig(self, bs, forward, stream_idx, *a, **k)
         graph, output = orig(self, bs, suppress_first_calls(forward, 2), stream_idx, *a, **k)
+        if _warmup_pass[0]:
+            return graph, output
         st = runtime.state()
         key = graph_ops.GraphKey("FULL", int(bs), int(bs), True, False, stream_idx)
         graph.save(os.path.join(st.config.workspace_dir, key.filename(st.capture_index)), output)
@@ -222,13 +239,7 @@ def _load_all_graphs(runner) -> int:
     ``runner.output_buffers`` in SAVE's capture order."""
     from ...graphs import CUDAGraph
 
-    cgr = importlib.import_module(_CGR)
-    if hasattr(cgr, "get_global_graph_memory_pool") and cgr.get_global_graph_memory_pool() is None:
-        import torch
-
-        cgr.set_global_graph_memory_pool(torch.cuda.graph_pool_handle())
     st = runtime.state()
-    runtime.preallocate_for_load_mode()
     plan = graph_ops.start_graph_builds(st.config.workspace_dir)
     by_index = sorted(plan.key_to_index.items(), key=lambda kv: kv[1])
     for key, idx in by_index:
@@ -240,21 +251,96 @@ def _load_all_graphs(runner) -> int:
     return len(by_index)
 
 
+def _bind_graph_pool() -> None:
+    """LOAD: the graph memory pool SGLang's capture loop would have created
+    (its replay and its NCCL allocator look the pool up)."""
+    cgr = importlib.import_module(_CGR)
+    if not hasattr(cgr, "get_global_graph_memory_pool"):
+        return
+    if cgr.get_global_graph_memory_pool() is None:
+        import torch
+
+        cgr.set_global_graph_memory_pool(torch.cuda.graph_pool_handle())
+    try:
+        alloc = importlib.import_module("sglang.srt.distributed.device_communicators.pynccl_allocator")
+    except ImportError:
+        return
+    if hasattr(alloc, "set_graph_pool_id"):
+        alloc.set_graph_pool_id(cgr.get_global_graph_memory_pool())
+
+
+def _run_warmup_pass(runner, orig) -> None:
+    """SAVE with DeepEP: one plain forward per batch size through SGLang's
+    own capture loop, nothing captured or saved, so the lazy initialisation
+    SGLang's (suppressed) warm-up forwards would do (DeepGEMM kernels for
+    each shape and the like) happens before the real capture. The region is
+    paused meanwhile: LOAD runs no such pass, so its activations must not
+    move the cursor; the caller empties the allocator cache afterwards."""
+    import torch
+
+    saved = runner.graphs, runner.output_buffers
+    runner.graphs, runner.output_buffers = {}, {}
+    _warmup_pass[0] = True
+    t0 = time.perf_counter()
+    stop_allocation_region()
+    try:
+        orig(runner)
+        if torch.cuda.is_initialized():
+            torch.cuda.synchronize()
+    finally:
+        resume_allocation_region()
+        _warmup_pass[0] = False
+        runner.graphs, runner.output_buffers = saved
+    log.info("[foundry] SGLang DeepEP warm-up pass: %.3f s", time.perf_counter() - t0)
+
+
 def _capture(orig):
     def wrapped(self, *a, **k):
         m = _mode()
+        if m == GraphExtensionMode.NONE:
+            return orig(self, *a, **k)
+        import torch
+
+        t0 = time.perf_counter()
+        # The same steps, in the same order, up to the capture loop (SAVE) or
+        # the graph builds (LOAD), so that what they allocate in the region
+        # lands at the same offsets in both runs.
+        deepep = prepass.ensure_deepep_buffer(self)
         if m == GraphExtensionMode.LOAD:
-            t0 = time.perf_counter()
-            n = _load_all_graphs(self)
-            runtime.capture_final_alloc_offset()
-            graph_ops.materialize_loaded(background=True)
-            log.info("[foundry TIMING] SGLang LOAD of %d graphs: %.3f s", n, time.perf_counter() - t0)
-            return None
-        r = orig(self, *a, **k)
+            _bind_graph_pool()
+            runtime.preallocate_for_load_mode()
+        per_bs = prepass.uses_per_batch_metadata(getattr(self, "attn_backend", None))
+        restore = None
+        if per_bs:
+            if m == GraphExtensionMode.SAVE:
+                restore = prepass.install_reuse(self)  # pre-pass, then the capture loop reuses it
+            else:
+                prepass.attention_metadata_prepass(self)
+        try:
+            if deepep:
+                if m == GraphExtensionMode.SAVE:
+                    _run_warmup_pass(self, orig)
+                torch.cuda.empty_cache()  # drops the warm-up pass's segments; LOAD mirrors the allocator state
+            if m == GraphExtensionMode.SAVE:
+                r = orig(self, *a, **k)
+        finally:
+            if restore is not None:
+                restore()
         if m == GraphExtensionMode.SAVE:
             graph_ops.finalize_save()
             runtime.capture_final_alloc_offset()
-        return r
+            return r
+        n = _load_all_graphs(self)
+        if not per_bs and hasattr(self, "attn_backend"):
+            # views over the backend's fixed workspace, filled by the loop LOAD replaces
+            prepass.attention_metadata_prepass(self)
+        adapter = getattr(self, "deepep_adapter", None)
+        if adapter is not None:
+            adapter.capture(is_extend_in_batch=False)  # the dispatch mode the saved graphs were captured in
+        runtime.capture_final_alloc_offset()
+        graph_ops.materialize_loaded(background=True)
+        log.info("[foundry TIMING] SGLang LOAD of %d graphs: %.3f s", n, time.perf_counter() - t0)
+        return None
 
     return wrapped
 

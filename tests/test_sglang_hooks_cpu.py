@@ -4,12 +4,15 @@ installed on this image), on the mock CUDA driver: install and uninstall,
 workspace rank with and without DP attention, device binding + region +
 scratch skip around init_torch_distributed, memory-pool config recorded in
 SAVE and applied in LOAD, kernel warm-up skipped, warm-up forwards
-suppressed, spawn sites exporting the preload and config."""
+suppressed, spawn sites exporting the preload and config, the FlashInfer
+per-batch-size metadata pre-pass and the DeepEP buffer bootstrap."""
 
 import os
 import subprocess
 import sys
 import textwrap
+
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 MOCK = os.path.join(ROOT, "foundry_b200", "lib", "libfoundry_mockcuda.so")
@@ -212,3 +215,192 @@ def test_serve_launcher_environment(tmp_path):
     assert env["PYTHONPATH"].split(os.pathsep)[-1] == "/x"
     assert env["NCCL_CUMEM_ENABLE"] == "0" and env["NCCL_NVLS_ENABLE"] == "1"  # explicit settings win
     assert "libfoundry_hook.so" in env.get("LD_PRELOAD", "")
+
+
+# A fake SGLang whose capture loop builds attention metadata per batch size the
+# way SGLang's FlashInfer backend does (a new wrapper object per call), and
+# whose MoE backend can be DeepEP: the pre-pass and the DeepEP bootstrap of
+# foundry_b200/integration/sglang/prepass.py against it.
+PREPASS_FAKE = {
+    "sglang/srt/layers/__init__.py": "",
+    "sglang/srt/layers/attention/__init__.py": "",
+    "sglang/srt/layers/attention/flashinfer_backend.py": """
+        EVENTS = []
+        class DecodeMetadata:
+            def __init__(self, wrappers):
+                self.decode_wrappers = wrappers
+        class PrefillMetadata:
+            def __init__(self, wrappers, use_ragged, extend_no_prefix):
+                self.prefill_wrappers = wrappers
+        class _Updater:
+            def update(self, req_pool_indices, seq_lens, seq_lens_cpu, seq_lens_sum, decode_wrappers=None,
+                       encoder_lens=None, spec_info=None, fixed_split_size=None, disable_split_kv=None):
+                EVENTS.append(("plan", len(seq_lens), id(decode_wrappers)))
+        class FlashInferAttnBackend:
+            def __init__(self):
+                self.indices_updater_decode = _Updater()
+                self.decode_cuda_graph_metadata = {}
+                self.forward_metadata = None
+                self.disable_cuda_graph_kv_split = False
+            def init_forward_metadata_capture_cuda_graph(self, bs, num_tokens, req_pool_indices, seq_lens,
+                                                         encoder_lens, forward_mode, spec_info):
+                wrappers = [object()]  # SGLang allocates a fresh workspace here
+                EVENTS.append(("alloc", bs))
+                self.decode_cuda_graph_metadata[bs] = wrappers
+                self.forward_metadata = DecodeMetadata(wrappers)
+        class FixedWorkspaceBackend:  # fa3-like: metadata are views over one start-up workspace
+            def __init__(self):
+                self.decode_cuda_graph_metadata = {}
+            def init_forward_metadata_capture_cuda_graph(self, bs, *a):
+                EVENTS.append(("view", bs))
+                self.decode_cuda_graph_metadata[bs] = "view"
+    """,
+    "sglang/srt/layers/moe/__init__.py": "",
+    "sglang/srt/layers/moe/utils.py": """
+        import os
+        class _Backend:
+            def is_deepep(self):
+                return os.environ.get("FAKE_DEEPEP") == "1"
+        def get_moe_a2a_backend():
+            return _Backend()
+    """,
+    "sglang/srt/layers/moe/token_dispatcher/__init__.py": "",
+    "sglang/srt/layers/moe/token_dispatcher/deepep.py": """
+        from sglang.srt.layers.attention.flashinfer_backend import EVENTS
+        class DeepEPBuffer:
+            _buffer = None
+        class _LowLatency:
+            def _get_buffer(self):
+                if DeepEPBuffer._buffer is None:
+                    EVENTS.append(("deepep_buffer",))
+                    DeepEPBuffer._buffer = object()
+                return DeepEPBuffer._buffer
+        class DeepEPDispatcher:
+            def __init__(self):
+                self._low_latency_dispatcher = _LowLatency()
+        class MaybeTboDeepEPDispatcher:
+            def __init__(self):
+                self._inners = [DeepEPDispatcher()]
+    """,
+}
+
+PREPASS_SCRIPT = r"""
+import os, sys, types
+sys.path.insert(0, FAKE_ROOT)
+sys.path.insert(0, ROOT)
+from foundry_b200.integration import runtime
+from foundry_b200.integration.sglang import hooks as H, prepass
+import sglang.srt.model_executor.model_runner as mr
+import sglang.srt.model_executor.cuda_graph_runner as cgr
+import sglang.srt.layers.attention.flashinfer_backend as fi
+from sglang.srt.layers.moe.token_dispatcher import deepep
+
+SIZES = [1, 2, 4, 8]
+
+class Mode:
+    def is_decode_or_idle(self): return True
+    def is_target_verify(self): return False
+    def is_draft_extend(self): return False
+
+class Adapter:
+    def capture(self, is_extend_in_batch):
+        fi.EVENTS.append(("adapter_capture", is_extend_in_batch))
+
+class Layer:
+    def __init__(self):
+        self.dispatcher = deepep.MaybeTboDeepEPDispatcher()
+
+class Model:
+    def modules(self):
+        return [object(), Layer(), Layer()]
+
+def real_capture(self):
+    # the upstream loop: per batch size, metadata init then one forward
+    for bs in reversed(self.capture_bs):
+        self.attn_backend.init_forward_metadata_capture_cuda_graph(
+            bs, bs, self.buffers.req_pool_indices[:bs], self.buffers.seq_lens[:bs], None, Mode(), None)
+        fi.EVENTS.append(("forward", bs, H._warmup_pass[0], deepep.DeepEPBuffer._buffer is not None))
+    return "captured"
+cgr.CudaGraphRunner.capture = real_capture
+
+toml = os.path.join(TMP, MODE + ".toml")
+with open(toml, "w") as fh:
+    fh.write('mode = "%s"\nbase_addr = "0x620000000000"\nregion_size = "1GB"\nscratch_space_size = "32MB"\n'
+             'workspace_root = "%s"\n' % (MODE, os.path.join(TMP, "arch")))
+H.install_hooks(toml)
+runtime.setup_graph_extension(H._config, 0)
+
+g = cgr.CudaGraphRunner()
+g.graphs, g.output_buffers = {"keep": 1}, {}
+g.capture_bs = SIZES
+g.num_tokens_per_bs = 1
+g.capture_forward_mode = Mode()
+g.get_spec_info = lambda n: None
+g.buffers = types.SimpleNamespace(req_pool_indices=list(range(8)), seq_lens=__import__("torch").ones(8, dtype=__import__("torch").int32),
+                                  encoder_lens=None)
+g.attn_backend = fi.FlashInferAttnBackend() if BACKEND == "flashinfer" else fi.FixedWorkspaceBackend()
+g.model_runner = types.SimpleNamespace(model=Model())
+g.deepep_adapter = Adapter()
+real_init = g.attn_backend.init_forward_metadata_capture_cuda_graph
+
+# the warm-up flag turns the graph capture into one plain forward
+H._warmup_pass[0] = True
+assert cgr.CudaGraphRunner._capture_graph(g, None, None, None, lambda: 5) == 5
+H._warmup_pass[0] = False
+
+r = g.capture()
+ev = fi.EVENTS
+allocs = [e[1] for e in ev if e[0] == "alloc"]
+deep = os.environ.get("FAKE_DEEPEP") == "1"
+if deep:
+    assert ev[0] == ("deepep_buffer",), ev  # before any metadata or forward
+else:
+    assert ("deepep_buffer",) not in ev
+if BACKEND == "flashinfer":
+    assert allocs == [8, 4, 2, 1], allocs  # pre-pass only, largest first; the loops allocate nothing more
+    assert g.attn_backend.init_forward_metadata_capture_cuda_graph == real_init  # shim removed after capture
+if MODE == "save":
+    assert r == "captured" and g.graphs == {"keep": 1}
+    fw = [e for e in ev if e[0] == "forward"]
+    if deep:  # a warm-up pass (flag set, buffer already there), then the real loop
+        assert [e[1:] for e in fw] == [(b, True, True) for b in (8, 4, 2, 1)] + [(b, False, True) for b in (8, 4, 2, 1)], fw
+    else:
+        assert [e[1:3] for e in fw] == [(b, False) for b in (8, 4, 2, 1)], fw
+    if BACKEND == "flashinfer":
+        plans = [e for e in ev if e[0] == "plan"]
+        assert len(plans) == len(fw), (plans, fw)  # each loop iteration re-planned a pre-pass wrapper
+else:
+    assert r is None and not [e for e in ev if e[0] == "forward"]  # LOAD runs no capture loop
+    if BACKEND != "flashinfer":
+        assert [e[1] for e in ev if e[0] == "view"] == [8, 4, 2, 1]
+    assert ("adapter_capture", False) in ev
+print("PREPASS_OK", " ".join(repr(e) for e in ev if e[0] in ("alloc", "deepep_buffer")))
+H.uninstall_hooks()
+"""
+
+
+
+@pytest.mark.parametrize("backend", ["flashinfer", "fixed"])
+@pytest.mark.parametrize("deep", ["0", "1"])
+def test_sglang_prepass_and_deepep_bootstrap(tmp_path, backend, deep):
+    """SAVE and LOAD build FlashInfer's per-batch-size metadata in the same
+    order before the capture loop / graph load (SAVE's loop then reuses it),
+    create the DeepEP buffer first, run SAVE's DeepEP warm-up pass with the
+    flag that makes the capture a plain forward, and set DeepEP's captured
+    mode after LOAD; fixed-workspace backends get their views after LOAD."""
+    fake = tmp_path / "fake"
+    _fake_tree(fake)
+    for rel, src in PREPASS_FAKE.items():
+        p = fake / rel
+        p.parent.mkdir(parents=True, exist_ok=True)
+        p.write_text(textwrap.dedent(src))
+    env = dict(os.environ, FOUNDRY_CUDA_DRIVER=MOCK, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="", FAKE_DEEPEP=deep)
+    env.pop("LD_PRELOAD", None)
+    outs = {}
+    for mode in ("save", "load"):
+        code = (f"ROOT={ROOT!r}; TMP={str(tmp_path)!r}; FAKE_ROOT={str(fake)!r}; MODE={mode!r}; "
+                f"BACKEND={backend!r}\n" + PREPASS_SCRIPT)
+        r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=180)
+        assert r.returncode == 0 and "PREPASS_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+        outs[mode] = [line for line in r.stdout.splitlines() if line.startswith("PREPASS_OK")][0]
+    assert outs["save"] == outs["load"]  # same region-visible steps in the same order
