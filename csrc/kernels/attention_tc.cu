@@ -33,6 +33,7 @@ constexpr int PAGE = 64;
 constexpr int CHUNK = 128;       // tokens per MMA chunk (two pages)
 constexpr int NH = 16;           // padded head count (MMA N)
 constexpr int BOX_BYTES = 64 * 128;              // 64 tokens x 64 dims x 2 B
+constexpr int SUB_BYTES = 16 * 128;              // 16 tokens x 64 dims x 2 B (tail boxes)
 constexpr int KV_BYTES = 2 * 2 * BOX_BYTES;      // one chunk of K (or V): 2 pages x 2 dim-halves
 constexpr int STAGE_BYTES = 2 * KV_BYTES;        // K + V
 constexpr int HALF_STRIDE = 2 * BOX_BYTES;       // dim-half block: 128 tokens x 128 B
@@ -43,10 +44,13 @@ struct Smem {
   uint8_t kv[STAGES][STAGE_BYTES];  // per stage: K [half][128 tok][128B], V same
   uint8_t q[QP_BYTES];
   uint8_t p[QP_BYTES];
-  uint64_t full[STAGES], empty[STAGES];
+  // K and V of a stage fill and drain separately: the next chunk's K loads
+  // while this chunk's softmax and PV run.
+  uint64_t kfull[STAGES], vfull[STAGES], kempty[STAGES], vempty[STAGES];
   uint64_t s_full, s_empty, p_full, o_full, o_empty, q_ready;
   float red_max[4][8];
   float red_l[4][8];
+  float alpha[8];  // this chunk's rescale factor per head (the same in every softmax thread)
   uint32_t tmem;
   int abort;
 };
@@ -102,7 +106,8 @@ __device__ __forceinline__ Item decode_item(int idx, int Hkv, int S, int chunks_
 }
 
 template <int G, int STAGES>
-__device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensorMap* tmV, const bf16* __restrict__ q,
+__device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensorMap* tmV, const CUtensorMap* tmK16,
+                                          const CUtensorMap* tmV16, const bf16* __restrict__ q,
                                           const int* __restrict__ block_tables, int max_blocks,
                                           const int* __restrict__ seq_lens, bf16* __restrict__ out,
                                           float* __restrict__ o_part, float* __restrict__ ml_part, int B, int Hkv,
@@ -115,8 +120,10 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.kfull[s], 1);
+      mbar_init(&sm.vfull[s], 1);
+      mbar_init(&sm.kempty[s], 1);
+      mbar_init(&sm.vempty[s], 1);
     }
     mbar_init(&sm.s_full, 1);
     mbar_init(&sm.o_full, 1);
@@ -131,6 +138,8 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(tmK);
     tma_prefetch_desc(tmV);
+    tma_prefetch_desc(tmK16);
+    tma_prefetch_desc(tmV16);
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem, 32);
@@ -157,34 +166,60 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
         const Item it = decode_item(idx, Hkv, S, chunks_per_split, seq_lens);
         const int* bt = block_tables + static_cast<size_t>(it.b) * max_blocks;
         for (int c = it.c0; c < it.c1; ++c) {
-          if (!mbar_wait(&sm.empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
-            sm.abort = 1;
-            break;
+          // Only the live tokens of the chunk are read: whole pages, and the
+          // last page in 16-token row blocks (a 16-row box at a 2 KB offset
+          // lands in the same 128B-swizzled image as the rows of a full box).
+          // Rows not loaded keep stale data: their scores are masked and their
+          // V rows zeroed by the softmax warps before the PV MMA reads them.
+          const int live = min(it.tok1, (c + 1) * CHUNK) - c * CHUNK;
+          int blocks[2];  // 16-token blocks loaded per page (4 = the whole page)
+          int rows[2];
+#pragma unroll
+          for (int pg = 0; pg < 2; ++pg) {
+            const int n = min(max(live - pg * PAGE, 0), PAGE);
+            blocks[pg] = (n + 15) / 16;
+            rows[pg] = blocks[pg] ? (bt[2 * c + pg] * Hkv + it.kvh) * PAGE : 0;
           }
-          mbar_arrive_expect_tx(&sm.full[stage], STAGE_BYTES);
-          const int p0 = 2 * c;
-          const int np = (it.seq_len + PAGE - 1) / PAGE;
-          // A chunk whose second page does not exist reloads the first page:
-          // the duplicated tokens are masked, and the data stays finite.
-          const int p1 = (p0 + 1 < np) ? p0 + 1 : p0;
-          const int rows[2] = {(bt[p0] * Hkv + it.kvh) * PAGE, (bt[p1] * Hkv + it.kvh) * PAGE};
+          const uint32_t bytes = static_cast<uint32_t>(blocks[0] + blocks[1]) * (2 * SUB_BYTES);  // K or V
           uint8_t* kbuf = sm.kv[stage];
-          uint8_t* vbuf = kbuf + KV_BYTES;
 #pragma unroll
-          for (int pg = 0; pg < 2; ++pg)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              tma_load_2d(kbuf + h * HALF_STRIDE + pg * BOX_BYTES, tmK, &sm.full[stage], h * 64, rows[pg]);
-              tma_load_2d(vbuf + h * HALF_STRIDE + pg * BOX_BYTES, tmV, &sm.full[stage], h * 64, rows[pg]);
+          for (int kv = 0; kv < 2; ++kv) {  // K, then V
+            uint64_t* empty = kv ? &sm.vempty[stage] : &sm.kempty[stage];
+            uint64_t* full = kv ? &sm.vfull[stage] : &sm.kfull[stage];
+            if (!mbar_wait(empty, phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+              sm.abort = 1;
+              continue;  // no copies for this chunk; the loop ends below
             }
+            mbar_arrive_expect_tx(full, bytes);
+            const CUtensorMap* whole = kv ? tmV : tmK;
+            const CUtensorMap* part = kv ? tmV16 : tmK16;
+            uint8_t* buf = kbuf + kv * KV_BYTES;
+#pragma unroll
+            for (int pg = 0; pg < 2; ++pg) {
+              if (blocks[pg] == 0) continue;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint8_t* dst = buf + h * HALF_STRIDE + pg * BOX_BYTES;
+                if (blocks[pg] == 4) {
+                  tma_load_2d(dst, whole, full, h * 64, rows[pg]);
+                } else {
+                  for (int j = 0; j < blocks[pg]; ++j)
+                    tma_load_2d(dst + j * SUB_BYTES, part, full, h * 64, rows[pg] + 16 * j);
+                }
+              }
+            }
+          }
+          if (*(volatile int*)&sm.abort) break;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      // Drain: every issued load has been consumed (or the kernel aborted).
       for (int s = 0; s < STAGES; ++s) {
-        mbar_wait(&sm.empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        mbar_wait(&sm.kempty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        mbar_wait(&sm.vempty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
@@ -207,7 +242,7 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
         if (!mbar_wait(&sm.q_ready, items_done & 1, FB_KERR_TIMEOUT_FULL)) { ok = false; break; }
         ++items_done;
         for (int c = it.c0; c < it.c1; ++c, ++cc) {
-          if (!mbar_wait(&sm.full[stage], phase, FB_KERR_TIMEOUT_FULL) ||
+          if (!mbar_wait(&sm.kfull[stage], phase, FB_KERR_TIMEOUT_FULL) ||
               !mbar_wait(&sm.s_empty, (cc & 1) ^ 1, FB_KERR_TIMEOUT_TMEM)) {
             ok = false;
             break;
@@ -224,8 +259,10 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
                      j > 0 ? 1u : 0u);
           }
           mma_commit(&sm.s_full);
+          mma_commit(&sm.kempty[stage]);  // K is free once QK completes
           if (!mbar_wait(&sm.p_full, cc & 1, FB_KERR_TIMEOUT_TMEM) ||
-              !mbar_wait(&sm.o_empty, (cc & 1) ^ 1, FB_KERR_TIMEOUT_TMEM)) {
+              !mbar_wait(&sm.o_empty, (cc & 1) ^ 1, FB_KERR_TIMEOUT_TMEM) ||
+              !mbar_wait(&sm.vfull[stage], phase, FB_KERR_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
@@ -237,7 +274,7 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
                      id_pv, j > 0 ? 1u : 0u);
           }
           mma_commit(&sm.o_full);
-          mma_commit(&sm.empty[stage]);
+          mma_commit(&sm.vempty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -286,8 +323,8 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
           break;
         }
         tc_fence_after();
-        uint32_t sr[16];
-        tmem_ld16(t_s + lane_base, sr);
+        uint32_t sr[G];  // only the G head columns of S are live
+        tmem_ld_cols<G>(t_s + lane_base, sr);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
@@ -297,7 +334,9 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
         if (!valid) {
           // The PV MMA reads all 128 token rows of V: rows past the sequence
           // hold stale or never-written cache memory, and 0 * NaN = NaN, so
-          // masked rows are zeroed here (the TMA data landed before QK ran).
+          // masked rows are zeroed here, after this chunk's V copies landed
+          // (a 16-row tail box can cover tokens past the end).
+          if (!mbar_wait(&sm.vfull[cc % STAGES], (cc / STAGES) & 1, FB_KERR_TIMEOUT_FULL)) sm.abort = 1;
           uint8_t* vrow = sm.kv[cc % STAGES] + KV_BYTES + r * 128;
 #pragma unroll
           for (int h = 0; h < 2; ++h)
@@ -305,26 +344,26 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
             for (int i = 0; i < 8; ++i)
               reinterpret_cast<uint4*>(vrow + h * HALF_STRIDE)[i] = make_uint4(0, 0, 0, 0);
         }
-        float s[G], cmax[G];
+        float s[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           s[g] = valid ? __uint_as_float(sr[g]) * scale_log2 : -INFINITY;
-          cmax[g] = warp_max(s[g]);
-        }
-        if (lane == 0) {
-#pragma unroll
-          for (int g = 0; g < G; ++g) sm.red_max[quarter][g] = cmax[g];
+          const float cmax = warp_max(s[g]);
+          if (lane == 0) sm.red_max[quarter][g] = cmax;
         }
         named_sync_softmax();
-        float alpha[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           const float mx = fmaxf(fmaxf(sm.red_max[0][g], sm.red_max[1][g]), fmaxf(sm.red_max[2][g], sm.red_max[3][g]));
           const float m_new = fmaxf(m_run[g], mx);
-          alpha[g] = exp2f(m_run[g] - m_new);
+          const float alpha = exp2f(m_run[g] - m_new);
+          // Kept in shared memory until the PV result arrives (registers are
+          // the limit at three CTAs per SM); rewritten next chunk only after
+          // every thread has passed that chunk's first barrier.
+          if (r == 0) sm.alpha[g] = alpha;
           const float p = exp2f(s[g] - m_new);
           m_run[g] = m_new;
-          l_thr[g] = l_thr[g] * alpha[g] + p;
+          l_thr[g] = l_thr[g] * alpha + p;
           *reinterpret_cast<bf16*>(sm.p + qp_offset(g, r)) = f2bf(p);
         }
         fence_proxy_async();
@@ -336,14 +375,14 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
           break;
         }
         tc_fence_after();
-        uint32_t orr[16];
-        tmem_ld16(t_o + lane_base, orr);
+        uint32_t orr[G];
+        tmem_ld_cols<G>(t_o + lane_base, orr);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.o_empty);
 #pragma unroll
-        for (int g = 0; g < G; ++g) o[g] = o[g] * alpha[g] + __uint_as_float(orr[g]);
+        for (int g = 0; g < G; ++g) o[g] = o[g] * sm.alpha[g] + __uint_as_float(orr[g]);
       }
       // l per head: sum over the 128 token lanes.
       float lsum[G];
@@ -387,11 +426,12 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
 
 #define FB_ATTN_TC_INSTANCE(G, ST, CTAS)                                                                         \
   extern "C" __global__ void __launch_bounds__(192, CTAS) fb_decode_attn_tc_g##G##_s##ST(                        \
-      const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const bf16* q,           \
+      const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,                         \
+      const __grid_constant__ CUtensorMap tmK16, const __grid_constant__ CUtensorMap tmV16, const bf16* q,       \
       const int* block_tables, int max_blocks, const int* seq_lens, bf16* out, float* o_part, float* ml_part,    \
       int B, int Hkv, int S, int chunks_per_split, float scale_log2) {                                            \
-    attn_body<G, ST>(&tmK, &tmV, q, block_tables, max_blocks, seq_lens, out, o_part, ml_part, B, Hkv, S,         \
-                     chunks_per_split, scale_log2);                                                               \
+    attn_body<G, ST>(&tmK, &tmV, &tmK16, &tmV16, q, block_tables, max_blocks, seq_lens, out, o_part, ml_part, B, \
+                     Hkv, S, chunks_per_split, scale_log2);                                                       \
   }
 
 // 3-stage ring, one CTA per SM; or a single stage and three CTAs per SM.

@@ -34,15 +34,17 @@ def decode_splits(batch: int, n_kv: int, max_pages: int, sms: int | None = None)
 _tmaps: dict[tuple, bytes] = {}
 
 
-def _cache_tmap(cache: torch.Tensor) -> bytes:
-    """TMA map of a paged cache [blocks, Hkv, 64, 128] viewed as [rows, 128]: 64x64 boxes, 128B swizzle."""
-    key = (cache.data_ptr(), cache.shape)
+def _cache_tmap(cache: torch.Tensor, box_rows: int = 64) -> bytes:
+    """TMA map of a paged cache [blocks, Hkv, 64, 128] viewed as [rows, 128]:
+    64-column x ``box_rows`` boxes, 128B swizzle (64 rows load whole pages, 16
+    rows the live row blocks of a sequence's last page)."""
+    key = (cache.data_ptr(), cache.shape, box_rows)
     m = _tmaps.get(key)
     if m is None:
         from .._native import core
 
         rows = cache.shape[0] * cache.shape[1] * cache.shape[2]
-        m = core().make_tmap_2d(cache.data_ptr(), 9, 128, rows, 256, 64, 64, 3)
+        m = core().make_tmap_2d(cache.data_ptr(), 9, 128, rows, 256, 64, box_rows, 3)
         if len(_tmaps) > 4096:
             _tmaps.clear()
         _tmaps[key] = m
@@ -91,7 +93,8 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         items = b * n_kv * s
         grid = min(items, _rt.sm_count() * ctas_per_sm)
         _rt.launch("attention_tc", f"fb_decode_attn_tc_g{g}_s{stages}", (grid,), (192,), [
-            _cache_tmap(k_cache), _cache_tmap(v_cache), q.data_ptr(), block_tables.data_ptr(),
+            _cache_tmap(k_cache), _cache_tmap(v_cache), _cache_tmap(k_cache, 16), _cache_tmap(v_cache, 16),
+            q.data_ptr(), block_tables.data_ptr(),
             block_tables.shape[1], seq_lens.data_ptr(), out.data_ptr(), ws.o_part.data_ptr(), ws.ml_part.data_ptr(),
             b, n_kv, s, pps // 2, float(scale * LOG2E),
         ], smem=TC_SMEM[stages])
