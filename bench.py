@@ -303,7 +303,7 @@ def main():
     cold = {}
     if not args.skip_cold_start:
         cold = run_cli(["load", *common, "--dist-port", str(port + 19)],
-                       {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns())})["load"]
+                       {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns()), "FOUNDRY_EARLY_CUDA_INIT": str(local)})["load"]
 
     # 2b) Restore at scale: a second archive of 256 decode graphs per rank,
     # SAVE and fresh-process LOAD; the LOAD times until every graph of the
@@ -317,7 +317,7 @@ def main():
         common256[common256.index("--graph-sizes") + 1] = args.restore_graphs
         save256 = run_cli(["save", *common256, "--dist-port", str(port + 23)])["save"]
         load256 = run_cli(["load", *common256, "--dist-port", str(port + 29), "--materialize-all"],
-                          {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns())})["load"]
+                          {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns()), "FOUNDRY_EARLY_CUDA_INIT": str(local)})["load"]
         scale = {"graphs": load256["num_graphs"], "topology_groups": load256["num_groups"],
                  "capture_s": save256.get("capture_s"), "restore_s": load256["restore_s"],
                  "cold_start_first_token_s": load256["cold_start_first_token_s"],
@@ -459,7 +459,8 @@ def main():
                 "cold_start_first_token_s": round(cold_max, 3) if cold else None,
                 "cold_start_restore_s": cold.get("restore_s"),
                 "cold_start_breakdown_s": {k: cold.get(k) for k in ("python_import_s", "modules_s", "arena_s",
-                                                                    "restore_s", "load_total_s")},
+                                                                    "restore_s", "load_total_s",
+                                                                    "cold_start_steps_s", "early_cuda_context")},
                 "prefill_s": round(prefill_s, 3),
                 "restore_at_scale": dict(scale, restore_s=round(scale_restore_max, 4),
                                          cold_start_first_token_s=round(scale_cold_max, 3),

@@ -128,7 +128,7 @@ uintptr_t rt_get_function(uint64_t hash, const std::string& name, int max_dynami
 }
 
 void rt_launch(uintptr_t fn, py::tuple grid, py::tuple block, unsigned smem, uintptr_t stream,
-               py::sequence args, py::tuple cluster) {
+               py::sequence args, py::tuple cluster, bool pdl) {
   CUfunction f = reinterpret_cast<CUfunction>(fn);
   const FuncInfo& info = func_info(f);
   std::vector<uint8_t> buf;
@@ -144,16 +144,25 @@ void rt_launch(uintptr_t fn, py::tuple grid, py::tuple block, unsigned smem, uin
   cfg.blockDimZ = py::len(block) > 2 ? block[2].cast<unsigned>() : 1;
   cfg.sharedMemBytes = smem;
   cfg.hStream = reinterpret_cast<CUstream>(stream);
-  CUlaunchAttribute attr;
-  memset(&attr, 0, sizeof(attr));
+  CUlaunchAttribute attrs[2];
+  memset(attrs, 0, sizeof(attrs));
+  unsigned n = 0;
   if (py::len(cluster) > 0 && cluster[0].cast<unsigned>() > 1) {
-    attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-    attr.value.clusterDim.x = cluster[0].cast<unsigned>();
-    attr.value.clusterDim.y = py::len(cluster) > 1 ? cluster[1].cast<unsigned>() : 1;
-    attr.value.clusterDim.z = py::len(cluster) > 2 ? cluster[2].cast<unsigned>() : 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
+    attrs[n].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attrs[n].value.clusterDim.x = cluster[0].cast<unsigned>();
+    attrs[n].value.clusterDim.y = py::len(cluster) > 1 ? cluster[1].cast<unsigned>() : 1;
+    attrs[n].value.clusterDim.z = py::len(cluster) > 2 ? cluster[2].cast<unsigned>() : 1;
+    ++n;
   }
+  if (pdl) {
+    // may start before the previous kernel of the stream completes; the
+    // kernel waits for it with griddepcontrol.wait
+    attrs[n].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attrs[n].value.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = n ? attrs : nullptr;
+  cfg.numAttrs = n;
   check_drv(fb_driver()->cuLaunchKernelEx(&cfg, f, ptrs.data(), nullptr), "cuLaunchKernelEx");
 }
 
@@ -404,7 +413,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("load_image_file", &rt_load_image_file);
   m.def("get_function", &rt_get_function, py::arg("hash"), py::arg("name"), py::arg("max_dynamic_smem") = 0);
   m.def("launch", &rt_launch, py::arg("fn"), py::arg("grid"), py::arg("block"), py::arg("smem"),
-        py::arg("stream"), py::arg("args"), py::arg("cluster") = py::tuple());
+        py::arg("stream"), py::arg("args"), py::arg("cluster") = py::tuple(), py::arg("pdl") = false);
   m.def("make_tmap_2d", &rt_make_tmap_2d, py::arg("ptr"), py::arg("dtype"), py::arg("inner"), py::arg("outer"),
         py::arg("row_stride_bytes"), py::arg("box_inner"), py::arg("box_outer"), py::arg("swizzle"),
         py::arg("l2promo") = 2);

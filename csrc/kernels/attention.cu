@@ -242,6 +242,7 @@ __device__ __forceinline__ void decode_attn(const bf16* __restrict__ q, const bf
       const bf16* q, const bf16* k_cache, const bf16* v_cache, const int* block_tables, int max_blocks,           \
       const int* seq_lens, bf16* out, float* o_part, float* ml_part, int Hkv, int pages_per_split,                \
       float scale_log2) {                                                                                          \
+    pdl_entry();                                                                                                   \
     decode_attn<G>(q, k_cache, v_cache, block_tables, max_blocks, seq_lens, out, o_part, ml_part, Hkv,           \
                    pages_per_split, scale_log2);                                                                   \
   }
@@ -253,6 +254,7 @@ FB_DECODE_INSTANCE(8)
 extern "C" __global__ void __launch_bounds__(128) fb_decode_attn_combine(const float* __restrict__ o_part,
                                                                           const float* __restrict__ ml_part,
                                                                           bf16* __restrict__ out, int Hq, int S) {
+  pdl_entry();
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const size_t base = (static_cast<size_t>(b) * Hq + h) * S;
   float M = -INFINITY;
@@ -279,6 +281,7 @@ extern "C" __global__ void __launch_bounds__(128) fb_prefill_attn(
     const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, int ld_q, int ld_k, int ld_v,
     bf16* __restrict__ out, int ld_o, const int* __restrict__ cu_seqlens, const int* __restrict__ tile_seq,
     const int* __restrict__ tile_start, int Hq, int Hkv, float scale_log2) {
+  pdl_entry();
   __shared__ __align__(16) bf16 ks[PK][D + 8];
   __shared__ __align__(16) bf16 vs[PK][D + 8];
   const int tile = blockIdx.x, h = blockIdx.y;

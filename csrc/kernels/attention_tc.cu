@@ -154,6 +154,8 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
+  pdl_wait();  // set-up above overlapped the previous kernel; its outputs (q, caches) are read below
   const uint32_t tmem = sm.tmem;
   const uint32_t t_s = tmem, t_o = tmem + NH;
 

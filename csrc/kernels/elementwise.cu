@@ -21,6 +21,7 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 
 extern "C" __global__ void fb_init_normal_bf16(bf16* __restrict__ p, unsigned long long n, unsigned long long seed,
                                                float mean, float std) {
+  pdl_entry();
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   for (uint64_t pair = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; 2 * pair < n; pair += stride) {
     const uint64_t r = mix64(seed ^ mix64(pair));
@@ -37,6 +38,7 @@ extern "C" __global__ void fb_init_normal_bf16(bf16* __restrict__ p, unsigned lo
 }
 
 extern "C" __global__ void fb_fill_bf16(bf16* __restrict__ p, unsigned long long n, float v) {
+  pdl_entry();
   const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
   const bf16 b = f2bf(v);
   for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n; i += stride) p[i] = b;
@@ -46,6 +48,7 @@ extern "C" __global__ void fb_fill_bf16(bf16* __restrict__ p, unsigned long long
 // out[t, :] = table[ids[t], :]; H % 8 == 0.
 extern "C" __global__ void fb_embedding(const int* __restrict__ ids, const bf16* __restrict__ table,
                                         bf16* __restrict__ out, int T, int H, int vocab) {
+  pdl_entry();
   const int t = blockIdx.x;
   if (t >= T) return;
   int id = ids[t];
@@ -102,6 +105,7 @@ __device__ __forceinline__ void rmsnorm_row(const bf16* __restrict__ x, const bf
 
 extern "C" __global__ void __launch_bounds__(256) fb_rmsnorm(const bf16* __restrict__ x, const bf16* __restrict__ w,
                                                               bf16* __restrict__ out, int T, int H, float eps) {
+  pdl_entry();
   const int t = blockIdx.x;
   if (t >= T) return;
   if (H > 8 * 256 * 8) {
@@ -118,6 +122,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_rmsnorm(const bf16* __restr
 extern "C" __global__ void __launch_bounds__(256) fb_add_rmsnorm_partials(
     const float* __restrict__ part, int S, long long stride, bf16* __restrict__ h, const bf16* __restrict__ w,
     bf16* __restrict__ x, int T, int H, float eps) {
+  pdl_entry();
   constexpr int VPT = 4;  // H <= 256 threads * 4 vectors * 8
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -176,6 +181,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_add_rmsnorm_partials(
 // ---- SiLU * mul ---------------------------------------------------------------------
 // gu[t] = [gate (I) | up (I)]; out[t, i] = silu(gate) * up.
 extern "C" __global__ void fb_silu_mul(const bf16* __restrict__ gu, bf16* __restrict__ out, int T, int I) {
+  pdl_entry();
   const int nv = I / 8;
   const uint64_t total = static_cast<uint64_t>(T) * nv;
   for (uint64_t k = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; k < total;
@@ -207,6 +213,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_rope_kv_write(
     bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, const int* __restrict__ slots,
     int T, int Hq, int Hkv, int page, bf16* __restrict__ k_out, bf16* __restrict__ v_out,
     const float* __restrict__ part, int S, long long part_stride) {
+  pdl_entry();
   const int t = blockIdx.x;
   const int h = blockIdx.y * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -278,6 +285,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_rope_kv_write(
 // out[t] = argmax_v logits[t, v] (lowest index on ties). One CTA per row.
 extern "C" __global__ void __launch_bounds__(512) fb_argmax(const bf16* __restrict__ logits, int* __restrict__ out,
                                                              int T, int V, long long ld) {
+  pdl_entry();
   const int t = blockIdx.x;
   if (t >= T) return;
   const bf16* row = logits + static_cast<size_t>(t) * ld;
@@ -335,6 +343,7 @@ extern "C" __global__ void __launch_bounds__(512) fb_argmax(const bf16* __restri
 extern "C" __global__ void fb_decode_advance(int* __restrict__ seq_lens, int* __restrict__ positions,
                                              int* __restrict__ slots, const int* __restrict__ block_tables,
                                              int max_blocks, int page, int B, const int* __restrict__ active) {
+  pdl_entry();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   if (active && !active[b]) {
@@ -351,6 +360,7 @@ extern "C" __global__ void fb_decode_advance(int* __restrict__ seq_lens, int* __
 
 // Copies next-step input ids from the sampled tokens (device-side feedback).
 extern "C" __global__ void fb_copy_i32(const int* __restrict__ src, int* __restrict__ dst, int n) {
+  pdl_entry();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) dst[i] = src[i];
 }

@@ -42,6 +42,26 @@ __device__ __forceinline__ uint64_t globaltimer() {
 
 __device__ __forceinline__ void set_status(unsigned code) { atomicOr(&fb_status, code); }
 
+// ---- programmatic dependent launch ------------------------------------------------
+// Kernels of the decode step may be launched with programmatic stream
+// serialization: such a launch can start while the previous kernel of the
+// stream is still running (once all of that kernel's blocks have called
+// pdl_trigger or exited), so its set-up (barrier init, TMEM allocation,
+// descriptor and weight prefetch) overlaps the previous kernel's tail.
+// pdl_wait blocks the calling thread until every prerequisite grid has
+// completed and its memory is visible; every thread calls it before its first
+// access to global memory that another kernel writes or reads (weights, which
+// no kernel of the step writes, may be read before). Without the launch
+// attribute both are no-ops. Every kernel that can be launched this way calls
+// pdl_wait on every path, so a grid never completes before its predecessor.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Both, at the top of a kernel with no set-up worth overlapping.
+__device__ __forceinline__ void pdl_entry() {
+  pdl_trigger();
+  pdl_wait();
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -50,6 +50,12 @@ constexpr int EPI_B_STREAM = 8;  // L2 evict-first hint on B loads
 // mode bits 8..15: how many k-blocks ahead of the ring A tiles are prefetched into L2
 constexpr int EPI_MCAST = 1 << 16;  // `out` is an NVLS multicast address: stores reach every rank
 constexpr int EPI_TMA_OUT = 1 << 17;  // transposed output written by TMA stores through tmO (and tmR)
+constexpr int EPI_A_CONST = 1 << 18;  // A is not written by any kernel of the step (weights): loaded before pdl_wait
+// SwiGLU epilogue (MT == 2, swap-AB, TMA output): A is [gate; up] with M/2
+// rows each; a unit's two A tiles are gate rows r..r+127 and the up rows of
+// the same features (M/2 + r..), and the epilogue writes silu(gate) * up
+// (bf16, [tokens][M/2]) instead of the two projections.
+constexpr int EPI_SWIGLU = 1 << 19;
 constexpr int NUM_THREADS = 192;
 
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int32_t c0, int32_t c1) {
@@ -125,6 +131,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   const int KB = (K + BK - 1) / BK;
   const int kb_per = (KB + splits - 1) / splits;
   const int num_units = num_m * num_n * splits;
+  // First A row of tile mt of unit row-block m_blk.
+  auto a_row = [&](int m_blk, int mt) {
+    return (mode & EPI_SWIGLU) ? mt * (M / 2) + m_blk * BM : (m_blk * MT + mt) * BM;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -157,6 +167,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -166,6 +177,32 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       uint32_t phase = 0;
       const uint64_t pol = policy_evict_first();
       const int pf_dist = (mode >> 8) & 0xFF;  // k-blocks of L2 prefetch lead (0 = off)
+      auto load_a = [&](int st, int kb, int m_blk) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint8_t* dst = sA + (st * MT + mt) * C::A_BYTES;
+          const int row = a_row(m_blk, mt);
+          if (mode & EPI_A_STREAM)
+            tma_load_2d_hint(dst, tmA, &full[st], kb * BK, row, pol);
+          else
+            tma_load_2d(dst, tmA, &full[st], kb * BK, row);
+        }
+      };
+      // Before waiting for the previous kernel: the first unit's A tiles of
+      // the whole ring, when A is an operand no kernel of the step writes
+      // (the weights of a swap-AB GEMM; EPI_A_CONST). B (activations) and the
+      // outputs wait for pdl_wait below.
+      int pre = 0;
+      if ((mode & EPI_A_CONST) && blockIdx.x < num_units) {
+        const int mn = blockIdx.x / splits, sp = blockIdx.x % splits;
+        const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
+        pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          load_a(i, kb0 + i, mn % num_m);
+        }
+      }
+      pdl_wait();
       for (int u = blockIdx.x; u < num_units && !*(volatile int*)abort_flag; u += gridDim.x) {
         const int mn = u / splits, sp = u % splits;
         const int m_blk = mn % num_m, n_blk = mn / num_m;
@@ -173,27 +210,23 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
         // Streamed A tiles: keep the L2 pf_dist k-blocks ahead of the ring.
         for (int kb = kb0; kb < min(kb1, kb0 + pf_dist); ++kb)
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt) tma_prefetch_2d(tmA, kb * BK, (m_blk * MT + mt) * BM);
+          for (int mt = 0; mt < MT; ++mt) tma_prefetch_2d(tmA, kb * BK, a_row(m_blk, mt));
         for (int kb = kb0; kb < kb1; ++kb) {
           if (pf_dist && kb + pf_dist < kb1) {
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, (m_blk * MT + mt) * BM);
+            for (int mt = 0; mt < MT; ++mt) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, a_row(m_blk, mt));
           }
-          if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
-            *(volatile int*)abort_flag = 1;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          // Operands read exactly once per launch (decode weights) are hinted
-          // evict-first so they do not push reused activations out of L2.
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            uint8_t* dst = sA + (stage * MT + mt) * C::A_BYTES;
-            const int row = (m_blk * MT + mt) * BM;
-            if (mode & EPI_A_STREAM)
-              tma_load_2d_hint(dst, tmA, &full[stage], kb * BK, row, pol);
-            else
-              tma_load_2d(dst, tmA, &full[stage], kb * BK, row);
+          if (pre > 0 && u == blockIdx.x && kb - kb0 < pre) {
+            // stage armed and its A tiles issued before pdl_wait
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+              *(volatile int*)abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            // Operands read exactly once per launch (decode weights) are hinted
+            // evict-first so they do not push reused activations out of L2.
+            load_a(stage, kb, m_blk);
           }
           if (mode & EPI_B_STREAM)
             tma_load_2d_hint(sB + stage * C::B_BYTES, tmB, &full[stage], kb * BK, n_blk * BN, pol);
@@ -265,6 +298,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();  // residual reads and output writes follow the previous kernel
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int et = threadIdx.x - 64;  // 0..127 over the four epilogue warps; 0 issues the tile stores
     const bool tma_out = (mode & EPI_TMA_OUT) && (mode & EPI_TRANSPOSE) && !(mode & EPI_MCAST);
@@ -292,6 +326,38 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       }
       tc_fence_after();
       float* part = splits > 1 ? ws + static_cast<size_t>(sp) * split_stride : nullptr;
+      if (MT == 2 && (mode & EPI_SWIGLU) && tma_out) {
+        // act[token][feature] = silu(gate) * up: this thread holds both
+        // projections of feature m_blk * 128 + f (accumulators 0 and 1).
+        constexpr int EC = BN < EPI_COLS ? BN : EPI_COLS;
+        const int f = quarter * 32 + lane;
+        const uint32_t t_g = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::ACC_COLS;
+#pragma unroll 1
+        for (int c1 = 0; c1 < BN && ok; c1 += EC, ++chunk) {
+          const int buf = chunk & 1;
+          bf16* sb = reinterpret_cast<bf16*>(stg) + buf * (EPI_COLS * BM);
+          uint32_t rg[EC], ru[EC];
+#pragma unroll
+          for (int j = 0; j < EC / 16; ++j) {
+            tmem_ld16(t_g + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(rg + 16 * j));
+            tmem_ld16(t_g + BN + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(ru + 16 * j));
+          }
+          tmem_ld_wait();
+          if (et == 0 && chunk >= 2) bulk_wait_read_1();  // this buffer's previous store has read it
+          if (!(ok = epi_sync())) break;
+#pragma unroll
+          for (int t = 0; t < EC; ++t) {
+            const float g = __uint_as_float(rg[t]);
+            sb[t * BM + f] = f2bf(g / (1.f + __expf(-g)) * __uint_as_float(ru[t]));
+          }
+          fence_proxy_async();
+          if (!(ok = epi_sync())) break;
+          if (et == 0) {
+            tma_store_2d(tmO, sb, m_blk * BM, n_blk * BN + c1);
+            bulk_commit();
+          }
+        }
+      } else
 #pragma unroll 1
       for (int mt = 0; mt < MT && ok; ++mt) {
         const int gm = (m_blk * MT + mt) * BM + quarter * 32 + lane;  // D row of this thread
@@ -509,14 +575,16 @@ FB_GEMM_INSTANCE(256, 2)
 // tiles, so 224 tiles on 148 SMs take 1.51 tile-times instead of 2. A CTA's
 // range is cut into segments at tile boundaries; with at least one tile per
 // CTA a tile is split between at most two neighbouring CTAs (b, b + 1). Both
-// halves meet through slot b of a workspace: per epilogue warp (32 output
-// rows) an atomic ticket decides who arrives first; the first writes its fp32
-// partial and releases a flag, the second adds the partner's partial to its
-// own (a + b == b + a in fp32, so the result does not depend on the order),
-// writes the bf16 output and resets the ticket and flag for the next launch.
-// Nobody waits for a CTA that has not started: the first arriver never waits
-// and the second only waits for a write already in progress (bounded).
-// Output: transposed (out[token][feature]) with optional residual.
+// halves meet through slot b of a workspace: an atomic ticket (one per slot,
+// taken by one epilogue thread for the whole 128-row tile) decides who
+// arrives first; the first writes its fp32 partial and releases a flag, the
+// second adds the partner's partial to its own (a + b == b + a in fp32, so
+// the result does not depend on the order), stores the bf16 tile and resets
+// the ticket and flag for the next launch. Nobody waits for a CTA that has
+// not started: the first arriver never waits and the second only waits for a
+// write already in progress (bounded).
+// Output: transposed (out[token][feature]) with optional residual, through
+// the same staged TMA-store epilogue as fb_gemm_bf16 (tmO / tmR required).
 namespace {
 
 __device__ __forceinline__ void st_release_gpu(int* p, int v) {
@@ -529,8 +597,8 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 }
 
 template <int BN>
-__device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
-                                             const bf16* residual, int M, int N, int K, int ldo, int mode,
+__device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmO,
+                                             const CUtensorMap* tmR, int M, int N, int K, int mode,
                                              float* __restrict__ ws, int* __restrict__ flags) {
   using C = Cfg<BN, 1>;
   constexpr int STAGES = C::STAGES;
@@ -539,12 +607,16 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* stg = smem + STAGES * C::STAGE_BYTES;  // epilogue tiles (STG_BYTES)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* ebar = tempty + 2;  // the four epilogue warps' rendezvous
+  uint64_t* rbar = ebar + 1;    // residual tile loads, one per buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* tile_ticket = abort_flag + 1;  // the ticket this CTA drew for its current split tile
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -564,6 +636,9 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
+    mbar_init(ebar, 4);
+    mbar_init(&rbar[0], 1);
+    mbar_init(&rbar[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async();
@@ -571,6 +646,8 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(tmA);
     tma_prefetch_desc(tmB);
+    tma_prefetch_desc(tmO);
+    if (mode & EPI_RESIDUAL) tma_prefetch_desc(tmR);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -579,6 +656,8 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
+  pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -668,9 +747,21 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
+    constexpr int EC = BN < EPI_COLS ? BN : EPI_COLS;
     const int quarter = warp & 3;
+    const int et = threadIdx.x - 64;    // 0..127; 0 draws tickets and issues the tile stores
+    const int f = quarter * 32 + lane;  // D row (output feature within the tile) of this thread
+    uint32_t ephase = 0, rphase = 0, chunk = 0;
+    bool ok = true;
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ebar);
+      const bool done = mbar_wait(ebar, ephase, FB_KERR_TIMEOUT_TMEM);
+      ephase ^= 1;
+      return done;
+    };
     int seg = 0;
-    for (long long it = it0; it < it1 && !*(volatile int*)abort_flag; ++seg) {
+    for (long long it = it0; ok && it < it1 && !*(volatile int*)abort_flag; ++seg) {
       const int tile = static_cast<int>(it / KB);
       const int kb0 = static_cast<int>(it % KB);
       const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
@@ -679,23 +770,23 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
       const int acc = NBUF == 2 ? (seg & 1) : 0;
       const uint32_t aphase = NBUF == 2 ? ((seg >> 1) & 1) : (seg & 1);
       if (!mbar_wait(&tfull[acc], aphase, FB_KERR_TIMEOUT_TMEM)) {
-        *(volatile int*)abort_flag = 1;
+        ok = false;
         break;
       }
       tc_fence_after();
-      const int gm = m_blk * BM + quarter * 32 + lane;  // output feature of this thread
+      const int gm0 = m_blk * BM;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::ACC_COLS;
       // Split tile: the prefix owner is the CTA whose range ends inside it.
       const bool split = !(kb0 == 0 && kb1 == KB);
       const int slot = (kb0 == 0) ? blockIdx.x : blockIdx.x - 1;
-      int* ticket = flags + slot * 8 + quarter;
-      int* ready = flags + slot * 8 + 4 + quarter;
-      float* part = ws + (static_cast<size_t>(slot) * BM + quarter * 32 + lane) * BN;
+      int* ticket = flags + slot * 8;
+      int* ready = flags + slot * 8 + 4;
+      float* part = ws + (static_cast<size_t>(slot) * BM + f) * BN;  // this thread's fp32 row
       bool first = false;
       if (split) {
-        int t = 0;
-        if (lane == 0) t = atomicAdd(ticket, 1);
-        first = __shfl_sync(0xffffffffu, t, 0) == 0;
+        if (et == 0) *tile_ticket = atomicAdd(ticket, 1);
+        if (!(ok = epi_sync())) break;
+        first = *(volatile int*)tile_ticket == 0;
         if (!first) {
           // the partner is writing its partial: bounded wait for its flag
           const uint64_t t0 = globaltimer();
@@ -703,66 +794,93 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
           while (ld_acquire_gpu(ready) == 0) {
             if ((++spins & 255u) == 0 && globaltimer() - t0 > FB_WAIT_NS) {
               set_status(FB_KERR_TIMEOUT_PEER);
+              ok = false;
               break;
             }
           }
+          if (!ok) break;
         }
       }
+      if (split && first) {
+        // fp32 partial: row f of the slot, BN contiguous floats per thread
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(t_row + c0, r);
-        tmem_ld_wait();
-        if (split && first) {
-          float4* dst = reinterpret_cast<float4*>(part + c0);
+        for (int c1 = 0; c1 < BN; c1 += EC) {
+          uint32_t rr[EC];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-          continue;
+          for (int j = 0; j < EC / 16; ++j)
+            tmem_ld16(t_row + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(rr + 16 * j));
+          tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(part + c1);
+#pragma unroll
+          for (int i = 0; i < EC / 4; ++i)
+            dst[i] = make_float4(__uint_as_float(rr[4 * i]), __uint_as_float(rr[4 * i + 1]),
+                                 __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3]));
         }
-        float v[16];
+        __threadfence();
+        if (!(ok = epi_sync())) break;  // all 128 rows written
+        if (et == 0) st_release_gpu(ready, 1);
+      } else {
+        // whole tile, or the second half of a split one: bf16 [EC tokens][128
+        // features] staging tiles stored by TMA, double-buffered
+#pragma unroll 1
+        for (int c1 = 0; c1 < BN && ok; c1 += EC, ++chunk) {
+          const int buf = chunk & 1;
+          const int gn0 = n_blk * BN + c1;
+          bf16* sb = reinterpret_cast<bf16*>(stg) + buf * (EPI_COLS * BM);
+          bf16* sr = reinterpret_cast<bf16*>(stg + STG_BYTES / 2) + buf * (EPI_COLS * BM);
+          uint32_t rr[EC];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-        if (split) {
+          for (int j = 0; j < EC / 16; ++j)
+            tmem_ld16(t_row + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(rr + 16 * j));
+          tmem_ld_wait();
+          float v[EC];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float4 p = __ldcg(reinterpret_cast<const float4*>(part + c0) + i);
-            v[4 * i] += p.x;
-            v[4 * i + 1] += p.y;
-            v[4 * i + 2] += p.z;
-            v[4 * i + 3] += p.w;
-          }
-        }
-        if (gm < M) {
+          for (int t = 0; t < EC; ++t) v[t] = __uint_as_float(rr[t]);
+          if (split) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int gn = n_blk * BN + c0 + i;
-            if (gn < N) {
-              const size_t idx = static_cast<size_t>(gn) * ldo + gm;
-              float x = v[i];
-              if (mode & EPI_RESIDUAL) x += bf2f(residual[idx]);
-              out[idx] = f2bf(x);
+            for (int i = 0; i < EC / 4; ++i) {
+              const float4 q = __ldcg(reinterpret_cast<const float4*>(part + c1) + i);
+              v[4 * i] += q.x;
+              v[4 * i + 1] += q.y;
+              v[4 * i + 2] += q.z;
+              v[4 * i + 3] += q.w;
             }
           }
-        }
-      }
-      if (split) {
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) {
-          if (first) {
-            st_release_gpu(ready, 1);
+          if (et == 0 && chunk >= 2) bulk_wait_read_1();  // this buffer's previous store has read it
+          if (!(ok = epi_sync())) break;
+          if (mode & EPI_RESIDUAL) {
+            if (et == 0) {
+              mbar_arrive_expect_tx(&rbar[buf], EC * BM * 2);
+              tma_load_2d(sr, tmR, &rbar[buf], gm0, gn0);
+            }
+            if (!(ok = mbar_wait(&rbar[buf], (rphase >> buf) & 1u, FB_KERR_TIMEOUT_FULL))) break;
+            rphase ^= 1u << buf;
+#pragma unroll
+            for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(v[t] + bf2f(sr[t * BM + f]));
           } else {
-            *ticket = 0;  // reset for the next launch (kernel boundary orders it)
-            *ready = 0;
+#pragma unroll
+            for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(v[t]);
+          }
+          fence_proxy_async();  // generic-proxy writes -> visible to the TMA engine
+          if (!(ok = epi_sync())) break;
+          if (et == 0) {
+            tma_store_2d(tmO, sb, gm0, gn0);
+            bulk_commit();
           }
         }
+        // every thread read its partner rows before the last rendezvous
+        if (ok && split && et == 0) {
+          *ticket = 0;  // reset for the next launch (kernel boundary orders it)
+          *ready = 0;
+        }
       }
+      if (!ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (!ok) *(volatile int*)abort_flag = 1;
+    if (et == 0) bulk_wait_all();  // the tile stores have read shared memory and landed
   }
 
   tc_fence_before();
@@ -775,9 +893,10 @@ __device__ __forceinline__ void gemm_sk_body(const CUtensorMap* tmA, const CUten
 
 #define FB_GEMM_SK_INSTANCE(BN)                                                                                     \
   extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_sk_bn##BN(                                  \
-      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
-      const bf16* residual, int M, int N, int K, int ldo, int mode, float* ws, int* flags) {                        \
-    gemm_sk_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, ws, flags);                                     \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,                             \
+      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, int M, int N, int K,        \
+      int mode, float* ws, int* flags) {                                                                            \
+    gemm_sk_body<BN>(&tmA, &tmB, &tmO, &tmR, M, N, K, mode, ws, flags);                                             \
   }
 
 FB_GEMM_SK_INSTANCE(16)
@@ -916,6 +1035,8 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
   tc_fence_before();
   cluster_sync_all();  // both CTAs' barriers initialised before either signals the other
   tc_fence_after();
+  pdl_trigger();
+  pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {

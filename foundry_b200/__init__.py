@@ -18,8 +18,13 @@ python/foundry/__init__.py:3-32 and ops.pyi):
 
 from __future__ import annotations
 
-from ._native import core, hook_library_path, use_mock_driver
-from .allocation_region import (
+from . import _early_cuda
+
+# Before anything imports torch: build the CUDA context meanwhile, if asked.
+_early_cuda.start_from_env()
+
+from ._native import core, hook_library_path, use_mock_driver  # noqa: E402
+from .allocation_region import (  # noqa: E402
     allocation_region,
     free_preallocated_region,
     get_current_alloc_offset,

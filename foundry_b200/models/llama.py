@@ -241,8 +241,10 @@ class LlamaModel:
 
     def _mlp(self, st, x, h, lw, rows):
         """SwiGLU FFN of x; returns the pending output that the next norm adds into h."""
-        gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:rows], streamk=getattr(st, "sk", None))
-        ops.silu_mul(gu, st.act[:rows])
+        # decode batches: one GEMM whose epilogue applies SiLU(gate) * up
+        if ops.linear_swiglu(x, lw["gate_up"], st.act[:rows]) is None:
+            gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:rows], streamk=getattr(st, "sk", None))
+            ops.silu_mul(gu, st.act[:rows])
         return self._row_parallel(st, st.act[:rows], lw["down"], h, rows, which=1)
 
     def _row_parallel(self, st, inp, weight, h, rows, which):

@@ -21,7 +21,7 @@ from .basic import (
     rope_kv_write,
     silu_mul,
 )
-from .gemm import Partial, PartialBuffer, StreamKBuffer, linear, linear_multicast, plan
+from .gemm import Partial, PartialBuffer, StreamKBuffer, linear, linear_multicast, linear_swiglu, plan
 
 status = _rt.status
 clear_status = _rt.clear_status
@@ -29,6 +29,6 @@ clear_status = _rt.clear_status
 __all__ = [
     "DecodeWorkspace", "Partial", "PartialBuffer", "StreamKBuffer", "add_rmsnorm_partials", "argmax", "clear_status", "copy_i32", "decode_advance",
     "decode_attention", "decode_splits", "embedding", "fill_", "init_normal_",
-    "linear", "plan", "prefill_attention", "prefill_tiles", "rmsnorm", "rope_cos_sin", "rope_kv_write",
+    "linear", "linear_multicast", "linear_swiglu", "plan", "prefill_attention", "prefill_tiles", "rmsnorm", "rope_cos_sin", "rope_kv_write",
     "silu_mul", "status",
 ]

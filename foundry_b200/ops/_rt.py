@@ -10,6 +10,8 @@ no fallback path.
 
 from __future__ import annotations
 
+import contextlib
+import os
 import threading
 
 import torch
@@ -53,12 +55,41 @@ def function(image: str, name: str, smem: int = 0) -> int:
     return f
 
 
+# Programmatic dependent launch: inside ``pdl()`` the kernels of these images
+# are launched with programmatic stream serialization, so each may start (and
+# run its set-up) while the previous kernel of the stream finishes; every
+# kernel of these images calls griddepcontrol.wait before it touches memory
+# another kernel writes (csrc/kernels/fb_common.cuh). Kernels of other images
+# (the peer-memory collectives, MoE) launch in plain stream order. Set
+# FOUNDRY_PDL=0 to launch everything in plain order.
+PDL_IMAGES = frozenset({"elementwise", "attention", "attention_tc", "gemm_bf16"})
+PDL_ENABLED = os.environ.get("FOUNDRY_PDL", "1") != "0"
+_pdl = threading.local()
+
+
+@contextlib.contextmanager
+def pdl():
+    """Launches in this block (this thread) may use programmatic dependent
+    launch. Used around the decode step, whose weights no kernel writes."""
+    depth = getattr(_pdl, "depth", 0)
+    _pdl.depth = depth + 1
+    try:
+        yield
+    finally:
+        _pdl.depth = depth
+
+
+def pdl_active() -> bool:
+    return PDL_ENABLED and getattr(_pdl, "depth", 0) > 0
+
+
 def launch(image: str, name: str, grid, block, args, smem: int = 0, stream: int | None = None,
            cluster=()) -> None:
     if stream is None:
         stream = torch.cuda.current_stream().cuda_stream
     fn = function(image, name, smem)
-    core().launch(fn, tuple(grid), tuple(block), smem, stream, args, tuple(cluster))
+    core().launch(fn, tuple(grid), tuple(block), smem, stream, args, tuple(cluster),
+                  pdl_active() and image in PDL_IMAGES)
 
 
 def status(image: str) -> int:

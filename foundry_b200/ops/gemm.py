@@ -28,6 +28,8 @@ BM, BK = 128, 64
 EPI_TRANSPOSE, EPI_RESIDUAL, EPI_A_STREAM, EPI_B_STREAM = 1, 2, 4, 8
 EPI_MCAST = 1 << 16
 EPI_TMA_OUT = 1 << 17
+EPI_A_CONST = 1 << 18  # A (the weights of a swap-AB GEMM) may be loaded before the PDL wait
+EPI_SWIGLU = 1 << 19  # two A tiles per unit (gate rows, up rows); the epilogue writes silu(gate) * up
 EPI_COLS = 32  # tokens per epilogue store chunk of the one-SM kernel
 _BF16 = 9  # CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
 _F32 = 7  # CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -242,10 +244,10 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
         best.pf = 4
     # Stream-K: whole-tile plans whose tile count is not a multiple of the SM
     # count leave the last wave part empty; equal (tile, k-block) shares
-    # remove that tail. Measured on B200 (Llama-3-8B gate_up, 224 tiles):
-    # 47.3 -> 40.8 us at 64 tokens (bn 64), 52.6 -> 51.1 us at 128 (bn 128),
-    # but 71.8 -> 76.3 us at 256 (bn 256: the partial-tile exchange costs more
-    # than the half-empty second wave), so only narrow tiles use it.
+    # remove that tail. Measured on B200 (Llama-3-8B gate_up, 224 tiles, both
+    # with the TMA-store epilogue, CUDA-graph timed): 43.4 -> 35.0 us at 32
+    # tokens (bn 32), 44.6 -> 38.3 us at 64 (bn 64), but 56.7 -> 68.0 us at
+    # 256 (bn 256) and 77.0 us with bn 128, so only narrow tiles use it.
     if _PAIR == "1" and best.swap and best.bn >= 64 and mg >= 2 * BM:
         return pair_plan(mg, ng, k, best.bn, sms, allow_split, best.pf)
     if allow_streamk and best.swap and best.splits == 1 and best.mt == 1 and best.bn <= 64:
@@ -280,6 +282,64 @@ def pair_plan(mg: int, ng: int, k: int, bn: int, sms: int, allow_split: bool = T
     return Plan(bn=bn, splits=best_s, grid=2 * min(units, pairs), swap=True, est_us=best_t * 1e6, pf=pf, pair=True)
 
 
+# FOUNDRY_SWIGLU=0 turns the fused gate/up + SiLU*mul GEMM off (separate
+# GEMM and silu_mul kernel, for comparison).
+SWIGLU_ENABLED = os.environ.get("FOUNDRY_SWIGLU", "1") != "0"
+
+
+def plan_swiglu(m_tok: int, inter: int, k: int, sms: int | None = None) -> Plan | None:
+    """Plan of the fused gate/up GEMM + SiLU*mul (swap-AB, two 128-row A
+    tiles per unit, no split-K since the epilogue is not linear in the sum);
+    None when the shape does not allow it."""
+    if not SWIGLU_ENABLED or m_tok > 256 or inter % BM:
+        return None
+    sms = sms or _rt.sm_count()
+    kb = math.ceil(k / BK)
+    tm = inter // BM
+    dram = (2 * inter * k + m_tok * k) * 2 / _HBM_BPS
+    best = None
+    for bn in (32, 64, 128, 256):
+        if bn < min(m_tok, 256) / 4 and bn != 256:
+            continue
+        units = tm * math.ceil(m_tok / bn)
+        stage = 2 * BM * BK * 2 + bn * BK * 2
+        stages = min(8, (192 * 1024) // stage)
+        mma = 2 * 2 * BM * bn * BK / _SM_MMA_FLOPS
+        t_kb = max((_TMA_LATENCY + mma) / stages, stage / _CTA_FILL_BPS_MAX, mma)
+        t = max(math.ceil(units / sms) * (kb * t_kb + 3e-6), dram)
+        if best is None or t < best.est_us * 1e-6 * 0.97:
+            best = Plan(bn=bn, splits=1, grid=min(units, sms), swap=True, est_us=t * 1e6, mt=2,
+                        pf=4 if kb >= 8 else 0)
+    return best
+
+
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor,
+                  plan_override: Plan | None = None) -> torch.Tensor | None:
+    """out = silu(x @ gate.T) * (x @ up.T) in one GEMM, where w_gu is [gate;
+    up] ([2 * I, K], gate rows first) and out is [T, I] bf16. Returns None
+    (nothing launched) when the shape has no fused plan: more than 256 tokens,
+    I not a multiple of 128, or rows the TMA stores cannot address."""
+    t_tok, k = x.shape
+    two_i, k2 = w_gu.shape
+    inter = two_i // 2
+    assert k == k2 and out.shape == (t_tok, inter) and out.stride(1) == 1
+    p = plan_override or plan_swiglu(t_tok, inter, k)
+    if p is None:
+        return None
+    om = out_maps(out.data_ptr(), 0, inter, t_tok, out.stride(0), p.bn)
+    if om is None:
+        return None
+    mode = EPI_TRANSPOSE | EPI_TMA_OUT | EPI_SWIGLU | ((min(p.pf, 255) & 0xFF) << 8)
+    if math.ceil(t_tok / p.bn) == 1:
+        mode |= EPI_A_STREAM
+    if _rt.pdl_active():
+        mode |= EPI_A_CONST
+    args = [tmap(w_gu, BM), tmap(x, p.bn), om[0], _NO_MAP, out.data_ptr(), 0, two_i, t_tok, k, out.stride(0), mode,
+            1, 0, 0]
+    _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)
+    return out
+
+
 def linear_multicast(x: torch.Tensor, w: torch.Tensor, target: int, plan_override: Plan | None = None) -> None:
     """x @ w.T written by the GEMM epilogue straight to ``target``, an NVLS
     multicast address: every tile lands in the same slot of every rank's
@@ -310,7 +370,11 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     n_out, k2 = w.shape
     assert k == k2, f"K mismatch {k} vs {k2}"
     p = plan_override or plan(t_tok, n_out, k, allow_split=partials is not None, allow_streamk=streamk is not None)
-    if p.streamk and (streamk is None or not streamk.fits(p.grid, p.bn)):
+    sk_maps = None
+    if p.streamk and streamk is not None and streamk.fits(p.grid, p.bn) and out is not None:
+        sk_maps = out_maps(out.data_ptr(), residual.data_ptr() if residual is not None else 0, n_out, t_tok,
+                           out.stride(0), p.bn)
+    if p.streamk and sk_maps is None:  # no workspace, or rows the TMA stores cannot address
         p = plan(t_tok, n_out, k, allow_split=partials is not None)
     mode = 0
     if p.swap:
@@ -318,6 +382,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         mode |= EPI_TRANSPOSE
         if math.ceil(ng / p.bn) == 1:
             mode |= EPI_A_STREAM  # each weight byte is read once: evict-first
+        if _rt.pdl_active():
+            mode |= EPI_A_CONST  # inside the decode step no kernel writes the weights
     else:
         a, b, mg, ng = x, w, t_tok, n_out
     mode |= (min(p.pf, 255) & 0xFF) << 8
@@ -347,8 +413,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         # needs at least one whole tile per CTA.
         if math.ceil(mg / BM) * math.ceil(ng / p.bn) < p.grid:
             raise ValueError(f"stream-K plan has fewer tiles than its {p.grid} CTAs")
-        args = [tmap(a, BM), tmap(b, p.bn), out.data_ptr(), residual.data_ptr() if residual is not None else 0,
-                mg, ng, k, out.stride(0), mode, streamk.ws.data_ptr(), streamk.flags.data_ptr()]
+        args = [tmap(a, BM), tmap(b, p.bn), *sk_maps, mg, ng, k, mode | EPI_TMA_OUT, streamk.ws.data_ptr(),
+                streamk.flags.data_ptr()]
         _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, 1))
         return out
     maps = []

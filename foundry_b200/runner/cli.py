@@ -119,10 +119,15 @@ def _main(argv=None):
 
     import torch
 
+    marks = {"main_s": time.time_ns()}
     if args.device is not None:
-        torch.cuda.set_device(args.device)
+        torch.cuda.set_device(args.device)  # creates the device's primary context
+    marks["cuda_context_s"] = time.time_ns()
     init_dist(args)
+    marks["process_group_s"] = time.time_ns()
     from . import persist
+
+    marks["runner_import_s"] = time.time_ns()
 
     if args.cmd == "save":
         from .engine import LLMEngine
@@ -139,6 +144,7 @@ def _main(argv=None):
     if args.cmd == "load":
         eng, timings = persist.load(args.archive)
         _ENGINES.append(eng)
+        marks["archive_load_s"] = time.time_ns()
         # First token of a fresh request through the restored engine.
         g = torch.Generator().manual_seed(args.seed + 7)
         prompt = torch.randint(0, eng.ecfg.model.vocab, (args.prompt_len,), generator=g).tolist()
@@ -160,6 +166,17 @@ def _main(argv=None):
             "cold_start_first_decode_token_s": (second - _t0_ns()) / 1e9,
             "python_import_s": (T_IMPORT0 - _t0_ns()) / 1e9 if os.environ.get("FOUNDRY_SPAWN_T0_NS") else None,
         })
+        # Where the time to the first token went, step by step from the
+        # end of the imports (seconds per step, in order).
+        marks["first_token_s"] = first
+        prev, steps = T_IMPORT0, {}
+        for k, t in marks.items():
+            steps[k] = round((t - prev) / 1e9, 4)
+            prev = t
+        timings["cold_start_steps_s"] = steps
+        from .. import _early_cuda
+
+        timings["early_cuda_context"] = _early_cuda.result()
         print(json.dumps({"load": timings}))
         return 0
 

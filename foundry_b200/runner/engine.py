@@ -428,9 +428,14 @@ class LLMEngine:
         return self.h_out[:b]
 
     def _decode_body(self, b: int) -> None:
+        from ..ops import _rt
+
         st = self.state
-        # Padding rows are inactive: no cache writes, no attention.
-        self.model.decode(st, b)
+        # Padding rows are inactive: no cache writes, no attention. Kernels
+        # start under programmatic dependent launch (set-up and weight loads
+        # overlap the previous kernel).
+        with _rt.pdl():
+            self.model.decode(st, b)
 
     def generate(self, prompts: list[list[int]], max_new_tokens: int) -> list[list[int]]:
         reqs = self.add_requests(prompts, max_new_tokens)

@@ -345,3 +345,60 @@ def test_linear_streamk(t, n, k):
     torch.testing.assert_close(out.float(), ref + res.float(), atol=3e-2, rtol=2e-2)
     assert int(sk.flags.abs().sum()) == 0
     assert ops.status("gemm_bf16") == 0
+
+
+@pytest.mark.parametrize("t,n,k,bn", [(256, 28672, 4096, 256), (200, 19000, 1024, 128), (256, 128256, 4096, 256)])
+def test_linear_streamk_wide_tiles(t, n, k, bn):
+    """Stream-K with 128- and 256-token tiles (the TMA-store epilogue and a
+    per-tile ticket), forced through a plan override: matches fp32 with and
+    without the residual, bit-identical across launches, tickets reset."""
+    import dataclasses
+
+    from foundry_b200 import ops
+    from foundry_b200.ops.gemm import plan
+
+    p = dataclasses.replace(plan(t, n, k), bn=bn, splits=1, mt=1, grid=148, streamk=True, pair=False)
+    x = _bf(t, k, seed=41)
+    w = _bf(n, k, seed=42, scale=0.02)
+    sk = ops.StreamKBuffer(torch.empty(148 * 128 * 256, device="cuda"),
+                           torch.zeros(1024 * 8, dtype=torch.int32, device="cuda"))
+    ref = x.float() @ w.float().T
+    outs = []
+    for _ in range(2):
+        out = torch.full((t, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        ops.linear(x, w, out=out, streamk=sk, plan_override=p)
+        outs.append(out)
+    torch.testing.assert_close(outs[0].float(), ref, atol=2e-2, rtol=2e-2)
+    assert torch.equal(outs[0], outs[1])
+    res = _bf(t, n, seed=43)
+    out = res.clone()
+    ops.linear(x, w, out=out, residual=out, streamk=sk, plan_override=p)
+    torch.testing.assert_close(out.float(), ref + res.float(), atol=3e-2, rtol=2e-2)
+    assert int(sk.flags.abs().sum()) == 0
+    assert ops.status("gemm_bf16") == 0
+
+
+@pytest.mark.parametrize("t,inter,k,bn", [(256, 14336, 4096, None), (200, 1024, 512, None), (1, 1024, 512, None),
+                                          (64, 3584, 8192, None), (256, 1024, 512, 256), (100, 1024, 512, 32),
+                                          (130, 2048, 1024, 128), (40, 1024, 2048, 64)])
+def test_linear_swiglu(t, inter, k, bn):
+    """gate/up GEMM with the SiLU(gate) * up epilogue (two A tiles per unit:
+    gate rows and the matching up rows) against fp32, for the planner's
+    choice and forced tile widths."""
+    import dataclasses
+
+    from foundry_b200 import ops
+    from foundry_b200.ops.gemm import plan_swiglu
+
+    x = _bf(t, k, seed=51)
+    w = _bf(2 * inter, k, seed=52, scale=0.05)
+    p = plan_swiglu(t, inter, k)
+    assert p is not None and p.mt == 2
+    if bn is not None:
+        p = dataclasses.replace(p, bn=bn, grid=min(148, (inter // 128) * -(-t // bn)))
+    out = torch.full((t, inter), float("nan"), dtype=torch.bfloat16, device="cuda")
+    assert ops.linear_swiglu(x, w, out, plan_override=p) is out
+    gu = x.float() @ w.float().T
+    ref = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=2e-2)
+    assert ops.status("gemm_bf16") == 0
