@@ -15,7 +15,9 @@ tokens it prints one JSON line per variant:
 ``--ops`` restricts the run to some layers (e.g. ``gate_up,lm_head``).
 
 Each line gives the plan (tile width, splits, grid) and the mean time of
-``--iters`` back-to-back launches (CUDA events, after ``--warmup``).
+``--iters`` back-to-back launches (CUDA events, after ``--warmup``);
+``--pdl`` launches them with programmatic dependent launch as in the decode
+step, ``--flush`` (with ``--graph``) evicts L2 before each launch.
 Weights larger than the 126 MB L2 (Llama-3-8B gate_up, down, lm_head) stream
 from HBM on every launch. Smaller ones (qkv 50 MB, o 34 MB) may partly stay
 in L2 across back-to-back launches, which they do not inside a decode step.
@@ -25,6 +27,7 @@ With ``--check`` each variant's output is compared against fp32.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import dataclasses
 import json
 import sys
@@ -52,6 +55,11 @@ def main(argv=None) -> int:
     ap.add_argument("--graph", action="store_true",
                     help="time one CUDA-graph replay of --iters launches (no host launch overhead)")
     ap.add_argument("--shape", default="", help="n,k: one custom weight shape instead of the model's layers")
+    ap.add_argument("--pdl", action="store_true",
+                    help="launch with programmatic dependent launch, as inside the decode step")
+    ap.add_argument("--flush", action="store_true",
+                    help="with --graph: write a 256 MB buffer before every launch (weights cold in L2, as in "
+                         "the decode step) and report the time minus that of the flushes alone")
     a = ap.parse_args(argv)
 
     import torch
@@ -69,6 +77,7 @@ def main(argv=None) -> int:
     if a.shape:
         n_, k_ = (int(v) for v in a.shape.split(","))
         todo = [("custom", a.tokens, n_, k_)]
+    flush_buf = torch.empty(64 << 20, dtype=torch.float32, device="cuda") if a.flush else None
     for name, t, n, k in todo:
         if only and name not in only:
             continue
@@ -109,30 +118,47 @@ def main(argv=None) -> int:
                                   torch.zeros(sms * 8, dtype=torch.int32, device="cuda")) if p.streamk else None
 
             def run():
-                return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p,
-                                streamk=skb)
+                with G._rt.pdl() if a.pdl else contextlib.nullcontext():
+                    return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p,
+                                    streamk=skb)
 
             for _ in range(a.warmup):
                 run()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            flush_us = 0.0
             if a.graph:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
                     for _ in range(a.iters):
+                        if a.flush:
+                            flush_buf.fill_(1.0)
                         r = run()
                 g.replay()
                 torch.cuda.synchronize()
                 e0.record()
                 g.replay()
                 e1.record()
+                if a.flush:
+                    gf = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gf):
+                        for _ in range(a.iters):
+                            flush_buf.fill_(1.0)
+                    gf.replay()
+                    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    torch.cuda.synchronize()
+                    f0.record()
+                    gf.replay()
+                    f1.record()
+                    torch.cuda.synchronize()
+                    flush_us = f0.elapsed_time(f1) * 1000 / a.iters
             else:
                 e0.record()
                 for _ in range(a.iters):
                     r = run()
                 e1.record()
             torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1000 / a.iters
+            us = e0.elapsed_time(e1) * 1000 / a.iters - flush_us
             line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v, "kernel": p.kernel, "bn": p.bn,
                     "splits": p.splits, "grid": p.grid, "us": round(us, 1),
                     "weight_tbps": round(n * k * 2 / (us * 1e-6) / 1e12, 2),
