@@ -102,11 +102,66 @@ struct Cfg {
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(ACC_BUFS * ACC_COLS);
 };
 
-template <int BN, int MT>
+// ---- fused all-reduce of a row-parallel (tensor-parallel) GEMM ----------------------
+//
+// fb_gemm_bf16_ar_bn{BN}: every rank computes its partial product of the same
+// output and the epilogue all-reduces it tile by tile over NVSwitch while the
+// next tile's MMAs run:
+//   1. the partial tile is stored into P, this rank's slot of a symmetric
+//      buffer (local memory bound to an NVLS multicast object);
+//   2. one thread adds 1 to ready[tile] on every rank (multimem.red.release);
+//   3. once ready[tile] == world here (all ranks' partials of the tile are
+//      in place), the CTA reduces its 1/world share of the tile's rows in the
+//      switch (multimem.ld_reduce, fp32 accumulation) and multicasts the sums
+//      into O on every rank (multimem.st) - the reduce-scatter and the
+//      all-gather of the tile - then adds 1 to done on every rank;
+//   4. before exiting, every CTA waits for done == world * tiles here, so the
+//      kernel's completion means O holds the full sum on this rank.
+// Every rank runs the same tiles on the same CTAs in the same order, and a
+// CTA signals its tile before it waits for anyone, so no CTA waits for work
+// that cannot progress; all waits are bounded.
+// Counters live in a control block per buffer in symmetric memory: an epoch
+// word E (local, +1 by the last CTA to exit), a CTA exit ticket, done[2] and
+// ready[2][AR_MAX_TILES], indexed by the parity of E. A launch clears the
+// other parity's counters before it signals anything; every rank's next use
+// of that parity comes after this launch has completed everywhere.
+constexpr int EPI_AR = 1 << 20;
+constexpr int AR_EPOCH = 0, AR_TICKET = 1, AR_DONE = 2, AR_READY = 16;
+constexpr int AR_MAX_TILES = 4096;
+struct ArArgs {
+  uint64_t p_local;   // this rank's P (row stride ldo, bf16)
+  uint64_t p_mc;      // P through the multicast object
+  uint64_t o_mc;      // O (same layout as P) through the multicast object
+  uint64_t flags;     // this rank's control block
+  uint64_t flags_mc;  // the control block through the multicast object
+  int rank, world;
+};
+__device__ __forceinline__ void mc_red_add_release(uint64_t addr, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(uint64_t addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+// Bounded wait until the local counter at addr reaches want (false on timeout).
+__device__ __forceinline__ bool wait_counter(uint64_t addr, uint32_t want) {
+  const uint64_t t0 = globaltimer();
+  uint32_t spins = 0;
+  while (static_cast<int32_t>(ld_acquire_sys_u32(addr) - want) < 0) {
+    if ((++spins & 255u) == 0 && globaltimer() - t0 > FB_WAIT_NS) {
+      set_status(FB_KERR_TIMEOUT_PEER);
+      return false;
+    }
+  }
+  return true;
+}
+
+template <int BN, int MT, bool AR = false>
 __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmO,
                                           const CUtensorMap* tmR, bf16* __restrict__ out, const bf16* residual, int M,
                                           int N, int K, int ldo, int mode, int splits, float* __restrict__ ws,
-                                          long long split_stride) {
+                                          long long split_stride, ArArgs ar = ArArgs{}) {
   using C = Cfg<BN, MT>;
   constexpr int STAGES = C::STAGES;
   constexpr int NBUF = C::ACC_BUFS;
@@ -314,6 +369,17 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       ephase ^= 1;
       return done;
     };
+    uint32_t ar_par = 0;  // parity of this launch's counters
+    if constexpr (AR) {
+      uint32_t* fl = reinterpret_cast<uint32_t*>(ar.flags);
+      const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(fl + AR_EPOCH);
+      ar_par = epoch & 1u;
+      // Clear the other parity (this CTA's share) before signalling anything.
+      uint32_t* old_ready = fl + AR_READY + (ar_par ^ 1u) * AR_MAX_TILES;
+      for (int i = blockIdx.x * 128 + et; i < AR_MAX_TILES; i += gridDim.x * 128) old_ready[i] = 0;
+      if (blockIdx.x == 0 && et == 0) fl[AR_DONE + (ar_par ^ 1u)] = 0;
+      __threadfence_system();
+    }
     int it = 0;
     for (int u = blockIdx.x; ok && u < num_units && !*(volatile int*)abort_flag; u += gridDim.x, ++it) {
       const int mn = u / splits, sp = u % splits;
@@ -536,8 +602,75 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if constexpr (AR) {
+        // (1) this rank's partial tile is complete in P and visible system-wide
+        if (et == 0 && tma_out) {
+          bulk_wait_all();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+        __threadfence_system();
+        if (!(ok = epi_sync())) break;
+        // (2) announce it on every rank
+        const uint64_t ready = AR_READY * 4ull + (ar_par * AR_MAX_TILES + u) * 4ull;
+        if (et == 0) mc_red_add_release(ar.flags_mc + ready, 1);
+        // (3) all ranks' partials of this tile are in P: reduce this rank's
+        // share of its rows in the switch and multicast the sums into O
+        if (et == 0 && !wait_counter(ar.flags + ready, static_cast<uint32_t>(ar.world)))
+          *(volatile int*)abort_flag = 1;  // a peer never announced its tile: every thread stops
+        if (!(ok = epi_sync()) || *(volatile int*)abort_flag) {
+          ok = false;
+          break;
+        }
+        (void)ld_acquire_sys_u32(ar.flags + ready);  // acquire for this thread's reads below
+        const bool tr = (mode & EPI_TRANSPOSE) != 0;  // rows = tokens along N (swap-AB) or along M
+        const int r0 = tr ? n_blk * BN : m_blk * BM, c0 = tr ? m_blk * BM : n_blk * BN;
+        const int nr = min(tr ? BN : BM, (tr ? N : M) - r0), nc = min(tr ? BM : BN, (tr ? M : N) - c0);
+        const int vpr = nc >> 3;  // 16-byte vectors per row (nc % 8 == 0: checked by the host)
+        const int mine = (nr - ar.rank + ar.world - 1) / ar.world;  // rows r0 + rank + k * world
+        const int nv = mine * vpr;
+        constexpr int UNR = 8;
+#pragma unroll 1
+        for (int v0 = et; v0 < nv; v0 += 128 * UNR) {
+          uint32_t q[UNR][4];
+          uint64_t off[UNR];
+#pragma unroll
+          for (int j = 0; j < UNR; ++j) {
+            const int v = v0 + j * 128;
+            if (v < nv) {
+              const int row = r0 + ar.rank + (v / vpr) * ar.world, col = c0 + (v % vpr) * 8;
+              off[j] = (static_cast<uint64_t>(row) * ldo + col) * 2ull;
+              asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(q[j][0]), "=r"(q[j][1]), "=r"(q[j][2]), "=r"(q[j][3])
+                           : "l"(ar.p_mc + off[j])
+                           : "memory");
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < UNR; ++j) {
+            if (v0 + j * 128 < nv)
+              asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(ar.o_mc + off[j]),
+                           "r"(q[j][0]), "r"(q[j][1]), "r"(q[j][2]), "r"(q[j][3])
+                           : "memory");
+          }
+        }
+        __threadfence_system();
+        if (!(ok = epi_sync())) break;
+        if (et == 0) mc_red_add_release(ar.flags_mc + (AR_DONE + ar_par) * 4ull, 1);
+      }
     }
     if (et == 0 && tma_out) bulk_wait_all();  // the tile stores have read shared memory and landed
+    if constexpr (AR) {
+      if (et == 0) {
+        // (4) every rank's share of every tile has reached this rank's O
+        if (ok) ok = wait_counter(ar.flags + (AR_DONE + ar_par) * 4ull,
+                                  static_cast<uint32_t>(ar.world) * static_cast<uint32_t>(num_units));
+        uint32_t* fl = reinterpret_cast<uint32_t*>(ar.flags);
+        if (atomicAdd(fl + AR_TICKET, 1u) == gridDim.x - 1) {  // last CTA out: next launch, other parity
+          fl[AR_TICKET] = 0;
+          fl[AR_EPOCH] = fl[AR_EPOCH] + 1;
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -557,6 +690,16 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap* tmA, const CUtensor
     gemm_body<BN, MT>(&tmA, &tmB, &tmO, &tmR, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);        \
   }
 
+#define FB_GEMM_AR_INSTANCE(BN)                                                                                     \
+  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_bf16_ar_bn##BN(                              \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,                             \
+      const __grid_constant__ CUtensorMap tmO, bf16* out, int M, int N, int K, int ldo, int mode,                   \
+      unsigned long long p_mc, unsigned long long o_mc, unsigned long long flags, unsigned long long flags_mc,        \
+      int rank, int world) {                                                                                         \
+    const ArArgs ar{reinterpret_cast<uint64_t>(out), p_mc, o_mc, flags, flags_mc, rank, world};                     \
+    gemm_body<BN, 1, true>(&tmA, &tmB, &tmO, &tmO, out, nullptr, M, N, K, ldo, mode | EPI_AR, 1, nullptr, 0, ar);   \
+  }
+
 FB_GEMM_INSTANCE(16, 1)
 FB_GEMM_INSTANCE(32, 1)
 FB_GEMM_INSTANCE(64, 1)
@@ -567,6 +710,11 @@ FB_GEMM_INSTANCE(32, 2)
 FB_GEMM_INSTANCE(64, 2)
 FB_GEMM_INSTANCE(128, 2)
 FB_GEMM_INSTANCE(256, 2)
+FB_GEMM_AR_INSTANCE(16)
+FB_GEMM_AR_INSTANCE(32)
+FB_GEMM_AR_INSTANCE(64)
+FB_GEMM_AR_INSTANCE(128)
+FB_GEMM_AR_INSTANCE(256)
 
 // ==== stream-K variant (swap-AB decode GEMMs with more tiles than SMs) =================
 //
@@ -978,13 +1126,14 @@ struct PairCfg {
   static constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 A rows per K step
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's half of the B rows
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
   static constexpr int ACC_BUFS = (2 * BN <= 512) ? 2 : 1;
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(ACC_BUFS * BN);
 };
 
 template <int BN>
-__device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUtensorMap* tmB, bf16* __restrict__ out,
+__device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUtensorMap* tmB, const CUtensorMap* tmO,
+                                               const CUtensorMap* tmR, bf16* __restrict__ out,
                                                const bf16* residual, int M, int N, int K, int ldo, int mode,
                                                int splits, float* __restrict__ ws, long long split_stride) {
   using C = PairCfg<BN>;
@@ -994,11 +1143,14 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                           // [STAGES][128 x 64]
   uint8_t* sB = smem + STAGES * C::A_BYTES;     // [STAGES][BN/2 x 64]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* stg = smem + STAGES * C::STAGE_BYTES;  // epilogue tiles of this CTA (STG_BYTES)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + STG_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* ebar = tempty + 2;  // this CTA's four epilogue warps' rendezvous
+  uint64_t* rbar = ebar + 1;    // residual tile loads, one per buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 2);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -1020,6 +1172,9 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 8);
     }
+    mbar_init(ebar, 4);
+    mbar_init(&rbar[0], 1);
+    mbar_init(&rbar[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async();
@@ -1027,6 +1182,10 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(tmA);
     tma_prefetch_desc(tmB);
+    if (mode & EPI_TMA_OUT) {
+      tma_prefetch_desc(tmO);
+      if (mode & EPI_RESIDUAL) tma_prefetch_desc(tmR);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -1129,6 +1288,17 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int quarter = warp & 3;
     const uint32_t tempty0 = mapa_cta(&tempty[0], 0), tempty1 = mapa_cta(&tempty[1], 0);
+    const int et = threadIdx.x - 64;  // 0..127; 0 issues this CTA's tile stores
+    const bool tma_out = (mode & EPI_TMA_OUT) && (mode & EPI_TRANSPOSE);
+    uint32_t ephase = 0, rphase = 0, chunk = 0;
+    bool ok = true;
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ebar);
+      const bool done = mbar_wait(ebar, ephase, FB_KERR_TIMEOUT_TMEM);
+      ephase ^= 1;
+      return done;
+    };
     int it = 0;
     for (int u = pair; u < num_units && !*(volatile int*)abort_flag; u += num_pairs, ++it) {
       const int mn = u / splits, sp = u % splits;
@@ -1143,6 +1313,63 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
       float* part = splits > 1 ? ws + static_cast<size_t>(sp) * split_stride : nullptr;
       const int gm = m_blk * 2 * BM + rank * BM + quarter * 32 + lane;  // D row of this thread
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      if (tma_out) {
+        // Staged TMA-store epilogue (as fb_gemm_bf16): per 32-token chunk a
+        // [32 tokens][128 features] tile of this CTA's rows, double-buffered.
+        constexpr int EC = BN < EPI_COLS ? BN : EPI_COLS;
+        const int gm0 = m_blk * 2 * BM + rank * BM;
+        const int f = quarter * 32 + lane;
+#pragma unroll 1
+        for (int c1 = 0; c1 < BN && ok; c1 += EC, ++chunk) {
+          const int buf = chunk & 1;
+          const int gn0 = n_blk * BN + c1;
+          float* sf = reinterpret_cast<float*>(stg) + buf * (EPI_COLS * BM);
+          bf16* sb = reinterpret_cast<bf16*>(stg) + buf * (EPI_COLS * BM);
+          bf16* sr = reinterpret_cast<bf16*>(stg + STG_BYTES / 2) + buf * (EPI_COLS * BM);
+          uint32_t rr[EC];
+#pragma unroll
+          for (int j = 0; j < EC / 16; ++j)
+            tmem_ld16(t_row + c1 + 16 * j, *reinterpret_cast<uint32_t(*)[16]>(rr + 16 * j));
+          tmem_ld_wait();
+          if (et == 0 && chunk >= 2) bulk_wait_read_1();  // this buffer's previous store has read it
+          if (!(ok = epi_sync())) break;
+          if (!part && (mode & EPI_RESIDUAL)) {
+            if (et == 0) {
+              mbar_arrive_expect_tx(&rbar[buf], EC * BM * 2);
+              tma_load_2d(sr, tmR, &rbar[buf], gm0, gn0);
+            }
+            if (!(ok = mbar_wait(&rbar[buf], (rphase >> buf) & 1u, FB_KERR_TIMEOUT_FULL))) break;
+            rphase ^= 1u << buf;
+          }
+          if (part) {
+#pragma unroll
+            for (int t = 0; t < EC; ++t) sf[t * BM + f] = __uint_as_float(rr[t]);
+          } else if (mode & EPI_RESIDUAL) {
+#pragma unroll
+            for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(__uint_as_float(rr[t]) + bf2f(sr[t * BM + f]));
+          } else {
+#pragma unroll
+            for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(__uint_as_float(rr[t]));
+          }
+          fence_proxy_async();  // generic-proxy writes -> visible to the TMA engine
+          if (!(ok = epi_sync())) break;
+          if (et == 0) {
+            if (part)
+              tma_store_3d(tmO, sf, gm0, gn0, sp);
+            else
+              tma_store_2d(tmO, sb, gm0, gn0);
+            bulk_commit();
+          }
+        }
+        if (!ok) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+        continue;
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
@@ -1184,6 +1411,7 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? tempty1 : tempty0);
     }
+    if (et == 0 && tma_out) bulk_wait_all();  // the tile stores have read shared memory and landed
   }
 
   tc_fence_before();
@@ -1196,10 +1424,11 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
 
 #define FB_GEMM_PAIR_INSTANCE(BN)                                                                                   \
   extern "C" __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1) fb_gemm2_bf16_bn##BN(      \
-      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, bf16* out,                  \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,                             \
+      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmR, bf16* out,                  \
       const bf16* residual, int M, int N, int K, int ldo, int mode, int splits, float* ws,                          \
       long long split_stride) {                                                                                      \
-    gemm_pair_body<BN>(&tmA, &tmB, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);                   \
+    gemm_pair_body<BN>(&tmA, &tmB, &tmO, &tmR, out, residual, M, N, K, ldo, mode, splits, ws, split_stride);       \
   }
 
 FB_GEMM_PAIR_INSTANCE(64)

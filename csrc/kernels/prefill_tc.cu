@@ -33,6 +33,7 @@ constexpr int BKV = 128;  // keys per tile
 constexpr int HALF = BQ * 128;          // one 64-dim half of a 128-row tile: 128 rows x 128 B
 constexpr int TILE = 2 * HALF;           // 128 rows x 128 dims bf16
 constexpr int STAGES = 2;
+constexpr float RESCALE_LOG2 = 8.f;  // lazy-rescale threshold (log2 units: p <= 256)
 
 struct Smem {
   uint8_t q[TILE];
@@ -210,22 +211,27 @@ extern "C" __global__ void __launch_bounds__(192, 1) fb_prefill_attn_tc(
       tc_fence_after();
       const uint32_t t_s = tmem + sb * 128 + lane_base;
       const int kpos0 = j * BKV;  // key positions of this tile: kpos0 + c
-      // pass 1: row max over the valid keys
+      // pass 1: row max over the valid keys (64 columns per TMEM round trip)
       float mx = -INFINITY;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BKV; c0 += 16) {
-        uint32_t sr[16];
-        tmem_ld16(t_s + c0, sr);
+      for (int c1 = 0; c1 < BKV; c1 += 64) {
+        uint32_t sr[64];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld16(t_s + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(sr + 16 * q));
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int kp = kpos0 + c0 + i;
+        for (int i = 0; i < 64; ++i) {
+          const int kp = kpos0 + c1 + i;
           if (qvalid && kp <= qpos) mx = fmaxf(mx, __uint_as_float(sr[i]) * scale_log2);
         }
       }
-      const float m_new = fmaxf(m_run, mx);
+      // Lazy rescaling: the running max of a row moves (and O is rescaled)
+      // only when the tile's max exceeds it by more than RESCALE_LOG2; until
+      // then p = exp2(s - m) stays below 2^RESCALE_LOG2, exact in the fp32
+      // sums. A warp rescales its O rows only if one of them moved.
+      const float m_new = (mx > m_run + RESCALE_LOG2 || m_run == -INFINITY) ? fmaxf(m_run, mx) : m_run;
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m_run - m_use);  // 0 on the first tile (m_run = -inf)
+      const float alpha = exp2f(m_run - m_use);  // 0 on the first tile (m_run = -inf), else 1 unless moved
       // P_j may only be written once PV_{j-1} has consumed P_{j-1}; O is
       // rescaled in place before PV_j accumulates into it.
       if (j > 0) {
@@ -236,13 +242,17 @@ extern "C" __global__ void __launch_bounds__(192, 1) fb_prefill_attn_tc(
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c0 = 0; c0 < D; c0 += 16) {
-            uint32_t orr[16];
-            tmem_ld16(t_o + lane_base + c0, orr);
+          for (int c1 = 0; c1 < D; c1 += 64) {
+            uint32_t orr[64];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              tmem_ld16(t_o + lane_base + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(orr + 16 * q));
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
-            tmem_st16(t_o + lane_base + c0, orr);
+            for (int i = 0; i < 64; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              tmem_st16(t_o + lane_base + c1 + 16 * q, *reinterpret_cast<const uint32_t(*)[16]>(orr + 16 * q));
           }
           tmem_st_wait();
         }
@@ -250,27 +260,32 @@ extern "C" __global__ void __launch_bounds__(192, 1) fb_prefill_attn_tc(
       // pass 2: p = exp2(s - m), row sum, P row to shared memory
       float rs = 0.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BKV; c0 += 16) {
-        uint32_t sr[16];
-        tmem_ld16(t_s + c0, sr);
+      for (int c1 = 0; c1 < BKV; c1 += 64) {
+        uint32_t sr[64];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld16(t_s + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(sr + 16 * q));
         tmem_ld_wait();
-        float p[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int kp = kpos0 + c0 + i;
-          p[i] = (qvalid && kp <= qpos) ? exp2f(__uint_as_float(sr[i]) * scale_log2 - m_use) : 0.f;
-          rs += p[i];
-        }
-        uint4 lo, hi;
-        bf162* l2 = reinterpret_cast<bf162*>(&lo);
-        bf162* h2 = reinterpret_cast<bf162*>(&hi);
+        for (int c2 = 0; c2 < 64; c2 += 16) {
+          const int c0 = c1 + c2;
+          float p[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          l2[i] = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
-          h2[i] = __floats2bfloat162_rn(p[8 + 2 * i], p[8 + 2 * i + 1]);
+          for (int i = 0; i < 16; ++i) {
+            const int kp = kpos0 + c0 + i;
+            p[i] = (qvalid && kp <= qpos) ? exp2f(__uint_as_float(sr[c2 + i]) * scale_log2 - m_use) : 0.f;
+            rs += p[i];
+          }
+          uint4 lo, hi;
+          bf162* l2 = reinterpret_cast<bf162*>(&lo);
+          bf162* h2 = reinterpret_cast<bf162*>(&hi);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            l2[i] = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
+            h2[i] = __floats2bfloat162_rn(p[8 + 2 * i], p[8 + 2 * i + 1]);
+          }
+          *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0)) = lo;
+          *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0 + 8)) = hi;
         }
-        *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0)) = lo;
-        *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0 + 8)) = hi;
       }
       tc_fence_before();
       __syncwarp();

@@ -255,6 +255,9 @@ class LlamaModel:
             from ..parallel import comm
 
             ex = st.tp.slots
+            if _TP_REDUCE == "fused" and ex.gemm_allreduce(inp, weight, which):
+                # one kernel: GEMM tiles reduced in the switch and multicast as they finish
+                return ("reduced", which)
             if ex.symm.multicast and (rows >= NVLS_MIN_ROWS_2 or (rows >= NVLS_MIN_ROWS and (
                     ex.symm.world > 2 or _TP_REDUCE == "nvls"))):
                 # many rows: partial sums reduced in the switch (one copy of the

@@ -58,19 +58,22 @@ def smem_bytes(bn: int, mt: int = 1) -> int:
 
 
 def smem_bytes_pair(bn: int) -> int:
-    """Shared memory of one CTA of the two-SM kernel (its 128 A rows + bn/2 B rows per stage)."""
+    """Shared memory of one CTA of the two-SM kernel (its 128 A rows + bn/2 B
+    rows per stage, ring of 192 KB at most), staging, barriers."""
     stage = BM * BK * 2 + (bn // 2) * BK * 2
-    stages = min(8, (200 * 1024) // stage)
-    return stages * stage + 1024 + 256
+    stages = min(8, (192 * 1024) // stage)
+    return stages * stage + STG_BYTES + 1024 + 256
 
 
-# Two-SM (cta_group::2) tiles for swap-AB decode GEMMs: "1" uses them for
-# every swap plan with tiles of 64+ tokens, "0" (default) never. Measured on
-# B200 at 256 tokens (us, one-SM -> two-SM): gate_up 4096->28672 72.8 -> 68.3,
-# lm_head 4096->128256 243.8 -> 232.6, but qkv 21.9 -> 25.4, o 19.2 -> 23.0,
-# down 33.6 -> 37.1 and 64/128-token gate_up 48.2 -> 53.0 / 53.9 -> 58.0:
-# halving each SM's token-operand traffic is not what bounds these GEMMs.
-_PAIR = os.environ.get("FOUNDRY_GEMM_PAIR", "0")
+# Two-SM (cta_group::2) tiles for swap-AB decode GEMMs: "auto" (default) uses
+# them, with 256-token tiles, for 256-token batches; "1" for every swap plan
+# with tiles of 64+ tokens; "0" never. Measured on B200 at 256 tokens with both
+# kernels on the staged TMA-store epilogue (CUDA graph of 20 launches, L2
+# flushed before each, programmatic dependent launch; us, one-SM -> two-SM):
+# qkv 19.8 -> 19.3, o 17.5 -> 16.6 (4 splits), down 36.7 -> 31.9, lm_head
+# 242.5 -> 225.3. Each SM loads half the token tile per k-block, so a stage
+# is 32 KB instead of 48 KB at the same tensor work.
+_PAIR = os.environ.get("FOUNDRY_GEMM_PAIR", "auto")
 
 
 @dataclass
@@ -200,7 +203,7 @@ class Plan:
 
 
 def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bool = True,
-         allow_streamk: bool = False) -> Plan:
+         allow_streamk: bool = False, allow_pair: bool = True) -> Plan:
     """Chooses the tile width and split count with a small cost model:
     waves of CTAs x k-blocks per CTA x time per k-block, bounded below by the
     HBM time of the operands, plus the traffic of split slices."""
@@ -248,8 +251,11 @@ def plan(m_tok: int, n_out: int, k: int, sms: int | None = None, allow_split: bo
     # with the TMA-store epilogue, CUDA-graph timed): 43.4 -> 35.0 us at 32
     # tokens (bn 32), 44.6 -> 38.3 us at 64 (bn 64), but 56.7 -> 68.0 us at
     # 256 (bn 256) and 77.0 us with bn 128, so only narrow tiles use it.
-    if _PAIR == "1" and best.swap and best.bn >= 64 and mg >= 2 * BM:
-        return pair_plan(mg, ng, k, best.bn, sms, allow_split, best.pf)
+    if allow_pair and best.swap and mg >= 2 * BM and not (allow_streamk and best.bn <= 64):
+        if _PAIR == "1" and best.bn >= 64:
+            return pair_plan(mg, ng, k, best.bn, sms, allow_split, best.pf)
+        if _PAIR == "auto" and ng >= 256:
+            return pair_plan(mg, ng, k, 256, sms, allow_split, best.pf)
     if allow_streamk and best.swap and best.splits == 1 and best.mt == 1 and best.bn <= 64:
         tiles = math.ceil(mg / BM) * math.ceil(ng / best.bn)
         if tiles > sms and tiles % sms:
@@ -265,7 +271,7 @@ def pair_plan(mg: int, ng: int, k: int, bn: int, sms: int, allow_split: bool = T
     kb = math.ceil(k / BK)
     tiles = math.ceil(mg / (2 * BM)) * math.ceil(ng / bn)
     stage = BM * BK * 2 + (bn // 2) * BK * 2  # per SM
-    stages = min(8, (200 * 1024) // stage)
+    stages = min(8, (192 * 1024) // stage)
     mma = 2 * BM * bn * BK / _SM_MMA_FLOPS
     t_kb = max((_TMA_LATENCY + mma) / stages, stage / _CTA_FILL_BPS_MAX, mma)
     dram = (mg * k + ng * k) * 2 / _HBM_BPS
@@ -346,8 +352,8 @@ def linear_multicast(x: torch.Tensor, w: torch.Tensor, target: int, plan_overrid
     buffer as soon as it is computed (the GEMM half of a fused all-reduce)."""
     t_tok, k = x.shape
     n_out = w.shape[0]
-    p = plan_override or plan(t_tok, n_out, k, allow_split=False)
-    assert p.splits == 1
+    p = plan_override or plan(t_tok, n_out, k, allow_split=False, allow_pair=False)
+    assert p.splits == 1 and not p.pair
     if p.swap:
         a, b, mg, ng, mode = w, x, n_out, t_tok, EPI_TRANSPOSE | EPI_MCAST
     else:
@@ -392,12 +398,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         need = p.splits * t_tok * n_out
         if need > partials.numel:
             raise RuntimeError(f"split-K slice buffer too small: need {need} floats, have {partials.numel}")
-        maps = []
-        if not p.pair:
-            pm = partial_map(partials.buf.data_ptr(), n_out, t_tok, p.splits, p.bn) if p.swap else None
-            if pm is not None:
-                mode |= EPI_TMA_OUT
-            maps = [pm or _NO_MAP, _NO_MAP]
+        pm = partial_map(partials.buf.data_ptr(), n_out, t_tok, p.splits, p.bn) if p.swap else None
+        if pm is not None:
+            mode |= EPI_TMA_OUT
+        maps = [pm or _NO_MAP, _NO_MAP]
         args = [tmap(a, BM), tmap(b, p.b_box), *maps, 0, 0, mg, ng, k, n_out, mode, p.splits,
                 partials.buf.data_ptr(), t_tok * n_out]
         _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)
@@ -417,15 +421,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
                 streamk.flags.data_ptr()]
         _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=smem_bytes(p.bn, 1))
         return out
-    maps = []
-    if not p.pair:
-        om = None
-        if p.swap:
-            om = out_maps(out.data_ptr(), residual.data_ptr() if residual is not None else 0, n_out, t_tok,
-                          out.stride(0), p.bn)
-        if om is not None:
-            mode |= EPI_TMA_OUT
-        maps = list(om) if om is not None else [_NO_MAP, _NO_MAP]
+    om = None
+    if p.swap:
+        om = out_maps(out.data_ptr(), residual.data_ptr() if residual is not None else 0, n_out, t_tok,
+                      out.stride(0), p.bn)
+    if om is not None:
+        mode |= EPI_TMA_OUT
+    maps = list(om) if om is not None else [_NO_MAP, _NO_MAP]
     args = [tmap(a, BM), tmap(b, p.b_box), *maps, out.data_ptr(), residual.data_ptr() if residual is not None else 0,
             mg, ng, k, out.stride(0), mode, 1, 0, 0]
     _rt.launch("gemm_bf16", p.kernel, (p.grid,), (192,), args, smem=p.smem)

@@ -47,10 +47,19 @@ def all_reduce(symm: SymmetricMemory, offset: int, n: int, out: torch.Tensor, al
     return out
 
 
-class SlotExchange:
-    """Two alternating [world][rows][cols] bf16 slot buffers in symmetric memory."""
+# Control block of the fused GEMM + all-reduce kernel (csrc/kernels/gemm_bf16.cu,
+# fb_gemm_bf16_ar_bn*): epoch, exit ticket, done[2], ready[2][AR_MAX_TILES]
+# (u32 words from word 16), one block per slot buffer.
+AR_MAX_TILES = 4096
+AR_BLOCK_BYTES = -(-((16 + 2 * AR_MAX_TILES) * 4) // 4096) * 4096
 
-    def __init__(self, symm: SymmetricMemory, offset: int, rows: int, cols: int):
+
+class SlotExchange:
+    """Two alternating [world][rows][cols] bf16 slot buffers in symmetric
+    memory, and (``ar_offset``) the two control blocks of the fused GEMM +
+    all-reduce, zeroed by the owner before first use."""
+
+    def __init__(self, symm: SymmetricMemory, offset: int, rows: int, cols: int, ar_offset: int | None = None):
         self.symm = symm
         self.rows, self.cols = rows, cols
         self.slot_bytes = rows * cols * 2
@@ -58,7 +67,53 @@ class SlotExchange:
         self.offset = offset
         if offset + 2 * self.buf_bytes > symm.size:
             raise ValueError("symmetric buffer too small for the slot exchange")
+        if ar_offset is not None and ar_offset + 2 * AR_BLOCK_BYTES > symm.size:
+            raise ValueError("symmetric buffer too small for the all-reduce control blocks")
+        self.ar_offset = ar_offset
         self.which = 0
+
+    def gemm_allreduce(self, x: torch.Tensor, w: torch.Tensor, which: int) -> bool:
+        """x @ w.T summed over ranks into slot 1 of buffer ``which`` on every
+        rank, by one kernel: the GEMM epilogue writes this rank's partial tile
+        into slot 0, and as soon as every rank has its tile the CTA reduces
+        its 1/world share of the tile's rows in the switch and multicasts the
+        sums (a tile-granular reduce-scatter + all-gather over NVSwitch that
+        overlaps the next tile's MMAs). Returns False, launching nothing,
+        when this buffer has no multicast object or control block, or the
+        shape does not fit the kernel (then use another path)."""
+        from ..ops import gemm as G
+
+        s = self.symm
+        t_tok, k = x.shape
+        n_out = w.shape[0]
+        if not s.multicast or self.ar_offset is None or t_tok > self.rows or n_out != self.cols or n_out % 8:
+            return False
+        p = G.plan(t_tok, n_out, k, allow_split=False, allow_pair=False)
+        units = math.ceil((n_out if p.swap else t_tok) / G.BM) * math.ceil((t_tok if p.swap else n_out) / p.bn)
+        if units > AR_MAX_TILES:
+            return False
+        part = self.slot(which, 0)[:t_tok]
+        if p.swap:
+            a, b, mg, ng = w, x, n_out, t_tok
+            om = G.out_maps(part.data_ptr(), 0, n_out, t_tok, part.stride(0), p.bn)
+            if om is None:
+                return False
+            mode = G.EPI_TRANSPOSE | G.EPI_TMA_OUT
+            if math.ceil(ng / p.bn) == 1:
+                mode |= G.EPI_A_STREAM
+            if _rt.pdl_active():
+                mode |= G.EPI_A_CONST
+            omap = om[0]
+        else:
+            a, b, mg, ng, mode, omap = x, w, t_tok, n_out, 0, G._NO_MAP
+        mode |= (min(p.pf, 255) & 0xFF) << 8
+        p_mc = s.mc_ptr + self._buf_off(which)
+        fl = self.ar_offset + which * AR_BLOCK_BYTES
+        _rt.launch("gemm_bf16", f"fb_gemm_bf16_ar_bn{p.bn}", (min(units, _rt.sm_count()),), (192,), [
+            G.tmap(a, G.BM), G.tmap(b, p.bn), omap, part.data_ptr(), mg, ng, k, part.stride(0), mode,
+            p_mc, p_mc + self.slot_bytes, s.ptr(s.rank, fl), s.mc_ptr + fl, s.rank, s.world,
+        ], smem=G.smem_bytes(p.bn, 1))
+        return True
 
     @property
     def nbytes(self) -> int:

@@ -92,13 +92,25 @@ class TPContext:
         from ..parallel.symm import CTRL_BYTES, SymmetricMemory
         import torch.distributed as dist
 
+        from ..parallel.comm import AR_BLOCK_BYTES
+
         world = dist.get_world_size(group)
         pairs_bytes = -(-(world * pair_rows * 8) // 4096) * 4096
         slot_off = CTRL_BYTES + pairs_bytes
-        self.symm = SymmetricMemory(slot_off + 2 * world * rows * hidden * 2, group)
+        ar_off = -(-(slot_off + 2 * world * rows * hidden * 2) // 4096) * 4096
+        self.symm = SymmetricMemory(ar_off + 2 * AR_BLOCK_BYTES, group)
         self.pairs_offset = CTRL_BYTES
-        self.slots = SlotExchange(self.symm, slot_off, rows, hidden)
+        self.slots = SlotExchange(self.symm, slot_off, rows, hidden, ar_offset=ar_off)
         self.rank, self.world = self.symm.rank, world
+        # counters of the fused GEMM + all-reduce start at zero on every rank
+        if self.symm.mock:
+            import ctypes
+
+            ctypes.memset(self.symm.ptr(self.rank, ar_off), 0, 2 * AR_BLOCK_BYTES)
+        else:
+            self.symm.tensor(self.rank, (2 * AR_BLOCK_BYTES,), torch.uint8, ar_off).zero_()
+            torch.cuda.synchronize()
+        dist.barrier(group=group)
 
     def close(self) -> None:
         self.symm.close()

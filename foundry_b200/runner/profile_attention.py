@@ -64,6 +64,8 @@ def main(argv=None) -> int:
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--check", action="store_true")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="force this many KV splits per sequence (0 = the planner's choice)")
     a = ap.parse_args(argv)
     from foundry_b200 import ops
     from foundry_b200.ops.attention import DecodeWorkspace, decode_splits
@@ -83,6 +85,9 @@ def main(argv=None) -> int:
     q = torch.randn(b, hq, d, device=dev, generator=gen, dtype=torch.bfloat16)
     scale = 1.0 / math.sqrt(d)
     splits = decode_splits(b, hkv, max_pages)
+    if a.splits:
+        cps = math.ceil(math.ceil(max_pages / 2) / a.splits)
+        splits = (math.ceil(math.ceil(max_pages / 2) / cps), 2 * cps)
     ws = DecodeWorkspace(b, hq, max(splits[0], 1), device=dev)
     live = int(lens.sum())
     algo_bytes = live * hkv * d * 2 * 2 + 2 * q.numel() * 2

@@ -60,7 +60,17 @@ def test_pair_plans_are_launchable(t, n, k):
     assert p.splits == 1 or kb // p.splits >= 4
 
 
-def test_pair_tiles_are_opt_in():
-    assert G._PAIR == os.environ.get("FOUNDRY_GEMM_PAIR", "0")
-    if G._PAIR != "1":
-        assert not any(G.plan(t, n, k, sms=148).pair for (t, n, k) in SHAPES)
+def test_pair_tile_policy():
+    """Default ("auto"): two-SM tiles, 256 tokens wide, exactly for swap-AB
+    plans of 256-token batches with at least 256 weight rows; never when the
+    caller cannot take them (multicast / all-reduce epilogues)."""
+    assert G._PAIR == os.environ.get("FOUNDRY_GEMM_PAIR", "auto")
+    for (t, n, k) in SHAPES:
+        assert not G.plan(t, n, k, sms=148, allow_pair=False).pair
+        if G._PAIR == "auto":
+            p = G.plan(t, n, k, sms=148)
+            assert p.pair == (t == 256 and n >= 256), (t, n, k, p)
+            if p.pair:
+                assert p.bn == 256 and p.kernel in KERNELS
+        elif G._PAIR == "0":
+            assert not any(G.plan(t, n, k, sms=148).pair for (t, n, k) in SHAPES)

@@ -124,11 +124,12 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def _run_ranks(body, world, archive):
+def _run_ranks(body, world, archive, reduce="nvls"):
     port = _free_port()
     # FOUNDRY_TP_REDUCE=nvls: prefill rows (>= 128) take the NVLS reduce path
-    # even at 2 ranks, decode rows the multicast slot exchange
-    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", FOUNDRY_TP_REDUCE="nvls")
+    # even at 2 ranks, decode rows the multicast slot exchange; "fused": every
+    # row-parallel GEMM all-reduces in its own epilogue
+    env = dict(os.environ, PYTHONPATH=ROOT, NCCL_NVLS_ENABLE="0", FOUNDRY_TP_REDUCE=reduce)
     procs = []
     for rank in range(world):
         code = f"ROOT={ROOT!r}; PORT={port}; RANK={rank}; WORLD={world}; ARCHIVE={archive!r}\n" + body
@@ -146,3 +147,78 @@ def test_tensor_parallel_decode_save_load(tmp_path):
     archive = str(tmp_path / "tp_archive")
     _run_ranks(SAVE, world, archive)
     _run_ranks(LOAD, world, archive)
+
+
+AR_KERNEL = r"""
+import os, sys
+sys.path.insert(0, ROOT)
+import torch, torch.distributed as dist
+torch.cuda.set_device(RANK)
+dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % PORT, rank=RANK, world_size=WORLD)
+from foundry_b200 import ops
+from foundry_b200.ops import _rt
+from foundry_b200.runner.engine import TPContext
+from foundry_b200.graphs import CUDAGraph, graph
+
+ROWS, H = 1024, 1024
+tp = TPContext(ROWS, H, 16)
+ex = tp.slots
+assert ex.symm.multicast, "no NVLS multicast on this node"
+g = torch.Generator(device="cuda").manual_seed(99)
+for t, k in ((7, 512), (64, 2048), (256, 1024), (300, 512), (1024, 256)):
+    # every rank's own x and w shard; the reference sums all ranks' products
+    xs = [(torch.randn(t, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16) for _ in range(WORLD)]
+    ws = [(torch.randn(H, k, device="cuda", generator=g) * 0.05).to(torch.bfloat16) for _ in range(WORLD)]
+    ref = sum(x.float() @ w.float().T for x, w in zip(xs, ws))
+    for which in (0, 1, 0, 1):  # parity of each control block flips every launch
+        ex.slot(which, 1)[:t].fill_(float("nan"))
+        dist.barrier()
+        with _rt.pdl():
+            assert ex.gemm_allreduce(xs[RANK], ws[RANK], which)
+        torch.cuda.synchronize()
+        got = ex.slot(which, 1)[:t].float()
+        torch.testing.assert_close(got, ref, atol=3e-2, rtol=2e-2)
+        dist.barrier()
+    # captured in a CUDA graph and replayed (the epoch advances on the device)
+    gr = CUDAGraph()
+    with graph(gr):
+        with _rt.pdl():
+            ex.gemm_allreduce(xs[RANK], ws[RANK], 0)
+            ex.gemm_allreduce(xs[RANK], ws[RANK], 1)
+    for _ in range(3):
+        ex.slot(0, 1)[:t].zero_()
+        ex.slot(1, 1)[:t].zero_()
+        dist.barrier()
+        gr.replay()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(ex.slot(0, 1)[:t].float(), ref, atol=3e-2, rtol=2e-2)
+        torch.testing.assert_close(ex.slot(1, 1)[:t].float(), ref, atol=3e-2, rtol=2e-2)
+        dist.barrier()
+    del gr
+assert ops.status("gemm_bf16") == 0, ops.status("gemm_bf16")
+dist.barrier()
+tp.close()
+dist.destroy_process_group()
+print("RANK_OK", RANK)
+"""
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+def test_fused_gemm_allreduce_kernel():
+    """fb_gemm_bf16_ar_bn*: the row-parallel GEMM whose epilogue all-reduces
+    its tiles over NVSwitch equals the fp32 sum of every rank's product, on
+    swap-AB (decode) and token-major (prefill) shapes, on repeated launches
+    of both control blocks and replayed from a CUDA graph."""
+    world = min(torch.cuda.device_count(), 8)
+    _run_ranks(AR_KERNEL, world, "")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+def test_tensor_parallel_fused_allreduce_save_load(tmp_path):
+    """The TP engine with every row-parallel GEMM all-reducing in its own
+    epilogue: greedy tokens match the fp32 reference, and a SAVEd archive
+    LOADs and replays to the same tokens."""
+    world = 2 if torch.cuda.device_count() < 4 else min(torch.cuda.device_count(), 8)
+    archive = str(tmp_path / "tp_fused_archive")
+    _run_ranks(SAVE, world, archive, reduce="fused")
+    _run_ranks(LOAD, world, archive, reduce="fused")
