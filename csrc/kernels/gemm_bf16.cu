@@ -1195,7 +1195,6 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
   cluster_sync_all();  // both CTAs' barriers initialised before either signals the other
   tc_fence_after();
   pdl_trigger();
-  pdl_wait();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -1206,6 +1205,21 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
       const uint64_t pol_a = (mode & EPI_A_STREAM) ? policy_evict_first() : policy_evict_last();
       const uint64_t pol_b = (mode & EPI_B_STREAM) ? policy_evict_first() : policy_evict_last();
       const int pf_dist = (mode >> 8) & 0xFF;
+      // Before waiting for the previous kernel: the first unit's weight (A)
+      // tiles of the whole ring, when no kernel of the step writes A
+      // (EPI_A_CONST); the token tiles (B) follow pdl_wait.
+      int pre = 0;
+      if ((mode & EPI_A_CONST) && pair < num_units) {
+        const int mn = pair / splits, sp = pair % splits;
+        const int kb0 = sp * kb_per, kb1 = min(KB, kb0 + kb_per);
+        const int a_row = (mn % num_m) * 2 * BM + rank * BM;
+        pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(sA + i * C::A_BYTES, tmA, mapa_cta(&full[i], 0), (kb0 + i) * BK, a_row, pol_a);
+        }
+      }
+      pdl_wait();
       for (int u = pair; u < num_units && !*(volatile int*)abort_flag; u += num_pairs) {
         const int mn = u / splits, sp = u % splits;
         const int m_blk = mn % num_m, n_blk = mn / num_m;
@@ -1215,13 +1229,15 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
         for (int kb = kb0; kb < min(kb1, kb0 + pf_dist); ++kb) tma_prefetch_2d(tmA, kb * BK, a_row);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (pf_dist && kb + pf_dist < kb1) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, a_row);
-          if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
-            *(volatile int*)abort_flag = 1;
-            break;
-          }
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
           const uint32_t bar = mapa_cta(&full[stage], 0);
-          tma_load_2d_pair(sA + stage * C::A_BYTES, tmA, bar, kb * BK, a_row, pol_a);
+          if (!(u == pair && kb - kb0 < pre)) {  // else armed, A issued before pdl_wait
+            if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+              *(volatile int*)abort_flag = 1;
+              break;
+            }
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(sA + stage * C::A_BYTES, tmA, bar, kb * BK, a_row, pol_a);
+          }
           tma_load_2d_pair(sB + stage * C::B_BYTES, tmB, bar, kb * BK, b_row, pol_b);
           if (++stage == STAGES) {
             stage = 0;
@@ -1286,6 +1302,7 @@ __device__ __forceinline__ void gemm_pair_body(const CUtensorMap* tmA, const CUt
     }
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    pdl_wait();  // residual reads and output writes follow the previous kernel
     const int quarter = warp & 3;
     const uint32_t tempty0 = mapa_cta(&tempty[0], 0), tempty1 = mapa_cta(&tempty[1], 0);
     const int et = threadIdx.x - 64;  // 0..127; 0 issues this CTA's tile stores

@@ -402,3 +402,37 @@ def test_linear_swiglu(t, inter, k, bn):
     ref = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
     torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=2e-2)
     assert ops.status("gemm_bf16") == 0
+
+
+@pytest.mark.parametrize("t,n,k", [(256, 4096, 4096), (256, 6144, 4096), (200, 4096, 1024), (64, 28672, 512)])
+def test_linear_under_programmatic_dependent_launch(t, n, k):
+    """Decode GEMMs launched with programmatic dependent launch (as inside
+    the decode step: the weight tiles of the first ring are loaded before
+    griddepcontrol.wait), back to back with kernels that write their inputs
+    and outputs: same results as fp32, one-SM and two-SM plans, with and
+    without split-K slices."""
+    from foundry_b200 import ops
+    from foundry_b200.ops import _rt
+
+    w = _bf(n, k, seed=61, scale=0.02)
+    ref_out = []
+    outs = []
+    pb = ops.PartialBuffer(8 * t * n)
+    with _rt.pdl():
+        for i in range(3):
+            x0 = _bf(t, k, seed=70 + i)
+            h = _bf(t, n, seed=80 + i)
+            out = h.clone()
+            ones = torch.ones(k, dtype=torch.bfloat16, device="cuda")
+            x = torch.empty_like(x0)
+            ops.rmsnorm(x0, ones, x, 1e-5)  # our kernel writes x right before the GEMMs read it
+            ops.linear(x, w, out=out, residual=out)
+            r = ops.linear(x, w, partials=pb)
+            total = r.buf[: r.splits * r.stride].view(r.splits, t, n).sum(0) if isinstance(r, ops.Partial) else r.float()
+            outs.append((out.float(), total.clone()))
+            ref_out.append((h.float() + x.float() @ w.float().T, x.float() @ w.float().T))
+    torch.cuda.synchronize()
+    for (o, tot), (ro, rt) in zip(outs, ref_out):
+        torch.testing.assert_close(o, ro, atol=4e-2, rtol=2e-2)
+        torch.testing.assert_close(tot, rt, atol=4e-2, rtol=2e-2)
+    assert ops.status("gemm_bf16") == 0
