@@ -473,6 +473,16 @@ PYBIND11_MODULE(_C, m) {
           if (n.type == NodeType::Kernel) v.push_back(n.kernel.func_name);
         return v;
       })
+      .def("edges", [](const GraphDesc& g) {
+        // (from, to, from_port, to_port, type) per dependency; ports and type 0 = a plain edge
+        py::list out;
+        for (size_t i = 0; i < g.deps.size(); ++i) {
+          const bool has = !g.edge_data.empty();
+          out.append(py::make_tuple(g.deps[i].first, g.deps[i].second, has ? g.edge_data[i].from_port : 0,
+                                    has ? g.edge_data[i].to_port : 0, has ? g.edge_data[i].type : 0));
+        }
+        return out;
+      })
       .def("node_types", [](const GraphDesc& g) {
         std::vector<std::string> v;
         for (const auto& n : g.nodes) v.push_back(node_type_name(n.type));

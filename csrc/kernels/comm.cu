@@ -44,6 +44,7 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(uint64_t addr) {
 
 extern "C" __global__ void __launch_bounds__(64) fb_sym_barrier(unsigned long long base,
                                                                  unsigned long long stride, int rank, int world) {
+  pdl_entry();
   __shared__ uint32_t epoch;
   const int t = threadIdx.x;
   if (t == 0) {
@@ -73,6 +74,7 @@ extern "C" __global__ void __launch_bounds__(64) fb_sym_barrier(unsigned long lo
 extern "C" __global__ void fb_allreduce_oneshot_bf16(unsigned long long base, unsigned long long stride,
                                                      unsigned long long offset, bf16* __restrict__ out,
                                                      long long n, int world) {
+  pdl_entry();
   const long long nv = n / 8;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < nv;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -90,6 +92,7 @@ extern "C" __global__ void fb_allreduce_oneshot_bf16(unsigned long long base, un
 
 extern "C" __global__ void fb_allreduce_nvls_bf16(unsigned long long mc_in, unsigned long long mc_out,
                                                   long long n, int rank, int world) {
+  pdl_entry();
   const long long nv = n / 8;
   const long long per = (nv + world - 1) / world;
   const long long lo = rank * per, hi = min(nv, lo + per);
@@ -110,6 +113,7 @@ extern "C" __global__ void fb_allreduce_nvls_bf16(unsigned long long mc_in, unsi
 extern "C" __global__ void __launch_bounds__(256) fb_add_rmsnorm_slots(
     const bf16* __restrict__ slots, int W, long long slot_stride, bf16* __restrict__ h,
     const bf16* __restrict__ w, bf16* __restrict__ x, int T, int H, float eps) {
+  pdl_entry();
   constexpr int VPT = 4;
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -171,6 +175,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_add_rmsnorm_slots(
 extern "C" __global__ void __launch_bounds__(512) fb_argmax_shard(
     const bf16* __restrict__ logits, long long ld, int T, int V, int vocab_offset, unsigned long long mc_pairs,
     unsigned long long base, unsigned long long stride, unsigned long long pairs_off, int rank, int world) {
+  pdl_entry();
   const int t = blockIdx.x;
   if (t >= T) return;
   const bf16* row = logits + static_cast<size_t>(t) * ld;
@@ -221,6 +226,7 @@ extern "C" __global__ void __launch_bounds__(512) fb_argmax_shard(
 }
 
 extern "C" __global__ void fb_argmax_combine(const uint32_t* __restrict__ pairs, int T, int W, int* __restrict__ out) {
+  pdl_entry();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   float best = -INFINITY;
@@ -242,6 +248,7 @@ extern "C" __global__ void fb_argmax_combine(const uint32_t* __restrict__ pairs,
 extern "C" __global__ void fb_sym_broadcast(const uint4* __restrict__ src, unsigned long long base,
                                             unsigned long long stride, unsigned long long offset, long long nbytes,
                                             int world) {
+  pdl_entry();
   const long long nv = nbytes / 16;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < nv;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {

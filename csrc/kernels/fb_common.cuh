@@ -52,8 +52,12 @@ __device__ __forceinline__ void set_status(unsigned code) { atomicOr(&fb_status,
 // completed and its memory is visible; every thread calls it before its first
 // access to global memory that another kernel writes or reads (weights, which
 // no kernel of the step writes, may be read before). Without the launch
-// attribute both are no-ops. Every kernel that can be launched this way calls
-// pdl_wait on every path, so a grid never completes before its predecessor.
+// attribute both are no-ops. Every kernel of every image calls pdl_wait on
+// every path, so a grid never completes before its predecessor - including
+// kernels launched without the attribute: in graphs rebuilt from an archive,
+// a kernel launched plainly after one that had triggered its dependents was
+// seen to start early (a tensor-parallel decode step read peers' slots
+// before they were written until the collective kernels waited too).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Both, at the top of a kernel with no set-up worth overlapping.

@@ -353,6 +353,7 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
       const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const float* w_scale,       \
       const float* x_scale, const int4* chunks, const int* meta, bf16* out, const bf16* residual, int O, int K,     \
       int ldo, int mode, long long peer_stride) {                                                                    \
+    pdl_entry();                                                                                                    \
     moe_gemm_body<BN>(&tmW, &tmX, w_scale, x_scale, chunks, meta, out, residual, O, K, ldo, mode, peer_stride);     \
   }
 
@@ -366,6 +367,7 @@ FB_MOE_GEMM_INSTANCE(64)
 extern "C" __global__ void __launch_bounds__(256) fb_moe_topk(const bf16* __restrict__ logits, int ld, int T, int E,
                                                              int topk, int renorm, int* __restrict__ ids,
                                                              float* __restrict__ weights) {
+  pdl_entry();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -437,6 +439,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_topk(const bf16* __rest
 extern "C" __global__ void __launch_bounds__(1024) fb_moe_plan(const int* __restrict__ ids, int P, int E, int bn,
                                                               int* __restrict__ pos, int* __restrict__ counts,
                                                               int4* __restrict__ chunks, int* __restrict__ meta) {
+  pdl_entry();
   __shared__ int cnt[256], off[256], coff[256];
   __shared__ int wbase[32][257];  // [warp][expert]; odd stride: the scan in (2) reads a column
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -543,6 +546,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_dispatch_local(const bf
                                                                        int H, const int* __restrict__ pos, int topk,
                                                                        uint8_t* __restrict__ xq,
                                                                        float* __restrict__ xs) {
+  pdl_entry();
   constexpr int BPW = 4;
   const int nb = H / QBLK;
   const int groups = (nb + BPW - 1) / BPW;
@@ -584,6 +588,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_silu_mul_quant(const bf
                                                                        const int* __restrict__ meta,
                                                                        uint8_t* __restrict__ aq,
                                                                        float* __restrict__ as) {
+  pdl_entry();
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int n = meta ? min(rows, meta[1]) : rows;
@@ -620,6 +625,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_silu_mul_quant(const bf
 extern "C" __global__ void __launch_bounds__(256) fb_moe_combine_add_rmsnorm(
     const bf16* __restrict__ y, int ldy, const int* __restrict__ pos, const float* __restrict__ w, int topk,
     bf16* __restrict__ h, const bf16* __restrict__ norm_w, bf16* __restrict__ x, int T, int H, float eps) {
+  pdl_entry();
   const int t = blockIdx.x;
   __shared__ float red[8];
   float acc[2][8] = {};
@@ -669,6 +675,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_combine_add_rmsnorm(
 extern "C" __global__ void __launch_bounds__(256) fb_quant_block_fp8(const bf16* __restrict__ w, int R, int Cc,
                                                                     uint8_t* __restrict__ q,
                                                                     float* __restrict__ scales) {
+  pdl_entry();
   const int bc = blockIdx.x, br = blockIdx.y;
   __shared__ float red[8];
   float am = 0.f;
@@ -709,6 +716,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_quant_block_fp8(const bf16*
 extern "C" __global__ void __launch_bounds__(256) fb_init_fp8_block(uint8_t* __restrict__ q, float* __restrict__ scales,
                                                                    int R, int Cc, unsigned long long seed, float std,
                                                                    long long row_offset) {
+  pdl_entry();
   const int bc = blockIdx.x, br = blockIdx.y;
   __shared__ float red[8];
   const int r0 = threadIdx.x / 16, c0 = (threadIdx.x % 16) * 8;
@@ -748,6 +756,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_init_fp8_block(uint8_t* __r
 // Dense layers as a one-"expert" grouped GEMM: chunk table of ceil(T / bn)
 // chunks over rows [0, T) with meta = {chunks, T}. One thread per chunk.
 extern "C" __global__ void fb_moe_dense_chunks(int T, int bn, int4* __restrict__ chunks, int* __restrict__ meta) {
+  pdl_entry();
   const int n = (T + bn - 1) / bn;
   for (int c = threadIdx.x; c < n; c += blockDim.x) chunks[c] = make_int4(0, c * bn, min(bn, T - c * bn), 0);
   if (threadIdx.x == 0) {
@@ -1079,6 +1088,7 @@ __device__ __forceinline__ void w8_gemm_body(const CUtensorMap* tmW, const CUten
   extern "C" __global__ void __launch_bounds__(W8_THREADS, 1) fb_moe_gemm_w8_bn##BN(                               \
       const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const float* w_scale,       \
       const int4* chunks, const int* meta, bf16* out, const bf16* residual, int O, int K, int ldo, int mode) {      \
+    pdl_entry();                                                                                                    \
     w8_gemm_body<BN>(&tmW, &tmX, w_scale, chunks, meta, out, residual, O, K, ldo, mode);                           \
   }
 
@@ -1091,6 +1101,7 @@ FB_W8_GEMM_INSTANCE(128)
 extern "C" __global__ void __launch_bounds__(256) fb_moe_scatter_rows(const bf16* __restrict__ src, int lds, int T,
                                                                      int H, const int* __restrict__ pos, int topk,
                                                                      bf16* __restrict__ dst) {
+  pdl_entry();
   const int t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < H; c += 256 * 8) {
     const uint4 v = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(t) * lds + c);
@@ -1119,6 +1130,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_moe_scatter_rows(const bf16
 extern "C" __global__ void __launch_bounds__(256) fb_ep_count(const int* __restrict__ ids, int P, int E, int rank,
                                                              int world, unsigned long long base,
                                                              long long stride, long long counts_off) {
+  pdl_entry();
   __shared__ int cnt[256];
   for (int e = threadIdx.x; e < E; e += 256) cnt[e] = 0;
   __syncthreads();
@@ -1136,6 +1148,7 @@ extern "C" __global__ void __launch_bounds__(1024) fb_ep_plan(const int* __restr
                                                              const int* __restrict__ ids, int P, int E, int El,
                                                              int rank, int world, int bn, int* __restrict__ dst_row,
                                                              int4* __restrict__ chunks, int* __restrict__ meta) {
+  pdl_entry();
   __shared__ int tot[256], base[256], before[256], run[256], coff[256];
   __shared__ int wcnt[32][256];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1208,6 +1221,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_ep_dispatch(
     const bf16* __restrict__ x, int ldx, int T, int H, const int* __restrict__ ids, const int* __restrict__ dst_row,
     int topk, int El, int rank, unsigned long long base, long long stride, long long q_off, long long s_off,
     long long map_off) {
+  pdl_entry();
   constexpr int BPW = 4;
   const int nb = H / QBLK, nbp = kb_pad(nb);
   const int groups = (nb + BPW - 1) / BPW;
@@ -1253,6 +1267,7 @@ extern "C" __global__ void __launch_bounds__(256) fb_ep_dispatch(
 extern "C" __global__ void __launch_bounds__(256) fb_dequant_block_fp8(const uint8_t* __restrict__ q,
                                                                       const float* __restrict__ scales, int R,
                                                                       int Cc, bf16* __restrict__ out) {
+  pdl_entry();
   const int bc = blockIdx.x, br = blockIdx.y;
   const float s = scales[static_cast<size_t>(br) * kb_pad(Cc / 128) + bc];
   const int r0 = threadIdx.x / 16, c0 = (threadIdx.x % 16) * 8;

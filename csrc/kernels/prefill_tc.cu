@@ -83,6 +83,7 @@ extern "C" __global__ void __launch_bounds__(192, 1) fb_prefill_attn_tc(
     const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
     const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ out, int ld_o, const int* __restrict__ cu_seqlens,
     const int* __restrict__ tile_seq, const int* __restrict__ tile_start, int Hq, int Hkv, float scale_log2) {
+  pdl_entry();
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -10,6 +10,8 @@ Paths:
              RMSNorm (Llama-3-70B down projection shapes, tp = N)
   tp_nvls    same GEMM into the local slot, barrier, NVLS reduce-scatter +
              multicast (multimem.ld_reduce / multimem.st), barrier, add + RMSNorm
+  gemm_ar    one kernel: the GEMM epilogue reduces each tile in the switch
+             once every rank has it and multicasts the sums, then add + RMSNorm
   ep         Qwen3-30B-A3B MoE layer exchange at 512 tokens per rank: count
              exchange + plan + fused e4m3 quantise/dispatch (P2P stores),
              grouped GEMMs, down GEMM with the combine fused into its epilogue
@@ -78,8 +80,12 @@ def tp_paths(reps: int) -> dict:
     hidden, inter = 8192, 28672
     k = inter // w_
     out = {}
-    symm = SymmetricMemory(CTRL_BYTES + 2 * w_ * 1024 * hidden * 2 + (1 << 20))
-    ex = comm.SlotExchange(symm, CTRL_BYTES, 1024, hidden)
+    ar_off = -(-(CTRL_BYTES + 2 * w_ * 1024 * hidden * 2) // 4096) * 4096
+    symm = SymmetricMemory(ar_off + 2 * comm.AR_BLOCK_BYTES + (1 << 20))
+    ex = comm.SlotExchange(symm, CTRL_BYTES, 1024, hidden, ar_offset=ar_off)
+    symm.tensor(symm.rank, (2 * comm.AR_BLOCK_BYTES,), torch.uint8, ar_off).zero_()
+    torch.cuda.synchronize()
+    dist.barrier()
     g = torch.Generator(device="cuda").manual_seed(1 + symm.rank)
     wt = (torch.randn(hidden, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     nw = torch.ones(hidden, dtype=torch.bfloat16, device="cuda")
@@ -118,6 +124,16 @@ def tp_paths(reps: int) -> dict:
             roof2 = max(t_c, t_h, nv2 / NVLINK) * 1e6
             r["nvls"] = {"total_us": t_nvls, "nvlink_ingress_MB": nv2 / 1e6, "roofline_us": roof2,
                          "fraction": roof2 / t_nvls}
+
+            def gemm_ar():
+                ex.gemm_allreduce(x, wt, 0)
+                comm.add_rmsnorm_slots(ex.local_slots(0)[1:2], b, h, nw, xo, 1e-5)
+
+            # fb_gemm_bf16_ar_bn*: tiles reduced in the switch and multicast by
+            # the GEMM's own epilogue (no barrier or reduce kernel)
+            t_ar = graph_time_us(gemm_ar, reps)
+            r["gemm_ar"] = {"total_us": t_ar, "nvlink_ingress_MB": nv2 / 1e6, "roofline_us": roof2,
+                            "fraction": roof2 / t_ar}
         r["compute_us"], r["hbm_us"] = t_c * 1e6, t_h * 1e6
         out[f"b{b}"] = r
     torch.cuda.synchronize()
