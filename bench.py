@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--parallel", default=None, choices=["dp", "tp", "ep"])
     ap.add_argument("--workdir", default=None)
     ap.add_argument("--skip-cold-start", action="store_true")
+    ap.add_argument("--skip-full-generation", action="store_true",
+                    help="leave out the timed whole generation after the decode window (its second prefill)")
     ap.add_argument("--restore-graphs", default="4:1024:4",
                     help="graph sizes of the restore-at-scale SAVE/LOAD (default: 256 graphs); 'none' skips it")
     args = ap.parse_args()
@@ -385,20 +387,22 @@ def main():
     # .. prompt_len+gen-1), each with its H2D input and D2H token copy.
     n_full = len(reqs)
     eng.release(reqs)
-    freqs = eng.add_requests(prompts, max_new_tokens=args.gen)
-    eng.prefill(freqs)
-    fb = eng.start_decode(freqs)
-    if world > 1:
-        dist.barrier()
-    f_start, f_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    f_start.record()
-    for _ in range(args.gen - 1):
-        eng.decode_step(fb)
-    f_end.record()
-    torch.cuda.synchronize()
-    full_ms = f_start.elapsed_time(f_end)
-    eng.release(freqs)
+    full_ms, fb = 0.0, b
+    if not args.skip_full_generation:
+        freqs = eng.add_requests(prompts, max_new_tokens=args.gen)
+        eng.prefill(freqs)
+        fb = eng.start_decode(freqs)
+        if world > 1:
+            dist.barrier()
+        f_start, f_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        f_start.record()
+        for _ in range(args.gen - 1):
+            eng.decode_step(fb)
+        f_end.record()
+        torch.cuda.synchronize()
+        full_ms = f_start.elapsed_time(f_end)
+        eng.release(freqs)
 
     n_active = n_full
     per_rank = [dev_ms, e2e_ms, full_ms, restore["restore_s"], cold.get("cold_start_first_token_s") or 0.0,
@@ -441,7 +445,7 @@ def main():
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * b,
                     "d2h_bytes_per_step": 4 * b, "ms_per_step": round(e2e_ms / args.steps, 4),
                     "decode_context": e2e_ctx},
-            "full_generation": {
+            "full_generation": None if args.skip_full_generation else {
                 "value": round(full_tokens / (full_ms / 1e3), 1), "unit": "tokens/s",
                 "decode_steps": args.gen - 1, "decode_context": [ctx0, args.prompt_len + args.gen - 1],
                 "ms_per_step": round(full_ms / (args.gen - 1), 4), "h2d_bytes_per_step": 4 * fb,
