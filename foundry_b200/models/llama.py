@@ -80,12 +80,15 @@ CONFIGS = {"llama-3-8b": llama3_8b, "llama-3-70b": llama3_70b}
 # summed by an NVLS reduce-scatter + multicast instead of the slot exchange.
 NVLS_MIN_ROWS = 128
 NVLS_MIN_ROWS_2 = 512  # at 2 ranks (measured: slots faster at 256 rows, NVLS at 1024)
-# "auto": from those row counts the GEMM all-reduces in its own epilogue (tiles
-# reduced in the switch as they finish: fb_gemm_bf16_ar_bn*), else the NVLS
-# reduce kernel; below them the slot exchange. Measured at 2 ranks on the
-# Llama-3-70B down projection (profile_comm; us, slots / NVLS / fused): 64
-# rows 83.5 / 93.0 / 105.6, 256 rows 97.0 / 109.4 / 120.0, 1024 rows 383.3 /
-# 262.1 / 247.7. "nvls": the NVLS kernel from NVLS_MIN_ROWS rows at any rank
+# "auto": from those row counts, at 2 ranks the GEMM all-reduces in its own
+# epilogue (tiles reduced in the switch as they finish: fb_gemm_bf16_ar_bn*)
+# and at more ranks the separate NVLS reduce kernel runs; below them the slot
+# exchange. Measured on the Llama-3-70B down projection (profile_comm; us,
+# slots / NVLS / fused): 2 ranks, 64 rows 83.5 / 93.0 / 105.6, 256 rows
+# 97.0 / 109.4 / 120.0, 1024 rows 383.3 / 262.1 / 247.7; 8 ranks, 64 rows
+# 43.8 / 41.8 / 56.6, 256 rows 87.0 / 53.2 / 68.5, 1024 rows 871.1 / 118.9 /
+# 137.1 (at 8 ranks each CTA waits for eight ranks' tiles and reduces only an
+# eighth of each). "nvls": the NVLS kernel from NVLS_MIN_ROWS rows at any rank
 # count (tests); "fused": the fused kernel for every row count.
 _TP_REDUCE = __import__("os").environ.get("FOUNDRY_TP_REDUCE", "auto")
 
@@ -262,7 +265,8 @@ class LlamaModel:
             ex = st.tp.slots
             many = ex.symm.multicast and (rows >= NVLS_MIN_ROWS_2 or (rows >= NVLS_MIN_ROWS and (
                 ex.symm.world > 2 or _TP_REDUCE == "nvls")))
-            if (_TP_REDUCE == "fused" or (_TP_REDUCE == "auto" and many)) and ex.gemm_allreduce(inp, weight, which):
+            fused = _TP_REDUCE == "fused" or (_TP_REDUCE == "auto" and many and ex.symm.world == 2)
+            if fused and ex.gemm_allreduce(inp, weight, which):
                 # one kernel: GEMM tiles reduced in the switch and multicast as they finish
                 return ("reduced", which)
             if many:
