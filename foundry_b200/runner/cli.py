@@ -120,11 +120,13 @@ def _main(argv=None):
     import torch
 
     marks = {"main_s": time.time_ns()}
-    if args.device is not None:
-        torch.cuda.set_device(args.device)  # creates the device's primary context
-    marks["cuda_context_s"] = time.time_ns()
+    # The (gloo) process group first: it needs no GPU, so it overlaps the CUDA
+    # context that FOUNDRY_EARLY_CUDA_INIT may be building on its thread.
     init_dist(args)
     marks["process_group_s"] = time.time_ns()
+    if args.device is not None:
+        torch.cuda.set_device(args.device)  # creates (or waits for) the device's primary context
+    marks["cuda_context_s"] = time.time_ns()
     from . import persist
 
     marks["runner_import_s"] = time.time_ns()
