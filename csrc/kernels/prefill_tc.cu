@@ -212,21 +212,19 @@ extern "C" __global__ void __launch_bounds__(192, 1) fb_prefill_attn_tc(
       tc_fence_after();
       const uint32_t t_s = tmem + sb * 128 + lane_base;
       const int kpos0 = j * BKV;  // key positions of this tile: kpos0 + c
-      // S row of this thread: all 128 columns into registers in one TMEM
-      // pass, then the S buffer is free for QK_{j+2} at once.
-      uint32_t sr[BKV];
-#pragma unroll
-      for (int q = 0; q < BKV / 16; ++q) tmem_ld16(t_s + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(sr + 16 * q));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_empty[sb]);
-      // row max over the valid keys
+      // pass 1: row max over the valid keys (64 columns per TMEM round trip)
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c1 = 0; c1 < BKV; c1 += 64) {
+        uint32_t sr[64];
 #pragma unroll
-      for (int i = 0; i < BKV; ++i) {
-        const int kp = kpos0 + i;
-        if (qvalid && kp <= qpos) mx = fmaxf(mx, __uint_as_float(sr[i]) * scale_log2);
+        for (int q = 0; q < 4; ++q) tmem_ld16(t_s + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(sr + 16 * q));
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int kp = kpos0 + c1 + i;
+          if (qvalid && kp <= qpos) mx = fmaxf(mx, __uint_as_float(sr[i]) * scale_log2);
+        }
       }
       // Lazy rescaling: the running max of a row moves (and O is rescaled)
       // only when the tile's max exceeds it by more than RESCALE_LOG2; until
@@ -245,43 +243,54 @@ extern "C" __global__ void __launch_bounds__(192, 1) fb_prefill_attn_tc(
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-          for (int c1 = 0; c1 < D; c1 += 32) {
-            uint32_t orr[32];
+          for (int c1 = 0; c1 < D; c1 += 64) {
+            uint32_t orr[64];
 #pragma unroll
-            for (int q = 0; q < 2; ++q)
+            for (int q = 0; q < 4; ++q)
               tmem_ld16(t_o + lane_base + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(orr + 16 * q));
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
+            for (int i = 0; i < 64; ++i) orr[i] = __float_as_uint(__uint_as_float(orr[i]) * alpha);
 #pragma unroll
-            for (int q = 0; q < 2; ++q)
+            for (int q = 0; q < 4; ++q)
               tmem_st16(t_o + lane_base + c1 + 16 * q, *reinterpret_cast<const uint32_t(*)[16]>(orr + 16 * q));
           }
           tmem_st_wait();
         }
       }
-      // p = exp2(s - m), row sum, P row to shared memory
+      // pass 2: p = exp2(s - m), row sum, P row to shared memory
       float rs = 0.f;
+#pragma unroll 1
+      for (int c1 = 0; c1 < BKV; c1 += 64) {
+        uint32_t sr[64];
 #pragma unroll
-      for (int c0 = 0; c0 < BKV; c0 += 16) {
-        float p[16];
+        for (int q = 0; q < 4; ++q) tmem_ld16(t_s + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(sr + 16 * q));
+        tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int kp = kpos0 + c0 + i;
-          p[i] = (qvalid && kp <= qpos) ? exp2f(__uint_as_float(sr[c0 + i]) * scale_log2 - m_use) : 0.f;
-          rs += p[i];
+        for (int c2 = 0; c2 < 64; c2 += 16) {
+          const int c0 = c1 + c2;
+          float p[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int kp = kpos0 + c0 + i;
+            p[i] = (qvalid && kp <= qpos) ? exp2f(__uint_as_float(sr[c2 + i]) * scale_log2 - m_use) : 0.f;
+            rs += p[i];
+          }
+          uint4 lo, hi;
+          bf162* l2 = reinterpret_cast<bf162*>(&lo);
+          bf162* h2 = reinterpret_cast<bf162*>(&hi);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            l2[i] = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
+            h2[i] = __floats2bfloat162_rn(p[8 + 2 * i], p[8 + 2 * i + 1]);
+          }
+          *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0)) = lo;
+          *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0 + 8)) = hi;
         }
-        uint4 lo, hi;
-        bf162* l2 = reinterpret_cast<bf162*>(&lo);
-        bf162* h2 = reinterpret_cast<bf162*>(&hi);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          l2[i] = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
-          h2[i] = __floats2bfloat162_rn(p[8 + 2 * i], p[8 + 2 * i + 1]);
-        }
-        *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0)) = lo;
-        *reinterpret_cast<uint4*>(sm.p + sw_offset(r, c0 + 8)) = hi;
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.s_empty[sb]);  // S buffer free for QK_{j+2}
       l_run = l_run * alpha + rs;
       m_run = m_new;
       fence_proxy_async();  // P (generic-proxy stores) -> visible to the tensor core
