@@ -291,21 +291,33 @@ def main():
     # dp: independent engines, one archive per rank; tp / ep: one multi-rank
     # engine whose archive holds a rank_<r> folder per rank
     archive = os.path.join(workdir, f"rank_{rank}") if mode == "dp" else workdir
+    # A data-parallel replica needs no other GPU: its SAVE / LOAD processes see
+    # only their own device, so CUDA initialises one device instead of every
+    # GPU of the node (with eight ranks starting at once, context creation was
+    # most of the time to first token). TP / EP ranks map peers' memory and see
+    # all devices.
+    child_env, child_dev = {}, local
+    if mode == "dp":
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        ids = [v for v in vis.split(",") if v] if vis else []
+        child_env = {"CUDA_VISIBLE_DEVICES": ids[local] if local < len(ids) else str(local)}
+        child_dev = 0
     common = ["--archive", archive, "--model", args.model, "--prompts", str(args.batch), "--prompt-len",
-              str(args.prompt_len), "--gen", str(gen), "--device", str(local), "--graph-sizes", args.graph_sizes,
+              str(args.prompt_len), "--gen", str(gen), "--device", str(child_dev), "--graph-sizes", args.graph_sizes,
               "--region-size", args.region_size]
     if mode in ("tp", "ep"):
         common += [f"--{mode}", str(world), "--rank", str(rank), "--world", str(world)]
 
     # 1) SAVE in a fresh process: capture the decode graphs and write the archive.
     t0 = time.perf_counter()
-    save_info = run_cli(["save", *common, "--dist-port", str(port + 17)])["save"]
+    save_info = run_cli(["save", *common, "--dist-port", str(port + 17)], child_env)["save"]
     save_wall = time.perf_counter() - t0
     # 2) LOAD in a fresh process: cold start (spawn -> first token) and restore time.
     cold = {}
     if not args.skip_cold_start:
         cold = run_cli(["load", *common, "--dist-port", str(port + 19)],
-                       {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns()), "FOUNDRY_EARLY_CUDA_INIT": str(local)})["load"]
+                       dict(child_env, FOUNDRY_SPAWN_T0_NS=str(time.time_ns()),
+                            FOUNDRY_EARLY_CUDA_INIT=str(child_dev)))["load"]
 
     # 2b) Restore at scale: a second archive of 256 decode graphs per rank,
     # SAVE and fresh-process LOAD; the LOAD times until every graph of the
@@ -317,9 +329,10 @@ def main():
         common256 = list(common)
         common256[common256.index("--archive") + 1] = archive256
         common256[common256.index("--graph-sizes") + 1] = args.restore_graphs
-        save256 = run_cli(["save", *common256, "--dist-port", str(port + 23)])["save"]
+        save256 = run_cli(["save", *common256, "--dist-port", str(port + 23)], child_env)["save"]
         load256 = run_cli(["load", *common256, "--dist-port", str(port + 29), "--materialize-all"],
-                          {"FOUNDRY_SPAWN_T0_NS": str(time.time_ns()), "FOUNDRY_EARLY_CUDA_INIT": str(local)})["load"]
+                          dict(child_env, FOUNDRY_SPAWN_T0_NS=str(time.time_ns()),
+                               FOUNDRY_EARLY_CUDA_INIT=str(child_dev)))["load"]
         scale = {"graphs": load256["num_graphs"], "topology_groups": load256["num_groups"],
                  "capture_s": save256.get("capture_s"), "restore_s": load256["restore_s"],
                  "cold_start_first_token_s": load256["cold_start_first_token_s"],
