@@ -13,10 +13,13 @@
 //                K-major TMA load produced
 //   O            accumulated in registers (one TMEM lane = one head dim per
 //                thread): o = o * alpha + O^T_chunk
-// K/V pages stream through a 2-stage TMA ring (64 KB per chunk) while the
-// previous chunk is in the softmax; the grid is persistent (one CTA per SM)
-// and walks work items, so the producer runs ahead across item boundaries.
-// Each KV byte is read from HBM exactly once per decode step.
+// K/V pages stream through TMA (64 KB per chunk): one stage per CTA with
+// three CTAs per SM (default), or a 3-stage ring with one CTA per SM; K and V
+// have their own full/empty barriers, so the next chunk's K loads while this
+// chunk's softmax and PV run. Only the live tokens of a sequence's last page
+// are loaded (16-token row boxes). The grid is persistent and walks work
+// items, so the producer runs ahead across item boundaries. Each live KV byte
+// is read from HBM once per decode step.
 //
 // Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2..5
 // softmax/epilogue. No TMA multicast. All waits bounded (fb_common.cuh).
@@ -51,6 +54,7 @@ struct Smem {
   float red_max[4][8];
   float red_l[4][8];
   float alpha[8];  // this chunk's rescale factor per head (the same in every softmax thread)
+  float mrun[2][8];  // running max per head, by chunk parity (uniform across the softmax threads)
   uint32_t tmem;
   int abort;
 };
@@ -167,21 +171,30 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
       for (int idx = blockIdx.x; idx < num_items && !*(volatile int*)&sm.abort; idx += gridDim.x) {
         const Item it = decode_item(idx, Hkv, S, chunks_per_split, seq_lens);
         const int* bt = block_tables + static_cast<size_t>(it.b) * max_blocks;
-        for (int c = it.c0; c < it.c1; ++c) {
-          // Only the live tokens of the chunk are read: whole pages, and the
-          // last page in 16-token row blocks (a 16-row box at a 2 KB offset
-          // lands in the same 128B-swizzled image as the rows of a full box).
-          // Rows not loaded keep stale data: their scores are masked and their
-          // V rows zeroed by the softmax warps before the PV MMA reads them.
+        // Only the live tokens of a chunk are read: whole pages, and the last
+        // page in 16-token row blocks (a 16-row box at a 2 KB offset lands in
+        // the same 128B-swizzled image as the rows of a full box). Rows not
+        // loaded keep stale data: their scores are masked and their V rows
+        // zeroed by the softmax warps before the PV MMA reads them.
+        // The page ids of chunk c + 1 are read from the block table while
+        // chunk c waits for its buffers, off the critical path.
+        auto chunk_pages = [&](int c, int (&blocks)[2], int (&pages)[2]) {
           const int live = min(it.tok1, (c + 1) * CHUNK) - c * CHUNK;
-          int blocks[2];  // 16-token blocks loaded per page (4 = the whole page)
-          int rows[2];
 #pragma unroll
           for (int pg = 0; pg < 2; ++pg) {
             const int n = min(max(live - pg * PAGE, 0), PAGE);
-            blocks[pg] = (n + 15) / 16;
-            rows[pg] = blocks[pg] ? (bt[2 * c + pg] * Hkv + it.kvh) * PAGE : 0;
+            blocks[pg] = (n + 15) / 16;  // 16-token blocks loaded (4 = the whole page)
+            pages[pg] = blocks[pg] ? bt[2 * c + pg] : 0;
           }
+        };
+        int nblocks[2] = {0, 0}, npages[2] = {0, 0};
+        if (it.c0 < it.c1) chunk_pages(it.c0, nblocks, npages);
+        for (int c = it.c0; c < it.c1; ++c) {
+          int blocks[2] = {nblocks[0], nblocks[1]};
+          int rows[2];
+#pragma unroll
+          for (int pg = 0; pg < 2; ++pg) rows[pg] = (npages[pg] * Hkv + it.kvh) * PAGE;
+          if (c + 1 < it.c1) chunk_pages(c + 1, nblocks, npages);
           const uint32_t bytes = static_cast<uint32_t>(blocks[0] + blocks[1]) * (2 * SUB_BYTES);  // K or V
           uint8_t* kbuf = sm.kv[stage];
 #pragma unroll
@@ -312,10 +325,15 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.q_ready);
 
-      float m_run[G], l_thr[G], o[G];
+      // The running max is the same in every softmax thread: kept in shared
+      // memory (registers are the limit at three CTAs per SM). Chunk k reads
+      // mrun[k & 1] and thread 0 writes the new max to mrun[(k + 1) & 1]
+      // after the chunk's first barrier, so no read of a buffer overlaps its
+      // next write.
+      float l_thr[G], o[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        m_run[g] = -INFINITY;
+        if (r == 0) sm.mrun[cc & 1][g] = -INFINITY;
         l_thr[g] = 0.f;
         o[g] = 0.f;
       }
@@ -357,14 +375,15 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           const float mx = fmaxf(fmaxf(sm.red_max[0][g], sm.red_max[1][g]), fmaxf(sm.red_max[2][g], sm.red_max[3][g]));
-          const float m_new = fmaxf(m_run[g], mx);
-          const float alpha = exp2f(m_run[g] - m_new);
+          const float m_old = sm.mrun[cc & 1][g];
+          const float m_new = fmaxf(m_old, mx);
+          const float alpha = exp2f(m_old - m_new);
           // Kept in shared memory until the PV result arrives (registers are
           // the limit at three CTAs per SM); rewritten next chunk only after
           // every thread has passed that chunk's first barrier.
           if (r == 0) sm.alpha[g] = alpha;
           const float p = exp2f(s[g] - m_new);
-          m_run[g] = m_new;
+          if (r == 0) sm.mrun[(cc + 1) & 1][g] = m_new;
           l_thr[g] = l_thr[g] * alpha + p;
           *reinterpret_cast<bf16*>(sm.p + qp_offset(g, r)) = f2bf(p);
         }
@@ -410,7 +429,7 @@ __device__ __forceinline__ void attn_body(const CUtensorMap* tmK, const CUtensor
           const size_t pidx = (static_cast<size_t>(it.b) * Hq + hq) * S + it.split;
           o_part[pidx * D + r] = o[g];
           if (r == 0) {
-            ml_part[2 * pidx] = m_run[g];
+            ml_part[2 * pidx] = sm.mrun[cc & 1][g];  // written by this thread in the last chunk
             ml_part[2 * pidx + 1] = lsum[g];
           }
         }
