@@ -121,6 +121,15 @@ struct GemmCfg {
 //   TMA loads of the K loop; warp 1 lane 0: per k-block 4 MMAs into a fresh
 //   TMEM partial (NBUF buffers); warps 2-5: per k-block promote the partial
 //   with sw[kb] * sx[t][kb], per unit store the 128 x BN tile transposed.
+// ssc[kb][t] = sw[kb] * sx[t][kb] for the unit's KB k-blocks (128 threads).
+template <int BN>
+__device__ __noinline__ void combine_scales(float* ssc, const float* xsu, const float* wsu, int KB, int KBp, int et) {
+  for (int i = et; i < KB * BN; i += 128) {
+    const int kb = i / BN, t = i - kb * BN;
+    ssc[i] = xsu[t * KBp + kb] * wsu[kb];
+  }
+}
+
 template <int BN>
 __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUtensorMap* tmX,
                                               const float* __restrict__ w_scale, const float* __restrict__ x_scale,
@@ -136,7 +145,8 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
   uint8_t* sB = smem + STAGES * C::A_BYTES;
   float* sxs = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);  // [2][BN * KBp]
   float* sws = sxs + 2 * C::XS_FLOATS;                                       // [2][MAX_KB]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sws + 2 * MAX_KB);
+  float* ssc = sws + 2 * MAX_KB;  // [MAX_KB][BN]: sw[kb] * sx[t][kb] of the unit being promoted
+  uint64_t* full = reinterpret_cast<uint64_t*>(ssc + MAX_KB * BN);
   uint64_t* empty = full + STAGES;
   uint64_t* pfull = empty + STAGES;
   uint64_t* pempty = pfull + NBUF;
@@ -286,6 +296,15 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
       }
       const float* xsu = sxs + slot * C::XS_FLOATS;
       const float* wsu = sws + slot * MAX_KB;
+      // One combined scale per (k-block, token), laid out k-block-major (one
+      // broadcast load and one FMA per token in the promote): the four epilogue warps
+      // first wait for each other (the previous unit's promote is done with
+      // ssc), fill it, and wait again. The scale slot is free after that.
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      combine_scales<BN>(ssc, xsu, wsu, KB, KBp, threadIdx.x - 64);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[slot]);
       float acc[BN];
 #pragma unroll
       for (int t = 0; t < BN; ++t) acc[t] = 0.f;
@@ -305,12 +324,10 @@ __device__ __forceinline__ void moe_gemm_body(const CUtensorMap* tmW, const CUte
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&pempty[buf]);
-        const float sw = wsu[kb];
+        const float* sc = ssc + kb * BN;
 #pragma unroll
-        for (int t = 0; t < BN; ++t) acc[t] = fmaf(__uint_as_float(r[t]), sw * xsu[t * KBp + kb], acc[t]);
+        for (int t = 0; t < BN; ++t) acc[t] = fmaf(__uint_as_float(r[t]), sc[t], acc[t]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sempty[slot]);
       if (!ok) {
         *(volatile int*)abort_flag = 1;
         break;

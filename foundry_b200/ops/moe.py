@@ -47,7 +47,7 @@ def gemm_smem(bn: int) -> int:
     stage = 128 * QBLK + bn * QBLK
     budget = {1: 200, 2: 100, 3: 60}[GEMM_CTAS[bn]] * 1024
     stages = min(10, budget // stage)
-    return stages * stage + 2 * bn * MAX_KB * 4 + 2 * MAX_KB * 4 + 8 * (2 * stages + 2 * NBUF + 4) + 16 + 1024
+    return stages * stage + 3 * bn * MAX_KB * 4 + 2 * MAX_KB * 4 + 8 * (2 * stages + 2 * NBUF + 4) + 16 + 1024
 
 
 def kb_pad(kb: int) -> int:
