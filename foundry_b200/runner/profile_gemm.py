@@ -11,7 +11,8 @@ tokens it prints one JSON line per variant:
 - ``bn<B>s<S>[m<T>]``: one-SM tiles of B tokens, S splits, T weight tiles per
   unit (default 1);
 - ``pair<B>s<S>``: two-SM tiles of B tokens with S splits;
-- ``sk<B>``: stream-K over one-SM tiles of B tokens.
+- ``sk<B>``: stream-K over one-SM tiles of B tokens;
+- ``cublas``: ``torch.matmul`` on the same operands (cuBLAS), for comparison.
 ``--ops`` restricts the run to some layers (e.g. ``gate_up,lm_head``).
 
 Each line gives the plan (tile width, splits, grid) and the mean time of
@@ -88,7 +89,8 @@ def main(argv=None) -> int:
         ref = (x.float() @ w.float().T) if a.check else None
         base = G.plan(t, n, k)
         for v in a.variants.split(","):
-            if v == "plan":
+            cublas = v == "cublas"  # torch.matmul (cuBLAS / cuBLASLt) on the same operands, for comparison
+            if v in ("plan", "cublas"):
                 p = base
             elif v == "pair":
                 if not base.swap or n < 256:
@@ -118,6 +120,8 @@ def main(argv=None) -> int:
                                   torch.zeros(sms * 8, dtype=torch.int32, device="cuda")) if p.streamk else None
 
             def run():
+                if cublas:
+                    return torch.matmul(x, w.T, out=out)
                 with G._rt.pdl() if a.pdl else contextlib.nullcontext():
                     return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p,
                                     streamk=skb)
@@ -159,7 +163,8 @@ def main(argv=None) -> int:
                 e1.record()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000 / a.iters - flush_us
-            line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v, "kernel": p.kernel, "bn": p.bn,
+            line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v,
+                    "kernel": "cublas" if cublas else p.kernel, "bn": p.bn,
                     "splits": p.splits, "grid": p.grid, "us": round(us, 1),
                     "weight_tbps": round(n * k * 2 / (us * 1e-6) / 1e12, 2),
                     "tflops": round(2 * t * n * k / (us * 1e-6) / 1e12, 1)}
