@@ -135,6 +135,15 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def replica_visibility(local: int, environ) -> tuple[dict, int]:
+    """(environment, device ordinal) for a data-parallel replica's SAVE / LOAD
+    processes: only the replica's own GPU visible (``local`` indexes the
+    launcher's CUDA_VISIBLE_DEVICES list when it has one), as device 0."""
+    vis = environ.get("CUDA_VISIBLE_DEVICES")
+    ids = [v.strip() for v in vis.split(",") if v.strip()] if vis else []
+    return {"CUDA_VISIBLE_DEVICES": ids[local] if local < len(ids) else str(local)}, 0
+
+
 def run_cli(cmd: list[str], env_extra: dict | None = None, timeout: int = 1800) -> dict:
     # The runner gets its rank and rendezvous from its own arguments; the
     # launcher's variables (TORCHELASTIC_USE_AGENT_STORE in particular, which
@@ -296,12 +305,7 @@ def main():
     # GPU of the node (with eight ranks starting at once, context creation was
     # most of the time to first token). TP / EP ranks map peers' memory and see
     # all devices.
-    child_env, child_dev = {}, local
-    if mode == "dp":
-        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        ids = [v for v in vis.split(",") if v] if vis else []
-        child_env = {"CUDA_VISIBLE_DEVICES": ids[local] if local < len(ids) else str(local)}
-        child_dev = 0
+    child_env, child_dev = ({}, local) if mode != "dp" else replica_visibility(local, os.environ)
     common = ["--archive", archive, "--model", args.model, "--prompts", str(args.batch), "--prompt-len",
               str(args.prompt_len), "--gen", str(gen), "--device", str(child_dev), "--graph-sizes", args.graph_sizes,
               "--region-size", args.region_size]

@@ -36,3 +36,14 @@ def test_presets(monkeypatch, argv, want):
     args = bench.parse()
     for k, v in want.items():
         assert getattr(args, k) == v, (k, getattr(args, k), v)
+
+
+def test_replica_visibility():
+    """A data-parallel replica's child processes see only their own GPU."""
+    import bench
+
+    assert bench.replica_visibility(3, {}) == ({"CUDA_VISIBLE_DEVICES": "3"}, 0)
+    assert bench.replica_visibility(1, {"CUDA_VISIBLE_DEVICES": "4,5,6"}) == ({"CUDA_VISIBLE_DEVICES": "5"}, 0)
+    assert bench.replica_visibility(0, {"CUDA_VISIBLE_DEVICES": "GPU-abc, GPU-def"}) == (
+        {"CUDA_VISIBLE_DEVICES": "GPU-abc"}, 0)
+    assert bench.replica_visibility(2, {"CUDA_VISIBLE_DEVICES": ""}) == ({"CUDA_VISIBLE_DEVICES": "2"}, 0)
