@@ -1053,6 +1053,392 @@ FB_GEMM_SK_INSTANCE(64)
 FB_GEMM_SK_INSTANCE(128)
 FB_GEMM_SK_INSTANCE(256)
 
+// ==== fused gate/up + SwiGLU, stream-K over every SM ====================================
+//
+// fb_gemm_swiglu_sk_bn256: the decode-step gate/up projection of
+// fb_gemm_bf16_bn256_m2 (units of 128 features: gate rows f.., up rows
+// I + f..; both accumulators in TMEM; epilogue silu(gate) * up) with the
+// (unit, k-block) iterations shared equally by all CTAs. With fewer units
+// than SMs (Llama-3-8B: 112 units on 148 SMs) the one-unit-per-CTA kernel
+// leaves SMs idle; here CTA b runs iterations [T*b/G, T*(b+1)/G) of the
+// T = units * k-blocks, so a unit is cut into pieces run by consecutive CTAs
+// (at most SWIGLU_SK_MAXP; the host checks). A piece's CTA draws a ticket for
+// its unit when its MMAs are done; every piece but the last to draw writes
+// its fp32 gate and up rows to its slot of `ws` and raises its ready flag;
+// the last waits for the others' flags (bounded), sums the pieces in piece
+// order (the same result whichever CTA is last) with its own TMEM values,
+// applies SiLU * up and stores the bf16 tile by TMA. It then clears the
+// unit's ticket and flags for the next launch. No CTA waits for work that has
+// not started: the last to draw waits only for pieces whose CTAs drew before.
+namespace {
+
+constexpr int SWIGLU_SK_MAXP = 3;  // pieces per unit (flags: ticket + one ready word per piece)
+
+template <int BN>
+__device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
+                                                    const CUtensorMap* tmO, int M, int N, int K, int mode,
+                                                    float* __restrict__ ws, int* __restrict__ flags) {
+  using C = Cfg<BN, 2>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int NBUF = C::ACC_BUFS;
+  constexpr int EC = EPI_COLS;
+  static_assert(BN % EC == 0, "epilogue chunks");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                              // [STAGES][2][128 x 64]
+  uint8_t* sB = smem + STAGES * 2 * C::A_BYTES;     // [STAGES][BN x 64]
+  uint8_t* stg = smem + STAGES * C::STAGE_BYTES;    // epilogue tiles (STG_BYTES)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + STG_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* ebar = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  int* unit_ticket = abort_flag + 1;  // the ticket this CTA drew for its current unit
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int half = M / 2;  // up rows start here
+  const int units = half / BM;
+  const int KB = (K + BK - 1) / BK;
+  const int G = gridDim.x;
+  const long long T = static_cast<long long>(units) * KB;
+  auto cta_start = [&](int b) -> long long { return T * b / G; };
+  const long long it0 = cta_start(blockIdx.x);
+  const long long it1 = cta_start(blockIdx.x + 1);
+  // CTA whose range holds iteration i.
+  auto cta_of = [&](long long i) -> int {
+    int b = static_cast<int>(i * G / T);
+    while (b + 1 < G && cta_start(b + 1) <= i) ++b;
+    while (b > 0 && cta_start(b) > i) --b;
+    return b;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(ebar, 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(tmA);
+    tma_prefetch_desc(tmB);
+    tma_prefetch_desc(tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint64_t pol = policy_evict_first();
+      const int pf_dist = (mode >> 8) & 0xFF;
+      auto load_a = [&](int st, int kb, int u) {
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint8_t* dst = sA + (st * 2 + mt) * C::A_BYTES;
+          const int row = mt * half + u * BM;
+          if (mode & EPI_A_STREAM)
+            tma_load_2d_hint(dst, tmA, &full[st], kb * BK, row, pol);
+          else
+            tma_load_2d(dst, tmA, &full[st], kb * BK, row);
+        }
+      };
+      // The first segment's A tiles of the whole ring go out before the wait
+      // for the previous kernel when A is the weights (EPI_A_CONST).
+      int pre = 0;
+      if ((mode & EPI_A_CONST) && it0 < it1) {
+        const int u = static_cast<int>(it0 / KB);
+        const int kb0 = static_cast<int>(it0 % KB);
+        const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it0)));
+        pre = min(STAGES, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          load_a(i, kb0 + i, u);
+        }
+      }
+      pdl_wait();
+      bool first_seg = true;
+      for (long long it = it0; it < it1 && !*(volatile int*)abort_flag;) {
+        const int u = static_cast<int>(it / KB);
+        const int kb0 = static_cast<int>(it % KB);
+        const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
+        for (int kb = kb0; kb < min(kb1, kb0 + pf_dist); ++kb)
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) tma_prefetch_2d(tmA, kb * BK, mt * half + u * BM);
+        bool stop = false;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (pf_dist && kb + pf_dist < kb1) {
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) tma_prefetch_2d(tmA, (kb + pf_dist) * BK, mt * half + u * BM);
+          }
+          if (first_seg && kb - kb0 < pre) {
+            // stage armed and its A tiles issued before pdl_wait
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY)) {
+              *(volatile int*)abort_flag = 1;
+              stop = true;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            load_a(stage, kb, u);
+          }
+          tma_load_2d(sB + stage * C::B_BYTES, tmB, &full[stage], kb * BK, 0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (stop) break;
+        first_seg = false;
+        it += kb1 - kb0;
+      }
+      // Drain: every armed stage must complete before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s) {
+        mbar_wait(&empty[stage], phase ^ 1, FB_KERR_TIMEOUT_EMPTY);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: one accumulator pair per segment ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16<BM, BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int seg = 0;
+      for (long long it = it0; it < it1 && !*(volatile int*)abort_flag; ++seg) {
+        const int kb0 = static_cast<int>(it % KB);
+        const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
+        const int acc = NBUF == 2 ? (seg & 1) : 0;
+        const uint32_t aphase = NBUF == 2 ? ((seg >> 1) & 1) : (seg & 1);
+        if (!mbar_wait(&tempty[acc], aphase ^ 1, FB_KERR_TIMEOUT_TMEM)) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::ACC_COLS;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, FB_KERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES));
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            const uint64_t adesc = sdesc_sw128(smem_u32(sA + (stage * 2 + mt) * C::A_BYTES));
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              mma_bf16(d_tmem + mt * BN, adesc + (uint64_t)(k * 2), bdesc + (uint64_t)(k * 2), idesc,
+                       (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit(&tfull[acc]);
+        if (!ok) {
+          *(volatile int*)abort_flag = 1;
+          break;
+        }
+        it += kb1 - kb0;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    pdl_wait();  // flag and output writes follow the previous kernel
+    const int quarter = warp & 3;
+    const int et = threadIdx.x - 64;    // 0..127; 0 draws tickets and issues the tile stores
+    const int f = quarter * 32 + lane;  // feature (TMEM lane) of this thread within the unit
+    uint32_t ephase = 0, chunk = 0;
+    bool ok = true;
+    auto epi_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ebar);
+      const bool done = mbar_wait(ebar, ephase, FB_KERR_TIMEOUT_TMEM);
+      ephase ^= 1;
+      return done;
+    };
+    // One piece's slot: gate then up, each [BN / 4][128 features][4 columns]
+    // of fp32, so that a warp's float4 accesses of one column group are 512
+    // contiguous bytes.
+    constexpr size_t SLOT = static_cast<size_t>(2) * BM * BN;
+    int seg = 0;
+    for (long long it = it0; ok && it < it1 && !*(volatile int*)abort_flag; ++seg) {
+      const int u = static_cast<int>(it / KB);
+      const int kb0 = static_cast<int>(it % KB);
+      const int kb1 = static_cast<int>(min(static_cast<long long>(KB), kb0 + (it1 - it)));
+      it += kb1 - kb0;
+      const int acc = NBUF == 2 ? (seg & 1) : 0;
+      const uint32_t aphase = NBUF == 2 ? ((seg >> 1) & 1) : (seg & 1);
+      if (!mbar_wait(&tfull[acc], aphase, FB_KERR_TIMEOUT_TMEM)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_g = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::ACC_COLS;
+      const int first = cta_of(static_cast<long long>(u) * KB);
+      const int npieces = cta_of(static_cast<long long>(u) * KB + KB - 1) - first + 1;
+      const int piece = static_cast<int>(blockIdx.x) - first;
+      if (npieces > SWIGLU_SK_MAXP) {  // the host sizes the grid so that this cannot happen
+        set_status(FB_KERR_BAD_ARG);
+        ok = false;
+        break;
+      }
+      int* ticket = flags + u * (1 + SWIGLU_SK_MAXP);
+      int* ready = ticket + 1;
+      bool last = true;
+      if (npieces > 1) {
+        if (et == 0) *unit_ticket = atomicAdd(ticket, 1);
+        if (!(ok = epi_sync())) break;
+        last = *(volatile int*)unit_ticket == npieces - 1;
+      }
+      if (!last) {
+        // fp32 gate and up rows of this piece: row f, BN contiguous floats each
+        float4* slot = reinterpret_cast<float4*>(ws + static_cast<size_t>(u * SWIGLU_SK_MAXP + piece) * SLOT);
+#pragma unroll 1
+        for (int j = 0; j < 2; ++j) {
+          float4* dst = slot + static_cast<size_t>(j) * (BM * BN / 4) + f;
+#pragma unroll 1
+          for (int c1 = 0; c1 < BN; c1 += EC) {
+            uint32_t rr[EC];
+#pragma unroll
+            for (int q = 0; q < EC / 16; ++q)
+              tmem_ld16(t_g + j * BN + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(rr + 16 * q));
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < EC / 4; ++i)
+              dst[(c1 / 4 + i) * BM] = make_float4(__uint_as_float(rr[4 * i]), __uint_as_float(rr[4 * i + 1]),
+                                                   __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3]));
+          }
+        }
+        __threadfence();
+        if (!(ok = epi_sync())) break;  // all 128 rows written
+        if (et == 0) st_release_gpu(ready + piece, 1);
+      } else {
+        // Last piece: the other pieces' rows must be in place (their CTAs drew
+        // their tickets before this one; bounded wait for their flags).
+        for (int q = 0; q < npieces && ok; ++q) {
+          if (q == piece) continue;
+          const uint64_t t0 = globaltimer();
+          uint32_t spins = 0;
+          while (ld_acquire_gpu(ready + q) == 0) {
+            if ((++spins & 255u) == 0 && globaltimer() - t0 > FB_WAIT_NS) {
+              set_status(FB_KERR_TIMEOUT_PEER);
+              ok = false;
+              break;
+            }
+          }
+        }
+        if (!ok) break;
+        const float* slots = ws + static_cast<size_t>(u * SWIGLU_SK_MAXP) * SLOT;
+#pragma unroll 1
+        for (int c1 = 0; c1 < BN && ok; c1 += EC, ++chunk) {
+          const int buf = chunk & 1;
+          bf16* sb = reinterpret_cast<bf16*>(stg) + buf * (EPI_COLS * BM);
+          uint32_t rg[EC], ru[EC];
+#pragma unroll
+          for (int q = 0; q < EC / 16; ++q) {
+            tmem_ld16(t_g + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(rg + 16 * q));
+            tmem_ld16(t_g + BN + c1 + 16 * q, *reinterpret_cast<uint32_t(*)[16]>(ru + 16 * q));
+          }
+          tmem_ld_wait();
+          // sum of the pieces in piece order, this CTA's own from TMEM
+          float g[EC], v[EC];
+#pragma unroll
+          for (int t = 0; t < EC; ++t) g[t] = v[t] = 0.f;
+#pragma unroll 1
+          for (int q = 0; q < npieces; ++q) {
+            if (q == piece) {
+#pragma unroll
+              for (int t = 0; t < EC; ++t) {
+                g[t] += __uint_as_float(rg[t]);
+                v[t] += __uint_as_float(ru[t]);
+              }
+            } else {
+              const float4* pg = reinterpret_cast<const float4*>(slots + q * SLOT) + (c1 / 4) * BM + f;
+              const float4* pu = pg + BM * BN / 4;
+#pragma unroll
+              for (int i = 0; i < EC / 4; ++i) {
+                const float4 a = __ldcg(pg + i * BM), b = __ldcg(pu + i * BM);
+                g[4 * i] += a.x;
+                g[4 * i + 1] += a.y;
+                g[4 * i + 2] += a.z;
+                g[4 * i + 3] += a.w;
+                v[4 * i] += b.x;
+                v[4 * i + 1] += b.y;
+                v[4 * i + 2] += b.z;
+                v[4 * i + 3] += b.w;
+              }
+            }
+          }
+          if (et == 0 && chunk >= 2) bulk_wait_read_1();  // this buffer's previous store has read it
+          if (!(ok = epi_sync())) break;
+#pragma unroll
+          for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(g[t] / (1.f + __expf(-g[t])) * v[t]);
+          fence_proxy_async();  // generic-proxy writes -> visible to the TMA engine
+          if (!(ok = epi_sync())) break;
+          if (et == 0) {
+            tma_store_2d(tmO, sb, u * BM, c1);
+            bulk_commit();
+          }
+        }
+        // every piece has been read: clear the unit's counters for the next launch
+        if (ok && npieces > 1 && et == 0) {
+          *ticket = 0;
+          for (int q = 0; q < npieces; ++q) ready[q] = 0;
+        }
+      }
+      if (!ok) break;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (!ok) *(volatile int*)abort_flag = 1;
+    if (et == 0) bulk_wait_all();  // the tile stores have read shared memory and landed
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace
+
+#define FB_GEMM_SWIGLU_SK_INSTANCE(BN)                                                                              \
+  extern "C" __global__ void __launch_bounds__(NUM_THREADS, 1) fb_gemm_swiglu_sk_bn##BN(                            \
+      const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,                             \
+      const __grid_constant__ CUtensorMap tmO, int M, int N, int K, int mode, float* ws, int* flags) {              \
+    gemm_swiglu_sk_body<BN>(&tmA, &tmB, &tmO, M, N, K, mode, ws, flags);                                            \
+  }
+
+FB_GEMM_SWIGLU_SK_INSTANCE(256)
+
 // ==== two-SM variant (cta_group::2) ======================================================
 //
 // fb_gemm2_bf16_bn{BN}: a cluster of two CTAs (the two SMs of a TPC) computes

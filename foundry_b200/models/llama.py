@@ -250,7 +250,7 @@ class LlamaModel:
     def _mlp(self, st, x, h, lw, rows):
         """SwiGLU FFN of x; returns the pending output that the next norm adds into h."""
         # decode batches: one GEMM whose epilogue applies SiLU(gate) * up
-        if ops.linear_swiglu(x, lw["gate_up"], st.act[:rows]) is None:
+        if ops.linear_swiglu(x, lw["gate_up"], st.act[:rows], sk=getattr(st, "swiglu_sk", None)) is None:
             gu = ops.linear(x, lw["gate_up"], out=st.gate_up[:rows], streamk=getattr(st, "sk", None))
             ops.silu_mul(gu, st.act[:rows])
         return self._row_parallel(st, st.act[:rows], lw["down"], h, rows, which=1)

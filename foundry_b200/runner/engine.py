@@ -30,7 +30,7 @@ from .. import ops
 from ..models import family
 from ..models.llama import LlamaConfig, LlamaWeights
 from ..ops.attention import PREFILL_TILE, DecodeWorkspace, decode_splits, prefill_tiles
-from ..ops.gemm import MAX_SPLITS, PartialBuffer
+from ..ops.gemm import MAX_SPLITS, SWIGLU_SK_ENABLED, PartialBuffer, swiglu_sk_sizes
 from .arena import Arena
 
 PAGE = 64
@@ -148,11 +148,16 @@ class DecodeState:
         self.k_cache, self.v_cache = k_cache, v_cache
         _model_buffers(self, ecfg.model, w, arena, b)
         # fp32 split-K slices of the decode GEMMs (consumed by the next op)
-        self.part = PartialBuffer(buf=arena.empty((MAX_SPLITS * b * max(w.qkv_dim_l, cfg.hidden),), torch.float32))
-        # stream-K GEMMs (gate_up, lm_head) keep their partial tiles in the
-        # split-K slice buffer (free between the ops that use it) and their
-        # tickets in a zeroed flag array that every launch leaves zeroed
+        part_n = MAX_SPLITS * b * max(w.qkv_dim_l, cfg.hidden)
+        sk_ws_n, sk_fl_n = swiglu_sk_sizes(w.inter_l) if w.inter_l and SWIGLU_SK_ENABLED else (0, 0)
+        self.part = PartialBuffer(buf=arena.empty((max(part_n, sk_ws_n),), torch.float32))
+        # stream-K GEMMs (gate_up, lm_head, and the fused gate/up + SwiGLU
+        # when FOUNDRY_SWIGLU_SK=1) keep their partial tiles in the split-K
+        # slice buffer (free between the ops that use it) and their tickets in
+        # zeroed flag arrays that every launch leaves zeroed
         self.sk = ops.StreamKBuffer(self.part.buf, arena.zeros((1024 * 8,), torch.int32))
+        self.swiglu_sk = (ops.StreamKBuffer(self.part.buf, arena.zeros((sk_fl_n,), torch.int32))
+                          if sk_fl_n else None)
         sizes = ecfg.graph_sizes or default_graph_sizes(b)
         self.attn_splits = {s: decode_splits(s, nkv, self.max_pages) for s in sizes}
         for s in range(1, b + 1):

@@ -12,7 +12,12 @@ tokens it prints one JSON line per variant:
   unit (default 1);
 - ``pair<B>s<S>``: two-SM tiles of B tokens with S splits;
 - ``sk<B>``: stream-K over one-SM tiles of B tokens;
-- ``cublas``: ``torch.matmul`` on the same operands (cuBLAS), for comparison.
+- ``cublas``: ``torch.matmul`` on the same operands (cuBLAS), for comparison;
+- ``swiglu`` (gate_up only): the fused gate/up GEMM whose epilogue writes
+  silu(gate) * up (``fb_gemm_bf16_bn*_m2``, one 128-feature unit per CTA);
+- ``swiglusk`` (gate_up only): its stream-K form (``fb_gemm_swiglu_sk_bn256``,
+  every CTA an equal share of the unit x k-block iterations; off in the
+  decode step unless FOUNDRY_SWIGLU_SK=1).
 ``--ops`` restricts the run to some layers (e.g. ``gate_up,lm_head``).
 
 Each line gives the plan (tile width, splits, grid) and the mean time of
@@ -90,8 +95,21 @@ def main(argv=None) -> int:
         base = G.plan(t, n, k)
         for v in a.variants.split(","):
             cublas = v == "cublas"  # torch.matmul (cuBLAS / cuBLASLt) on the same operands, for comparison
+            swiglu = v in ("swiglu", "swiglusk")
+            swiglu_sk = None
             if v in ("plan", "cublas"):
                 p = base
+            elif swiglu:
+                if name != "gate_up":
+                    continue
+                p = G.plan_swiglu(t, n // 2, k) if v == "swiglu" else G.plan_swiglu_sk(t, n // 2, k, force=True)
+                if p is None:
+                    continue
+                act = torch.empty(t, n // 2, dtype=torch.bfloat16, device="cuda")
+                if p.streamk:
+                    ws_n, fl_n = G.swiglu_sk_sizes(n // 2)
+                    swiglu_sk = G.StreamKBuffer(torch.empty(ws_n, dtype=torch.float32, device="cuda"),
+                                                torch.zeros(fl_n, dtype=torch.int32, device="cuda"))
             elif v == "pair":
                 if not base.swap or n < 256:
                     continue
@@ -116,13 +134,17 @@ def main(argv=None) -> int:
             else:
                 raise SystemExit(f"unknown variant {v!r}")
 
-            skb = G.StreamKBuffer(torch.empty(sms * 128 * 256, dtype=torch.float32, device="cuda"),
-                                  torch.zeros(sms * 8, dtype=torch.int32, device="cuda")) if p.streamk else None
+            skb = None
+            if p.streamk and not swiglu:
+                skb = G.StreamKBuffer(torch.empty(sms * 128 * 256, dtype=torch.float32, device="cuda"),
+                                      torch.zeros(sms * 8, dtype=torch.int32, device="cuda"))
 
             def run():
                 if cublas:
                     return torch.matmul(x, w.T, out=out)
                 with G._rt.pdl() if a.pdl else contextlib.nullcontext():
+                    if swiglu:
+                        return G.linear_swiglu(x, w, act, plan_override=p, sk=swiglu_sk)
                     return G.linear(x, w, out=out, partials=pb if p.splits > 1 else None, plan_override=p,
                                     streamk=skb)
 
@@ -164,14 +186,18 @@ def main(argv=None) -> int:
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1000 / a.iters - flush_us
             line = {"op": name, "tokens": t, "n": n, "k": k, "variant": v,
-                    "kernel": "cublas" if cublas else p.kernel, "bn": p.bn,
+                    "kernel": "cublas" if cublas else (f"fb_gemm_swiglu_sk_bn{p.bn}" if swiglu_sk else p.kernel),
+                    "bn": p.bn,
                     "splits": p.splits, "grid": p.grid, "us": round(us, 1),
                     "weight_tbps": round(n * k * 2 / (us * 1e-6) / 1e12, 2),
                     "tflops": round(2 * t * n * k / (us * 1e-6) / 1e12, 1)}
             if a.check:
                 y = (r.buf[: r.splits * r.stride].view(r.splits, t, n).sum(0) if isinstance(r, G.Partial)
                      else r.float())
-                line["max_err"] = round((y - ref).abs().max().item(), 4)
+                want = ref
+                if swiglu:  # [gate; up] rows: silu(x @ gate.T) * (x @ up.T)
+                    want = torch.nn.functional.silu(ref[:, : n // 2]) * ref[:, n // 2:]
+                line["max_err"] = round((y - want).abs().max().item(), 4)
             line["status"] = ops.status("gemm_bf16")
             print(json.dumps(line), flush=True)
             if line["status"]:

@@ -404,6 +404,42 @@ def test_linear_swiglu(t, inter, k, bn):
     assert ops.status("gemm_bf16") == 0
 
 
+@pytest.mark.parametrize("t,inter,k,pdl", [(256, 14336, 4096, True), (200, 11008, 4096, False),
+                                           (160, 12288, 1024, True), (129, 9728, 2048, False)])
+def test_linear_swiglu_streamk(t, inter, k, pdl):
+    """Stream-K form of the fused gate/up + SwiGLU GEMM (every CTA an equal
+    share of the (unit, k-block) iterations, units cut into up to three
+    pieces summed by the last CTA) against fp32; a second launch gives the
+    same bits (piece-order sums) and every launch leaves the flags zero."""
+    import contextlib
+
+    from foundry_b200 import ops
+    from foundry_b200.ops import _rt
+    from foundry_b200.ops.gemm import plan_swiglu_sk, swiglu_sk_sizes
+
+    p = plan_swiglu_sk(t, inter, k, force=True)
+    assert p is not None and p.streamk
+    x = _bf(t, k, seed=61)
+    w = _bf(2 * inter, k, seed=62, scale=0.05)
+    ws_n, fl_n = swiglu_sk_sizes(inter)
+    sk = ops.StreamKBuffer(torch.full((ws_n,), float("nan"), device="cuda"),
+                           torch.zeros(fl_n, dtype=torch.int32, device="cuda"))
+    out = torch.full((t, inter), float("nan"), dtype=torch.bfloat16, device="cuda")
+    with _rt.pdl() if pdl else contextlib.nullcontext():
+        assert ops.linear_swiglu(x, w, out, plan_override=p, sk=sk) is out
+    first = out.clone()
+    gu = x.float() @ w.float().T
+    ref = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+    torch.testing.assert_close(out.float(), ref, atol=3e-2, rtol=2e-2)
+    assert int(sk.flags.abs().sum()) == 0
+    out.fill_(float("nan"))
+    with _rt.pdl() if pdl else contextlib.nullcontext():
+        ops.linear_swiglu(x, w, out, plan_override=p, sk=sk)
+    assert torch.equal(out, first)
+    assert int(sk.flags.abs().sum()) == 0
+    assert ops.status("gemm_bf16") == 0
+
+
 @pytest.mark.parametrize("t,n,k", [(256, 4096, 4096), (256, 6144, 4096), (200, 4096, 1024), (64, 28672, 512)])
 def test_linear_under_programmatic_dependent_launch(t, n, k):
     """Decode GEMMs launched with programmatic dependent launch (as inside
