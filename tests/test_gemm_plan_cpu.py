@@ -74,3 +74,32 @@ def test_pair_tile_policy():
                 assert p.bn == 256 and p.kernel in KERNELS
         elif G._PAIR == "0":
             assert not any(G.plan(t, n, k, sms=148).pair for (t, n, k) in SHAPES)
+
+
+def _pieces_brute(units, kb, grid):
+    """Pieces per unit by walking every iteration (the kernel's ranges)."""
+    total = units * kb
+    owner = [max(b for b in range(grid) if total * b // grid <= i) for i in range(total)]
+    return max(len(set(owner[u * kb:(u + 1) * kb])) for u in range(units))
+
+
+@pytest.mark.parametrize("units,kb,grid", [(112, 64, 148), (96, 16, 148), (76, 32, 148), (140, 64, 148), (28, 128, 148),
+                                           (112, 64, 147), (10, 8, 37)])
+def test_swiglu_streamk_pieces(units, kb, grid):
+    """The host's count of CTAs sharing one unit matches a walk over the
+    kernel's iteration ranges; the plan exists only when it stays within the
+    kernel's slot count, and names an exported kernel."""
+    assert G.swiglu_sk_pieces(units, kb, grid) == _pieces_brute(units, kb, grid)
+    src = open(os.path.join(ROOT, "csrc", "kernels", "gemm_bf16.cu")).read()
+    assert f"constexpr int SWIGLU_SK_MAXP = {G.SWIGLU_SK_MAXP};" in src
+    assert re.search(rf"^FB_GEMM_SWIGLU_SK_INSTANCE\({G.SWIGLU_SK_BN}\)", src, re.M)
+    p = G.plan_swiglu_sk(256, units * G.BM, kb * G.BK, sms=grid, force=True)
+    ok = units < grid and units * kb >= grid and G.swiglu_sk_pieces(units, kb, grid) <= G.SWIGLU_SK_MAXP
+    assert (p is not None) == ok
+    if p is not None:
+        assert p.streamk and p.mt == 2 and p.grid == grid and p.bn == G.SWIGLU_SK_BN
+    # off unless asked for: the default plan never picks it
+    if not G.SWIGLU_SK_ENABLED:
+        assert G.plan_swiglu_sk(256, units * G.BM, kb * G.BK, sms=grid) is None
+    ws_n, fl_n = G.swiglu_sk_sizes(units * G.BM)
+    assert ws_n == units * G.SWIGLU_SK_MAXP * 2 * G.BM * G.SWIGLU_SK_BN and fl_n == units * (1 + G.SWIGLU_SK_MAXP)
