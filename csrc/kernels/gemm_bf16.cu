@@ -1074,6 +1074,15 @@ namespace {
 
 constexpr int SWIGLU_SK_MAXP = 3;  // pieces per unit (flags: ticket + one ready word per piece)
 
+// Bulk (non-tensor) global -> shared copy, completion on `bar`; both
+// addresses 16-byte aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 template <int BN>
 __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, const CUtensorMap* tmB,
                                                     const CUtensorMap* tmO, int M, int N, int K, int mode,
@@ -1093,7 +1102,13 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* ebar = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 1);
+  // Fix-up of the CTA's final segment: the other pieces' rows of one 32-column
+  // chunk (gate 16 KB + up 16 KB) per slot of the then idle TMA ring.
+  constexpr int PF_BYTES = 2 * EC * BM * 4;
+  constexpr int PF_SLOTS = (STAGES * C::STAGE_BYTES) / PF_BYTES;
+  static_assert(PF_SLOTS >= SWIGLU_SK_MAXP - 1, "one chunk of every other piece in flight");
+  uint64_t* pbar = ebar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pbar + PF_SLOTS);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   int* unit_ticket = abort_flag + 1;  // the ticket this CTA drew for its current unit
 
@@ -1125,6 +1140,7 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
       mbar_init(&tempty[a], 4);
     }
     mbar_init(ebar, 4);
+    for (int q = 0; q < PF_SLOTS; ++q) mbar_init(&pbar[q], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async();
@@ -1336,9 +1352,15 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
                                                    __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3]));
           }
         }
+        // The stores read registers: the accumulators go back to the MMA
+        // warp now, and the next piece's MMAs overlap the stores' drain.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
         __threadfence();
         if (!(ok = epi_sync())) break;  // all 128 rows written
         if (et == 0) st_release_gpu(ready + piece, 1);
+        continue;
       } else {
         // Last piece: the other pieces' rows must be in place (their CTAs drew
         // their tickets before this one; bounded wait for their flags).
@@ -1356,6 +1378,29 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
         }
         if (!ok) break;
         const float* slots = ws + static_cast<size_t>(u * SWIGLU_SK_MAXP) * SLOT;
+        // After the CTA's final segment the ring is idle (its MMAs are done
+        // and the producer issues nothing more): the other pieces' rows come
+        // in by bulk copies, PF_SLOTS chunks ahead, instead of one dependent
+        // L2 round trip per chunk and piece.
+        const int nq = npieces - 1;
+        const int items = (BN / EC) * nq;  // (chunk, other piece), chunk-major
+        const bool staged = nq > 0 && it >= it1;
+        int issued = 0, waited = 0;  // items issued (thread 0) / waited for (each thread)
+        auto issue = [&](int i) {
+          ++issued;
+          const int c = i / nq, qi = i % nq;
+          const int q = qi < piece ? qi : qi + 1;
+          const int sl = i % PF_SLOTS;
+          const float* src = slots + q * SLOT + static_cast<size_t>(c) * (EC * BM);
+          uint8_t* dst = smem + sl * PF_BYTES;
+          mbar_arrive_expect_tx(&pbar[sl], PF_BYTES);
+          bulk_copy_g2s(dst, src, PF_BYTES / 2, &pbar[sl]);
+          bulk_copy_g2s(dst + PF_BYTES / 2, src + BM * BN, PF_BYTES / 2, &pbar[sl]);
+        };
+        if (staged && et == 0) {
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // acquired rows -> bulk copy reads
+          for (int i = 0; i < min(items, PF_SLOTS); ++i) issue(i);
+        }
 #pragma unroll 1
         for (int c1 = 0; c1 < BN && ok; c1 += EC, ++chunk) {
           const int buf = chunk & 1;
@@ -1372,12 +1417,31 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
 #pragma unroll
           for (int t = 0; t < EC; ++t) g[t] = v[t] = 0.f;
 #pragma unroll 1
-          for (int q = 0; q < npieces; ++q) {
+          for (int q = 0; q < npieces && ok; ++q) {
             if (q == piece) {
 #pragma unroll
               for (int t = 0; t < EC; ++t) {
                 g[t] += __uint_as_float(rg[t]);
                 v[t] += __uint_as_float(ru[t]);
+              }
+            } else if (staged) {
+              const int i = (c1 / EC) * nq + (q < piece ? q : q - 1);
+              const int sl = i % PF_SLOTS;
+              if (!(ok = mbar_wait(&pbar[sl], (i / PF_SLOTS) & 1, FB_KERR_TIMEOUT_FULL))) break;
+              ++waited;
+              const float4* pg = reinterpret_cast<const float4*>(smem + sl * PF_BYTES) + f;
+              const float4* pu = pg + PF_BYTES / 2 / 16;
+#pragma unroll
+              for (int i4 = 0; i4 < EC / 4; ++i4) {
+                const float4 a = pg[i4 * BM], b = pu[i4 * BM];
+                g[4 * i4] += a.x;
+                g[4 * i4 + 1] += a.y;
+                g[4 * i4 + 2] += a.z;
+                g[4 * i4 + 3] += a.w;
+                v[4 * i4] += b.x;
+                v[4 * i4 + 1] += b.y;
+                v[4 * i4 + 2] += b.z;
+                v[4 * i4 + 3] += b.w;
               }
             } else {
               const float4* pg = reinterpret_cast<const float4*>(slots + q * SLOT) + (c1 / 4) * BM + f;
@@ -1396,8 +1460,15 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
               }
             }
           }
+          if (!ok) break;
           if (et == 0 && chunk >= 2) bulk_wait_read_1();  // this buffer's previous store has read it
           if (!(ok = epi_sync())) break;
+          if (staged && et == 0) {  // every thread has read this chunk's slots: refill them
+            for (int qi = 0; qi < nq; ++qi) {
+              const int i = (c1 / EC) * nq + qi + PF_SLOTS;
+              if (i < items) issue(i);
+            }
+          }
 #pragma unroll
           for (int t = 0; t < EC; ++t) sb[t * BM + f] = f2bf(g[t] / (1.f + __expf(-g[t])) * v[t]);
           fence_proxy_async();  // generic-proxy writes -> visible to the TMA engine
@@ -1407,6 +1478,10 @@ __device__ __forceinline__ void gemm_swiglu_sk_body(const CUtensorMap* tmA, cons
             bulk_commit();
           }
         }
+        // Copies still in flight after an error land before the CTA exits
+        // (bounded waits; items are issued and waited for in order).
+        if (staged && et == 0)
+          for (int i = waited; i < issued; ++i) mbar_wait(&pbar[i % PF_SLOTS], (i / PF_SLOTS) & 1, FB_KERR_TIMEOUT_FULL);
         // every piece has been read: clear the unit's counters for the next launch
         if (ok && npieces > 1 && et == 0) {
           *ticket = 0;

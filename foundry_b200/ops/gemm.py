@@ -323,14 +323,14 @@ def plan_swiglu(m_tok: int, inter: int, k: int, sms: int | None = None) -> Plan 
 # for 129-256 tokens with fewer 128-feature units than SMs, every CTA takes
 # an equal share of the (unit, k-block) iterations instead of one unit each.
 # Off unless FOUNDRY_SWIGLU_SK=1. Measured on B200 at the Llama-3-8B decode
-# shape (256 tokens, 14336 features = 112 units): 78.3 us against 62.6 us for
-# the one-unit-per-CTA kernel on 112 SMs (CUDA graph of 20 launches, L2
-# flushed before each, programmatic dependent launch), decode step 28.6k vs
-# 30.1k tok/s. Every SM gets the same MMA work (tensor pipe 50.5 % average,
-# 51.1 % max), but a CTA that writes a piece's fp32 rows in mid-range (the
-# 512-column accumulator pair fills TMEM, so its MMAs wait) and reads another
-# piece back at the end runs up to 119.6k cycles against 75.8k for one that
-# does neither: the fix-up costs more than the 36 idle SMs.
+# shape (256 tokens, 14336 features = 112 units; CUDA graph of 20 launches,
+# L2 flushed before each, programmatic dependent launch): 72.2 us against
+# 62.1 us for the one-unit-per-CTA kernel on 112 SMs. A first version (fix-up
+# reads straight from L2, accumulators held until the fp32 stores drained)
+# took 78.3 us and the decode step 28.6k vs 30.1k tok/s; there every SM got
+# the same MMA work (tensor pipe 50.5 % average, 51.1 % max) but CTAs that
+# write one piece and read another ran up to 119.6k cycles against 75.8k:
+# the fix-up costs more than the 36 idle SMs.
 SWIGLU_SK_ENABLED = os.environ.get("FOUNDRY_SWIGLU_SK", "0") == "1"
 SWIGLU_SK_BN = 256
 SWIGLU_SK_MAXP = 3  # pieces of one unit (csrc/kernels/gemm_bf16.cu, SWIGLU_SK_MAXP)
