@@ -15,6 +15,7 @@ while it reads its input. Callers that cannot consume slices pass no
 
 from __future__ import annotations
 
+import functools
 import math
 import os
 from dataclasses import dataclass
@@ -336,6 +337,7 @@ SWIGLU_SK_BN = 256
 SWIGLU_SK_MAXP = 3  # pieces of one unit (csrc/kernels/gemm_bf16.cu, SWIGLU_SK_MAXP)
 
 
+@functools.lru_cache(maxsize=64)
 def swiglu_sk_pieces(units: int, kb: int, grid: int) -> int:
     """Most CTAs that share one unit when ``grid`` CTAs split ``units * kb``
     iterations into ranges [T*b//grid, T*(b+1)//grid) (the kernel's split)."""
